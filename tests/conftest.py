@@ -1,0 +1,14 @@
+"""Pytest configuration: the ``gpu`` marker and the repository import path."""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config) -> None:
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) and the built CUDA library")
