@@ -1,0 +1,347 @@
+"""Throughput of the LSSO mixer layer on B200: tokens/s forward+backward.
+
+Workload (BASELINE config 2 at L=4096): ``LSSO(LSSOConfig(256, 8, 32))`` with
+seeded default init, x ~ N(0,1) cast to FP16 of shape [64, 4096, 256] per GPU
+(weak scaling: the batch grows with the number of ranks), shared positions,
+one step = forward + ``loss = y.float().square().mean()`` + backward (x
+carries a gradient, as in the reference's benchmarks/benchmark_ball.py) and,
+with several GPUs, one NCCL all-reduce of the flat gradient buffer.
+
+``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
+prints one JSON line (rank 0).  ``--impl reference`` times the CPU oracle
+restatement of the reference algorithm on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "LSSO mixer tokens/s fwd & fwd+bwd (L=4096,r=32) 1–8 B200; % HBM roofline"
+DIM, HEADS, RANK = 256, 8, 32
+PUBLISHED_FWD_BWD = 64 * 4096 / 29.160e-3  # RTX 5070 Ti, native contract 6, fwd+bwd at N=4096
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=64, help="samples per GPU")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def workload(args, world: int) -> dict:
+    return {
+        "workload": f"BASELINE config 2 (mixer bench shape) at L={args.seq}: LSSO(dim={DIM}, heads={HEADS}, "
+                    f"rank={RANK}) DYNAMIC + Rank-Rotary, x [B={args.batch} per GPU, {args.seq}, {DIM}] FP16, shared "
+                    "positions, fwd+bwd with loss=y.float().square().mean()",
+        "global_batch": args.batch * world,
+        "seq_len": args.seq,
+        "parallelism": f"dp{world}",
+        "l2": "inputs larger than L2 (x 134 MB, packed projection 268 MB per GPU at the default size)",
+    }
+
+
+# ---------------------------------------------------------------------------- CPU legs
+def cpu_fwd_bwd_tokens_per_s(seq: int, budget_s: float, steps: int | None = None, warmup: int = 1):
+    """Oracle restatement (FP32 reference CPU path) on one sample of the workload."""
+    import numpy as np
+
+    from oracle import lsso_oracle as O
+
+    params = O.init_params(DIM, HEADS, RANK, seed=0)
+    x = np.random.default_rng(0).standard_normal((1, seq, DIM)).astype(np.float32)
+
+    def one():
+        y, state = O.module_forward(params, x, None, None, heads=HEADS, rank=RANK, dtype=np.float32,
+                                    return_state=True)
+        O.module_backward(2.0 * y / y.size, state)
+
+    for _ in range(warmup):
+        one()
+    times = []
+    start = time.perf_counter()
+    while True:
+        t = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() - start >= budget_s and len(times) >= 3:
+            break
+    median = statistics.median(times)
+    return seq / median, len(times), median
+
+
+def reference_arm(args, rank: int, world: int) -> int:
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    value, n, median = cpu_fwd_bwd_tokens_per_s(args.seq, args.cpu_seconds, steps=args.steps, warmup=args.warmup)
+    sample = f"1 sample x {args.seq} tokens per step (bench shape), median of {n} steps"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * median, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload(args, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU NumPy restatement of the reference algorithm (oracle/lsso_oracle.py, FP32 reference-path "
+                "rounding); the reference's own PyTorch code does not travel to the GPU box",
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None) -> None:
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if gpu_id:
+            cmd += ["-i", gpu_id]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for row in out.strip().splitlines():
+            cols = [c.strip() for c in row.split(",")]
+            if len(cols) < 9:
+                continue
+            try:
+                sm.append(float(cols[1]))
+                smax.append(float(cols[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, cols[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- GPU arm
+def algorithmic_bytes(kernel: str, B: int, N: int) -> float | None:
+    """Compulsory HBM bytes of one launch of our kernels at this workload (2-byte elements)."""
+    D, W, HR = DIM, HEADS * RANK + DIM, HEADS * RANK
+    T = B * N
+    table = {
+        "moments_fwd": 2 * W * T,            # read the packed projection once
+        "readout": (2 * W + 2 * D) * T,      # read projection, write mixed coordinates
+        "moments_bwd": (2 * HR + 2 * D) * T,  # read relation and the upstream gradient
+        "grad": (2 * D + 4 * W) * T,         # read dY and projection, write the packed gradient
+    }
+    return table.get(kernel)
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def traffic_record() -> dict:
+    path = ROOT / "profiles" / "dram_traffic.json"
+    return json.loads(path.read_text()) if path.is_file() else {}
+
+
+def gpu_arm(args, rank: int, world: int, local: int) -> int:
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    from lsso import LSSO, LSSOConfig
+    from lsso.ball import cuda
+    from lsso_b200.ball import _native
+
+    cuda.load(device=local)
+    torch.manual_seed(0)
+    layer = LSSO(LSSOConfig(DIM, HEADS, RANK)).to(device)
+    params = list(layer.parameters())
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    B, N = args.batch, args.seq
+    x = torch.randn(B, N, DIM, device=device, generator=gen).half().requires_grad_()
+    flat = torch.empty(sum(p.numel() for p in params), device=device, dtype=torch.float32)
+
+    def reduce_gradients() -> None:
+        if world == 1:
+            return
+        torch.cat([p.grad.reshape(-1) for p in params], out=flat)
+        dist.all_reduce(flat)
+        flat.div_(world)
+        offset = 0
+        for p in params:
+            n = p.numel()
+            p.grad.copy_(flat[offset:offset + n].view_as(p))
+            offset += n
+
+    def train_step(xx):
+        for p in params:
+            p.grad = None
+        xx.grad = None
+        with torch.autocast("cuda", dtype=torch.float16):
+            loss = layer(xx, implementation="cuda").float().square().mean()
+        loss.backward()
+        reduce_gradients()
+        return loss
+
+    def fwd_step(xx):
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.float16):
+            layer(xx, implementation="cuda")
+
+    def timed(fn, steps: int) -> float:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([start.elapsed_time(end)], device=device)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    for _ in range(args.warmup):
+        train_step(x)
+    for _ in range(max(3, args.warmup)):
+        fwd_step(x)
+
+    # ---- device-resident fwd+bwd (the headline `value`), with per-kernel events and clocks
+    gpu_uuid = None
+    try:
+        gpu_uuid = str(torch.cuda.get_device_properties(device).uuid)
+        gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else "GPU-" + gpu_uuid
+    except Exception:  # noqa: BLE001
+        gpu_uuid = None
+    sampler = ClockSampler(gpu_uuid)
+    _native.profile_start()
+    train_ms = timed(lambda: train_step(x), args.steps)
+    kernels = _native.profile_stop()
+    clocks = sampler.stop()
+    fwd_ms = timed(lambda: fwd_step(x), args.steps)
+
+    # ---- end to end through the public API: pinned host x in, loss out, every step
+    x_host = x.detach().to("cpu").pin_memory()
+    loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x.detach())
+    counter = {"i": 0}
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        loss = train_step(x_dev.detach().requires_grad_())
+        loss_host[counter["i"] % args.steps].copy_(loss.detach(), non_blocking=True)
+        counter["i"] += 1
+
+    e2e_step()
+    counter["i"] = 0
+    e2e_ms = timed(e2e_step, args.steps)
+    status = cuda.device_status(reset=False)
+
+    tokens = B * N * world
+    value = tokens * args.steps / (train_ms / 1e3)
+    line = None
+    if rank == 0:
+        peaks = measured_peaks()
+        ours = {k: v for k, v in kernels.items() if algorithmic_bytes(k, B, N) is not None}
+        dominant = max(ours, key=lambda k: ours[k][0]) if ours else None
+        roofline = None
+        if dominant is not None:
+            total_ms, launches = ours[dominant]
+            per_launch_s = total_ms / launches / 1e3
+            alg = algorithmic_bytes(dominant, B, N)
+            achieved = alg / per_launch_s / 1e9
+            traffic = traffic_record().get(dominant)
+            roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                        "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
+                        "algorithmic_bytes_per_launch": alg, "avg_launch_ms": total_ms / launches}
+        step_kernels = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
+                            **({} if algorithmic_bytes(k, B, N) is None else
+                               {"gbs": algorithmic_bytes(k, B, N) / (v[0] / v[1] / 1e3) / 1e9})}
+                        for k, v in kernels.items()}
+        cpu = None
+        if world == 1:
+            cpu_value, n, median = cpu_fwd_bwd_tokens_per_s(N, args.cpu_seconds)
+            cpu = {"value": cpu_value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"1 sample x {N} tokens fwd+bwd (bench shape), median of {n} steps, NumPy oracle "
+                             "(FP32 reference-path rounding) on all host threads"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": train_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": value / PUBLISHED_FWD_BWD,
+            "vs_baseline_note": "BASELINE.md fwd+bwd at N=4096 (8.99 M tokens/s, RTX 5070 Ti, one GPU)",
+            "dtype": "bf16", "data": "synthetic", "config": workload(args, world),
+            "fwd": {"value": tokens * args.steps / (fwd_ms / 1e3), "unit": "tokens/s",
+                    "ms_per_step": fwd_ms / args.steps},
+            "e2e": {"value": tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(), "d2h_bytes_per_step": 4},
+            "roofline": roofline, "kernels": step_kernels, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": sum(v[1] for v in kernels.values()), "device_status": status,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line))
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    return gpu_arm(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

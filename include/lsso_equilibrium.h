@@ -1,0 +1,134 @@
+/*
+ * lsso_equilibrium.h -- C ABI of the B200 (sm_100a) LSSO mixer library
+ * (lsso_equilibrium_sm100.so).
+ *
+ * The library implements the strict native operator of Yang916-yy/LSSO: the
+ * complete DYNAMIC + Rank-Rotary mixer (forward and analytic first-order
+ * backward) on BF16 packed coordinates.  Each entry point replaces one
+ * operator of the reference's TORCH_LIBRARY(lsso_equilibrium) extension
+ * (csrc/ball/binding.cpp:79-107 in the LSSO project); the argument meaning,
+ * shapes and dtypes follow csrc/ball/common.cuh:194-269.
+ *
+ * Conventions
+ *  - All pointers are device pointers on the current CUDA device, except
+ *    where noted.  BF16 tensors are passed as void*.
+ *  - The caller allocates every output and the workspace; the library never
+ *    allocates device memory.  Sizes come from the *_workspace_size queries.
+ *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
+ *    legacy default stream).  Entry points do not synchronize.
+ *  - Return value 0 means success.  Non-zero codes are LSSO_ERR_*; the text
+ *    of the last error of the calling thread is lsso_last_error().  Entry
+ *    points never abort the process.
+ */
+#ifndef LSSO_EQUILIBRIUM_H_
+#define LSSO_EQUILIBRIUM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LSSO_CONTRACT_VERSION 8
+
+#if defined(__GNUC__)
+#define LSSO_API __attribute__((visibility("default")))
+#else
+#define LSSO_API
+#endif
+
+enum {
+  LSSO_OK = 0,
+  LSSO_ERR_INVALID_ARGUMENT = 1,
+  LSSO_ERR_UNSUPPORTED_DEVICE = 2,
+  LSSO_ERR_CUDA = 3,
+  LSSO_ERR_WORKSPACE = 4
+};
+
+/* Native contract version (8).  Replaces lsso_equilibrium::contract_version
+ * (csrc/ball/binding.cpp:73-75,80-83). */
+LSSO_API int lsso_contract_version(void);
+
+/* Compute capability the library was compiled for, as major*10+minor (100). */
+LSSO_API int lsso_compiled_sm(void);
+
+/* Check that CUDA device `device` is the compiled SM; 0 on success, else
+ * LSSO_ERR_UNSUPPORTED_DEVICE with the reference's mismatch message
+ * (csrc/ball/common.cuh:271-301). */
+LSSO_API int lsso_check_device(int device);
+
+/* Text of the calling thread's last error ("" if none). */
+LSSO_API const char* lsso_last_error(void);
+
+/* Read the kernel status word of the current device (0 = no kernel reported a
+ * failure, 1 = a bounded tensor-core wait ran out).  Synchronizes the device.
+ * reset != 0 clears it afterwards. */
+LSSO_API int lsso_device_status(int reset);
+
+/* Floats per (sample, head) row of the training tape:
+ * N*R + 3*R*R + 2*R*(D/H) + 1 (pinned by the reference's tape-size test,
+ * tests/cuda/test_fast_path.py:1508-1509). */
+LSSO_API int64_t lsso_tape_stride(int64_t N, int64_t H, int64_t D, int64_t R);
+
+/* Workspace bytes for lsso_forward with these sizes (train != 0: a tape is
+ * produced).  positions_batched != 0 when centered positions are [B, N]. */
+LSSO_API size_t lsso_forward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                                   int positions_batched, int train);
+
+/* Forward mixer.  Replaces lsso_equilibrium::forward_inference (tape == NULL,
+ * pivots == NULL) and lsso_equilibrium::forward_train
+ * (csrc/ball/binding.cpp:84-90, forward.cu:1505-1556).
+ *   projected          BF16 [B, N, H*R + D], contiguous; masked rows zero
+ *   core_base_raw      FP32 [H, R, R]
+ *   core_drive_weight  FP32 [H, D/H, R]
+ *   eta_raw            FP32 [H]
+ *   centered_positions FP32 [N] or [B, N] (positions_batched), or NULL for t-(N-1)/2
+ *   valid_counts       FP32 [B] (max(n_valid, 1)) or NULL for N
+ *   mixed              BF16 [B, N, D] output
+ *   tape               FP32 [B*H, lsso_tape_stride(...)] output or NULL
+ *   pivots             INT32 [B*H, R] output (one-based) or NULL
+ * R must be 16, 32, 48 or 64; D must be a positive multiple of H. */
+LSSO_API int lsso_forward(const void* projected, const float* core_base_raw, const float* core_drive_weight,
+                 const float* eta_raw, const float* centered_positions, int positions_batched,
+                 const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                 void* mixed, float* tape, int32_t* pivots, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Workspace bytes for lsso_backward. */
+LSSO_API size_t lsso_backward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                                    int positions_batched);
+
+/* Analytic first-order backward.  Replaces lsso_equilibrium::backward
+ * (csrc/ball/binding.cpp:91-96, backward.cu:1634-1667).
+ *   grad_output            BF16 [B, N, D] (masked rows zero)
+ *   projected, core_*, eta_raw, centered_positions, valid_counts as in lsso_forward
+ *   tape, pivots           outputs of the training forward
+ *   grad_projected         BF16 [B, N, H*R + D] output
+ *   grad_core_base_raw     FP32 [H, R, R] output
+ *   grad_core_drive_weight FP32 [H, D/H, R] output
+ *   grad_eta_raw           FP32 [H] output
+ * Parameter gradients are reduced deterministically (no atomics). */
+LSSO_API int lsso_backward(const void* grad_output, const void* projected, const float* core_base_raw,
+                  const float* core_drive_weight, const float* eta_raw, const float* tape,
+                  const int32_t* pivots, const float* centered_positions, int positions_batched,
+                  const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                  void* grad_projected, float* grad_core_base_raw, float* grad_core_drive_weight,
+                  float* grad_eta_raw, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Per-kernel timing (no counterpart in the reference; instrumentation only).
+ * lsso_profile_start() makes every subsequent kernel launch of the library
+ * record a CUDA event pair on its launch stream; lsso_profile_stop()
+ * synchronizes those events, stops recording and reports, per kernel name,
+ * the summed device time in milliseconds and the launch count.  `names`
+ * receives `capacity` slots of 32 bytes each (NUL-terminated).  Returns the
+ * number of distinct kernels (or -1 on a CUDA error).  Intended for one
+ * thread at a time. */
+LSSO_API int lsso_profile_start(void);
+LSSO_API int lsso_profile_stop(int capacity, char* names, float* total_ms, int* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSSO_EQUILIBRIUM_H_ */

@@ -1,0 +1,387 @@
+// C ABI of lsso_equilibrium_sm100.so: argument validation, workspace layout
+// and the kernel sequences of the mixer.  See include/lsso_equilibrium.h.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/lsso_equilibrium.h"
+#include "mixer.h"
+#include "mixer_common.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(LSSO_ERR_CUDA, "CUDA error in %s: %s", where, cudaGetErrorString(e));
+}
+
+__device__ int g_status;
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+int* g_status_ptr[kMaxDevices];
+std::mutex g_device_mutex;
+
+int current_device(int* device) {
+  cudaError_t e = cudaGetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*device < 0 || *device >= kMaxDevices) return fail(LSSO_ERR_UNSUPPORTED_DEVICE, "device index out of range");
+  return LSSO_OK;
+}
+
+int check_sm(int device) {
+  int major = 0, minor = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if (major != 10 || minor != 0) {
+    return fail(LSSO_ERR_UNSUPPORTED_DEVICE,
+                "the loaded LSSO CUDA extension targets SM100 but received SM%d.%d; load the matching strict "
+                "artifact",
+                major, minor);
+  }
+  return LSSO_OK;
+}
+
+// Per-device facts resolved once: SM count and the status word's address.
+int device_info(int* device, int* sm_count, int** status) {
+  int rc = current_device(device);
+  if (rc != LSSO_OK) return rc;
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  if (g_status_ptr[*device] == nullptr) {
+    rc = check_sm(*device);
+    if (rc != LSSO_OK) return rc;
+    int count = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, *device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+    g_sm_count[*device] = count;
+    g_status_ptr[*device] = static_cast<int*>(ptr);
+  }
+  *sm_count = g_sm_count[*device];
+  *status = g_status_ptr[*device];
+  return LSSO_OK;
+}
+
+int validate_sizes(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R) {
+  if (B <= 0 || N <= 0 || H <= 0) return fail(LSSO_ERR_INVALID_ARGUMENT, "B, N, and H must be positive");
+  if (R != 16 && R != 32 && R != 48 && R != 64) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "the CUDA fast path supports rank in {16, 32, 48, 64}, got %lld",
+                static_cast<long long>(R));
+  }
+  if (D <= 0) return fail(LSSO_ERR_INVALID_ARGUMENT, "projected width must exceed H*R for a nonempty content channel");
+  if (D % H != 0) return fail(LSSO_ERR_INVALID_ARGUMENT, "projected content width D must be divisible by H");
+  // Grid sizes stay below 2^31 and chunk lengths in int range.
+  if (N > (int64_t(1) << 30) || B * H > (int64_t(1) << 24) || D / H > (int64_t(1) << 16)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "shape exceeds the supported launch range");
+  }
+  return LSSO_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct ForwardLayout {
+  size_t phase, partial, zbuf, rmat, total;
+};
+ForwardLayout forward_layout(const lsso::Plan& p, bool train) {
+  ForwardLayout l{};
+  size_t off = 0;
+  l.phase = off;
+  off = align256(off + sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
+  l.partial = off;
+  off = align256(off + sizeof(float) * p.BH * p.nchunks * p.ndt * 2 * p.R * (p.R + p.dt));
+  l.zbuf = off;
+  if (!train) off = align256(off + sizeof(float) * p.BH * p.R * p.d);
+  l.rmat = off;
+  off = align256(off + sizeof(uint16_t) * p.BH * p.d_pad * p.R);
+  l.total = off;
+  return l;
+}
+
+struct BackwardLayout {
+  size_t phase, partial, dbuf, lbuf, b1y, b1c, b1a, b2, gbase, gdrive, etastat, etadot, total;
+};
+BackwardLayout backward_layout(const lsso::Plan& p) {
+  BackwardLayout l{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  l.phase = take(sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
+  l.partial = take(sizeof(float) * p.BH * p.nchunks * p.ndt * 2 * p.R * p.dt);
+  l.dbuf = take(sizeof(float) * p.BH * p.R * p.d);
+  l.lbuf = take(sizeof(float) * p.BH * p.R * p.d);
+  l.b1y = take(sizeof(uint16_t) * p.BH * p.R * p.d_pad);
+  l.b1c = take(sizeof(uint16_t) * p.BH * p.R * p.d_pad);
+  l.b1a = take(sizeof(uint16_t) * p.BH * p.R * p.R);
+  l.b2 = take(sizeof(uint16_t) * p.BH * p.d_pad * p.R);
+  l.gbase = take(sizeof(float) * p.BH * p.R * p.R);
+  l.gdrive = take(sizeof(float) * p.BH * p.d * p.R);
+  l.etastat = take(sizeof(float) * p.BH * p.ntiles);
+  l.etadot = take(sizeof(float) * p.BH);
+  l.total = off;
+  return l;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int plan_for(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int positions_batched, lsso::Plan* plan) {
+  int rc = validate_sizes(B, N, H, D, R);
+  if (rc != LSSO_OK) return rc;
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  *plan = lsso::make_plan(B, N, H, D, R, positions_batched != 0, sms);
+  return LSSO_OK;
+}
+
+// ---------------------------------------------------------------- profiling
+struct ProfileRecord {
+  const char* name;
+  cudaEvent_t start;
+  cudaEvent_t stop;
+};
+std::vector<ProfileRecord> g_records;
+std::vector<cudaEvent_t> g_event_pool;
+size_t g_events_used = 0;
+
+cudaEvent_t take_event() {
+  if (g_events_used == g_event_pool.size()) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    g_event_pool.push_back(e);
+  }
+  return g_event_pool[g_events_used++];
+}
+
+void profile_before(const char* name, cudaStream_t stream) {
+  ProfileRecord r{name, take_event(), nullptr};
+  if (r.start != nullptr) cudaEventRecord(r.start, stream);
+  g_records.push_back(r);
+}
+
+void profile_after(const char* name, cudaStream_t stream) {
+  (void)name;
+  if (g_records.empty()) return;
+  cudaEvent_t e = take_event();
+  if (e != nullptr) cudaEventRecord(e, stream);
+  g_records.back().stop = e;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lsso_profile_start(void) {
+  g_records.clear();
+  g_events_used = 0;
+  lsso::g_before_launch = profile_before;
+  lsso::g_after_launch = profile_after;
+  return LSSO_OK;
+}
+
+int lsso_profile_stop(int capacity, char* names, float* total_ms, int* launches) {
+  lsso::g_before_launch = nullptr;
+  lsso::g_after_launch = nullptr;
+  std::vector<std::string> keys;
+  std::vector<float> totals;
+  std::vector<int> counts;
+  for (const ProfileRecord& r : g_records) {
+    if (r.start == nullptr || r.stop == nullptr) return -1;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess) return -1;
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess) return -1;
+    size_t k = 0;
+    while (k < keys.size() && keys[k] != r.name) ++k;
+    if (k == keys.size()) {
+      keys.emplace_back(r.name);
+      totals.push_back(0.0f);
+      counts.push_back(0);
+    }
+    totals[k] += ms;
+    counts[k] += 1;
+  }
+  g_records.clear();
+  g_events_used = 0;
+  const int n = static_cast<int>(keys.size());
+  for (int k = 0; k < n && k < capacity; ++k) {
+    if (names != nullptr) {
+      std::memset(names + 32 * k, 0, 32);
+      std::strncpy(names + 32 * k, keys[k].c_str(), 31);
+    }
+    if (total_ms != nullptr) total_ms[k] = totals[k];
+    if (launches != nullptr) launches[k] = counts[k];
+  }
+  return n;
+}
+
+int lsso_contract_version(void) { return LSSO_CONTRACT_VERSION; }
+
+int lsso_compiled_sm(void) { return 100; }
+
+int lsso_check_device(int device) {
+  g_last_error.clear();
+  return check_sm(device);
+}
+
+const char* lsso_last_error(void) { return g_last_error.c_str(); }
+
+int lsso_device_status(int reset) {
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  if (device_info(&device, &sms, &status) != LSSO_OK) return -1;
+  int value = 0;
+  if (cudaMemcpy(&value, status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (reset != 0) {
+    const int zero = 0;
+    if (cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+  }
+  return value;
+}
+
+int64_t lsso_tape_stride(int64_t N, int64_t H, int64_t D, int64_t R) {
+  if (H <= 0) return 0;
+  return N * R + 3 * R * R + 2 * R * (D / H) + 1;
+}
+
+size_t lsso_forward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int positions_batched,
+                                   int train) {
+  lsso::Plan p{};
+  if (plan_for(B, N, H, D, R, positions_batched, &p) != LSSO_OK) return 0;
+  return forward_layout(p, train != 0).total;
+}
+
+size_t lsso_backward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int positions_batched) {
+  lsso::Plan p{};
+  if (plan_for(B, N, H, D, R, positions_batched, &p) != LSSO_OK) return 0;
+  return backward_layout(p).total;
+}
+
+int lsso_forward(const void* projected, const float* core_base_raw, const float* core_drive_weight,
+                 const float* eta_raw, const float* centered_positions, int positions_batched,
+                 const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, void* mixed,
+                 float* tape, int32_t* pivots, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (projected == nullptr || core_base_raw == nullptr || core_drive_weight == nullptr || eta_raw == nullptr ||
+      mixed == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward: a required pointer is NULL");
+  }
+  if ((tape == nullptr) != (pivots == nullptr)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward: tape and pivots must be given together");
+  }
+  const bool batched = centered_positions != nullptr && positions_batched != 0;
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, batched ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const bool train = tape != nullptr;
+  const ForwardLayout l = forward_layout(p, train);
+  if (workspace_bytes < l.total || (l.total > 0 && workspace == nullptr)) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_forward: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, l.total);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  lsso::ForwardBuffers fb{};
+  fb.projected = static_cast<const lsso::bf16*>(projected);
+  fb.base = core_base_raw;
+  fb.drive = core_drive_weight;
+  fb.eta_raw = eta_raw;
+  fb.positions = centered_positions;
+  fb.positions_batched = batched ? 1 : 0;
+  fb.counts = valid_counts;
+  fb.mixed = static_cast<lsso::bf16*>(mixed);
+  fb.tape = tape;
+  fb.pivots = pivots;
+  fb.phase = reinterpret_cast<__half2*>(ws + l.phase);
+  fb.partial = reinterpret_cast<float*>(ws + l.partial);
+  fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.zbuf);
+  fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
+  fb.status = status;
+  fb.vec = p.vec && aligned16(projected) && aligned16(mixed);
+  const cudaError_t e = lsso::launch_forward(p, fb, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_forward");
+  return LSSO_OK;
+}
+
+int lsso_backward(const void* grad_output, const void* projected, const float* core_base_raw,
+                  const float* core_drive_weight, const float* eta_raw, const float* tape, const int32_t* pivots,
+                  const float* centered_positions, int positions_batched, const float* valid_counts, int64_t B,
+                  int64_t N, int64_t H, int64_t D, int64_t R, void* grad_projected, float* grad_core_base_raw,
+                  float* grad_core_drive_weight, float* grad_eta_raw, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  g_last_error.clear();
+  (void)core_base_raw;  // Theta (and with it the base) is read from the tape
+  (void)pivots;         // the LU factors carry no row exchanges (one-based identity)
+  (void)valid_counts;   // the tape records each sample's count
+  if (grad_output == nullptr || projected == nullptr || core_drive_weight == nullptr || eta_raw == nullptr ||
+      tape == nullptr || grad_projected == nullptr || grad_core_base_raw == nullptr ||
+      grad_core_drive_weight == nullptr || grad_eta_raw == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_backward: a required pointer is NULL");
+  }
+  const bool batched = centered_positions != nullptr && positions_batched != 0;
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, batched ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const BackwardLayout l = backward_layout(p);
+  if (workspace_bytes < l.total || workspace == nullptr) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_backward: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, l.total);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  lsso::BackwardBuffers bb{};
+  bb.grad_output = static_cast<const lsso::bf16*>(grad_output);
+  bb.projected = static_cast<const lsso::bf16*>(projected);
+  bb.drive = core_drive_weight;
+  bb.eta_raw = eta_raw;
+  bb.tape = tape;
+  bb.positions = centered_positions;
+  bb.grad_projected = static_cast<lsso::bf16*>(grad_projected);
+  bb.grad_base = grad_core_base_raw;
+  bb.grad_drive = grad_core_drive_weight;
+  bb.grad_eta = grad_eta_raw;
+  bb.phase = reinterpret_cast<__half2*>(ws + l.phase);
+  bb.partial = reinterpret_cast<float*>(ws + l.partial);
+  bb.dbuf = reinterpret_cast<float*>(ws + l.dbuf);
+  bb.lbuf = reinterpret_cast<float*>(ws + l.lbuf);
+  bb.b1y = reinterpret_cast<lsso::bf16*>(ws + l.b1y);
+  bb.b1c = reinterpret_cast<lsso::bf16*>(ws + l.b1c);
+  bb.b1a = reinterpret_cast<lsso::bf16*>(ws + l.b1a);
+  bb.b2 = reinterpret_cast<lsso::bf16*>(ws + l.b2);
+  bb.gbase = reinterpret_cast<float*>(ws + l.gbase);
+  bb.gdrive = reinterpret_cast<float*>(ws + l.gdrive);
+  bb.etastat = reinterpret_cast<float*>(ws + l.etastat);
+  bb.etadot = reinterpret_cast<float*>(ws + l.etadot);
+  bb.status = status;
+  bb.vec = p.vec && aligned16(projected) && aligned16(grad_output) && aligned16(grad_projected);
+  const cudaError_t e = lsso::launch_backward(p, bb, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_backward");
+  return LSSO_OK;
+}
+
+}  // extern "C"

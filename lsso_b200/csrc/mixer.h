@@ -1,0 +1,151 @@
+// Argument blocks and launchers of the mixer kernels (internal to the library).
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace lsso {
+
+struct Plan;
+using bf16 = __nv_bfloat16;
+
+struct MomentArgs {
+  const bf16* proj;      // [B, N, W] packed (relation | content)
+  const bf16* vsrc;      // second operand source (content: proj; backward: grad_output)
+  const __half2* phase;  // [pos_rows, N, R/2]
+  float* partial;        // [B*H][nchunks][ndt][2R][NC]
+  int* status;
+  int64_t N, W, v_stride, v_col0;
+  int H, d, dt, ndt, nchunks, chunk_len, pos_batched, vec;
+};
+
+struct SolveFwdArgs {
+  const float* partial;
+  const float* base;
+  const float* drive;
+  const float* eta_raw;
+  const float* counts;
+  float* zbuf;  // [B*H][R][d] when no tape
+  bf16* rmat;   // [B*H][d_pad x R] readout operand (K-major canonical)
+  float* tape;  // nullable
+  int* pivots;  // nullable
+  int64_t N, tape_stride;
+  int H, d, d_pad, dt, ndt, nchunks;
+};
+
+struct ReadoutArgs {
+  const bf16* proj;
+  const __half2* phase;
+  const bf16* rmat;
+  const float* eta_raw;
+  bf16* out;
+  int* status;
+  int64_t N, W, out_stride;
+  int H, d, d_pad, nb, njd, ntiles, pos_batched, vec;
+};
+
+struct SolveBwdArgs {
+  const float* partial;
+  const float* tape;
+  const float* drive;
+  const float* eta_raw;
+  float* dbuf;  // [B*H][R][d]
+  float* lbuf;  // [B*H][R][d]
+  bf16* b1y;    // [B*H][R x d_pad]
+  bf16* b1c;    // [B*H][R x d_pad]
+  bf16* b1a;    // [B*H][R x R]
+  bf16* b2;     // [B*H][d_pad x R]
+  float* gbase;   // [B*H][R][R]
+  float* gdrive;  // [B*H][d][R]
+  float* etadot;  // [B*H]
+  int64_t N, tape_stride;
+  int H, d, d_pad, dt, ndt, nchunks;
+};
+
+struct GradArgs {
+  const bf16* gout;
+  const bf16* proj;
+  const __half2* phase;
+  const bf16* b1y;
+  const bf16* b1c;
+  const bf16* b1a;
+  const bf16* b2;
+  const float* eta_raw;
+  bf16* gproj;
+  float* etastat;  // [B*H][ntiles]
+  int* status;
+  int64_t N, W, D;
+  int H, d, d_pad, nb, njd, ntiles, pos_batched, vec;
+};
+
+struct ParamReduceArgs {
+  const float* gbase;
+  const float* gdrive;
+  const float* etastat;
+  const float* etadot;
+  const float* eta_raw;
+  float* grad_base;
+  float* grad_drive;
+  float* grad_eta;
+  int64_t B, H, R, d, ntiles;
+};
+
+struct ForwardBuffers {
+  const bf16* projected;
+  const float* base;
+  const float* drive;
+  const float* eta_raw;
+  const float* positions;  // nullable
+  int positions_batched;
+  const float* counts;     // nullable
+  bf16* mixed;
+  float* tape;             // nullable (inference)
+  int* pivots;             // nullable (inference)
+  __half2* phase;
+  float* partial;
+  float* zbuf;
+  bf16* rmat;
+  int* status;
+  int vec;
+};
+
+struct BackwardBuffers {
+  const bf16* grad_output;
+  const bf16* projected;
+  const float* drive;
+  const float* eta_raw;
+  const float* tape;
+  const float* positions;
+  bf16* grad_projected;
+  float* grad_base;
+  float* grad_drive;
+  float* grad_eta;
+  __half2* phase;
+  float* partial;
+  float* dbuf;
+  float* lbuf;
+  bf16* b1y;
+  bf16* b1c;
+  bf16* b1a;
+  bf16* b2;
+  float* gbase;
+  float* gdrive;
+  float* etastat;
+  float* etadot;
+  int* status;
+  int vec;
+};
+
+// Optional per-kernel timing: when set, called around every kernel launch
+// (on the launching thread, with the launch stream).  Used by the profiling
+// entry points of the C ABI; null in normal operation.
+using LaunchHook = void (*)(const char* kernel, cudaStream_t stream);
+extern LaunchHook g_before_launch;
+extern LaunchHook g_after_launch;
+
+cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream);
+cudaError_t launch_backward(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream);
+
+}  // namespace lsso

@@ -40,9 +40,10 @@ ETA_INIT_RAW = math.atanh(0.9)  # lsso/ball/model.py:22-23
 def round_bf16(value: np.ndarray) -> np.ndarray:
     """Round to the nearest BF16 value (ties to even), returned as float32."""
     as32 = np.ascontiguousarray(value, dtype=np.float32)
-    bits = as32.view(np.uint32).astype(np.uint64)
-    rounding = ((bits >> 16) & 1) + 0x7FFF
-    rounded = ((bits + rounding) >> 16) << 16
+    bits = as32.view(np.uint32)
+    # uint32 cannot overflow here: only NaN bit patterns exceed 0xFFFF7FFF,
+    # and those are restored below.
+    rounded = ((bits + (((bits >> 16) & 1) + np.uint32(0x7FFF))) >> 16) << 16
     out = rounded.astype(np.uint32).view(np.float32)
     # NaN/Inf keep their class.
     special = ~np.isfinite(as32)
