@@ -116,6 +116,34 @@ LSSO_API int lsso_backward(const void* grad_output, const void* projected, const
                   void* grad_projected, float* grad_core_base_raw, float* grad_core_drive_weight,
                   float* grad_eta_raw, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the fixed scratch area of lsso_forward_inference_noalloc (32 MiB). */
+#define LSSO_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* Inference forward that allocates nothing -- no counterpart in the
+ * reference (its operators always allocate through PyTorch).
+ *
+ * For callers that cannot call cudaMalloc where they run the mixer: a host
+ * that owns all device memory through its own arena and forbids allocation
+ * inside plugin calls, or a serving loop whose memory is fixed up front so
+ * that no call can fail for lack of memory or stall in the allocator.  The
+ * caller still passes every input and the output (`mixed`, BF16 [B, N, D]);
+ * arguments mean what they mean for lsso_forward without a tape.  The kernels'
+ * scratch (phase table, moment partials, compact state, readout operand) lives
+ * in one static device array of LSSO_NOALLOC_SCRATCH_BYTES inside the
+ * library, which every GPU that loads the library holds until the process
+ * exits.  Shapes whose scratch would exceed it are rejected with
+ * LSSO_ERR_WORKSPACE and a message naming the size (use lsso_forward then).
+ * The first call on a device resolves the array's device address with
+ * cudaGetSymbolAddress while that device is current; make that first call
+ * before any stream capture.  All calls share the array and every call
+ * overwrites the parts it reads, so nothing needs clearing; calls whose
+ * kernels overlap on the same GPU (e.g. on two streams) race on it. */
+LSSO_API int lsso_forward_inference_noalloc(const void* projected, const float* core_base_raw,
+                                            const float* core_drive_weight, const float* eta_raw,
+                                            const float* centered_positions, int positions_batched,
+                                            const float* valid_counts, int64_t B, int64_t N, int64_t H,
+                                            int64_t D, int64_t R, void* mixed, void* stream);
+
 /* Per-kernel timing (no counterpart in the reference; instrumentation only).
  * lsso_profile_start() makes every subsequent kernel launch of the library
  * record a CUDA event pair on its launch stream; lsso_profile_stop()

@@ -22,7 +22,7 @@ CONTRACT_VERSION = 8
 EXPORTED_SYMBOLS = (
     "lsso_contract_version", "lsso_compiled_sm", "lsso_check_device", "lsso_last_error", "lsso_device_status",
     "lsso_tape_stride", "lsso_forward_workspace_size", "lsso_forward", "lsso_backward_workspace_size",
-    "lsso_backward", "lsso_profile_start", "lsso_profile_stop",
+    "lsso_backward", "lsso_profile_start", "lsso_profile_stop", "lsso_forward_inference_noalloc",
 )
 
 _LIBRARY: "NativeLibrary | None" = None

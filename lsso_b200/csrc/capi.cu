@@ -11,6 +11,12 @@
 #include "mixer.h"
 #include "mixer_common.cuh"
 
+// Fixed device scratch of lsso_forward_inference_noalloc (see below).  Host
+// code must never pass `g_noalloc_scratch` itself to a kernel: on the host it
+// names a stand-in, not device memory.  Its device address is resolved once
+// per device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LSSO_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -154,6 +160,17 @@ int plan_for(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int position
   return LSSO_OK;
 }
 
+// ---------------------------------------------------------------- allocation-free inference
+// Scratch of lsso_forward_inference_noalloc: a fixed area inside the library
+// image, so that callers which must not allocate device memory can still run
+// the mixer.  Every device that loads the library holds it until the process
+// exits.  All calls share it: the forward overwrites every byte it later
+// reads (phase table, moment partials, compact state, readout operand), so
+// nothing needs clearing between calls; two calls whose kernels overlap on
+// the same GPU (for example on two streams) race on it.
+constexpr size_t kNoallocScratchBytes = size_t(LSSO_NOALLOC_SCRATCH_BYTES);
+void* g_noalloc_scratch_addr[kMaxDevices];
+
 // ---------------------------------------------------------------- profiling
 struct ProfileRecord {
   const char* name;
@@ -190,6 +207,66 @@ void profile_after(const char* name, cudaStream_t stream) {
 }  // namespace
 
 extern "C" {
+
+int lsso_forward_inference_noalloc(const void* projected, const float* core_base_raw,
+                                   const float* core_drive_weight, const float* eta_raw,
+                                   const float* centered_positions, int positions_batched,
+                                   const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D,
+                                   int64_t R, void* mixed, void* stream) {
+  g_last_error.clear();
+  if (projected == nullptr || core_base_raw == nullptr || core_drive_weight == nullptr || eta_raw == nullptr ||
+      mixed == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward_inference_noalloc: a required pointer is NULL");
+  }
+  const bool batched = centered_positions != nullptr && positions_batched != 0;
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, batched ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const ForwardLayout l = forward_layout(p, false);
+  if (l.total > kNoallocScratchBytes) {
+    return fail(LSSO_ERR_WORKSPACE,
+                "lsso_forward_inference_noalloc: this shape needs %zu bytes of scratch, more than the library's "
+                "fixed %zu-byte area; use lsso_forward with a caller-allocated workspace",
+                l.total, kNoallocScratchBytes);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  void* scratch = nullptr;
+  {
+    // First call on this device (which is current): resolve the array's device address.
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (g_noalloc_scratch_addr[device] == nullptr) {
+      void* ptr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+      g_noalloc_scratch_addr[device] = ptr;
+    }
+    scratch = g_noalloc_scratch_addr[device];
+  }
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  lsso::ForwardBuffers fb{};
+  fb.projected = static_cast<const lsso::bf16*>(projected);
+  fb.base = core_base_raw;
+  fb.drive = core_drive_weight;
+  fb.eta_raw = eta_raw;
+  fb.positions = centered_positions;
+  fb.positions_batched = batched ? 1 : 0;
+  fb.counts = valid_counts;
+  fb.mixed = static_cast<lsso::bf16*>(mixed);
+  fb.tape = nullptr;
+  fb.pivots = nullptr;
+  fb.phase = reinterpret_cast<__half2*>(ws + l.phase);
+  fb.partial = reinterpret_cast<float*>(ws + l.partial);
+  fb.zbuf = reinterpret_cast<float*>(ws + l.zbuf);
+  fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
+  fb.status = status;
+  fb.vec = p.vec && aligned16(projected) && aligned16(mixed);
+  const cudaError_t e = lsso::launch_forward(p, fb, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_forward_inference_noalloc");
+  return LSSO_OK;
+}
 
 int lsso_profile_start(void) {
   g_records.clear();
