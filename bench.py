@@ -169,6 +169,10 @@ def algorithmic_bytes(kernel: str, B: int, N: int) -> float | None:
         "readout": (2 * W + 2 * D) * T,      # read projection, write mixed coordinates
         "moments_bwd": (2 * HR + 2 * D) * T,  # read relation and the upstream gradient
         "grad": (2 * D + 4 * W) * T,         # read dY and projection, write the packed gradient
+        # projection GEMMs, averaged over the launches of one step: x->projected, mixed->y,
+        # dy->dmixed, dprojected->dx (4 launches) and the two weight gradients (read g and x)
+        "linear": (12 * D + 4 * W) * T / 4,
+        "wgrad": (2 * W + 6 * D) * T / 2,
     }
     return table.get(kernel)
 

@@ -116,6 +116,42 @@ LSSO_API int lsso_backward(const void* grad_output, const void* projected, const
                   void* grad_projected, float* grad_core_base_raw, float* grad_core_drive_weight,
                   float* grad_eta_raw, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace bytes of lsso_linear (the BF16 copy of the weight in tensor-core
+ * layout) for an [M, K] x [Nout, K]^T product; 0 if the shape is unsupported
+ * (K must be a positive multiple of 8, at most 1024). */
+LSSO_API size_t lsso_linear_workspace_size(int64_t M, int64_t K, int64_t Nout);
+
+/* Projection GEMM of the LSSO layer.  Replaces the reference's
+ * tensor_core_linear products (lsso/ball/reference.py:58-97,170-247,347-408;
+ * cuBLAS / Triton there):
+ *   out[t, n] = sum_k bf16(a[t, k]) * bf16(w[n, k]) (+ bias[n]),
+ * FP32 accumulation and bias, one final rounding to out_dtype; rows with
+ * row_mask[t] == 0 are written as zero.
+ *   a            [M, K] row-major, a_dtype 0 = BF16, 1 = FP16 (rounded to BF16)
+ *   weight       FP32 [Nout, K] row-major, or [K, Nout] if weight_transposed
+ *   bias         FP32 [Nout] or NULL;  row_mask  uint8/bool [M] or NULL
+ *   out          [M, ldo] of out_dtype 0 = BF16, 1 = FP16, 2 = FP32
+ * `a` must be 16-byte aligned.  Runs on tcgen05 tensor cores fed by TMA. */
+LSSO_API int lsso_linear(const void* a, int a_dtype, int64_t M, int64_t K, const float* weight,
+                         int weight_transposed, int64_t Nout, const float* bias, const uint8_t* row_mask,
+                         void* out, int out_dtype, int64_t ldo, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Workspace bytes of lsso_linear_wgrad for T tokens, Nout outputs, K inputs
+ * (per-split FP32 partial tiles); 0 if unsupported (Nout and K must be
+ * positive multiples of 8). */
+LSSO_API size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_t K);
+
+/* Weight gradient of a projection.  Replaces the weight VJP of the
+ * reference's tensor_core_linear (lsso/ball/reference.py:229-234; cuBLAS there):
+ *   dw[n, k] = sum_t bf16(g[t, n]) * bf16(x[t, k])  over tokens with row_mask[t] != 0,
+ * FP32 accumulation, deterministic (fixed-order reduction of per-split
+ * partials, no atomics).  g [T, Nout] and x [T, K] row-major, dtype 0 = BF16,
+ * 1 = FP16 (rounded to BF16); dw FP32 [Nout, K]; both inputs 16-byte aligned. */
+LSSO_API int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask,
+                               int64_t T, int64_t Nout, int64_t K, float* dw, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Size of the fixed scratch area of lsso_forward_inference_noalloc (32 MiB). */
 #define LSSO_NOALLOC_SCRATCH_BYTES (32u << 20)
 

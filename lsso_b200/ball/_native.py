@@ -23,6 +23,7 @@ EXPORTED_SYMBOLS = (
     "lsso_contract_version", "lsso_compiled_sm", "lsso_check_device", "lsso_last_error", "lsso_device_status",
     "lsso_tape_stride", "lsso_forward_workspace_size", "lsso_forward", "lsso_backward_workspace_size",
     "lsso_backward", "lsso_profile_start", "lsso_profile_stop", "lsso_forward_inference_noalloc",
+    "lsso_linear_workspace_size", "lsso_linear", "lsso_linear_wgrad_workspace_size", "lsso_linear_wgrad",
 )
 
 _LIBRARY: "NativeLibrary | None" = None
@@ -48,6 +49,11 @@ class NativeLibrary:
             "lsso_backward_workspace_size": (sz, [i64, i64, i64, i64, i64, ci]),
             "lsso_backward": (ci, [vp, vp, vp, vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp, vp, vp,
                                    vp, sz, vp]),
+            "lsso_linear_workspace_size": (sz, [i64, i64, i64]),
+            "lsso_linear": (ci, [vp, ci, i64, i64, vp, ci, i64, vp, vp, vp, ci, i64, vp, sz, vp]),
+            "lsso_linear_wgrad_workspace_size": (sz, [i64, i64, i64]),
+            "lsso_linear_wgrad": (ci, [vp, ci, vp, ci, vp, i64, i64, i64, vp, vp, sz, vp]),
+            "lsso_forward_inference_noalloc": (ci, [vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp]),
             "lsso_profile_start": (ci, []),
             "lsso_profile_stop": (ci, [ci, c.c_char_p, c.POINTER(c.c_float), c.POINTER(c.c_int)]),
         }

@@ -1,28 +1,132 @@
 """Input and output projections of the CUDA path (reference model.py:370-404).
 
 Input projection: ``projected = bf16(x) bf16(W_bc)^T (+ FP32 bias)`` rounded
-once to BF16, masked rows zeroed before and after.  Output projection:
+once to BF16, masked rows zero.  Output projection:
 ``y = bf16(mixed) bf16(W_o)^T (+ FP32 bias)`` stored in ``x.dtype``, masked
-rows zeroed.  Both use BF16 multiplicands with FP32 accumulation and the
-first-order VJP of the reference's ``_TensorCoreLinear`` (reference.py:170-247).
+rows zero.  Both run on the library's tcgen05 GEMM (``lsso_linear``): BF16
+multiplicands, FP32 accumulation and bias, a single final rounding, the mask
+applied in the epilogue.  The first-order VJP follows the reference's
+``_TensorCoreLinear`` (reference.py:170-247): the input gradient is
+``bf16(g) bf16(W)`` stored in the input's dtype (same GEMM), the weight
+gradient ``bf16(g)^T bf16(x)`` in FP32 and the bias gradient an FP32 sum.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
+from torch.autograd.function import once_differentiable
 
-from .reference import tensor_core_linear
+from . import _native
+
+_OUT_CODES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 
 
-def _masked(value: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
-    if mask is None:
-        return value
-    return torch.where(mask[:, :, None], value, torch.zeros_like(value))
+def _pad_features(value: torch.Tensor, multiple: int = 8) -> torch.Tensor:
+    extra = (-value.shape[-1]) % multiple
+    return value if extra == 0 else F.pad(value, (0, extra))
+
+
+def linear(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, row_mask: torch.Tensor | None,
+           out_dtype: torch.dtype, *, weight_transposed: bool = False) -> torch.Tensor:
+    """One native GEMM: ``a [.., K] (BF16/FP16) x W -> [.., Nout]`` in ``out_dtype``.
+
+    ``weight`` is FP32 ``[Nout, K]`` (or ``[K, Nout]`` with ``weight_transposed``).
+    """
+    lib = _native.library()
+    lead = a.shape[:-1]
+    k = a.shape[-1]
+    flat = a.reshape(-1, k)
+    w = weight.detach().float()
+    if k % 8:
+        flat = _pad_features(flat)
+        w = F.pad(w, (0, 0, 0, (-k) % 8)) if weight_transposed else _pad_features(w)
+    flat = flat.contiguous()
+    w = w.contiguous()
+    m, kp = flat.shape
+    nout = w.shape[1] if weight_transposed else w.shape[0]
+    out = torch.empty((m, nout), dtype=out_dtype, device=a.device)
+    mask = None
+    if row_mask is not None:
+        mask = row_mask.reshape(-1).contiguous().view(torch.uint8)
+    with torch.cuda.device(a.device):
+        size = lib.lib.lsso_linear_workspace_size(m, kp, nout)
+        if size == 0:
+            lib.check(1)
+        workspace = torch.empty((size,), dtype=torch.uint8, device=a.device)
+        lib.check(lib.lib.lsso_linear(
+            flat.data_ptr(), 1 if flat.dtype == torch.float16 else 0, m, kp, w.data_ptr(), int(weight_transposed),
+            nout, None if bias is None else bias.detach().float().contiguous().data_ptr(),
+            None if mask is None else mask.data_ptr(), out.data_ptr(), _OUT_CODES[out_dtype], nout,
+            workspace.data_ptr(), size, torch.cuda.current_stream(a.device).cuda_stream))
+    return out.reshape(*lead, nout)
+
+
+def weight_gradient(g: torch.Tensor, x: torch.Tensor, row_mask: torch.Tensor | None) -> torch.Tensor:
+    """``bf16(g)^T bf16(x)`` over valid rows, FP32 ``[Nout, K]`` (native, deterministic)."""
+    lib = _native.library()
+    nout, k = g.shape[-1], x.shape[-1]
+    gf = g.reshape(-1, nout)
+    xf = x.reshape(-1, k)
+    if gf.dtype not in (torch.float16, torch.bfloat16):
+        gf = gf.to(torch.bfloat16)
+    if xf.dtype not in (torch.float16, torch.bfloat16):
+        xf = xf.to(torch.bfloat16)
+    gf = _pad_features(gf).contiguous()
+    xf = _pad_features(xf).contiguous()
+    t, np_, kp = gf.shape[0], gf.shape[1], xf.shape[1]
+    mask = None if row_mask is None else row_mask.reshape(-1).contiguous().view(torch.uint8)
+    dw = torch.empty((np_, kp), dtype=torch.float32, device=g.device)
+    with torch.cuda.device(g.device):
+        size = lib.lib.lsso_linear_wgrad_workspace_size(t, np_, kp)
+        if size == 0:
+            lib.check(1)
+        workspace = torch.empty((size,), dtype=torch.uint8, device=g.device)
+        lib.check(lib.lib.lsso_linear_wgrad(
+            gf.data_ptr(), 1 if gf.dtype == torch.float16 else 0, xf.data_ptr(),
+            1 if xf.dtype == torch.float16 else 0, None if mask is None else mask.data_ptr(), t, np_, kp,
+            dw.data_ptr(), workspace.data_ptr(), size, torch.cuda.current_stream(g.device).cuda_stream))
+    return dw[:nout, :k] if (np_ != nout or kp != k) else dw
+
+
+class _ProjectionFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, value, weight, bias, row_mask, out_dtype):
+        if value.dtype not in (torch.float16, torch.bfloat16):
+            value = value.to(torch.bfloat16)
+        out = linear(value, weight, bias, row_mask, out_dtype)
+        ctx.save_for_backward(value, weight, row_mask)
+        ctx.has_bias = bias is not None
+        ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        value, weight, row_mask = ctx.saved_tensors
+        g = grad_output
+        if g.dtype not in (torch.float16, torch.bfloat16):
+            g = g.to(torch.bfloat16)
+        g = g.contiguous()
+        grad_value = grad_weight = grad_bias = None
+        # Masked rows: the input-gradient GEMM writes them as zero and the
+        # weight-gradient kernel skips them, so only the bias sum masks here.
+        if ctx.needs_input_grad[0]:
+            grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True)
+        if ctx.needs_input_grad[1]:
+            grad_weight = weight_gradient(g, value, row_mask)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            dims = tuple(range(grad_output.ndim - 1))
+            src = grad_output if row_mask is None else torch.where(row_mask[..., None], grad_output,
+                                                                   torch.zeros_like(grad_output))
+            total = src.sum(dim=dims, dtype=torch.float32) if dims else src.float()
+            grad_bias = total.to(device=ctx.bias_meta[1], dtype=ctx.bias_meta[0])
+        return grad_value, grad_weight, grad_bias, None, None
 
 
 def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                      mask: torch.Tensor | None) -> torch.Tensor:
-    projected = _masked(tensor_core_linear(_masked(x, mask), weight, bias, output_dtype=torch.bfloat16), mask)
+    projected = _ProjectionFunction.apply(x, weight, bias, mask, torch.bfloat16)
     if not projected.is_contiguous():
         raise RuntimeError("implementation='cuda' requires w_bc to produce contiguous projected coordinates")
     return projected
@@ -30,7 +134,7 @@ def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor |
 
 def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                       dtype: torch.dtype, mask: torch.Tensor | None) -> torch.Tensor:
-    return _masked(tensor_core_linear(mixed, weight, bias, output_dtype=dtype), mask)
+    return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype)
 
 
-__all__ = ["input_projection", "output_projection"]
+__all__ = ["input_projection", "linear", "output_projection", "weight_gradient"]

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/lsso_equilibrium.h"
+#include "linear.h"
 #include "mixer.h"
 #include "mixer_common.cuh"
 
@@ -207,6 +208,118 @@ void profile_after(const char* name, cudaStream_t stream) {
 }  // namespace
 
 extern "C" {
+
+size_t lsso_linear_workspace_size(int64_t M, int64_t K, int64_t Nout) {
+  g_last_error.clear();
+  if (M <= 0 || Nout <= 0 || !lsso::linear_shape_supported(K)) {
+    fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: K must be a positive multiple of 8 (at most 1024), M and Nout "
+                                    "positive");
+    return 0;
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  if (device_info(&device, &sms, &status) != LSSO_OK) return 0;
+  return lsso::make_linear_plan(M, K, Nout, sms).prep_bytes;
+}
+
+int lsso_linear(const void* a, int a_dtype, int64_t M, int64_t K, const float* weight, int weight_transposed,
+                int64_t Nout, const float* bias, const uint8_t* row_mask, void* out, int out_dtype, int64_t ldo,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (a == nullptr || weight == nullptr || out == nullptr || workspace == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: a required pointer is NULL");
+  }
+  if (M <= 0 || Nout <= 0 || !lsso::linear_shape_supported(K)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT,
+                "lsso_linear: K must be a positive multiple of 8 (at most 1024), M and Nout positive");
+  }
+  if (M > (int64_t(1) << 31) - 1 || Nout > (int64_t(1) << 20)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: shape exceeds the supported launch range");
+  }
+  if (a_dtype != 0 && a_dtype != 1) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: a_dtype must be 0 or 1");
+  if (out_dtype < 0 || out_dtype > 2) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: out_dtype must be 0..2");
+  if (ldo < Nout) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: ldo must be at least Nout");
+  if (!aligned16(a) || !aligned16(workspace)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear: a and workspace must be 16-byte aligned");
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  const lsso::LinearPlan plan = lsso::make_linear_plan(M, K, Nout, sms);
+  if (workspace_bytes < plan.prep_bytes) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_linear: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, plan.prep_bytes);
+  }
+  lsso::LinearCall c{};
+  c.a = a;
+  c.a_fp16 = a_dtype;
+  c.weight = weight;
+  c.weight_transposed = weight_transposed;
+  c.bias = bias;
+  c.row_mask = row_mask;
+  c.out = out;
+  c.ldo = ldo;
+  c.out_dtype = out_dtype;
+  c.prep = static_cast<uint8_t*>(workspace);
+  c.status = status;
+  const cudaError_t e = lsso::launch_linear(plan, c, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_linear");
+  return LSSO_OK;
+}
+
+size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_t K) {
+  g_last_error.clear();
+  if (T <= 0 || Nout <= 0 || K <= 0 || Nout % 8 != 0 || K % 8 != 0) {
+    fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: T positive, Nout and K positive multiples of 8");
+    return 0;
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  if (device_info(&device, &sms, &status) != LSSO_OK) return 0;
+  return lsso::make_wgrad_plan(T, Nout, K, sms).partial_bytes;
+}
+
+int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask, int64_t T,
+                      int64_t Nout, int64_t K, float* dw, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (g == nullptr || x == nullptr || dw == nullptr || workspace == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: a required pointer is NULL");
+  }
+  if (T <= 0 || Nout <= 0 || K <= 0 || Nout % 8 != 0 || K % 8 != 0) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: T positive, Nout and K positive multiples of 8");
+  }
+  if (T > (int64_t(1) << 31) - 1 || Nout > (int64_t(1) << 16) || K > (int64_t(1) << 16)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: shape exceeds the supported launch range");
+  }
+  if ((g_dtype != 0 && g_dtype != 1) || (x_dtype != 0 && x_dtype != 1)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: dtypes must be 0 (BF16) or 1 (FP16)");
+  }
+  if (!aligned16(g) || !aligned16(x) || !aligned16(workspace)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: g, x and workspace must be 16-byte aligned");
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  const lsso::WgradPlan plan = lsso::make_wgrad_plan(T, Nout, K, sms);
+  if (workspace_bytes < plan.partial_bytes) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_linear_wgrad: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, plan.partial_bytes);
+  }
+  lsso::WgradCall c{};
+  c.g = g;
+  c.g_fp16 = g_dtype;
+  c.x = x;
+  c.x_fp16 = x_dtype;
+  c.row_mask = row_mask;
+  c.dw = dw;
+  c.partial = static_cast<float*>(workspace);
+  c.status = status;
+  const cudaError_t e = lsso::launch_wgrad(plan, c, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_linear_wgrad");
+  return LSSO_OK;
+}
 
 int lsso_forward_inference_noalloc(const void* projected, const float* core_base_raw,
                                    const float* core_drive_weight, const float* eta_raw,

@@ -1,0 +1,654 @@
+// Projection GEMMs of the LSSO layer on sm_100a (tcgen05 + TMA).
+//
+//   out[t, n] = sum_k bf16(A[t, k]) * bf16(W[n, k])  (+ bias[n])   -> BF16 / FP16 / FP32
+//   dW[n, k]  = sum_t bf16(G[t, n]) * bf16(X[t, k])                  -> FP32 (weight gradient)
+//
+// FP32 accumulation and one final rounding, masked rows zero: the
+// tensor_core_linear contract of the reference (lsso/ball/reference.py:
+// 58-97,170-247,347-408).  FP16 operands are rounded to BF16 in shared memory
+// (never re-written to HBM), so the reference's FP16 -> BF16 cast costs no
+// DRAM pass.
+//
+// Operands are staged by TMA with 128-byte inner boxes and
+// CU_TENSOR_MAP_SWIZZLE_128B, which lands them directly in the tcgen05
+// 128-byte-swizzled canonical layout (K-major for activations and weights,
+// MN-major for the weight-gradient operands).  No multicast.
+//
+// Both kernels are warp-specialised, 512 threads, one CTA per SM:
+//   warp 0      TMA producer (one lane issues);
+//   warp 1      MMA issuer (one lane issues tcgen05.mma kind::f16, M=128);
+//   warps 2-7   FP16 -> BF16 rounding and row masking of staged tiles;
+//   warps 8-15  epilogue, two warps per TMEM sub-partition.
+// Every wait is bounded and an abort flag stops all roles after a timeout.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "linear.h"
+#include "mixer.h"
+#include "tc.cuh"
+
+namespace lsso {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kStageBytes = kBM * kBK * 2;  // 16 KB: 128 rows x 128 bytes
+constexpr int kThreads = 512;
+constexpr int kConvWarps = 6;
+constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kEpiWarps = 8;
+
+struct LinearArgs {
+  const uint8_t* bprep;     // prepared weight: NT tiles of [BN x K_pad], K-major SW128 canonical
+  const float* bias;        // nullable [Nout]
+  const uint8_t* row_mask;  // nullable [M], nonzero = valid
+  void* out;
+  int64_t ldo;
+  int out_dtype;            // 0 BF16, 1 FP16, 2 FP32
+  int M, Nout, K_pad, BN, NT, a_fp16;
+  int* status;
+};
+
+// Bounded wait that also gives up as soon as another role aborted.
+__device__ __forceinline__ bool lwait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
+  return false;
+}
+
+__device__ __forceinline__ uint32_t half2_to_bf162(uint32_t h) {
+  __half2 v = *reinterpret_cast<__half2*>(&h);
+  const float2 f = __half22float2(v);
+  return pack_bf16(f.x, f.y);
+}
+
+__device__ __forceinline__ uint4 half8_to_bf16(uint4 x) {
+  return make_uint4(half2_to_bf162(x.x), half2_to_bf162(x.y), half2_to_bf162(x.z), half2_to_bf162(x.w));
+}
+
+// Store 32 consecutive outputs of one row (compile-time indexing only, so the
+// values stay in registers).
+template <int OUT>
+__device__ __forceinline__ void store_row32(void* out, int64_t ldo, int64_t t, int n0, const float (&v)[32], int count,
+                                            bool vec) {
+  if (OUT == 2) {
+    float* o = static_cast<float*>(out) + t * ldo + n0;
+    if (vec && count == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < count) o[j] = v[j];
+    }
+    return;
+  }
+  uint16_t* o = static_cast<uint16_t*>(out) + t * ldo + n0;
+  if (vec && count == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 w;
+      if (OUT == 0) {
+        w = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]), pack_bf16(v[j + 4], v[j + 5]),
+                       pack_bf16(v[j + 6], v[j + 7]));
+      } else {
+        __half2 h0 = __floats2half2_rn(v[j], v[j + 1]), h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
+        __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]), h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
+        w = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                       *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+      }
+      *reinterpret_cast<uint4*>(o + j) = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < count) {
+        if (OUT == 0) {
+          __nv_bfloat16 b = __float2bfloat16_rn(v[j]);
+          o[j] = *reinterpret_cast<uint16_t*>(&b);
+        } else {
+          __half h = __float2half_rn(v[j]);
+          o[j] = *reinterpret_cast<uint16_t*>(&h);
+        }
+      }
+    }
+  }
+}
+
+// ============================================================================
+// Forward-type projection: out = A W^T (+ bias), persistent over M tiles.
+// Each CTA owns one N tile of the weight (resident in shared memory) and
+// streams 128 x 64 activation boxes through a 4-stage ring; two TMEM
+// accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+// ============================================================================
+template <int OUT>
+__global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                             const LinearArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sB = smem;
+  uint8_t* sA = smem + static_cast<size_t>(a.BN) * a.K_pad * 2;  // a multiple of 1024
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], conv[kStages], tfull[2], tempty[2], bbar;
+  __shared__ uint32_t tmem_s;
+  __shared__ int abort_flag;
+  volatile int* abort_v = &abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = static_cast<int>(blockIdx.x % a.NT);
+  const int mstart = static_cast<int>(blockIdx.x / a.NT);
+  const int mstep = static_cast<int>(gridDim.x / a.NT);
+  const int mtiles = (a.M + kBM - 1) / kBM;
+  const int ntile_local = mstart < mtiles ? (mtiles - mstart + mstep - 1) / mstep : 0;
+  const int KB = a.K_pad / kBK;
+  const int BN = a.BN;
+  const uint32_t tcols = tmem_cols_for(2 * BN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&conv[s]), kConvWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull[b]), 1);
+      mbar_init(smem_u32(&tempty[b]), kEpiWarps);
+    }
+    mbar_init(smem_u32(&bbar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(&tmem_s), tcols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_s;
+
+  if (warp == 0) {
+    // ---------------- producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap_a);
+      const uint32_t bbytes = static_cast<uint32_t>(BN) * a.K_pad * 2;
+      mbar_arrive_expect_tx(smem_u32(&bbar), bbytes);
+      const uint8_t* src = a.bprep + static_cast<size_t>(nt) * bbytes;
+      for (uint32_t off = 0; off < bbytes; off += 32768u) {
+        const uint32_t chunk = min(32768u, bbytes - off);
+        bulk_load(smem_u32(sB + off), src + off, chunk, smem_u32(&bbar));
+      }
+    }
+    __syncwarp();
+    int it = 0;
+    bool ok = true;
+    for (int i = 0; i < ntile_local && ok; ++i) {
+      const int m = mstart + i * mstep;
+      for (int kb = 0; kb < KB && ok; ++kb, ++it) {
+        const int s = it % kStages, u = it / kStages;
+        ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
+        if (ok && lane == 0) {
+          mbar_arrive_expect_tx(smem_u32(&full[s]), kStageBytes);
+          tma_load_2d(smem_u32(sA + s * kStageBytes), &tmap_a, kb * kBK, m * kBM, smem_u32(&full[s]));
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    bool ok = lwait(smem_u32(&bbar), 0, abort_v, a.status);
+    const uint32_t idesc = make_idesc(kBM, BN, false, false);
+    const uint32_t sa0 = smem_u32(sA), sb0 = smem_u32(sB);
+    const uint32_t b_region = static_cast<uint32_t>(BN) * 128;  // one 64-wide K region of the weight tile
+    int it = 0;
+    for (int i = 0; i < ntile_local && ok; ++i) {
+      const int b = i & 1, v = i >> 1;
+      ok = lwait(smem_u32(&tempty[b]), (v & 1) ^ 1, abort_v, a.status);
+      tc_fence_after();
+      const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+      for (int kb = 0; kb < KB && ok; ++kb, ++it) {
+        const int s = it % kStages, u = it / kStages;
+        ok = lwait(smem_u32(a.a_fp16 ? &conv[s] : &full[s]), u & 1, abort_v, a.status);
+        tc_fence_after();
+        if (ok && lane == 0) {
+#pragma unroll
+          for (int ks = 0; ks < kBK / 16; ++ks) {
+            const uint64_t ad = make_desc_sw128(sa0 + s * kStageBytes + ks * 32, 16, 1024);
+            const uint64_t bd = make_desc_sw128(sb0 + kb * b_region + ks * 32, 16, 1024);
+            mma_bf16(d, ad, bd, idesc, (kb | ks) != 0 ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&empty[s]));
+        }
+        __syncwarp();
+      }
+      if (ok && lane == 0) mma_commit(smem_u32(&tfull[b]));
+      __syncwarp();
+    }
+  } else if (warp < 2 + kConvWarps) {
+    // ---------------- FP16 -> BF16 rounding in shared memory
+    if (a.a_fp16) {
+      const int ct = threadIdx.x - 64;
+      int it = 0;
+      bool ok = true;
+      for (int i = 0; i < ntile_local && ok; ++i) {
+        for (int kb = 0; kb < KB && ok; ++kb, ++it) {
+          const int s = it % kStages, u = it / kStages;
+          ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
+          if (ok) {
+            uint4* p = reinterpret_cast<uint4*>(sA + s * kStageBytes);
+#pragma unroll 2
+            for (int j = ct; j < static_cast<int>(kStageBytes / 16); j += kConvThreads) p[j] = half8_to_bf16(p[j]);
+            fence_proxy_async();
+          }
+          __syncwarp();
+          if (ok && lane == 0) mbar_arrive(smem_u32(&conv[s]));
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: two warps per TMEM sub-partition
+    const int sub = warp & 3;
+    const int half = (warp - (2 + kConvWarps)) >> 2;
+    const int row = 32 * sub + lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * sub) << 16);
+    const bool vec = (a.ldo % (OUT == 2 ? 4 : 8)) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0;
+    bool ok = true;
+    for (int i = 0; i < ntile_local && ok; ++i) {
+      const int b = i & 1, v = i >> 1;
+      const int m = mstart + i * mstep;
+      ok = lwait(smem_u32(&tfull[b]), v & 1, abort_v, a.status);
+      tc_fence_after();
+      if (ok) {
+        const int64_t t = static_cast<int64_t>(m) * kBM + row;
+        const bool inside = t < a.M;
+        const bool live = inside && (a.row_mask == nullptr || a.row_mask[t] != 0);
+        for (int c0 = 32 * half; c0 < BN; c0 += 64) {
+          float vals[32];
+          tmem_ld32(lane_addr + static_cast<uint32_t>(b * BN + c0), vals);
+          tmem_ld_wait();
+          const int n0 = nt * BN + c0;
+          const int count = min(32, a.Nout - n0);
+          if (inside && count > 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float x = vals[j];
+              if (a.bias != nullptr && j < count) x += a.bias[n0 + j];
+              vals[j] = live ? x : 0.0f;
+            }
+            store_row32<OUT>(a.out, a.ldo, t, n0, vals, count, vec);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[b]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tcols);
+  }
+}
+
+// Weight (FP32, [Nout, K] or transposed [K, Nout]) -> BF16 K-major SW128
+// canonical tiles of BN rows: 64-wide K regions of BN rows x 128 bytes; row n
+// at (n/8)*1024 + (n%8)*128, its 16-byte chunk c stored at chunk c ^ (n%8).
+// Zero outside [Nout, K].
+__global__ void prep_weight_kernel(const float* __restrict__ w, int64_t Nout, int64_t K, int transposed, int BN,
+                                   int K_pad, int NT, uint8_t* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(NT) * BN * K_pad;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int64_t j = idx / (static_cast<int64_t>(BN) * K_pad);
+  const int64_t rem = idx % (static_cast<int64_t>(BN) * K_pad);
+  const int nl = static_cast<int>(rem / K_pad), k = static_cast<int>(rem % K_pad);
+  const int64_t n = j * BN + nl;
+  float v = 0.0f;
+  if (n < Nout && k < K) v = transposed ? w[static_cast<int64_t>(k) * Nout + n] : w[n * K + k];
+  const int kk = k % kBK;
+  const size_t off = static_cast<size_t>(j) * BN * K_pad * 2 + static_cast<size_t>(k / kBK) * BN * 128 +
+                     static_cast<size_t>(nl / 8) * 1024 + (nl % 8) * 128 + ((((kk * 2) / 16) ^ (nl % 8)) * 16) +
+                     (kk * 2) % 16;
+  *reinterpret_cast<__nv_bfloat16*>(out + off) = __float2bfloat16_rn(v);
+}
+
+// ============================================================================
+// Weight gradient: dW[n, k] = sum_t bf16(G[t, n]) * bf16(X[t, k]) over tokens
+// whose row_mask is set, FP32 (reference.py:229-234).  GEMM with M = n (128
+// per tile), N = k (BNW, a multiple of 64, up to 256), K = tokens; both
+// operands MN-major SW128: each stage holds 64 tokens, one 8 KB TMA box per
+// 64 features.  The token axis is split over CTAs; each CTA accumulates one
+// 128 x BNW tile in TMEM and writes an FP32 partial; wgrad_reduce sums the
+// partials in split order (deterministic, no atomics).
+// ============================================================================
+constexpr int kWT = 64;  // tokens per stage
+constexpr int kWStages = 4;
+constexpr uint32_t kWBox = 64 * kWT * 2;  // 8 KB: 64 tokens x 64 features
+
+struct WgradArgs {
+  const uint8_t* row_mask;  // nullable [T]
+  float* partial;           // [splits][tiles][128][BNW]
+  int T, Nout, K, BNW, mtiles, ntilesw, splits, tokens_per_split, g_fp16, x_fp16;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constant__ CUtensorMap tmap_g,
+                                                            const __grid_constant__ CUtensorMap tmap_x,
+                                                            const WgradArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int BNW = a.BNW;
+  const uint32_t ga_bytes = 2 * kWBox;                                // 128 features
+  const uint32_t xb_bytes = static_cast<uint32_t>(BNW / 64) * kWBox;  // BNW features
+  const uint32_t stage_bytes = ga_bytes + xb_bytes;
+  __shared__ __align__(8) uint64_t full[kWStages], empty[kWStages], conv[kWStages], done;
+  __shared__ uint32_t tmem_s;
+  __shared__ int abort_flag;
+  volatile int* abort_v = &abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = a.mtiles * a.ntilesw;
+  const int tile = static_cast<int>(blockIdx.x % tiles);
+  const int split = static_cast<int>(blockIdx.x / tiles);
+  const int mt = tile / a.ntilesw, ntw = tile % a.ntilesw;
+  const int t_begin = split * a.tokens_per_split;
+  const int t_end = min(a.T, t_begin + a.tokens_per_split);
+  const int nst = t_begin < t_end ? (t_end - t_begin + kWT - 1) / kWT : 0;
+  const bool need_conv = a.g_fp16 || a.x_fp16 || a.row_mask != nullptr;
+  const uint32_t tcols = tmem_cols_for(BNW);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+      mbar_init(smem_u32(&conv[s]), kConvWarps);
+    }
+    mbar_init(smem_u32(&done), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(&tmem_s), tcols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_s;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap_g);
+      prefetch_tmap(&tmap_x);
+    }
+    bool ok = true;
+    for (int i = 0; i < nst && ok; ++i) {
+      const int s = i % kWStages, u = i / kWStages;
+      ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
+      if (ok && lane == 0) {
+        const uint32_t dst = smem_u32(smem + s * stage_bytes);
+        const int t0 = t_begin + i * kWT;
+        mbar_arrive_expect_tx(smem_u32(&full[s]), stage_bytes);
+        tma_load_2d(dst, &tmap_g, mt * 128, t0, smem_u32(&full[s]));
+        tma_load_2d(dst + kWBox, &tmap_g, mt * 128 + 64, t0, smem_u32(&full[s]));
+        for (int g = 0; g < BNW / 64; ++g) {
+          tma_load_2d(dst + ga_bytes + g * kWBox, &tmap_x, ntw * BNW + g * 64, t0, smem_u32(&full[s]));
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    const uint32_t idesc = make_idesc(128, BNW, true, true);
+    bool ok = true;
+    for (int i = 0; i < nst && ok; ++i) {
+      const int s = i % kWStages, u = i / kWStages;
+      ok = lwait(smem_u32(need_conv ? &conv[s] : &full[s]), u & 1, abort_v, a.status);
+      tc_fence_after();
+      if (ok && lane == 0) {
+        const uint32_t base = smem_u32(smem + s * stage_bytes);
+#pragma unroll
+        for (int ks = 0; ks < kWT / 16; ++ks) {
+          const uint64_t ad = make_desc_sw128(base + ks * 2048, kWBox, 1024);
+          const uint64_t bd = make_desc_sw128(base + ga_bytes + ks * 2048, kWBox, 1024);
+          mma_bf16(tmem, ad, bd, idesc, (i | ks) != 0 ? 1u : 0u);
+        }
+        mma_commit(smem_u32(&empty[s]));
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      if (ok && nst > 0) {
+        mma_commit(smem_u32(&done));
+      } else {
+        mbar_arrive(smem_u32(&done));
+      }
+    }
+    __syncwarp();
+  } else if (warp < 2 + kConvWarps) {
+    if (need_conv) {
+      const int ct = threadIdx.x - 64;
+      bool ok = true;
+      for (int i = 0; i < nst && ok; ++i) {
+        const int s = i % kWStages, u = i / kWStages;
+        ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
+        if (ok) {
+          uint4* p = reinterpret_cast<uint4*>(smem + s * stage_bytes);
+          const int t0 = t_begin + i * kWT;
+          const int gchunks = static_cast<int>(ga_bytes / 16), total = static_cast<int>(stage_bytes / 16);
+          for (int j = ct; j < total; j += kConvThreads) {
+            const bool is_g = j < gchunks;
+            const int t = t0 + ((j % 512) >> 3);  // each 128-byte row of a box is one token
+            uint4 v = p[j];
+            if ((is_g && a.g_fp16) || (!is_g && a.x_fp16)) v = half8_to_bf16(v);
+            if (a.row_mask != nullptr && (t >= a.T || a.row_mask[t] == 0)) v = make_uint4(0u, 0u, 0u, 0u);
+            p[j] = v;
+          }
+          fence_proxy_async();
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(smem_u32(&conv[s]));
+      }
+    }
+  } else {
+    const int sub = warp & 3;
+    const int half = (warp - (2 + kConvWarps)) >> 2;
+    const int row = 32 * sub + lane;  // feature n within the tile
+    bool ok = lwait(smem_u32(&done), 0, abort_v, a.status);
+    tc_fence_after();
+    float* out = a.partial + (static_cast<size_t>(split) * tiles + tile) * 128 * BNW + static_cast<size_t>(row) * BNW;
+    for (int c0 = 32 * half; c0 < BNW; c0 += 64) {
+      float vals[32];
+      if (ok && nst > 0) {
+        tmem_ld32(tmem + (static_cast<uint32_t>(32 * sub) << 16) + c0, vals);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) vals[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(out + c0 + j) = make_float4(vals[j], vals[j + 1], vals[j + 2], vals[j + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tcols);
+  }
+}
+
+// dW[n, k] = sum over splits (ascending) of the partial tiles.
+__global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int mtiles, int ntilesw, int BNW,
+                                    int Nout, int K, float* __restrict__ dw) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(Nout) * K) return;
+  const int n = static_cast<int>(idx / K), k = static_cast<int>(idx % K);
+  const int tiles = mtiles * ntilesw;
+  const int tile = (n / 128) * ntilesw + k / BNW;
+  const size_t inner = static_cast<size_t>(n % 128) * BNW + (k % BNW);
+  float s = 0.0f;
+  for (int sp = 0; sp < splits; ++sp) s += partial[(static_cast<size_t>(sp) * tiles + tile) * 128 * BNW + inner];
+  dw[idx] = s;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  }
+  return fn;
+}
+
+// Row-major [rows, cols] 16-bit tensor, 64-column x box_rows boxes, 128-byte swizzle.
+CUresult encode_rows(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const void* ptr, int64_t rows,
+                     int64_t cols, int fp16, int box_rows) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return encode(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace
+
+LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
+  LinearPlan p{};
+  p.M = M;
+  p.K = K;
+  p.Nout = Nout;
+  p.K_pad = (K + kBK - 1) / kBK * kBK;
+  const int64_t n16 = (Nout + 15) / 16 * 16;
+  int bn = 256;
+  while (bn > 16 && (static_cast<int64_t>(bn) * p.K_pad * 2 > 128 * 1024 || bn / 2 >= n16)) bn /= 2;
+  p.BN = bn;
+  p.NT = static_cast<int>((Nout + bn - 1) / bn);
+  const int64_t mtiles = (M + kBM - 1) / kBM;
+  int64_t groups = (sm_count > 0 ? sm_count : 148) / p.NT;
+  if (groups < 1) groups = 1;
+  if (groups > mtiles) groups = mtiles;
+  p.grid = static_cast<int>(groups * p.NT);
+  p.smem = static_cast<size_t>(bn) * p.K_pad * 2 + kStages * kStageBytes;
+  p.prep_bytes = static_cast<size_t>(p.NT) * bn * p.K_pad * 2;
+  return p;
+}
+
+bool linear_shape_supported(int64_t K) { return K % 8 == 0 && K > 0 && K <= 1024; }
+
+WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count) {
+  WgradPlan p{};
+  p.T = T;
+  p.Nout = Nout;
+  p.K = K;
+  // A multiple of 64: MN-major operands come in 64-feature TMA boxes.
+  p.BNW = K >= 256 ? 256 : static_cast<int>((K + 63) / 64 * 64);
+  p.mtiles = static_cast<int>((Nout + 127) / 128);
+  p.ntilesw = static_cast<int>((K + p.BNW - 1) / p.BNW);
+  const int tiles = p.mtiles * p.ntilesw;
+  const int sms = sm_count > 0 ? sm_count : 148;
+  int splits = sms / tiles;
+  if (splits < 1) splits = 1;
+  const int64_t max_splits = (T + kWT - 1) / kWT;
+  if (splits > max_splits) splits = static_cast<int>(max_splits);
+  int64_t per = (T + splits - 1) / splits;
+  per = (per + kWT - 1) / kWT * kWT;
+  p.tokens_per_split = static_cast<int>(per);
+  p.splits = static_cast<int>((T + per - 1) / per);
+  p.grid = p.splits * tiles;
+  p.smem = static_cast<size_t>(kWStages) * (2 * kWBox + static_cast<size_t>(p.BNW / 64) * kWBox);
+  p.partial_bytes = static_cast<size_t>(p.splits) * tiles * 128 * p.BNW * sizeof(float);
+  return p;
+}
+
+cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t stream) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (encode == nullptr) return cudaErrorNotSupported;
+  {
+    const int64_t total = static_cast<int64_t>(p.NT) * p.BN * p.K_pad;
+    LaunchScope scope("prep_weight", stream);
+    prep_weight_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        c.weight, p.Nout, p.K, c.weight_transposed, p.BN, static_cast<int>(p.K_pad), p.NT, c.prep);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  CUtensorMap tmap{};
+  if (encode_rows(encode, &tmap, c.a, p.M, p.K, c.a_fp16, kBM) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  LinearArgs a{};
+  a.bprep = c.prep;
+  a.bias = c.bias;
+  a.row_mask = c.row_mask;
+  a.out = c.out;
+  a.ldo = c.ldo;
+  a.out_dtype = c.out_dtype;
+  a.M = static_cast<int>(p.M);
+  a.Nout = static_cast<int>(p.Nout);
+  a.K_pad = static_cast<int>(p.K_pad);
+  a.BN = p.BN;
+  a.NT = p.NT;
+  a.a_fp16 = c.a_fp16;
+  a.status = c.status;
+  cudaError_t e = cudaSuccess;
+  LaunchScope scope("linear", stream);
+  switch (c.out_dtype) {
+    case 0:
+      e = cudaFuncSetAttribute(linear_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+      if (e == cudaSuccess) linear_kernel<0><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
+      break;
+    case 1:
+      e = cudaFuncSetAttribute(linear_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+      if (e == cudaSuccess) linear_kernel<1><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
+      break;
+    default:
+      e = cudaFuncSetAttribute(linear_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+      if (e == cudaSuccess) linear_kernel<2><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
+      break;
+  }
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t stream) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (encode == nullptr) return cudaErrorNotSupported;
+  CUtensorMap mg{}, mx{};
+  if (encode_rows(encode, &mg, c.g, p.T, p.Nout, c.g_fp16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (encode_rows(encode, &mx, c.x, p.T, p.K, c.x_fp16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  WgradArgs a{};
+  a.row_mask = c.row_mask;
+  a.partial = c.partial;
+  a.T = static_cast<int>(p.T);
+  a.Nout = static_cast<int>(p.Nout);
+  a.K = static_cast<int>(p.K);
+  a.BNW = p.BNW;
+  a.mtiles = p.mtiles;
+  a.ntilesw = p.ntilesw;
+  a.splits = p.splits;
+  a.tokens_per_split = p.tokens_per_split;
+  a.g_fp16 = c.g_fp16;
+  a.x_fp16 = c.x_fp16;
+  a.status = c.status;
+  cudaError_t e = cudaFuncSetAttribute(wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(p.smem));
+  if (e != cudaSuccess) return e;
+  {
+    LaunchScope scope("wgrad", stream);
+    wgrad_kernel<<<p.grid, kThreads, p.smem, stream>>>(mg, mx, a);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t total = p.Nout * p.K;
+  LaunchScope scope("wgrad_reduce", stream);
+  wgrad_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      c.partial, p.splits, p.mtiles, p.ntilesw, p.BNW, static_cast<int>(p.Nout), static_cast<int>(p.K), c.dw);
+  return cudaGetLastError();
+}
+
+}  // namespace lsso

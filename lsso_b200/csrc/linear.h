@@ -1,0 +1,54 @@
+// Projection GEMM launch plan and entry (internal to the library).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lsso {
+
+struct LinearPlan {
+  int64_t M, K, Nout, K_pad;
+  int BN, NT, grid;
+  size_t smem, prep_bytes;
+};
+
+struct LinearCall {
+  const void* a;            // activations [M, K] row-major, BF16 or FP16
+  int a_fp16;
+  const float* weight;      // FP32 [Nout, K], or [K, Nout] when weight_transposed
+  int weight_transposed;
+  const float* bias;        // nullable FP32 [Nout]
+  const uint8_t* row_mask;  // nullable [M]
+  void* out;                // [M, ldo] of out_dtype
+  int64_t ldo;
+  int out_dtype;            // 0 BF16, 1 FP16, 2 FP32
+  uint8_t* prep;            // workspace for the prepared weight (plan.prep_bytes, 16-byte aligned)
+  int* status;
+};
+
+struct WgradPlan {
+  int64_t T, Nout, K;
+  int BNW, mtiles, ntilesw, splits, tokens_per_split, grid;
+  size_t smem, partial_bytes;
+};
+
+struct WgradCall {
+  const void* g;            // [T, Nout] BF16 or FP16
+  int g_fp16;
+  const void* x;            // [T, K] BF16 or FP16
+  int x_fp16;
+  const uint8_t* row_mask;  // nullable [T]
+  float* dw;                // FP32 [Nout, K]
+  float* partial;           // workspace (plan.partial_bytes)
+  int* status;
+};
+
+WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count);
+cudaError_t launch_wgrad(const WgradPlan& plan, const WgradCall& call, cudaStream_t stream);
+
+LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count);
+bool linear_shape_supported(int64_t K);
+cudaError_t launch_linear(const LinearPlan& plan, const LinearCall& call, cudaStream_t stream);
+
+}  // namespace lsso

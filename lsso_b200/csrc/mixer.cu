@@ -249,23 +249,30 @@ struct SolveSmem {
   static constexpr int CLD = kColChunk + 1;
 };
 
+// Right-looking Cholesky of the lower triangle of L (in place), run by warp 0
+// alone with warp-level synchronisation (the factorisation is a chain of R
+// short steps; block-wide barriers per step would dominate its latency).
+// Every thread of the block must call it; the upper triangle is zeroed.
 template <int R>
 __device__ __forceinline__ void cholesky_inplace(float* L) {
   constexpr int LD = R + 1;
   const int tid = threadIdx.x;
-  for (int k = 0; k < R; ++k) {
-    if (tid == 0) L[k * LD + k] = sqrtf(L[k * LD + k]);
-    __syncthreads();
-    const float piv = L[k * LD + k];
-    for (int i = k + 1 + tid; i < R; i += kSolveThreads) L[i * LD + k] /= piv;
-    __syncthreads();
-    const int m = R - k - 1;
-    for (int idx = tid; idx < m * m; idx += kSolveThreads) {
-      const int i = k + 1 + idx / m, jj = k + 1 + idx % m;
-      if (jj <= i) L[i * LD + jj] -= L[i * LD + k] * L[jj * LD + k];
+  __syncthreads();
+  if (tid < 32) {
+    for (int k = 0; k < R; ++k) {
+      const float piv = sqrtf(L[k * LD + k]);
+      __syncwarp();
+      if (tid == 0) L[k * LD + k] = piv;
+      for (int i = k + 1 + tid; i < R; i += 32) L[i * LD + k] /= piv;
+      __syncwarp();
+      for (int i = k + 1 + tid; i < R; i += 32) {
+        const float lik = L[i * LD + k];
+        for (int jj = k + 1; jj <= i; ++jj) L[i * LD + jj] -= lik * L[jj * LD + k];
+      }
+      __syncwarp();
     }
-    __syncthreads();
   }
+  __syncthreads();
   for (int idx = tid; idx < R * R; idx += kSolveThreads) {
     const int i = idx / R, jj = idx % R;
     if (jj > i) L[i * LD + jj] = 0.0f;
@@ -273,21 +280,27 @@ __device__ __forceinline__ void cholesky_inplace(float* L) {
   __syncthreads();
 }
 
+// Doolittle LU without pivoting (in place; unit lower factor below the
+// diagonal), run by warp 0 with warp-level synchronisation.  I + K has a
+// positive-definite symmetric part, so no pivoting is needed.
 template <int R>
 __device__ __forceinline__ void lu_inplace(float* M) {
   constexpr int LD = R + 1;
   const int tid = threadIdx.x;
-  for (int k = 0; k < R; ++k) {
-    const float piv = M[k * LD + k];
-    for (int i = k + 1 + tid; i < R; i += kSolveThreads) M[i * LD + k] /= piv;
-    __syncthreads();
-    const int m = R - k - 1;
-    for (int idx = tid; idx < m * m; idx += kSolveThreads) {
-      const int i = k + 1 + idx / m, jj = k + 1 + idx % m;
-      M[i * LD + jj] -= M[i * LD + k] * M[k * LD + jj];
+  __syncthreads();
+  if (tid < 32) {
+    for (int k = 0; k < R; ++k) {
+      const float piv = M[k * LD + k];
+      for (int i = k + 1 + tid; i < R; i += 32) M[i * LD + k] /= piv;
+      __syncwarp();
+      for (int i = k + 1 + tid; i < R; i += 32) {
+        const float lik = M[i * LD + k];
+        for (int jj = k + 1; jj < R; ++jj) M[i * LD + jj] -= lik * M[k * LD + jj];
+      }
+      __syncwarp();
     }
-    __syncthreads();
   }
+  __syncthreads();
 }
 
 // Column-wise triangular solves on a [R][CLD] column chunk (one thread per column).
@@ -1065,32 +1078,56 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
 // ============================================================================
 // Parameter gradients: deterministic sums over samples (ascending b).
 // ============================================================================
-__global__ void param_reduce_kernel(const ParamReduceArgs a) {
+constexpr int kReduceThreads = 256;
+
+// Blocks [0, main_blocks) sum the base/drive partials of one element each per
+// thread over samples; the last H blocks each reduce one head's complement
+// statistic over (sample, tile) with a fixed-order tree.  Deterministic.
+__global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const ParamReduceArgs a) {
   const int64_t R = a.R, d = a.d, H = a.H;
-  const int64_t nbase = H * R * R, ndrive = H * d * R;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx < nbase) {
-    const int64_t h = idx / (R * R), e = idx % (R * R);
-    float s = 0.0f;
-    for (int64_t b = 0; b < a.B; ++b) s += a.gbase[(b * H + h) * R * R + e];
-    a.grad_base[idx] = s;
-  } else if (idx < nbase + ndrive) {
-    const int64_t k = idx - nbase;
-    const int64_t h = k / (d * R), e = k % (d * R);
-    float s = 0.0f;
-    for (int64_t b = 0; b < a.B; ++b) s += a.gdrive[(b * H + h) * d * R + e];
-    a.grad_drive[k] = s;
-  } else if (idx < nbase + ndrive + H) {
-    const int64_t h = idx - nbase - ndrive;
-    float s = 0.0f;
-    for (int64_t b = 0; b < a.B; ++b) {
-      const int64_t bh = b * H + h;
-      float st = 0.0f;
-      for (int64_t t = 0; t < a.ntiles; ++t) st += a.etastat[bh * a.ntiles + t];
-      s += st - a.etadot[bh];
+  const int64_t nbase = H * R * R, nmain = nbase + H * d * R;
+  const int64_t main_blocks = (nmain + kReduceThreads - 1) / kReduceThreads;
+  if (static_cast<int64_t>(blockIdx.x) < main_blocks) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
+    if (idx >= nmain) return;
+    const bool is_base = idx < nbase;
+    const int64_t k = is_base ? idx : idx - nbase;
+    const int64_t per = is_base ? R * R : d * R;
+    const int64_t h = k / per, e = k % per;
+    const float* src = (is_base ? a.gbase : a.gdrive) + h * per + e;
+    const int64_t stride = H * per;
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int64_t b = 0;
+    for (; b + 4 <= a.B; b += 4) {
+      s0 += src[b * stride];
+      s1 += src[(b + 1) * stride];
+      s2 += src[(b + 2) * stride];
+      s3 += src[(b + 3) * stride];
     }
-    a.grad_eta[h] = s * bounded_complement_derivative(a.eta_raw[h]);
+    for (; b < a.B; ++b) s0 += src[b * stride];
+    const float total = (s0 + s1) + (s2 + s3);
+    if (is_base) {
+      a.grad_base[k] = total;
+    } else {
+      a.grad_drive[k] = total;
+    }
+    return;
   }
+  __shared__ float part[kReduceThreads];
+  const int64_t h = static_cast<int64_t>(blockIdx.x) - main_blocks;
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < a.B * a.ntiles; i += kReduceThreads) {
+    const int64_t b = i / a.ntiles, t = i % a.ntiles;
+    s += a.etastat[(b * H + h) * a.ntiles + t];
+  }
+  for (int64_t b = threadIdx.x; b < a.B; b += kReduceThreads) s -= a.etadot[b * H + h];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = kReduceThreads / 2; w > 0; w >>= 1) {
+    if (static_cast<int>(threadIdx.x) < w) part[threadIdx.x] += part[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) a.grad_eta[h] = part[0] * bounded_complement_derivative(a.eta_raw[h]);
 }
 
 // ============================================================================
@@ -1098,18 +1135,6 @@ __global__ void param_reduce_kernel(const ParamReduceArgs a) {
 // ============================================================================
 LaunchHook g_before_launch = nullptr;
 LaunchHook g_after_launch = nullptr;
-
-// Bracket one kernel launch with the timing hooks (no-ops unless profiling).
-struct LaunchScope {
-  const char* name;
-  cudaStream_t stream;
-  LaunchScope(const char* n, cudaStream_t s) : name(n), stream(s) {
-    if (g_before_launch != nullptr) g_before_launch(name, stream);
-  }
-  ~LaunchScope() {
-    if (g_after_launch != nullptr) g_after_launch(name, stream);
-  }
-};
 
 static cudaError_t set_smem(const void* fn, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
@@ -1334,9 +1359,9 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   pr.R = p.R;
   pr.d = p.d;
   pr.ntiles = p.ntiles;
-  const int64_t total = p.H * p.R * p.R + p.H * p.d * p.R + p.H;
+  const int64_t main_blocks = ceil_div(p.H * p.R * p.R + p.H * p.d * p.R, kReduceThreads);
   LaunchScope scope("param_reduce", stream);
-  param_reduce_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256, 0, stream>>>(pr);
+  param_reduce_kernel<<<static_cast<unsigned>(main_blocks + p.H), kReduceThreads, 0, stream>>>(pr);
   return cudaGetLastError();
 }
 

@@ -145,6 +145,18 @@ using LaunchHook = void (*)(const char* kernel, cudaStream_t stream);
 extern LaunchHook g_before_launch;
 extern LaunchHook g_after_launch;
 
+// Bracket one kernel launch with the timing hooks (no-ops unless profiling).
+struct LaunchScope {
+  const char* name;
+  cudaStream_t stream;
+  LaunchScope(const char* n, cudaStream_t s) : name(n), stream(s) {
+    if (g_before_launch != nullptr) g_before_launch(name, stream);
+  }
+  ~LaunchScope() {
+    if (g_after_launch != nullptr) g_after_launch(name, stream);
+  }
+};
+
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream);
 cudaError_t launch_backward(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream);
 

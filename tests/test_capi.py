@@ -82,3 +82,14 @@ def test_operator_registration_exposes_the_reference_schemas(library_path: Path)
     assert out.returncode == 0, out.stderr
     assert "Tensor? centered_positions=None, Tensor? valid_counts=None) -> (Tensor, Tensor, Tensor)" in out.stdout
     assert "Tensor tape, Tensor pivots" in out.stdout
+
+
+def test_every_exported_symbol_has_a_ctypes_signature(library_path: Path) -> None:
+    """Without argtypes, ctypes would pass 64-bit device pointers as C int."""
+    from lsso_b200.ball import _native
+
+    lib = _native.open_library(library_path).lib
+    for name in _native.EXPORTED_SYMBOLS:
+        fn = getattr(lib, name)
+        assert fn.argtypes is not None, name
+        assert fn.restype is not None or name.endswith("_start"), name

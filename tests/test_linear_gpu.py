@@ -1,0 +1,114 @@
+"""The projection GEMM (``lsso_linear``) against an FP64 evaluation of its contract.
+
+Contract (reference lsso/ball/reference.py:58-97,170-247): BF16 multiplicands,
+FP32 accumulation and bias, one rounding to the output dtype, masked rows zero.
+The FP64 product of the BF16-rounded operands differs from an FP32-accumulated
+one only by accumulation order, so outputs agree to FP32 accuracy before the
+final rounding (a BF16/FP16 store may differ by one rounding step).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from tests.gpu_util import require_native
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def native() -> None:
+    require_native()
+
+
+def _expected(a, w, bias, mask, transposed):
+    ad = a.to(torch.bfloat16).double()
+    wd = w.to(torch.bfloat16).double()
+    out = ad @ (wd if transposed else wd.T)
+    if bias is not None:
+        out = out + bias.double()
+    if mask is not None:
+        out = torch.where(mask.reshape(-1)[:, None], out, torch.zeros_like(out))
+    return out
+
+
+@pytest.mark.parametrize(("m", "k", "nout", "a_dtype", "out_dtype", "bias", "masked", "transposed"), [
+    (1000, 256, 512, torch.float16, torch.bfloat16, False, False, False),
+    (4096, 256, 256, torch.bfloat16, torch.float16, True, True, False),
+    (333, 512, 256, torch.bfloat16, torch.float32, False, False, True),
+    (257, 64, 66, torch.float16, torch.float32, True, False, False),
+    (130, 40, 1024, torch.bfloat16, torch.bfloat16, False, True, False),
+    (128, 24, 48, torch.float16, torch.float16, True, False, True),
+    (70000, 256, 512, torch.float16, torch.bfloat16, False, False, False),
+])
+def test_linear_matches_bf16_contract(m, k, nout, a_dtype, out_dtype, bias, masked, transposed) -> None:
+    from lsso_b200.ball.projection import linear
+
+    g = torch.Generator().manual_seed(m + k + nout)
+    a = (torch.randn(m, k, generator=g) * 3).to("cuda", a_dtype)
+    w = torch.randn((k, nout) if transposed else (nout, k), generator=g).cuda() / k ** 0.5
+    b = torch.randn(nout, generator=g).cuda() if bias else None
+    mask = (torch.rand(m, generator=g) > 0.3).cuda() if masked else None
+    out = linear(a, w, b, mask, out_dtype, weight_transposed=transposed)
+    torch.cuda.synchronize()
+    ref = _expected(a, w, b, mask, transposed)
+    assert out.dtype == out_dtype and out.shape == (m, nout)
+    diff = (out.double() - ref).abs()
+    if out_dtype == torch.float32:
+        tol = 1e-5 * ref.abs().max().item()
+    else:
+        eps = 2.0 ** -8 if out_dtype == torch.bfloat16 else 2.0 ** -11
+        tol = eps * ref.abs().max().item()
+    assert diff.max().item() <= tol, (diff.max().item(), tol)
+    if mask is not None:
+        assert torch.count_nonzero(out[~mask]) == 0
+
+
+def test_linear_fp16_input_rounds_through_bf16() -> None:
+    """An FP16 activation is rounded to BF16 before the product (reference.py:181)."""
+    from lsso_b200.ball.projection import linear
+
+    a = torch.full((128, 8), 1.0 + 2.0 ** -10, device="cuda", dtype=torch.float16)  # not representable in BF16
+    w = torch.zeros(8, 8, device="cuda")
+    w[0, 0] = 1.0
+    out = linear(a, w, None, None, torch.float32)
+    assert torch.all(out[:, 0] == 1.0)
+
+
+def test_linear_rejects_misaligned_k_through_the_abi() -> None:
+    from lsso_b200.ball import _native
+
+    lib = _native.library()
+    assert lib.lib.lsso_linear_workspace_size(128, 12, 64) == 0
+    assert "multiple of 8" in lib.last_error()
+
+
+@pytest.mark.parametrize(("t", "nout", "k", "g_dtype", "x_dtype", "masked"), [
+    (262144, 512, 256, torch.bfloat16, torch.float16, False),
+    (262144, 256, 256, torch.float16, torch.bfloat16, False),
+    (5000, 1024, 512, torch.bfloat16, torch.bfloat16, True),
+    (777, 72, 40, torch.float16, torch.float16, True),
+])
+def test_weight_gradient_matches_fp64(t, nout, k, g_dtype, x_dtype, masked) -> None:
+    from lsso_b200.ball.projection import weight_gradient
+
+    gen = torch.Generator().manual_seed(t + nout + k)
+    g = torch.randn(t, nout, generator=gen).to("cuda", g_dtype)
+    x = torch.randn(t, k, generator=gen).to("cuda", x_dtype)
+    mask = (torch.rand(t, generator=gen) > 0.25).cuda() if masked else None
+    if masked:
+        x[~mask] = float("nan")  # masked rows must not contribute, even when not finite
+    dw = weight_gradient(g, x, mask)
+    torch.cuda.synchronize()
+    gd = g.to(torch.bfloat16).double()
+    xd = torch.nan_to_num(x.to(torch.bfloat16).double())
+    if masked:
+        gd = gd * mask[:, None]
+        xd = xd * mask[:, None]
+    ref = gd.T @ xd
+    err = float((dw.double() - ref).norm() / ref.norm())
+    assert dw.shape == (nout, k) and dw.dtype == torch.float32
+    assert err < 1e-5, err
+    again = weight_gradient(g, x, mask)
+    assert torch.equal(dw, again)  # deterministic
