@@ -209,19 +209,13 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     B, N = args.batch, args.seq
     x = torch.randn(B, N, DIM, device=device, generator=gen).half().requires_grad_()
+    from lsso_b200.ball.distributed import allreduce_gradients
+
     flat = torch.empty(sum(p.numel() for p in params), device=device, dtype=torch.float32)
 
     def reduce_gradients() -> None:
-        if world == 1:
-            return
-        torch.cat([p.grad.reshape(-1) for p in params], out=flat)
-        dist.all_reduce(flat)
-        flat.div_(world)
-        offset = 0
-        for p in params:
-            n = p.numel()
-            p.grad.copy_(flat[offset:offset + n].view_as(p))
-            offset += n
+        if world > 1:
+            allreduce_gradients(params, buffer=flat)
 
     def train_step(xx):
         for p in params:
