@@ -217,19 +217,27 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         if world > 1:
             allreduce_gradients(params, buffer=flat)
 
-    def train_step(xx):
+    def fwd_bwd(xx):
+        # cache_enabled=False: autocast's weight-cast cache must not outlive a graph capture.
+        with torch.autocast("cuda", dtype=torch.float16, cache_enabled=False):
+            loss = layer(xx, implementation="cuda").float().square().mean()
+        loss.backward()
+        return loss
+
+    def clear_grads(xx) -> None:
         for p in params:
             p.grad = None
         xx.grad = None
-        with torch.autocast("cuda", dtype=torch.float16):
-            loss = layer(xx, implementation="cuda").float().square().mean()
-        loss.backward()
+
+    def train_step(xx):
+        clear_grads(xx)
+        loss = fwd_bwd(xx)
         reduce_gradients()
         return loss
 
     def fwd_step(xx):
-        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.float16):
-            layer(xx, implementation="cuda")
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.float16, cache_enabled=False):
+            return layer(xx, implementation="cuda")
 
     def timed(fn, steps: int) -> float:
         if world > 1:
@@ -248,12 +256,49 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         return float(ms.item())
 
+    def capture(fn, xx):
+        """CUDA graph of fn(xx) (the same public-API calls, launches recorded once)."""
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                if xx.requires_grad:
+                    clear_grads(xx)
+                fn(xx)
+        torch.cuda.current_stream(device).wait_stream(side)
+        if xx.requires_grad:
+            clear_grads(xx)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = fn(xx)
+        # The gradients this graph writes (reduced across ranks after each replay).
+        grads = [p.grad for p in params] if xx.requires_grad else None
+        return graph, out, grads
+
+    def use_grads(grads) -> None:
+        for p, g in zip(params, grads):
+            p.grad = g
+
     for _ in range(args.warmup):
         train_step(x)
     for _ in range(max(3, args.warmup)):
         fwd_step(x)
 
-    # ---- device-resident fwd+bwd (the headline `value`), with per-kernel events and clocks
+    # ---- eager pass with per-kernel CUDA events (kernel table, roofline, launch count)
+    _native.profile_start()
+    eager_ms = timed(lambda: train_step(x), args.steps)
+    kernels = _native.profile_stop()
+
+    # ---- device-resident fwd+bwd (the headline `value`): graph replay + eager gradient all-reduce
+    train_graph, _, train_grads = capture(fwd_bwd, x)
+    use_grads(train_grads)
+
+    def graph_train_step():
+        train_graph.replay()
+        reduce_gradients()
+
+    for _ in range(args.warmup):
+        graph_train_step()
     gpu_uuid = None
     try:
         gpu_uuid = str(torch.cuda.get_device_properties(device).uuid)
@@ -261,28 +306,57 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     except Exception:  # noqa: BLE001
         gpu_uuid = None
     sampler = ClockSampler(gpu_uuid)
-    _native.profile_start()
-    train_ms = timed(lambda: train_step(x), args.steps)
-    kernels = _native.profile_stop()
+    train_ms = timed(graph_train_step, args.steps)
     clocks = sampler.stop()
-    fwd_ms = timed(lambda: fwd_step(x), args.steps)
 
-    # ---- end to end through the public API: pinned host x in, loss out, every step
+    fwd_eager_ms = timed(lambda: fwd_step(x), args.steps)
+    with torch.inference_mode():
+        x_inf = x.detach().clone()
+        fwd_graph, _, _ = capture(fwd_step, x_inf)
+        for _ in range(args.warmup):
+            fwd_graph.replay()
+        fwd_ms = timed(fwd_graph.replay, args.steps)
+
+    # ---- end to end through the public API: every step copies its x from pinned
+    # host memory and reads its loss back.  Two input buffers, each with its own
+    # graph; the copy of step i+1 runs on a copy stream while step i computes.
     x_host = x.detach().to("cpu").pin_memory()
     loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
-    x_dev = torch.empty_like(x.detach())
-    counter = {"i": 0}
+    bufs = [torch.empty_like(x.detach()).requires_grad_() for _ in range(2)]
+    with torch.no_grad():
+        for buf in bufs:
+            buf.copy_(x)
+    graphs = [capture(fwd_bwd, buf) for buf in bufs]
+    copy_stream = torch.cuda.Stream(device)
+    compute = torch.cuda.current_stream(device)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        loss = train_step(x_dev.detach().requires_grad_())
-        loss_host[counter["i"] % args.steps].copy_(loss.detach(), non_blocking=True)
-        counter["i"] += 1
+    def issue_copy(i: int) -> None:
+        k = i % 2
+        copy_stream.wait_stream(compute) if i == 0 else copy_stream.wait_event(free[k])
+        with torch.cuda.stream(copy_stream), torch.no_grad():
+            bufs[k].copy_(x_host, non_blocking=True)
+            ready[k].record(copy_stream)
 
-    e2e_step()
-    counter["i"] = 0
-    e2e_ms = timed(e2e_step, args.steps)
+    def e2e_run() -> None:
+        issue_copy(0)
+        for i in range(args.steps):
+            if i + 1 < args.steps:
+                issue_copy(i + 1)
+            k = i % 2
+            compute.wait_event(ready[k])
+            graphs[k][0].replay()
+            if world > 1:
+                use_grads(graphs[k][2])
+                reduce_gradients()
+            free[k].record(compute)
+            loss_host[i].copy_(graphs[k][1].detach(), non_blocking=True)
+
+    timed(e2e_run, 1)
+    e2e_ms = timed(e2e_run, 1)
     status = cuda.device_status(reset=False)
+    del train_graph, fwd_graph, graphs
 
     tokens = B * N * world
     value = tokens * args.steps / (train_ms / 1e3)
@@ -319,9 +393,15 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             "vs_baseline_note": "BASELINE.md fwd+bwd at N=4096 (8.99 M tokens/s, RTX 5070 Ti, one GPU)",
             "dtype": "bf16", "data": "synthetic", "config": workload(args, world),
             "fwd": {"value": tokens * args.steps / (fwd_ms / 1e3), "unit": "tokens/s",
-                    "ms_per_step": fwd_ms / args.steps},
+                    "ms_per_step": fwd_ms / args.steps, "eager_ms_per_step": fwd_eager_ms / args.steps},
+            "eager": {"value": tokens * args.steps / (eager_ms / 1e3), "unit": "tokens/s",
+                      "ms_per_step": eager_ms / args.steps,
+                      "note": "same step launched op by op (per-kernel events on); `value` replays it as a CUDA graph"},
             "e2e": {"value": tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(), "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(), "d2h_bytes_per_step": 4,
+                    "ms_per_step": e2e_ms / args.steps,
+                    "note": "pinned host x -> device on a copy stream (double-buffered, overlapping the previous "
+                            "step), graph-replayed fwd+bwd, loss -> pinned host, every step"},
             "roofline": roofline, "kernels": step_kernels, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": sum(v[1] for v in kernels.values()), "device_status": status,
         }

@@ -599,15 +599,15 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   LaunchScope scope("linear", stream);
   switch (c.out_dtype) {
     case 0:
-      e = cudaFuncSetAttribute(linear_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+      e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<0>), p.smem);
       if (e == cudaSuccess) linear_kernel<0><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
       break;
     case 1:
-      e = cudaFuncSetAttribute(linear_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+      e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<1>), p.smem);
       if (e == cudaSuccess) linear_kernel<1><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
       break;
     default:
-      e = cudaFuncSetAttribute(linear_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+      e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<2>), p.smem);
       if (e == cudaSuccess) linear_kernel<2><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
       break;
   }
@@ -635,8 +635,7 @@ cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t st
   a.g_fp16 = c.g_fp16;
   a.x_fp16 = c.x_fp16;
   a.status = c.status;
-  cudaError_t e = cudaFuncSetAttribute(wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(p.smem));
+  cudaError_t e = allow_smem(reinterpret_cast<const void*>(&wgrad_kernel), p.smem);
   if (e != cudaSuccess) return e;
   {
     LaunchScope scope("wgrad", stream);

@@ -17,6 +17,8 @@
 //   grad_kernel           d relation / d content per 128-token tile
 //   param_reduce_kernel   deterministic sum of parameter gradients over samples
 #include <cstdio>
+#include <mutex>
+#include <vector>
 
 #include "mixer.h"
 #include "mixer_common.cuh"
@@ -1136,10 +1138,35 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
 LaunchHook g_before_launch = nullptr;
 LaunchHook g_after_launch = nullptr;
 
-static cudaError_t set_smem(const void* fn, size_t bytes) {
+cudaError_t allow_smem(const void* fn, size_t bytes) {
   if (bytes <= 48 * 1024) return cudaSuccess;
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  struct Entry {
+    int device;
+    const void* fn;
+    size_t bytes;
+  };
+  static std::mutex lock;
+  static std::vector<Entry> done;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> guard(lock);
+  for (const Entry& x : done) {
+    if (x.device == device && x.fn == fn && x.bytes >= bytes) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return e;
+  for (Entry& x : done) {
+    if (x.device == device && x.fn == fn) {
+      x.bytes = bytes;
+      return cudaSuccess;
+    }
+  }
+  done.push_back({device, fn, bytes});
+  return cudaSuccess;
 }
+
+static cudaError_t set_smem(const void* fn, size_t bytes) { return allow_smem(fn, bytes); }
 
 static InvFreq inverse_frequencies(int R) {
   InvFreq f{};

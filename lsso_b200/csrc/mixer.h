@@ -141,6 +141,11 @@ struct BackwardBuffers {
 // Optional per-kernel timing: when set, called around every kernel launch
 // (on the launching thread, with the launch stream).  Used by the profiling
 // entry points of the C ABI; null in normal operation.
+// Raise a kernel's dynamic shared-memory limit to `bytes` on the current
+// device; the attribute is set once per (device, kernel, size) so that launches
+// inside a CUDA graph capture issue no attribute calls.
+cudaError_t allow_smem(const void* fn, size_t bytes);
+
 using LaunchHook = void (*)(const char* kernel, cudaStream_t stream);
 extern LaunchHook g_before_launch;
 extern LaunchHook g_after_launch;
