@@ -222,7 +222,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         with torch.autocast("cuda", dtype=torch.float16, cache_enabled=False):
             loss = layer(xx, implementation="cuda").float().square().mean()
         loss.backward()
-        return loss
+        return loss.detach()
 
     def clear_grads(xx) -> None:
         for p in params:

@@ -41,6 +41,7 @@ constexpr int kThreads = 512;
 constexpr int kConvWarps = 6;
 constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kEpiWarps = 8;
+constexpr uint32_t kEpiStage = 4096;  // per epilogue warp: two 32x32 16-bit boxes or one FP32 box
 
 struct LinearArgs {
   const uint8_t* bprep;     // prepared weight: NT tiles of [BN x K_pad], K-major SW128 canonical
@@ -50,6 +51,7 @@ struct LinearArgs {
   int64_t ldo;
   int out_dtype;            // 0 BF16, 1 FP16, 2 FP32
   int M, Nout, K_pad, BN, NT, a_fp16;
+  int tma_out;              // output written by TMA tensor stores (else direct stores)
   int* status;
 };
 
@@ -123,21 +125,59 @@ __device__ __forceinline__ void store_row32(void* out, int64_t ldo, int64_t t, i
   }
 }
 
+// Write one 32-value output row into a TMA staging box (row = lane): 16-bit
+// outputs as 64-byte rows in the 64-byte swizzle (16-byte chunk c of row r at
+// chunk c ^ ((r >> 1) & 3)), FP32 as 128-byte rows in the 128-byte swizzle
+// (chunk c ^ (r & 7)).  Either way the eight lanes of one store phase hit
+// distinct banks.
+template <int OUT>
+__device__ __forceinline__ void stage_row32(uint8_t* box, int r, const float (&v)[32]) {
+  if (OUT == 2) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      *reinterpret_cast<float4*>(box + r * 128 + ((c ^ (r & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int j = 8 * c;
+    uint4 w;
+    if (OUT == 0) {
+      w = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]), pack_bf16(v[j + 4], v[j + 5]),
+                     pack_bf16(v[j + 6], v[j + 7]));
+    } else {
+      __half2 h0 = __floats2half2_rn(v[j], v[j + 1]), h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
+      __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]), h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
+      w = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                     *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+    }
+    *reinterpret_cast<uint4*>(box + r * 64 + ((c ^ ((r >> 1) & 3)) << 4)) = w;
+  }
+}
+
 // ============================================================================
 // Forward-type projection: out = A W^T (+ bias), persistent over M tiles.
 // Each CTA owns one N tile of the weight (resident in shared memory) and
 // streams 128 x 64 activation boxes through a 4-stage ring; two TMEM
-// accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+// accumulators let the epilogue of tile i overlap the MMAs of tile i+1.  The
+// epilogue stages each 32-row x 32-column box in shared memory and writes it
+// with one TMA tensor store, so a warp's output leaves as whole lines instead
+// of 32 row-strided 16-byte pieces per store instruction.
 // ============================================================================
 template <int OUT>
 __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                             const __grid_constant__ CUtensorMap tmap_out,
                                                              const LinearArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* sB = smem;
   uint8_t* sA = smem + static_cast<size_t>(a.BN) * a.K_pad * 2;  // a multiple of 1024
+  uint8_t* sOut = sA + kStages * kStageBytes;
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], conv[kStages], tfull[2], tempty[2], bbar;
   __shared__ uint32_t tmem_s;
   __shared__ int abort_flag;
+  __shared__ __align__(16) float sbias[256];  // this N tile's bias (zero past Nout)
   volatile int* abort_v = &abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -163,6 +203,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     mbar_init(smem_u32(&bbar), 1);
     abort_flag = 0;
     fence_mbar_init();
+  }
+  if (a.bias != nullptr) {
+    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
+      const int n = nt * BN + i;
+      sbias[i] = n < a.Nout ? a.bias[n] : 0.0f;
+    }
   }
   if (warp == 1) tmem_alloc(smem_u32(&tmem_s), tcols);
   tc_fence_before();
@@ -255,6 +301,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     const int row = 32 * sub + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * sub) << 16);
     const bool vec = (a.ldo % (OUT == 2 ? 4 : 8)) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0;
+    uint8_t* stage = sOut + (warp - (2 + kConvWarps)) * kEpiStage;
+    int sbuf = 0;
+    if (a.tma_out && lane == 0) prefetch_tmap(&tmap_out);
     bool ok = true;
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int b = i & 1, v = i >> 1;
@@ -262,7 +311,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       ok = lwait(smem_u32(&tfull[b]), v & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
-        const int64_t t = static_cast<int64_t>(m) * kBM + row;
+        const int64_t row0 = static_cast<int64_t>(m) * kBM + 32 * sub;
+        const int64_t t = row0 + lane;
         const bool inside = t < a.M;
         const bool live = inside && (a.row_mask == nullptr || a.row_mask[t] != 0);
         for (int c0 = 32 * half; c0 < BN; c0 += 64) {
@@ -271,13 +321,45 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           tmem_ld_wait();
           const int n0 = nt * BN + c0;
           const int count = min(32, a.Nout - n0);
-          if (inside && count > 0) {
+          if (count <= 0 || row0 >= a.M) continue;  // warp-uniform
+          // Bias from shared memory, masked rows zero.  (A per-element
+          // predicated global bias load here made the epilogue, and with it
+          // the whole GEMM, several times slower.)
+          if (a.bias != nullptr) {
+            const float4* bsm = reinterpret_cast<const float4*>(sbias + c0);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float x = vals[j];
-              if (a.bias != nullptr && j < count) x += a.bias[n0 + j];
-              vals[j] = live ? x : 0.0f;
+            for (int j = 0; j < 8; ++j) {
+              const float4 bv = bsm[j];
+              vals[4 * j] += bv.x;
+              vals[4 * j + 1] += bv.y;
+              vals[4 * j + 2] += bv.z;
+              vals[4 * j + 3] += bv.w;
             }
+          }
+          if (!live) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) vals[j] = 0.0f;
+          }
+          if (a.tma_out) {
+            uint8_t* box = stage + (OUT == 2 ? 0 : sbuf * 2048);
+            // The store that last read this box (two commits ago; one for FP32) is done reading.
+            if (lane == 0) {
+              if (OUT == 2) {
+                bulk_wait_read<0>();
+              } else {
+                bulk_wait_read<1>();
+              }
+            }
+            __syncwarp();
+            stage_row32<OUT>(box, lane, vals);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmap_out, smem_u32(box), n0, static_cast<int>(row0));
+              bulk_commit();
+            }
+            sbuf ^= 1;
+          } else if (inside) {
             store_row32<OUT>(a.out, a.ldo, t, n0, vals, count, vec);
           }
         }
@@ -286,6 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[b]));
     }
+    if (a.tma_out && lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -536,7 +620,7 @@ LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
   if (groups < 1) groups = 1;
   if (groups > mtiles) groups = mtiles;
   p.grid = static_cast<int>(groups * p.NT);
-  p.smem = static_cast<size_t>(bn) * p.K_pad * 2 + kStages * kStageBytes;
+  p.smem = static_cast<size_t>(bn) * p.K_pad * 2 + kStages * kStageBytes + kEpiWarps * kEpiStage;
   p.prep_bytes = static_cast<size_t>(p.NT) * bn * p.K_pad * 2;
   return p;
 }
@@ -579,9 +663,25 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  CUtensorMap tmap{};
+  CUtensorMap tmap{}, tmap_out{};
   if (encode_rows(encode, &tmap, c.a, p.M, p.K, c.a_fp16, kBM) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  const int64_t esize = c.out_dtype == 2 ? 4 : 2;
+  bool tma_out = (reinterpret_cast<uintptr_t>(c.out) & 15u) == 0 && (c.ldo * esize) % 16 == 0 && p.Nout >= 32 &&
+                 p.M >= 32;
+  if (tma_out) {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.Nout), static_cast<cuuint64_t>(p.M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(c.ldo * esize)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = c.out_dtype == 0   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : c.out_dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    tma_out = encode(&tmap_out, dt, 2, c.out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     c.out_dtype == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
   LinearArgs a{};
+  a.tma_out = tma_out ? 1 : 0;
   a.bprep = c.prep;
   a.bias = c.bias;
   a.row_mask = c.row_mask;
@@ -600,15 +700,15 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   switch (c.out_dtype) {
     case 0:
       e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<0>), p.smem);
-      if (e == cudaSuccess) linear_kernel<0><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
+      if (e == cudaSuccess) linear_kernel<0><<<p.grid, kThreads, p.smem, stream>>>(tmap, tmap_out, a);
       break;
     case 1:
       e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<1>), p.smem);
-      if (e == cudaSuccess) linear_kernel<1><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
+      if (e == cudaSuccess) linear_kernel<1><<<p.grid, kThreads, p.smem, stream>>>(tmap, tmap_out, a);
       break;
     default:
       e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<2>), p.smem);
-      if (e == cudaSuccess) linear_kernel<2><<<p.grid, kThreads, p.smem, stream>>>(tmap, a);
+      if (e == cudaSuccess) linear_kernel<2><<<p.grid, kThreads, p.smem, stream>>>(tmap, tmap_out, a);
       break;
   }
   if (e != cudaSuccess) return e;

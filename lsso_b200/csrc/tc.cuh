@@ -83,6 +83,24 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       "l"(tmap), "r"(c0), "r"(c1), "r"(bar)
       : "memory");
 }
+// 2-D tiled tensor store from this CTA's shared memory (bulk-group completion).
+// Rows/columns of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(tmap), "r"(src),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Wait until at most N committed bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups are incomplete (writes performed).
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;\n" ::"n"(N) : "memory");
+}
 // 3-D tiled tensor load into this CTA's shared memory, completion on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int c0, int c1, int c2, uint32_t bar) {
   asm volatile(
