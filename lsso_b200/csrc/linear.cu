@@ -577,19 +577,6 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int split
   dw[idx] = s;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-  }
-  return fn;
-}
-
 // Row-major [rows, cols] 16-bit tensor, 64-column x box_rows boxes, 128-byte swizzle.
 CUresult encode_rows(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const void* ptr, int64_t rows,
                      int64_t cols, int fp16, int box_rows) {
@@ -603,6 +590,19 @@ CUresult encode_rows(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map,
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  }
+  return fn;
+}
 
 LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
   LinearPlan p{};
@@ -653,7 +653,7 @@ WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count) {
 }
 
 cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t stream) {
-  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return cudaErrorNotSupported;
   {
     const int64_t total = static_cast<int64_t>(p.NT) * p.BN * p.K_pad;
@@ -716,7 +716,7 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
 }
 
 cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t stream) {
-  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return cudaErrorNotSupported;
   CUtensorMap mg{}, mx{};
   if (encode_rows(encode, &mg, c.g, p.T, p.Nout, c.g_fp16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;

@@ -3,6 +3,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace lsso {
@@ -43,6 +45,9 @@ struct WgradCall {
   float* partial;           // workspace (plan.partial_bytes)
   int* status;
 };
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (null if unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count);
 cudaError_t launch_wgrad(const WgradPlan& plan, const WgradCall& call, cudaStream_t stream);

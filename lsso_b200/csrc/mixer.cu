@@ -1224,7 +1224,12 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
   m.chunk_len = static_cast<int>(p.chunk_len);
   m.pos_batched = p.pos_rows > 1 ? 1 : 0;
   m.vec = fb.vec;
-  e = launch_moments<R, false>(p, m, stream);
+  const bool tiled = tiled_usable(p, {fb.projected, fb.mixed});
+  if (tiled) {
+    e = launch_moments_tiled(p, false, fb.projected, nullptr, fb.phase, fb.partial, fb.status, p.sms, stream);
+  } else {
+    e = launch_moments<R, false>(p, m, stream);
+  }
   if (e != cudaSuccess) return e;
 
   SolveFwdArgs s{};
@@ -1273,6 +1278,9 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
   r.ntiles = static_cast<int>(p.ntiles);
   r.pos_batched = m.pos_batched;
   r.vec = fb.vec;
+  if (tiled) {
+    return launch_readout_tiled(p, fb.projected, fb.phase, fb.rmat, fb.eta_raw, fb.mixed, fb.status, p.sms, stream);
+  }
   const size_t rsm = readout_smem<R>(static_cast<int>(p.nb));
   e = set_smem(reinterpret_cast<const void*>(&readout_kernel<R>), rsm);
   if (e != cudaSuccess) return e;
@@ -1304,7 +1312,12 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   m.chunk_len = static_cast<int>(p.chunk_len);
   m.pos_batched = pos_batched;
   m.vec = bb.vec;
-  e = launch_moments<R, true>(p, m, stream);
+  const bool tiled = tiled_usable(p, {bb.projected, bb.grad_output, bb.grad_projected});
+  if (tiled) {
+    e = launch_moments_tiled(p, true, bb.projected, bb.grad_output, bb.phase, bb.partial, bb.status, p.sms, stream);
+  } else {
+    e = launch_moments<R, true>(p, m, stream);
+  }
   if (e != cudaSuccess) return e;
 
   SolveBwdArgs s{};
@@ -1362,14 +1375,17 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   g.ntiles = static_cast<int>(p.ntiles);
   g.pos_batched = pos_batched;
   g.vec = bb.vec;
-  const size_t gsm = grad_smem<R>(static_cast<int>(p.nb));
-  e = set_smem(reinterpret_cast<const void*>(&grad_kernel<R>), gsm);
-  if (e != cudaSuccess) return e;
-  {
+  if (tiled) {
+    e = launch_grad_tiled(p, bb.grad_output, bb.projected, bb.phase, bb.b1y, bb.b1c, bb.b1a, bb.b2, bb.eta_raw,
+                          bb.grad_projected, bb.etastat, bb.status, p.sms, stream);
+  } else {
+    const size_t gsm = grad_smem<R>(static_cast<int>(p.nb));
+    e = set_smem(reinterpret_cast<const void*>(&grad_kernel<R>), gsm);
+    if (e != cudaSuccess) return e;
     LaunchScope scope("grad", stream);
     grad_kernel<R><<<static_cast<unsigned>(p.B * p.ntiles * p.H * p.njd), 128, gsm, stream>>>(g);
+    e = cudaGetLastError();
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
   ParamReduceArgs pr{};

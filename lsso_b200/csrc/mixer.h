@@ -1,6 +1,8 @@
 // Argument blocks and launchers of the mixer kernels (internal to the library).
 #pragma once
 
+#include <initializer_list>
+
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -161,6 +163,17 @@ struct LaunchScope {
     if (g_after_launch != nullptr) g_after_launch(name, stream);
   }
 };
+
+// Head-group tile kernels of the token passes (tokens.cu).  tiled_usable()
+// says whether the plan chose them and every pointer meets the TMA alignment.
+bool tiled_usable(const Plan& p, std::initializer_list<const void*> ptrs);
+cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const __half2* phase,
+                                 float* partial, int* status, int sm_count, cudaStream_t stream);
+cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2* phase, const bf16* rmat,
+                                 const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream);
+cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase, const bf16* b1y,
+                              const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
+                              float* etastat, int* status, int sm_count, cudaStream_t stream);
 
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream);
 cudaError_t launch_backward(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream);

@@ -44,7 +44,54 @@ struct Plan {
   int64_t tape_stride;           // floats per (b, h) training tape row
   int m_pad;                     // moment-pass MMA M (2R rounded up to 64/128)
   bool vec;                      // 16-byte vector path usable (d % 8 == 0)
+  // Head-group tiling of the token passes (tokens.cu): a work item is one
+  // 128-token tile of `hg` heads whose relation and content features fill
+  // whole 64-feature boxes (nrel / nval boxes); the moment pass sums `ct`
+  // tiles per chunk.
+  bool tiled;
+  int hg, groups, nrel, nval, ct;
+  int sms;                       // SM count the plan was made for
 };
+
+constexpr int kTileTokens = 128;
+
+// Choose the head group and the moment-pass chunking of the tiled token
+// kernels; leaves p.tiled false for shapes they do not cover (those use the
+// per-head kernels of mixer.cu).
+inline void plan_tiles(Plan& p, int sm_count) {
+  p.tiled = false;
+  const bool r_ok = p.R == 32 || p.R == 64;
+  const bool d_ok = p.d == 32 || p.d == 64;
+  if (!r_ok || !d_ok || (p.W % 8) != 0 || p.D != p.H * p.d) return;
+  const int hg = static_cast<int>(64 / (p.R < p.d ? p.R : p.d));
+  if (p.H % hg != 0) return;
+  p.hg = hg;
+  p.groups = static_cast<int>(p.H / hg);
+  p.nrel = static_cast<int>(hg * p.R / 64);
+  p.nval = static_cast<int>(hg * p.d / 64);
+  const int64_t ntiles = (p.N + kTileTokens - 1) / kTileTokens;
+  const int64_t pairs = p.B * p.groups;
+  const int64_t sms = sm_count > 0 ? sm_count : 148;
+  // Largest chunk (fewest partials) whose item count still balances over the SMs.
+  int best = 1;
+  double best_eff = -1.0;
+  for (int ct = 16; ct >= 1; ct /= 2) {
+    if (ct > ntiles && ct > 1) continue;
+    const int64_t items = pairs * ((ntiles + ct - 1) / ct);
+    const int64_t waves = (items + sms - 1) / sms;
+    const double eff = static_cast<double>(items) / static_cast<double>(waves * sms);
+    if (eff >= 0.9) {
+      best = ct;
+      break;
+    }
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = ct;
+    }
+  }
+  p.ct = best;
+  p.tiled = true;
+}
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
@@ -53,6 +100,7 @@ inline Plan make_plan(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, boo
                       int sm_count) {
   Plan p{};
   p.B = B; p.N = N; p.H = H; p.D = D; p.R = R;
+  p.sms = sm_count > 0 ? sm_count : 148;
   p.W = H * R + D;
   p.d = D / H;
   p.BH = B * H;
@@ -75,6 +123,13 @@ inline Plan make_plan(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, boo
   p.tape_stride = N * R + 3 * R * R + 2 * R * p.d + 1;
   p.m_pad = (2 * R <= 64) ? 64 : 128;
   p.vec = (p.d % 8) == 0;
+  plan_tiles(p, sm_count);
+  if (p.tiled) {
+    p.chunk_len = static_cast<int64_t>(p.ct) * kTileTokens;
+    p.nchunks = ceil_div(N, p.chunk_len);
+    p.dt = p.d_pad;
+    p.ndt = 1;
+  }
   return p;
 }
 

@@ -1,0 +1,886 @@
+// Token passes of the LSSO mixer on head-group tiles (sm_100a).
+//
+// A work item is one 128-token tile of one sample for a group of `hg` heads
+// whose relation features (hg * R) and content features (hg * d) each fill
+// whole 64-feature boxes.  One persistent CTA per SM walks the items; inside
+// a CTA the work is split by warp role:
+//
+//   warp 0        TMA producer: 128-token x 64-feature boxes of the packed
+//                 projection [B][N][W] (and of dY [B][N][D]) through 3-D
+//                 tensor maps with the 128-byte swizzle (tokens past N read
+//                 as zero), plus bulk copies of the per-(b, h) operand
+//                 matrices the solves produced;
+//   warp 1        tcgen05 MMA issuer (one lane);
+//   warps 2-5     Rank-Rotary rotation of the relation boxes in place (and,
+//                 for the moment pass, the BF16 hi/lo split into the
+//                 MN-major operand buffer);
+//   warps 6-13    epilogue: TMEM -> registers, combine with the staged
+//                 content / dY boxes, write the result back into the boxes
+//                 and store them with TMA tensor stores (tokens past N are
+//                 clipped), or drain moment accumulators to the partials.
+//
+// Kernels (same algebra as the per-head kernels of mixer.cu; reference
+// lsso/ball/reference.py:411-572,691-724, lsso/ball/model.py:245-268):
+//   moments_tile_kernel<R, false>  G/S partials  [hi|lo]^T [hi | C] per chunk of tiles
+//   moments_tile_kernel<R, true>   A'^T dY partials [hi|lo]^T dY
+//   readout_tile_kernel<R>         Y = eta C + A' R_d
+//   grad_tile_kernel<R>            dA' = dY B1y + C B1c + A' B1a (rotated back), dC = eta dY + A' B2,
+//                                  and the per-tile complement statistic sum(dY * C)
+//
+// Every wait is bounded (the status word records a timeout and all roles
+// stop); before exit the producer waits, bounded, for its last loads.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "linear.h"
+#include "mixer.h"
+#include "mixer_common.cuh"
+
+namespace lsso {
+
+namespace {
+
+constexpr int kTT = kTileTokens;             // tokens per tile
+constexpr uint32_t kBox = kTT * 128;         // 128 tokens x 64 BF16 features: 16 KB
+constexpr int kMaxSlots = 3;
+constexpr int kXWarp0 = 2, kXWarps = 4;      // rotation / split warps
+constexpr int kEWarp0 = 6, kEWarps = 8;      // epilogue warps (two per TMEM sub-partition)
+constexpr int kXThreads = kXWarps * 32;
+constexpr int kThreadsT = (kEWarp0 + kEWarps) * 32;
+constexpr size_t kSmemBudget = 230400;       // dynamic shared memory per CTA (1 KB of it for alignment)
+constexpr size_t kSmemFloor = 120 * 1024;    // forces one CTA per SM (each allocates all of TMEM)
+
+struct TileArgs {
+  const __half2* phase;
+  const float* eta_raw;
+  const bf16* m0;  // readout: R_d;  grad: B1y
+  const bf16* m1;  // grad: B1c
+  const bf16* m2;  // grad: B1a
+  const bf16* m3;  // grad: B2
+  float* partial;  // moment partials [B*H][nchunks][2R][NC]
+  float* etastat;  // [B*H][ntiles]
+  int* status;
+  int N, H, d, hg, groups, nrel, nval, ntiles, ct, nchunks, items, pos_batched, slots, nbuf, cols;
+  uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
+  uint32_t off_val;     // content (or dY) boxes
+  uint32_t off_aux;     // grad: dY boxes; moments: operand buffer
+  uint32_t off_mat;     // operand matrices
+  uint32_t load_bytes;  // transaction bytes per slot fill
+};
+
+struct TileShared {
+  uint64_t full[kMaxSlots];   // producer -> transform (TMA / bulk bytes landed)
+  uint64_t xdone[kMaxSlots];  // transform -> MMA
+  uint64_t sfree[kMaxSlots];  // slot released (MMA done, or output stored)
+  uint64_t edone[kMaxSlots];  // epilogue warps -> storing thread
+  uint64_t tfull[4];          // MMA -> epilogue (accumulator ready)
+  uint64_t tempty[4];         // epilogue -> MMA (accumulator drained)
+  uint32_t tmem;
+  int abort_flag;
+  float red[kMaxSlots][4][4];  // per slot, head, sub-partition: complement statistic
+};
+
+__device__ __forceinline__ bool twait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
+  return false;
+}
+
+// 16-byte chunk c (features 8c .. 8c+7) of token row r in a 128B-swizzled box
+// (1024-byte aligned): chunk c of row r lives at chunk c ^ (r % 8).
+__device__ __forceinline__ uint8_t* box_chunk(uint8_t* box, int r, int c) {
+  return box + r * 128 + ((c ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ uint4 phase8(const __half2* phase, int64_t prow, int tok, int N, int R, int q) {
+  if (tok >= N) return make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);  // cos 1, sin 0
+  return __ldg(reinterpret_cast<const uint4*>(phase + (prow + tok) * (R / 2) + 4 * q));
+}
+
+// Common prologue: barriers, TMEM (all 512 columns), 1024-byte aligned base.
+__device__ __forceinline__ uint8_t* tile_setup(TileShared& sh, uint8_t* raw, int slots, int nbuf, int tcount_mma,
+                                               int tcount_free) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      mbar_init(smem_u32(&sh.full[s]), 1);
+      mbar_init(smem_u32(&sh.xdone[s]), kXWarps);
+      mbar_init(smem_u32(&sh.sfree[s]), tcount_free);
+      mbar_init(smem_u32(&sh.edone[s]), kEWarps);
+    }
+    for (int b = 0; b < nbuf; ++b) {
+      mbar_init(smem_u32(&sh.tfull[b]), tcount_mma);
+      mbar_init(smem_u32(&sh.tempty[b]), kEWarps);
+    }
+    sh.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if ((threadIdx.x >> 5) == 1) tmem_alloc(smem_u32(&sh.tmem), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t base = smem_u32(raw);
+  return raw + (((base + 1023u) & ~1023u) - base);
+}
+
+// Common epilogue: producer drains its last loads (bounded), TMEM freed.
+__device__ __forceinline__ void tile_teardown(TileShared& sh, int slots, const int* last_use, int* status) {
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      if (last_use[s] >= 0) mbar_wait(smem_u32(&sh.full[s]), static_cast<uint32_t>(last_use[s]) & 1u, status);
+    }
+  }
+  if ((threadIdx.x >> 5) == 1) {
+    tc_fence_after();
+    tmem_dealloc(sh.tmem, 512);
+  }
+}
+
+// Item decode for the per-tile kernels: tile fastest, then head group, then sample.
+struct TileItem {
+  int b, g, t;
+};
+__device__ __forceinline__ TileItem decode_tile(int it, int ntiles, int groups) {
+  TileItem x;
+  x.t = it % ntiles;
+  const int rest = it / ntiles;
+  x.g = rest % groups;
+  x.b = rest / groups;
+  return x;
+}
+
+// Rotate the relation boxes of one slot in place (BF16 A' for the MMA).
+template <int R>
+__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const __half2* phase, int64_t prow, int tok0,
+                                             int N, int xt) {
+  const int total = nrel * kTT * 8;
+#pragma unroll 4
+  for (int idx = xt; idx < total; idx += kXThreads) {
+    const int j = idx / (kTT * 8), rem = idx % (kTT * 8);
+    const int r = rem >> 3, c = rem & 7;
+    const int q = ((j * 64 + 8 * c) % R) >> 3;
+    uint8_t* p = box_chunk(rel + j * kBox, r, c);
+    const uint4 ph = phase8(phase, prow, tok0 + r, N, R, q);
+    float v[8];
+    rotate8(*reinterpret_cast<const uint4*>(p), ph, v);
+    *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
+  }
+}
+
+// ============================================================================
+// Moment pass.  Item = (sample, head group, chunk of ct tiles); per tile the
+// transform warps write, per head, the MN-major operand [hi | lo] (2R
+// features x 128 tokens, 128B swizzle: rows = tokens, feature groups of 64 at
+// kBox stride) and the MMA warp accumulates, per head,
+//   D[:, 0:R)      += [hi | lo]^T hi           (forward)
+//   D[:, R:R+d)    += [hi | lo]^T C            (forward; C straight from its box)
+//   D[:, 0:d)      += [hi | lo]^T dY           (backward)
+// with M = 2R, K = 128 tokens.  At the end of the chunk the epilogue drains
+// the accumulators to partial[(b*H + h)][chunk][2R][NC].
+// ============================================================================
+template <int R, bool BWD>
+__global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid_constant__ CUtensorMap tm_rel,
+                                                                     const __grid_constant__ CUtensorMap tm_val,
+                                                                     const TileArgs a) {
+  constexpr int M2 = 2 * R;                       // MMA M (64 or 128)
+  constexpr uint32_t kHead = (M2 / 64) * kBox;    // operand bytes per head
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ TileShared sh;
+  volatile int* abort_v = &sh.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = a.d;
+  const int NC = (BWD ? 0 : R) + d;
+  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
+  const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                   static_cast<int>(gridDim.x);
+  int last_use[kMaxSlots] = {-1, -1, -1};
+
+  auto item_of = [&](int i, int& b, int& g, int& chunk, int& t0, int& nt) {
+    const int it = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+    chunk = it % a.nchunks;
+    const int rest = it / a.nchunks;
+    g = rest % a.groups;
+    b = rest / a.groups;
+    t0 = chunk * a.ct;
+    nt = min(a.ct, a.ntiles - t0);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_rel);
+      prefetch_tmap(&tm_val);
+    }
+    int k = 0;
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      int b, g, chunk, t0, nt;
+      item_of(i, b, g, chunk, t0, nt);
+      for (int tt = 0; tt < nt && ok; ++tt, ++k) {
+        const int s = k % a.slots, u = k / a.slots;
+        ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
+        if (ok && lane == 0) {
+          uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+          const uint32_t bar = smem_u32(&sh.full[s]);
+          mbar_arrive_expect_tx(bar, a.load_bytes);
+          const int row = (t0 + tt) * kTT;
+          for (int j = 0; j < a.nrel; ++j)
+            tma_load_3d(smem_u32(slot + j * kBox), &tm_rel, g * a.hg * R + j * 64, row, b, bar);
+          const int vcol0 = (BWD ? 0 : a.H * R) + g * a.hg * d;
+          for (int j = 0; j < a.nval; ++j)
+            tma_load_3d(smem_u32(slot + a.off_val + j * kBox), &tm_val, vcol0 + j * 64, row, b, bar);
+          last_use[s] = u;
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc_r = make_idesc(M2, R, true, true);
+    const uint32_t idesc_v = make_idesc(M2, d, true, true);
+    int k = 0;
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      int b, g, chunk, t0, nt;
+      item_of(i, b, g, chunk, t0, nt);
+      const int tb = i % a.nbuf, tu = i / a.nbuf;
+      ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
+      tc_fence_after();
+      for (int tt = 0; tt < nt && ok; ++tt, ++k) {
+        const int s = k % a.slots, u = k / a.slots;
+        ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
+        tc_fence_after();
+        if (ok && lane == 0) {
+          const uint32_t slot = smem_u32(smem + static_cast<size_t>(s) * a.slot_bytes);
+          for (int hl = 0; hl < a.hg; ++hl) {
+            const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols + hl * NC);
+            const uint32_t op = slot + a.off_aux + hl * kHead;
+            const int fv = hl * d;
+            const uint32_t vb = slot + a.off_val + (fv >> 6) * kBox + (fv & 63) * 2;
+#pragma unroll
+            for (int ks = 0; ks < kTT / 16; ++ks) {
+              const uint32_t acc = (tt > 0 || ks > 0) ? 1u : 0u;
+              const uint64_t ad = make_desc_sw128(op + ks * 2048, kBox, 1024);
+              if (!BWD) mma_bf16(dcol, ad, ad, idesc_r, acc);
+              mma_bf16(dcol + (BWD ? 0 : R), ad, make_desc_sw128(vb + ks * 2048, kBox, 1024), idesc_v, acc);
+            }
+          }
+          mma_commit(smem_u32(&sh.sfree[s]));
+          if (tt == nt - 1) mma_commit(smem_u32(&sh.tfull[tb]));
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp < kXWarp0 + kXWarps) {
+    // ------------------------------------------------------------ rotate + hi/lo split
+    const int xt = threadIdx.x - kXWarp0 * 32;
+    int k = 0;
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      int b, g, chunk, t0, nt;
+      item_of(i, b, g, chunk, t0, nt);
+      const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
+      for (int tt = 0; tt < nt && ok; ++tt, ++k) {
+        const int s = k % a.slots, u = k / a.slots;
+        ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
+        if (ok) {
+          uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+          uint8_t* op = slot + a.off_aux;
+          const int tok0 = (t0 + tt) * kTT;
+          const int total = a.nrel * kTT * 8;
+#pragma unroll 2
+          for (int idx = xt; idx < total; idx += kXThreads) {
+            const int j = idx / (kTT * 8), rem = idx % (kTT * 8);
+            const int r = rem >> 3, c = rem & 7;
+            const int f = j * 64 + 8 * c;
+            const int hl = f / R, k0 = f % R;
+            const uint4 ph = phase8(a.phase, prow, tok0 + r, a.N, R, k0 >> 3);
+            float v[8];
+            rotate8(*reinterpret_cast<const uint4*>(box_chunk(slot + j * kBox, r, c)), ph, v);
+            const uint4 hi = pack8_bf16(v);
+            const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
+            float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
+                           v[4] - h2.x, v[5] - h2.y, v[6] - h3.x, v[7] - h3.y};
+            uint8_t* ob = op + hl * kHead;
+            const int mh = k0, ml = R + k0;
+            *reinterpret_cast<uint4*>(box_chunk(ob + (mh >> 6) * kBox, r, (mh & 63) >> 3)) = hi;
+            *reinterpret_cast<uint4*>(box_chunk(ob + (ml >> 6) * kBox, r, (ml & 63) >> 3)) = pack8_bf16(lo);
+          }
+          fence_proxy_async();
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ drain accumulators
+    const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
+    const bool m64 = M2 == 64;
+    const int m = m64 ? 16 * sub + lane : 32 * sub + lane;
+    const bool valid = !m64 || lane < 16;
+    const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      int b, g, chunk, t0, nt;
+      item_of(i, b, g, chunk, t0, nt);
+      const int tb = i % a.nbuf, tu = i / a.nbuf;
+      ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
+      tc_fence_after();
+      if (ok) {
+        for (int hl = half; hl < a.hg; hl += 2) {
+          const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
+          float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + m) * static_cast<int64_t>(NC);
+          for (int c0 = 0; c0 < NC; c0 += 32) {
+            float v[32];
+            tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC + c0), v);
+            tmem_ld_wait();
+            if (valid) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh.tempty[tb]));
+    }
+  }
+  tile_teardown(sh, a.slots, last_use, a.status);
+}
+
+// ============================================================================
+// Readout: Y = eta C + A' R_d per (sample, head group, tile).  MMA per head:
+// M = 128 tokens, K = R (rotated relation, K-major straight from its box),
+// N = d (R_d, K-major canonical from the solve).  The epilogue writes
+// eta C + acc over the content box and stores it to the mixed output.
+// ============================================================================
+template <int R>
+__global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
+                                                                     const __grid_constant__ CUtensorMap tm_out,
+                                                                     const TileArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ TileShared sh;
+  volatile int* abort_v = &sh.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = a.d;
+  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
+  const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                   static_cast<int>(gridDim.x);
+  int last_use[kMaxSlots] = {-1, -1, -1};
+  const uint32_t mat_bytes = static_cast<uint32_t>(a.hg * d * R * 2);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_proj);
+      prefetch_tmap(&tm_out);
+    }
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+      const int s = i % a.slots, u = i / a.slots;
+      ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
+      if (ok && lane == 0) {
+        uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+        const uint32_t bar = smem_u32(&sh.full[s]);
+        mbar_arrive_expect_tx(bar, a.load_bytes);
+        const int row = x.t * kTT;
+        for (int j = 0; j < a.nrel; ++j)
+          tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
+        for (int j = 0; j < a.nval; ++j)
+          tma_load_3d(smem_u32(slot + a.off_val + j * kBox), &tm_proj, a.H * R + x.g * a.hg * d + j * 64, row, x.b,
+                      bar);
+        const int64_t bh0 = static_cast<int64_t>(x.b) * a.H + x.g * a.hg;
+        bulk_load(smem_u32(slot + a.off_mat), a.m0 + bh0 * d * R, mat_bytes, bar);
+        last_use[s] = u;
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    const uint32_t idesc = make_idesc(128, d, false, false);
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const int s = i % a.slots, u = i / a.slots;
+      const int tb = i % a.nbuf, tu = i / a.nbuf;
+      ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
+      if (ok) ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
+      tc_fence_after();
+      if (ok && lane == 0) {
+        const uint32_t slot = smem_u32(smem + static_cast<size_t>(s) * a.slot_bytes);
+        for (int hl = 0; hl < a.hg; ++hl) {
+          const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols + hl * d);
+#pragma unroll
+          for (int ks = 0; ks < R / 16; ++ks) {
+            const int f = hl * R + 16 * ks;
+            const uint64_t ad = make_desc_sw128(slot + (f >> 6) * kBox + (f & 63) * 2, 16, 1024);
+            const uint64_t bd = make_desc(slot + a.off_mat + hl * d * R * 2 + ks * 256, 128, R * 16);
+            mma_bf16(dcol, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          }
+        }
+        mma_commit(smem_u32(&sh.tfull[tb]));
+      }
+      __syncwarp();
+    }
+  } else if (warp < kXWarp0 + kXWarps) {
+    const int xt = threadIdx.x - kXWarp0 * 32;
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+      const int s = i % a.slots, u = i / a.slots;
+      ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
+      if (ok) {
+        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+        rotate_boxes<R>(smem + static_cast<size_t>(s) * a.slot_bytes, a.nrel, a.phase, prow, x.t * kTT, a.N, xt);
+        fence_proxy_async();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
+    }
+  } else {
+    const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
+    const int r = 32 * sub + lane;
+    const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+      const int s = i % a.slots, u = i / a.slots;
+      const int tb = i % a.nbuf, tu = i / a.nbuf;
+      ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
+      tc_fence_after();
+      uint8_t* con = smem + static_cast<size_t>(s) * a.slot_bytes + a.off_val;
+      if (ok) {
+        for (int hl = half; hl < a.hg; hl += 2) {
+          const float eta = bounded_complement(a.eta_raw[x.g * a.hg + hl]);
+          for (int c0 = 0; c0 < d; c0 += 32) {
+            float v[32];
+            tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + hl * d + c0), v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int f = hl * d + c0 + 8 * q;
+              uint4* p = reinterpret_cast<uint4*>(box_chunk(con + (f >> 6) * kBox, r, (f & 63) >> 3));
+              const uint4 cv = *p;
+              const float2 c01 = unpack_bf16(cv.x), c23 = unpack_bf16(cv.y), c45 = unpack_bf16(cv.z),
+                           c67 = unpack_bf16(cv.w);
+              float y[8] = {fmaf(eta, c01.x, v[8 * q]),     fmaf(eta, c01.y, v[8 * q + 1]),
+                            fmaf(eta, c23.x, v[8 * q + 2]), fmaf(eta, c23.y, v[8 * q + 3]),
+                            fmaf(eta, c45.x, v[8 * q + 4]), fmaf(eta, c45.y, v[8 * q + 5]),
+                            fmaf(eta, c67.x, v[8 * q + 6]), fmaf(eta, c67.y, v[8 * q + 7])};
+              *p = pack8_bf16(y);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&sh.tempty[tb]));
+        if (ok) mbar_arrive(smem_u32(&sh.edone[s]));
+      }
+      if (ok && warp == kEWarp0 && lane == 0) {
+        ok = twait(smem_u32(&sh.edone[s]), u & 1, abort_v, a.status);
+        if (ok) {
+          for (int j = 0; j < a.nval; ++j)
+            tma_store_3d(&tm_out, smem_u32(con + j * kBox), x.g * a.hg * d + j * 64, x.t * kTT, x.b);
+          bulk_commit();
+          bulk_wait_read<0>();
+          mbar_arrive(smem_u32(&sh.sfree[s]));
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    }
+    if (warp == kEWarp0 && lane == 0) bulk_wait<0>();
+  }
+  tile_teardown(sh, a.slots, last_use, a.status);
+}
+
+// ============================================================================
+// Gradient pass per (sample, head group, tile).  MMA per head (M = 128
+// tokens, A operands K-major straight from the boxes):
+//   dA' = dY B1y + C B1c + A' B1a   (N = R)     dC = A' B2   (N = d)
+// Epilogue: dA' rotated back with the transposed Rank-Rotary map into the
+// relation box, eta dY + dC into the content box (after the complement
+// statistic sum(dY * C) is taken), both stored to the packed gradient.
+// ============================================================================
+template <int R>
+__global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
+                                                                  const __grid_constant__ CUtensorMap tm_dy,
+                                                                  const __grid_constant__ CUtensorMap tm_gproj,
+                                                                  const TileArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ TileShared sh;
+  volatile int* abort_v = &sh.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = a.d;
+  const int NC = R + d;
+  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
+  const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                   static_cast<int>(gridDim.x);
+  int last_use[kMaxSlots] = {-1, -1, -1};
+  // Operand matrices of the group's heads, each block contiguous per head.
+  const uint32_t sz_y = static_cast<uint32_t>(R * d * 2), sz_a = static_cast<uint32_t>(R * R * 2);
+  const uint32_t off_y = 0, off_c = a.hg * sz_y, off_a = 2 * a.hg * sz_y, off_2 = off_a + a.hg * sz_a;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_proj);
+      prefetch_tmap(&tm_dy);
+      prefetch_tmap(&tm_gproj);
+    }
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+      const int s = i % a.slots, u = i / a.slots;
+      ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
+      if (ok && lane == 0) {
+        uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+        const uint32_t bar = smem_u32(&sh.full[s]);
+        mbar_arrive_expect_tx(bar, a.load_bytes);
+        const int row = x.t * kTT;
+        for (int j = 0; j < a.nrel; ++j)
+          tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
+        for (int j = 0; j < a.nval; ++j) {
+          tma_load_3d(smem_u32(slot + a.off_val + j * kBox), &tm_proj, a.H * R + x.g * a.hg * d + j * 64, row, x.b,
+                      bar);
+          tma_load_3d(smem_u32(slot + a.off_aux + j * kBox), &tm_dy, x.g * a.hg * d + j * 64, row, x.b, bar);
+        }
+        const int64_t bh0 = static_cast<int64_t>(x.b) * a.H + x.g * a.hg;
+        uint8_t* mat = slot + a.off_mat;
+        bulk_load(smem_u32(mat + off_y), a.m0 + bh0 * R * d, a.hg * sz_y, bar);
+        bulk_load(smem_u32(mat + off_c), a.m1 + bh0 * R * d, a.hg * sz_y, bar);
+        bulk_load(smem_u32(mat + off_a), a.m2 + bh0 * R * R, a.hg * sz_a, bar);
+        bulk_load(smem_u32(mat + off_2), a.m3 + bh0 * d * R, a.hg * sz_y, bar);
+        last_use[s] = u;
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    const uint32_t idesc_r = make_idesc(128, R, false, false);
+    const uint32_t idesc_d = make_idesc(128, d, false, false);
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const int s = i % a.slots, u = i / a.slots;
+      const int tb = i % a.nbuf, tu = i / a.nbuf;
+      ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
+      if (ok) ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
+      tc_fence_after();
+      if (ok && lane == 0) {
+        const uint32_t slot = smem_u32(smem + static_cast<size_t>(s) * a.slot_bytes);
+        const uint32_t mat = slot + a.off_mat;
+        for (int hl = 0; hl < a.hg; ++hl) {
+          const uint32_t da = sh.tmem + static_cast<uint32_t>(tb * a.cols + hl * NC);
+          for (int ks = 0; ks < d / 16; ++ks) {
+            const int f = hl * d + 16 * ks;
+            const uint32_t fo = (f >> 6) * kBox + (f & 63) * 2;
+            mma_bf16(da, make_desc_sw128(slot + a.off_aux + fo, 16, 1024),
+                     make_desc(mat + off_y + hl * sz_y + ks * 256, 128, d * 16), idesc_r, ks > 0 ? 1u : 0u);
+            mma_bf16(da, make_desc_sw128(slot + a.off_val + fo, 16, 1024),
+                     make_desc(mat + off_c + hl * sz_y + ks * 256, 128, d * 16), idesc_r, 1u);
+          }
+#pragma unroll
+          for (int ks = 0; ks < R / 16; ++ks) {
+            const int f = hl * R + 16 * ks;
+            const uint64_t ad = make_desc_sw128(slot + (f >> 6) * kBox + (f & 63) * 2, 16, 1024);
+            mma_bf16(da, ad, make_desc(mat + off_a + hl * sz_a + ks * 256, 128, R * 16), idesc_r, 1u);
+            mma_bf16(da + R, ad, make_desc(mat + off_2 + hl * sz_y + ks * 256, 128, R * 16), idesc_d,
+                     ks > 0 ? 1u : 0u);
+          }
+        }
+        mma_commit(smem_u32(&sh.tfull[tb]));
+      }
+      __syncwarp();
+    }
+  } else if (warp < kXWarp0 + kXWarps) {
+    const int xt = threadIdx.x - kXWarp0 * 32;
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+      const int s = i % a.slots, u = i / a.slots;
+      ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
+      if (ok) {
+        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+        rotate_boxes<R>(smem + static_cast<size_t>(s) * a.slot_bytes, a.nrel, a.phase, prow, x.t * kTT, a.N, xt);
+        fence_proxy_async();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
+    }
+  } else {
+    const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
+    const int r = 32 * sub + lane;
+    const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
+    bool ok = true;
+    for (int i = 0; i < nloc && ok; ++i) {
+      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+      const int s = i % a.slots, u = i / a.slots;
+      const int tb = i % a.nbuf, tu = i / a.nbuf;
+      ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
+      tc_fence_after();
+      uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+      uint8_t* con = slot + a.off_val;
+      uint8_t* dyb = slot + a.off_aux;
+      const int tok = x.t * kTT + r;
+      const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+      if (ok) {
+        for (int hl = half; hl < a.hg; hl += 2) {
+          const uint32_t tcol = lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC);
+          // relation gradient: rotate dA' back and overwrite the relation box
+          for (int r0 = 0; r0 < R; r0 += 32) {
+            float gv[32];
+            tmem_ld32(tcol + r0, gv);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int f = hl * R + r0 + 8 * q;
+              const uint4 ph = phase8(a.phase, prow, tok, a.N, R, (r0 >> 3) + q);
+              const float gi[8] = {gv[8 * q], gv[8 * q + 1], gv[8 * q + 2], gv[8 * q + 3],
+                                   gv[8 * q + 4], gv[8 * q + 5], gv[8 * q + 6], gv[8 * q + 7]};
+              float o[8];
+              rotate8_transpose(gi, ph, o);
+              *reinterpret_cast<uint4*>(box_chunk(slot + (f >> 6) * kBox, r, (f & 63) >> 3)) = pack8_bf16(o);
+            }
+          }
+          // content gradient eta dY + dC, and the statistic sum(dY * C)
+          const float eta = bounded_complement(a.eta_raw[x.g * a.hg + hl]);
+          float stat = 0.0f;
+          for (int c0 = 0; c0 < d; c0 += 32) {
+            float v[32];
+            tmem_ld32(tcol + R + c0, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int f = hl * d + c0 + 8 * q;
+              const int bo = (f >> 6) * kBox;
+              uint4* pc = reinterpret_cast<uint4*>(box_chunk(con + bo, r, (f & 63) >> 3));
+              const uint4 yv = *reinterpret_cast<const uint4*>(box_chunk(dyb + bo, r, (f & 63) >> 3));
+              const uint4 cv = *pc;
+              const uint32_t yy[4] = {yv.x, yv.y, yv.z, yv.w}, cc[4] = {cv.x, cv.y, cv.z, cv.w};
+              float o[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 y2 = unpack_bf16(yy[e]), c2 = unpack_bf16(cc[e]);
+                stat = fmaf(y2.x, c2.x, stat);
+                stat = fmaf(y2.y, c2.y, stat);
+                o[2 * e] = fmaf(eta, y2.x, v[8 * q + 2 * e]);
+                o[2 * e + 1] = fmaf(eta, y2.y, v[8 * q + 2 * e + 1]);
+              }
+              *pc = pack8_bf16(o);
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) stat += __shfl_xor_sync(0xffffffffu, stat, o);
+          if (lane == 0) sh.red[s][hl][sub] = stat;
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&sh.tempty[tb]));
+        if (ok) mbar_arrive(smem_u32(&sh.edone[s]));
+      }
+      if (ok && warp == kEWarp0 && lane == 0) {
+        ok = twait(smem_u32(&sh.edone[s]), u & 1, abort_v, a.status);
+        if (ok) {
+          for (int j = 0; j < a.nrel; ++j)
+            tma_store_3d(&tm_gproj, smem_u32(slot + j * kBox), x.g * a.hg * R + j * 64, x.t * kTT, x.b);
+          for (int j = 0; j < a.nval; ++j)
+            tma_store_3d(&tm_gproj, smem_u32(con + j * kBox), a.H * R + x.g * a.hg * d + j * 64, x.t * kTT, x.b);
+          bulk_commit();
+          for (int hl = 0; hl < a.hg; ++hl) {
+            const int64_t bh = static_cast<int64_t>(x.b) * a.H + x.g * a.hg + hl;
+            a.etastat[bh * a.ntiles + x.t] = (sh.red[s][hl][0] + sh.red[s][hl][1]) + (sh.red[s][hl][2] + sh.red[s][hl][3]);
+          }
+          bulk_wait_read<0>();
+          mbar_arrive(smem_u32(&sh.sfree[s]));
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    }
+    if (warp == kEWarp0 && lane == 0) bulk_wait<0>();
+  }
+  tile_teardown(sh, a.slots, last_use, a.status);
+}
+
+// ---------------------------------------------------------------------------- host side
+CUresult encode_boxes(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const void* ptr, int64_t cols,
+                      int64_t N, int64_t B) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * 2), static_cast<cuuint64_t>(N * cols * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTT), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Slot layout and counts shared by the launchers.  Returns false when fewer
+// than two slots fit (the caller then uses the per-head kernels).
+bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_count, size_t* smem, int* grid) {
+  slot_bytes = (slot_bytes + 1023u) & ~1023u;
+  int slots = static_cast<int>((kSmemBudget - 1024) / slot_bytes);
+  if (slots > kMaxSlots) slots = kMaxSlots;
+  if (slots < 2) return false;
+  int pc = 32;
+  while (pc < cols) pc *= 2;
+  if (pc > 512) return false;
+  a.nbuf = 512 / pc < 4 ? 512 / pc : 4;
+  a.cols = cols;
+  a.slots = slots;
+  a.slot_bytes = slot_bytes;
+  a.items = items;
+  size_t bytes = static_cast<size_t>(slots) * slot_bytes + 1024;
+  if (bytes < kSmemFloor) bytes = kSmemFloor;
+  *smem = bytes;
+  const int sms = sm_count > 0 ? sm_count : 148;
+  *grid = items < sms ? items : sms;
+  return items > 0;
+}
+
+TileArgs base_args(const Plan& p, const __half2* phase, const float* eta_raw, int* status) {
+  TileArgs a{};
+  a.phase = phase;
+  a.eta_raw = eta_raw;
+  a.status = status;
+  a.N = static_cast<int>(p.N);
+  a.H = static_cast<int>(p.H);
+  a.d = static_cast<int>(p.d);
+  a.hg = p.hg;
+  a.groups = p.groups;
+  a.nrel = p.nrel;
+  a.nval = p.nval;
+  a.ntiles = static_cast<int>(ceil_div(p.N, kTT));
+  a.ct = p.ct;
+  a.nchunks = static_cast<int>(p.nchunks);
+  a.pos_batched = p.pos_rows > 1 ? 1 : 0;
+  return a;
+}
+
+}  // namespace
+
+bool tiled_usable(const Plan& p, std::initializer_list<const void*> ptrs) {
+  if (!p.tiled || tensor_map_encoder() == nullptr) return false;
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return false;
+  return true;
+}
+
+cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const __half2* phase,
+                                 float* partial, int* status, int sm_count, cudaStream_t stream) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  CUtensorMap tm_rel{}, tm_val{};
+  if (encode_boxes(encode, &tm_rel, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (bwd) {
+    if (encode_boxes(encode, &tm_val, gout, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  } else {
+    tm_val = tm_rel;
+  }
+  TileArgs a = base_args(p, phase, nullptr, status);
+  a.partial = partial;
+  const uint32_t head = static_cast<uint32_t>(2 * p.R / 64) * kBox;
+  a.off_val = p.nrel * kBox;
+  a.off_aux = (p.nrel + p.nval) * kBox;
+  a.load_bytes = (p.nrel + p.nval) * kBox;
+  const int cols = p.hg * static_cast<int>((bwd ? 0 : p.R) + p.d);
+  const int items = static_cast<int>(p.B * p.groups * p.nchunks);
+  size_t smem = 0;
+  int grid = 0;
+  if (!finish_args(a, a.off_aux + p.hg * head, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
+  const void* fn = nullptr;
+  if (p.R == 32) {
+    fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<32, true>)
+             : reinterpret_cast<const void*>(&moments_tile_kernel<32, false>);
+  } else {
+    fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<64, true>)
+             : reinterpret_cast<const void*>(&moments_tile_kernel<64, false>);
+  }
+  cudaError_t e = allow_smem(fn, smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope(bwd ? "moments_bwd" : "moments_fwd", stream);
+  if (p.R == 32) {
+    if (bwd) moments_tile_kernel<32, true><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
+    else moments_tile_kernel<32, false><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
+  } else {
+    if (bwd) moments_tile_kernel<64, true><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
+    else moments_tile_kernel<64, false><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2* phase, const bf16* rmat,
+                                 const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  CUtensorMap tm_proj{}, tm_out{};
+  if (encode_boxes(encode, &tm_proj, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (encode_boxes(encode, &tm_out, out, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  TileArgs a = base_args(p, phase, eta_raw, status);
+  a.m0 = rmat;
+  a.off_val = p.nrel * kBox;
+  a.off_mat = (p.nrel + p.nval) * kBox;
+  const uint32_t mat = static_cast<uint32_t>(p.hg * p.d * p.R * 2);
+  a.load_bytes = (p.nrel + p.nval) * kBox + mat;
+  const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
+  size_t smem = 0;
+  int grid = 0;
+  if (!finish_args(a, a.off_mat + mat, p.hg * static_cast<int>(p.d), items, sm_count, &smem, &grid))
+    return cudaErrorInvalidValue;
+  const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
+                             : reinterpret_cast<const void*>(&readout_tile_kernel<64>);
+  cudaError_t e = allow_smem(fn, smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope("readout", stream);
+  if (p.R == 32) {
+    readout_tile_kernel<32><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_out, a);
+  } else {
+    readout_tile_kernel<64><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_out, a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase, const bf16* b1y,
+                              const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
+                              float* etastat, int* status, int sm_count, cudaStream_t stream) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  CUtensorMap tm_proj{}, tm_dy{}, tm_gproj{};
+  if (encode_boxes(encode, &tm_proj, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (encode_boxes(encode, &tm_dy, gout, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (encode_boxes(encode, &tm_gproj, gproj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  TileArgs a = base_args(p, phase, eta_raw, status);
+  a.m0 = b1y;
+  a.m1 = b1c;
+  a.m2 = b1a;
+  a.m3 = b2;
+  a.etastat = etastat;
+  a.off_val = p.nrel * kBox;
+  a.off_aux = (p.nrel + p.nval) * kBox;
+  a.off_mat = (p.nrel + 2 * p.nval) * kBox;
+  const uint32_t mat = static_cast<uint32_t>(p.hg * (3 * p.R * p.d + p.R * p.R) * 2);
+  a.load_bytes = (p.nrel + 2 * p.nval) * kBox + mat;
+  const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
+  size_t smem = 0;
+  int grid = 0;
+  if (!finish_args(a, a.off_mat + mat, p.hg * static_cast<int>(p.R + p.d), items, sm_count, &smem, &grid))
+    return cudaErrorInvalidValue;
+  const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
+                             : reinterpret_cast<const void*>(&grad_tile_kernel<64>);
+  cudaError_t e = allow_smem(fn, smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope("grad", stream);
+  if (p.R == 32) {
+    grad_tile_kernel<32><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+  } else {
+    grad_tile_kernel<64><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace lsso
