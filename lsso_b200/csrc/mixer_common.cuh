@@ -54,6 +54,32 @@ struct Plan {
 };
 
 constexpr int kTileTokens = 128;
+constexpr int64_t kTileBox = kTileTokens * 128;       // one 64-feature x 128-token BF16 box
+constexpr int64_t kTileSmemBudget = 230400;           // dynamic shared memory per tile CTA
+constexpr int kTileMaxSlots = 3;
+
+// Bytes of one pipeline slot of each tile kernel (a multiple of 1024):
+// kind 0 moments forward, 1 moments backward, 2 readout, 3 gradient.  Every
+// slot holds the item's boxes, its phase rows and its operand matrices.
+inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
+  const int64_t nrel = hg * R / 64, nval = hg * d / 64;
+  const int64_t phase = kTileTokens * R * 2;
+  int64_t bytes = 0;
+  if (kind <= 1) {
+    // R = 32: lo box + relation/hi box + values; R = 64: per-head [hi | lo] operands.
+    const int64_t ops = R == 32 ? nrel : hg * (2 * R / 64);
+    bytes = (nrel + nval + ops) * kTileBox + phase;
+  } else if (kind == 2) {
+    bytes = (nrel + nval) * kTileBox + phase + hg * d * R * 2;
+  } else {
+    bytes = (nrel + 2 * nval) * kTileBox + phase + hg * (3 * R * d + R * R) * 2;
+  }
+  return (bytes + 1023) / 1024 * 1024;
+}
+inline int tile_slots(int64_t slot_bytes) {
+  const int64_t n = (kTileSmemBudget - 1024) / slot_bytes;
+  return static_cast<int>(n > kTileMaxSlots ? kTileMaxSlots : n);
+}
 
 // Choose the head group and the moment-pass chunking of the tiled token
 // kernels; leaves p.tiled false for shapes they do not cover (those use the
@@ -65,6 +91,8 @@ inline void plan_tiles(Plan& p, int sm_count) {
   if (!r_ok || !d_ok || (p.W % 8) != 0 || p.D != p.H * p.d) return;
   const int hg = static_cast<int>(64 / (p.R < p.d ? p.R : p.d));
   if (p.H % hg != 0) return;
+  for (int kind = 0; kind < 4; ++kind)
+    if (tile_slots(tile_slot_bytes(kind, p.R, p.d, hg)) < 2) return;
   p.hg = hg;
   p.groups = static_cast<int>(p.H / hg);
   p.nrel = static_cast<int>(hg * p.R / 64);

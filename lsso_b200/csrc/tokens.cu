@@ -41,13 +41,12 @@ namespace lsso {
 namespace {
 
 constexpr int kTT = kTileTokens;             // tokens per tile
-constexpr uint32_t kBox = kTT * 128;         // 128 tokens x 64 BF16 features: 16 KB
-constexpr int kMaxSlots = 3;
-constexpr int kXWarp0 = 2, kXWarps = 4;      // rotation / split warps
-constexpr int kEWarp0 = 6, kEWarps = 8;      // epilogue warps (two per TMEM sub-partition)
+constexpr uint32_t kBox = kTileBox;          // 128 tokens x 64 BF16 features: 16 KB
+constexpr int kMaxSlots = kTileMaxSlots;
+constexpr int kXWarp0 = 2, kXWarps = 8;      // rotation / split warps
+constexpr int kEWarp0 = 10, kEWarps = 8;      // epilogue warps (two per TMEM sub-partition)
 constexpr int kXThreads = kXWarps * 32;
 constexpr int kThreadsT = (kEWarp0 + kEWarps) * 32;
-constexpr size_t kSmemBudget = 230400;       // dynamic shared memory per CTA (1 KB of it for alignment)
 constexpr size_t kSmemFloor = 120 * 1024;    // forces one CTA per SM (each allocates all of TMEM)
 
 struct TileArgs {
@@ -63,9 +62,11 @@ struct TileArgs {
   int N, H, d, hg, groups, nrel, nval, ntiles, ct, nchunks, items, pos_batched, slots, nbuf, cols;
   uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
   uint32_t off_val;     // content (or dY) boxes
-  uint32_t off_aux;     // grad: dY boxes; moments: operand buffer
+  uint32_t off_aux;     // grad: dY boxes; moments: operand buffer (R = 32: the lo box)
+  uint32_t off_rel;     // moments: relation boxes
   uint32_t off_mat;     // operand matrices
-  uint32_t load_bytes;  // transaction bytes per slot fill
+  uint32_t off_ph;      // phase rows of the tile (R/2 half2 per token)
+  uint32_t load_bytes;  // transaction bytes per slot fill, phase rows excluded
 };
 
 struct TileShared {
@@ -96,9 +97,17 @@ __device__ __forceinline__ uint8_t* box_chunk(uint8_t* box, int r, int c) {
   return box + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
-__device__ __forceinline__ uint4 phase8(const __half2* phase, int64_t prow, int tok, int N, int R, int q) {
+// Phases of rank chunk q (ranks 8q .. 8q+7) of tile row r, from the phase rows
+// staged in the slot; tokens past N rotate by the identity.
+__device__ __forceinline__ uint4 phase8(const uint8_t* ph, int r, int tok, int N, int R, int q) {
   if (tok >= N) return make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);  // cos 1, sin 0
-  return __ldg(reinterpret_cast<const uint4*>(phase + (prow + tok) * (R / 2) + 4 * q));
+  return *reinterpret_cast<const uint4*>(ph + r * (R * 2) + q * 16);
+}
+
+// Bytes of the phase rows of tile rows [t0, t0 + 128) inside the sequence.
+__device__ __forceinline__ uint32_t phase_bytes(int t0, int N, int R) {
+  const int rows = min(kTT, N - t0);
+  return static_cast<uint32_t>(rows * R * 2);
 }
 
 // Common prologue: barriers, TMEM (all 512 columns), 1024-byte aligned base.
@@ -156,8 +165,7 @@ __device__ __forceinline__ TileItem decode_tile(int it, int ntiles, int groups) 
 
 // Rotate the relation boxes of one slot in place (BF16 A' for the MMA).
 template <int R>
-__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const __half2* phase, int64_t prow, int tok0,
-                                             int N, int xt) {
+__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const uint8_t* phs, int tok0, int N, int xt) {
   const int total = nrel * kTT * 8;
 #pragma unroll 4
   for (int idx = xt; idx < total; idx += kXThreads) {
@@ -165,7 +173,7 @@ __device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const __hal
     const int r = rem >> 3, c = rem & 7;
     const int q = ((j * 64 + 8 * c) % R) >> 3;
     uint8_t* p = box_chunk(rel + j * kBox, r, c);
-    const uint4 ph = phase8(phase, prow, tok0 + r, N, R, q);
+    const uint4 ph = phase8(phs, r, tok0 + r, N, R, q);
     float v[8];
     rotate8(*reinterpret_cast<const uint4*>(p), ph, v);
     *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
@@ -173,22 +181,28 @@ __device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const __hal
 }
 
 // ============================================================================
-// Moment pass.  Item = (sample, head group, chunk of ct tiles); per tile the
-// transform warps write, per head, the MN-major operand [hi | lo] (2R
-// features x 128 tokens, 128B swizzle: rows = tokens, feature groups of 64 at
-// kBox stride) and the MMA warp accumulates, per head,
-//   D[:, 0:R)      += [hi | lo]^T hi           (forward)
-//   D[:, R:R+d)    += [hi | lo]^T C            (forward; C straight from its box)
-//   D[:, 0:d)      += [hi | lo]^T dY           (backward)
-// with M = 2R, K = 128 tokens.  At the end of the chunk the epilogue drains
-// the accumulators to partial[(b*H + h)][chunk][2R][NC].
+// Moment pass.  Item = (sample, head group, chunk of ct tiles), K = 128 tokens
+// per tile, accumulated in TMEM over the chunk; at its end the epilogue drains
+// partial[(b*H + h)][chunk][2R][NC] (rows [0, R) hi products, [R, 2R) lo).
+//
+// R = 32 (two heads per group, fused): slot = [lo box | relation box, rotated
+// to hi in place | value boxes | phase rows].  Per K-step ONE MMA covers both
+// heads: A = [lo | hi] (M = 128: lo_0, lo_1, hi_0, hi_1), B = [hi | values]
+// (forward: N = 64 + hg d: hi_0, hi_1, C_0, C_1) or B = dY (backward); the
+// two 64-feature groups of each operand are consecutive boxes (LBO = 16 KB).
+// The cross-head blocks of the product are computed and ignored.
+//
+// R = 64: per head an MN-major operand [hi | lo] (two groups) in its own
+// buffer and per K-step  D[:, 0:R) += [hi|lo]^T hi,  D[:, R:) += [hi|lo]^T C
+// (forward) or  D += [hi|lo]^T dY (backward).
 // ============================================================================
 template <int R, bool BWD>
 __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid_constant__ CUtensorMap tm_rel,
                                                                      const __grid_constant__ CUtensorMap tm_val,
                                                                      const TileArgs a) {
-  constexpr int M2 = 2 * R;                       // MMA M (64 or 128)
-  constexpr uint32_t kHead = (M2 / 64) * kBox;    // operand bytes per head
+  constexpr bool kFused = R == 32;
+  constexpr int M2 = 2 * R;                       // rows of one head's partial
+  constexpr uint32_t kHead = (M2 / 64) * kBox;    // unfused operand bytes per head
   extern __shared__ uint8_t smem_raw[];
   __shared__ TileShared sh;
   volatile int* abort_v = &sh.abort_flag;
@@ -227,10 +241,13 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
         if (ok && lane == 0) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
           const uint32_t bar = smem_u32(&sh.full[s]);
-          mbar_arrive_expect_tx(bar, a.load_bytes);
           const int row = (t0 + tt) * kTT;
+          const uint32_t pb = phase_bytes(row, a.N, R);
+          mbar_arrive_expect_tx(bar, a.load_bytes + pb);
+          const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
+          bulk_load(smem_u32(slot + a.off_ph), a.phase + (prow + row) * (R / 2), pb, bar);
           for (int j = 0; j < a.nrel; ++j)
-            tma_load_3d(smem_u32(slot + j * kBox), &tm_rel, g * a.hg * R + j * 64, row, b, bar);
+            tma_load_3d(smem_u32(slot + a.off_rel + j * kBox), &tm_rel, g * a.hg * R + j * 64, row, b, bar);
           const int vcol0 = (BWD ? 0 : a.H * R) + g * a.hg * d;
           for (int j = 0; j < a.nval; ++j)
             tma_load_3d(smem_u32(slot + a.off_val + j * kBox), &tm_val, vcol0 + j * 64, row, b, bar);
@@ -241,6 +258,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc_f = make_idesc(128, BWD ? 64 * a.nval : 64 + 64 * a.nval, true, true);
     const uint32_t idesc_r = make_idesc(M2, R, true, true);
     const uint32_t idesc_v = make_idesc(M2, d, true, true);
     int k = 0;
@@ -257,17 +275,27 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
         tc_fence_after();
         if (ok && lane == 0) {
           const uint32_t slot = smem_u32(smem + static_cast<size_t>(s) * a.slot_bytes);
-          for (int hl = 0; hl < a.hg; ++hl) {
-            const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols + hl * NC);
-            const uint32_t op = slot + a.off_aux + hl * kHead;
-            const int fv = hl * d;
-            const uint32_t vb = slot + a.off_val + (fv >> 6) * kBox + (fv & 63) * 2;
+          if constexpr (kFused) {
+            const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols);
+            const uint32_t bsrc = slot + (BWD ? a.off_val : a.off_rel);
 #pragma unroll
             for (int ks = 0; ks < kTT / 16; ++ks) {
-              const uint32_t acc = (tt > 0 || ks > 0) ? 1u : 0u;
-              const uint64_t ad = make_desc_sw128(op + ks * 2048, kBox, 1024);
-              if (!BWD) mma_bf16(dcol, ad, ad, idesc_r, acc);
-              mma_bf16(dcol + (BWD ? 0 : R), ad, make_desc_sw128(vb + ks * 2048, kBox, 1024), idesc_v, acc);
+              mma_bf16(dcol, make_desc_sw128(slot + a.off_aux + ks * 2048, kBox, 1024),
+                       make_desc_sw128(bsrc + ks * 2048, kBox, 1024), idesc_f, (tt > 0 || ks > 0) ? 1u : 0u);
+            }
+          } else {
+            for (int hl = 0; hl < a.hg; ++hl) {
+              const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols + hl * NC);
+              const uint32_t op = slot + a.off_aux + hl * kHead;
+              const int fv = hl * d;
+              const uint32_t vb = slot + a.off_val + (fv >> 6) * kBox + (fv & 63) * 2;
+#pragma unroll
+              for (int ks = 0; ks < kTT / 16; ++ks) {
+                const uint32_t acc = (tt > 0 || ks > 0) ? 1u : 0u;
+                const uint64_t ad = make_desc_sw128(op + ks * 2048, kBox, 1024);
+                if (!BWD) mma_bf16(dcol, ad, ad, idesc_r, acc);
+                mma_bf16(dcol + (BWD ? 0 : R), ad, make_desc_sw128(vb + ks * 2048, kBox, 1024), idesc_v, acc);
+              }
             }
           }
           mma_commit(smem_u32(&sh.sfree[s]));
@@ -284,32 +312,39 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
     for (int i = 0; i < nloc && ok; ++i) {
       int b, g, chunk, t0, nt;
       item_of(i, b, g, chunk, t0, nt);
-      const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
       for (int tt = 0; tt < nt && ok; ++tt, ++k) {
         const int s = k % a.slots, u = k / a.slots;
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+          uint8_t* rel = slot + a.off_rel;
           uint8_t* op = slot + a.off_aux;
+          const uint8_t* phs = slot + a.off_ph;
           const int tok0 = (t0 + tt) * kTT;
           const int total = a.nrel * kTT * 8;
-#pragma unroll 2
+#pragma unroll 4
           for (int idx = xt; idx < total; idx += kXThreads) {
             const int j = idx / (kTT * 8), rem = idx % (kTT * 8);
             const int r = rem >> 3, c = rem & 7;
             const int f = j * 64 + 8 * c;
             const int hl = f / R, k0 = f % R;
-            const uint4 ph = phase8(a.phase, prow, tok0 + r, a.N, R, k0 >> 3);
+            const uint4 ph = phase8(phs, r, tok0 + r, a.N, R, k0 >> 3);
+            uint8_t* src = box_chunk(rel + j * kBox, r, c);
             float v[8];
-            rotate8(*reinterpret_cast<const uint4*>(box_chunk(slot + j * kBox, r, c)), ph, v);
+            rotate8(*reinterpret_cast<const uint4*>(src), ph, v);
             const uint4 hi = pack8_bf16(v);
             const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
             float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
                            v[4] - h2.x, v[5] - h2.y, v[6] - h3.x, v[7] - h3.y};
-            uint8_t* ob = op + hl * kHead;
-            const int mh = k0, ml = R + k0;
-            *reinterpret_cast<uint4*>(box_chunk(ob + (mh >> 6) * kBox, r, (mh & 63) >> 3)) = hi;
-            *reinterpret_cast<uint4*>(box_chunk(ob + (ml >> 6) * kBox, r, (ml & 63) >> 3)) = pack8_bf16(lo);
+            if constexpr (kFused) {
+              *reinterpret_cast<uint4*>(src) = hi;                                        // hi in place
+              *reinterpret_cast<uint4*>(box_chunk(op + j * kBox, r, c)) = pack8_bf16(lo);  // lo, same position
+            } else {
+              uint8_t* ob = op + hl * kHead;
+              const int mh = k0, ml = R + k0;
+              *reinterpret_cast<uint4*>(box_chunk(ob + (mh >> 6) * kBox, r, (mh & 63) >> 3)) = hi;
+              *reinterpret_cast<uint4*>(box_chunk(ob + (ml >> 6) * kBox, r, (ml & 63) >> 3)) = pack8_bf16(lo);
+            }
           }
           fence_proxy_async();
         }
@@ -320,9 +355,6 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
   } else {
     // ------------------------------------------------------------ drain accumulators
     const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
-    const bool m64 = M2 == 64;
-    const int m = m64 ? 16 * sub + lane : 32 * sub + lane;
-    const bool valid = !m64 || lane < 16;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
@@ -332,17 +364,37 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
-        for (int hl = half; hl < a.hg; hl += 2) {
-          const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
-          float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + m) * static_cast<int64_t>(NC);
-          for (int c0 = 0; c0 < NC; c0 += 32) {
+        if constexpr (kFused) {
+          // TMEM lanes: sub 0 lo_0, 1 lo_1, 2 hi_0, 3 hi_1; columns hi_0, hi_1 | values of head 0, head 1.
+          const int hh = sub & 1;
+          const int row = (sub < 2 ? R : 0) + lane;
+          const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hh;
+          float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + row) * static_cast<int64_t>(NC);
+          for (int c0 = 32 * half; c0 < NC; c0 += 64) {
+            const int tc = BWD ? hh * d + c0 : (c0 < R ? 32 * hh + c0 : 64 + hh * d + (c0 - R));
             float v[32];
-            tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC + c0), v);
+            tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
             tmem_ld_wait();
-            if (valid) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+        } else {
+          const bool m64 = M2 == 64;
+          const int m = m64 ? 16 * sub + lane : 32 * sub + lane;
+          const bool valid = !m64 || lane < 16;
+          for (int hl = half; hl < a.hg; hl += 2) {
+            const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
+            float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + m) * static_cast<int64_t>(NC);
+            for (int c0 = 0; c0 < NC; c0 += 32) {
+              float v[32];
+              tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC + c0), v);
+              tmem_ld_wait();
+              if (valid) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              }
             }
           }
         }
@@ -389,8 +441,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
       if (ok && lane == 0) {
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
         const uint32_t bar = smem_u32(&sh.full[s]);
-        mbar_arrive_expect_tx(bar, a.load_bytes);
         const int row = x.t * kTT;
+        const uint32_t pb = phase_bytes(row, a.N, R);
+        mbar_arrive_expect_tx(bar, a.load_bytes + pb);
+        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+        bulk_load(smem_u32(slot + a.off_ph), a.phase + (prow + row) * (R / 2), pb, bar);
         for (int j = 0; j < a.nrel; ++j)
           tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
         for (int j = 0; j < a.nval; ++j)
@@ -435,8 +490,8 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
       const int s = i % a.slots, u = i / a.slots;
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
-        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
-        rotate_boxes<R>(smem + static_cast<size_t>(s) * a.slot_bytes, a.nrel, a.phase, prow, x.t * kTT, a.N, xt);
+        uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+        rotate_boxes<R>(slot, a.nrel, slot + a.off_ph, x.t * kTT, a.N, xt);
         fence_proxy_async();
       }
       __syncwarp();
@@ -542,8 +597,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
       if (ok && lane == 0) {
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
         const uint32_t bar = smem_u32(&sh.full[s]);
-        mbar_arrive_expect_tx(bar, a.load_bytes);
         const int row = x.t * kTT;
+        const uint32_t pb = phase_bytes(row, a.N, R);
+        mbar_arrive_expect_tx(bar, a.load_bytes + pb);
+        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+        bulk_load(smem_u32(slot + a.off_ph), a.phase + (prow + row) * (R / 2), pb, bar);
         for (int j = 0; j < a.nrel; ++j)
           tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
         for (int j = 0; j < a.nval; ++j) {
@@ -605,8 +663,8 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
       const int s = i % a.slots, u = i / a.slots;
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
-        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
-        rotate_boxes<R>(smem + static_cast<size_t>(s) * a.slot_bytes, a.nrel, a.phase, prow, x.t * kTT, a.N, xt);
+        uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+        rotate_boxes<R>(slot, a.nrel, slot + a.off_ph, x.t * kTT, a.N, xt);
         fence_proxy_async();
       }
       __syncwarp();
@@ -627,7 +685,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
       uint8_t* con = slot + a.off_val;
       uint8_t* dyb = slot + a.off_aux;
       const int tok = x.t * kTT + r;
-      const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+      const uint8_t* phs = slot + a.off_ph;
       if (ok) {
         for (int hl = half; hl < a.hg; hl += 2) {
           const uint32_t tcol = lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC);
@@ -639,7 +697,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int f = hl * R + r0 + 8 * q;
-              const uint4 ph = phase8(a.phase, prow, tok, a.N, R, (r0 >> 3) + q);
+              const uint4 ph = phase8(phs, r, tok, a.N, R, (r0 >> 3) + q);
               const float gi[8] = {gv[8 * q], gv[8 * q + 1], gv[8 * q + 2], gv[8 * q + 3],
                                    gv[8 * q + 4], gv[8 * q + 5], gv[8 * q + 6], gv[8 * q + 7]};
               float o[8];
@@ -726,9 +784,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Slot layout and counts shared by the launchers.  Returns false when fewer
 // than two slots fit (the caller then uses the per-head kernels).
 bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_count, size_t* smem, int* grid) {
-  slot_bytes = (slot_bytes + 1023u) & ~1023u;
-  int slots = static_cast<int>((kSmemBudget - 1024) / slot_bytes);
-  if (slots > kMaxSlots) slots = kMaxSlots;
+  const int slots = tile_slots(slot_bytes);
   if (slots < 2) return false;
   int pc = 32;
   while (pc < cols) pc *= 2;
@@ -786,15 +842,27 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   }
   TileArgs a = base_args(p, phase, nullptr, status);
   a.partial = partial;
-  const uint32_t head = static_cast<uint32_t>(2 * p.R / 64) * kBox;
-  a.off_val = p.nrel * kBox;
-  a.off_aux = (p.nrel + p.nval) * kBox;
+  if (p.R == 32) {
+    // [lo box | relation box (hi in place) | value boxes | phase rows]
+    a.off_aux = 0;
+    a.off_rel = kBox;
+    a.off_val = 2 * kBox;
+    a.off_ph = (2 + p.nval) * kBox;
+  } else {
+    // [relation boxes | value boxes | per-head [hi | lo] operands | phase rows]
+    a.off_rel = 0;
+    a.off_val = p.nrel * kBox;
+    a.off_aux = (p.nrel + p.nval) * kBox;
+    a.off_ph = a.off_aux + p.hg * static_cast<uint32_t>(2 * p.R / 64) * kBox;
+  }
   a.load_bytes = (p.nrel + p.nval) * kBox;
-  const int cols = p.hg * static_cast<int>((bwd ? 0 : p.R) + p.d);
+  const int cols = p.R == 32 ? (bwd ? 64 * p.nval : 64 + 64 * p.nval)
+                             : p.hg * static_cast<int>((bwd ? 0 : p.R) + p.d);
   const int items = static_cast<int>(p.B * p.groups * p.nchunks);
   size_t smem = 0;
   int grid = 0;
-  if (!finish_args(a, a.off_aux + p.hg * head, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
+  const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(bwd ? 1 : 0, p.R, p.d, p.hg));
+  if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
   const void* fn = nullptr;
   if (p.R == 32) {
     fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<32, true>)
@@ -825,14 +893,15 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2*
   TileArgs a = base_args(p, phase, eta_raw, status);
   a.m0 = rmat;
   a.off_val = p.nrel * kBox;
-  a.off_mat = (p.nrel + p.nval) * kBox;
+  a.off_ph = (p.nrel + p.nval) * kBox;
+  a.off_mat = a.off_ph + static_cast<uint32_t>(kTT * p.R * 2);
   const uint32_t mat = static_cast<uint32_t>(p.hg * p.d * p.R * 2);
   a.load_bytes = (p.nrel + p.nval) * kBox + mat;
   const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
   size_t smem = 0;
   int grid = 0;
-  if (!finish_args(a, a.off_mat + mat, p.hg * static_cast<int>(p.d), items, sm_count, &smem, &grid))
-    return cudaErrorInvalidValue;
+  const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(2, p.R, p.d, p.hg));
+  if (!finish_args(a, slot, p.hg * static_cast<int>(p.d), items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
   const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
                              : reinterpret_cast<const void*>(&readout_tile_kernel<64>);
   cudaError_t e = allow_smem(fn, smem);
@@ -862,13 +931,15 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   a.etastat = etastat;
   a.off_val = p.nrel * kBox;
   a.off_aux = (p.nrel + p.nval) * kBox;
-  a.off_mat = (p.nrel + 2 * p.nval) * kBox;
+  a.off_ph = (p.nrel + 2 * p.nval) * kBox;
+  a.off_mat = a.off_ph + static_cast<uint32_t>(kTT * p.R * 2);
   const uint32_t mat = static_cast<uint32_t>(p.hg * (3 * p.R * p.d + p.R * p.R) * 2);
   a.load_bytes = (p.nrel + 2 * p.nval) * kBox + mat;
   const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
   size_t smem = 0;
   int grid = 0;
-  if (!finish_args(a, a.off_mat + mat, p.hg * static_cast<int>(p.R + p.d), items, sm_count, &smem, &grid))
+  const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(3, p.R, p.d, p.hg));
+  if (!finish_args(a, slot, p.hg * static_cast<int>(p.R + p.d), items, sm_count, &smem, &grid))
     return cudaErrorInvalidValue;
   const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
                              : reinterpret_cast<const void*>(&grad_tile_kernel<64>);
