@@ -110,7 +110,7 @@ ForwardLayout forward_layout(const lsso::Plan& p, bool train) {
   ForwardLayout l{};
   size_t off = 0;
   l.phase = off;
-  off = align256(off + sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
+  off = align256(off + sizeof(float2) * p.pos_rows * p.N * (p.R / 2));
   l.partial = off;
   off = align256(off + sizeof(float) * p.BH * p.nchunks * p.ndt * 2 * p.R * (p.R + p.dt));
   l.zbuf = off;
@@ -122,7 +122,7 @@ ForwardLayout forward_layout(const lsso::Plan& p, bool train) {
 }
 
 struct BackwardLayout {
-  size_t phase, partial, dbuf, lbuf, b1y, b1c, b1a, b2, gbase, gdrive, etastat, etadot, total;
+  size_t phase, phase16, partial, dbuf, lbuf, b1y, b1c, b1a, b2, gbase, gdrive, etastat, etadot, total;
 };
 BackwardLayout backward_layout(const lsso::Plan& p) {
   BackwardLayout l{};
@@ -132,7 +132,8 @@ BackwardLayout backward_layout(const lsso::Plan& p) {
     off = align256(off + bytes);
     return at;
   };
-  l.phase = take(sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
+  l.phase = take(sizeof(float2) * p.pos_rows * p.N * (p.R / 2));
+  l.phase16 = take(sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
   l.partial = take(sizeof(float) * p.BH * p.nchunks * p.ndt * 2 * p.R * p.dt);
   l.dbuf = take(sizeof(float) * p.BH * p.R * p.d);
   l.lbuf = take(sizeof(float) * p.BH * p.R * p.d);
@@ -370,7 +371,7 @@ int lsso_forward_inference_noalloc(const void* projected, const float* core_base
   fb.mixed = static_cast<lsso::bf16*>(mixed);
   fb.tape = nullptr;
   fb.pivots = nullptr;
-  fb.phase = reinterpret_cast<__half2*>(ws + l.phase);
+  fb.phase = reinterpret_cast<float2*>(ws + l.phase);
   fb.partial = reinterpret_cast<float*>(ws + l.partial);
   fb.zbuf = reinterpret_cast<float*>(ws + l.zbuf);
   fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
@@ -504,7 +505,7 @@ int lsso_forward(const void* projected, const float* core_base_raw, const float*
   fb.mixed = static_cast<lsso::bf16*>(mixed);
   fb.tape = tape;
   fb.pivots = pivots;
-  fb.phase = reinterpret_cast<__half2*>(ws + l.phase);
+  fb.phase = reinterpret_cast<float2*>(ws + l.phase);
   fb.partial = reinterpret_cast<float*>(ws + l.partial);
   fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.zbuf);
   fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
@@ -555,7 +556,8 @@ int lsso_backward(const void* grad_output, const void* projected, const float* c
   bb.grad_base = grad_core_base_raw;
   bb.grad_drive = grad_core_drive_weight;
   bb.grad_eta = grad_eta_raw;
-  bb.phase = reinterpret_cast<__half2*>(ws + l.phase);
+  bb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  bb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
   bb.partial = reinterpret_cast<float*>(ws + l.partial);
   bb.dbuf = reinterpret_cast<float*>(ws + l.dbuf);
   bb.lbuf = reinterpret_cast<float*>(ws + l.lbuf);

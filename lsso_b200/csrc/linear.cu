@@ -57,13 +57,7 @@ struct LinearArgs {
 
 // Bounded wait that also gives up as soon as another role aborted.
 __device__ __forceinline__ bool lwait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && *abort_flag) return false;
-  }
-  *abort_flag = 1;
-  if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
-  return false;
+  return mbar_wait_bounded(bar, parity, abort_flag, status);
 }
 
 __device__ __forceinline__ uint32_t half2_to_bf162(uint32_t h) {

@@ -26,14 +26,15 @@
 namespace lsso {
 
 // ============================================================================
-// Phase table: half2(cos, sin) of pos * 10000^(-k/(R/2)), FP32 angle, FP16 store.
+// Phase table: (cos, sin) of pos * 10000^(-k/(R/2)), FP32 angle, rounded to
+// FP16 (reference.py:691-724) and stored as FP32 pairs.
 // ============================================================================
 struct InvFreq {
   float v[32];
 };
 
 __global__ void phase_kernel(const float* __restrict__ pos, int64_t rows, int64_t N, int half, InvFreq f,
-                             __half2* __restrict__ out) {
+                             float2* __restrict__ out, __half2* __restrict__ out16) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t total = rows * N * half;
   if (i >= total) return;
@@ -43,7 +44,9 @@ __global__ void phase_kernel(const float* __restrict__ pos, int64_t rows, int64_
   const float p = pos != nullptr ? pos[rt] : static_cast<float>(t) - 0.5f * static_cast<float>(N - 1);
   float s, c;
   sincosf(p * f.v[k], &s, &c);
-  out[i] = __floats2half2_rn(c, s);
+  const __half2 h = __floats2half2_rn(c, s);
+  out[i] = __half22float2(h);
+  if (out16 != nullptr) out16[i] = h;
 }
 
 // ============================================================================
@@ -157,8 +160,8 @@ __global__ void __launch_bounds__(128) moments_kernel(const MomentArgs a) {
       const int t = idx / RQ, q = idx % RQ;
       const int64_t tok = t0 + t;
       const uint4 rv = *reinterpret_cast<const uint4*>(raw + t * (R * 2) + q * 16);
-      uint4 ph = make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);  // cos 1, sin 0
-      if (tok < t_end) ph = __ldg(reinterpret_cast<const uint4*>(a.phase + ((pb * a.N + tok) * (R / 2) + 4 * q)));
+      Phase4 ph = phase_identity();
+      if (tok < t_end) ph = load_phase4(a.phase + ((pb * a.N + tok) * (R / 2) + 4 * q));
       float v[8];
       rotate8(rv, ph, v);
       const uint4 hi = pack8_bf16(v);
@@ -548,10 +551,10 @@ __global__ void __launch_bounds__(128) readout_kernel(const ReadoutArgs a) {
     const int t = idx / RQ, q = idx % RQ;
     const int64_t tok = tok0 + t;
     uint4 rv = make_uint4(0u, 0u, 0u, 0u);
-    uint4 ph = make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);
+    Phase4 ph = phase_identity();
     if (tok < a.N) {
       rv = load8_bf16(a.proj + (b * a.N + tok) * a.W + static_cast<int64_t>(h) * R + 8 * q, 8, vec);
-      ph = __ldg(reinterpret_cast<const uint4*>(a.phase + ((pb * a.N + tok) * (R / 2) + 4 * q)));
+      ph = load_phase4(a.phase + ((pb * a.N + tok) * (R / 2) + 4 * q));
     }
     float v[8];
     rotate8(rv, ph, v);
@@ -922,10 +925,10 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
     const int t = idx / RQ, q = idx % RQ;
     const int64_t tok = tok0 + t;
     uint4 rv = make_uint4(0u, 0u, 0u, 0u);
-    uint4 ph = make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);
+    Phase4 ph = phase_identity();
     if (tok < a.N) {
       rv = load8_bf16(a.proj + (b * a.N + tok) * a.W + static_cast<int64_t>(h) * R + 8 * q, 8, vec);
-      ph = __ldg(reinterpret_cast<const uint4*>(a.phase + ((pb * a.N + tok) * (R / 2) + 4 * q)));
+      ph = load_phase4(a.phase + ((pb * a.N + tok) * (R / 2) + 4 * q));
     }
     float v[8];
     rotate8(rv, ph, v);
@@ -1037,12 +1040,11 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
   bf16* grow = a.gproj + row * a.W;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * w) << 16);
   if (ok && lead) {
-    uint4 phz = make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);
     for (int r0 = 0; r0 < R; r0 += 8) {
       float g[8], out[8];
       tmem_ld8(lane_addr + r0, g);
       tmem_ld_wait();
-      const uint4 ph = live ? __ldg(reinterpret_cast<const uint4*>(a.phase + ((pb * a.N + tok) * (R / 2) + r0 / 2))) : phz;
+      const Phase4 ph = live ? load_phase4(a.phase + ((pb * a.N + tok) * (R / 2) + r0 / 2)) : phase_identity();
       rotate8_transpose(g, ph, out);
       if (live) store8_bf16(grow + static_cast<int64_t>(h) * R + r0, out, 8, vec);
     }
@@ -1179,13 +1181,14 @@ static InvFreq inverse_frequencies(int R) {
   return f;
 }
 
-static cudaError_t launch_phase(const Plan& p, const float* pos, __half2* table, cudaStream_t stream) {
+static cudaError_t launch_phase(const Plan& p, const float* pos, float2* table, __half2* table16,
+                                cudaStream_t stream) {
   const int half = static_cast<int>(p.R / 2);
   const int64_t total = p.pos_rows * p.N * half;
   const int threads = 256;
   LaunchScope scope("phase", stream);
   phase_kernel<<<static_cast<unsigned>(ceil_div(total, threads)), threads, 0, stream>>>(pos, p.pos_rows, p.N, half,
-                                                                                         inverse_frequencies(static_cast<int>(p.R)), table);
+                                                                                         inverse_frequencies(static_cast<int>(p.R)), table, table16);
   return cudaGetLastError();
 }
 
@@ -1204,7 +1207,7 @@ static cudaError_t launch_moments(const Plan& p, MomentArgs args, cudaStream_t s
 
 template <int R>
 static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {
-  cudaError_t e = launch_phase(p, fb.positions, fb.phase, stream);
+  cudaError_t e = launch_phase(p, fb.positions, fb.phase, nullptr, stream);
   if (e != cudaSuccess) return e;
   MomentArgs m{};
   m.proj = fb.projected;
@@ -1291,7 +1294,7 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
 
 template <int R>
 static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream) {
-  cudaError_t e = launch_phase(p, bb.positions, bb.phase, stream);
+  cudaError_t e = launch_phase(p, bb.positions, bb.phase, bb.phase16, stream);
   if (e != cudaSuccess) return e;
   const int pos_batched = p.pos_rows > 1 ? 1 : 0;
   MomentArgs m{};
@@ -1376,7 +1379,7 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   g.pos_batched = pos_batched;
   g.vec = bb.vec;
   if (tiled) {
-    e = launch_grad_tiled(p, bb.grad_output, bb.projected, bb.phase, bb.b1y, bb.b1c, bb.b1a, bb.b2, bb.eta_raw,
+    e = launch_grad_tiled(p, bb.grad_output, bb.projected, bb.phase16, bb.b1y, bb.b1c, bb.b1a, bb.b2, bb.eta_raw,
                           bb.grad_projected, bb.etastat, bb.status, p.sms, stream);
   } else {
     const size_t gsm = grad_smem<R>(static_cast<int>(p.nb));

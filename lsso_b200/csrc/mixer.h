@@ -16,7 +16,7 @@ using bf16 = __nv_bfloat16;
 struct MomentArgs {
   const bf16* proj;      // [B, N, W] packed (relation | content)
   const bf16* vsrc;      // second operand source (content: proj; backward: grad_output)
-  const __half2* phase;  // [pos_rows, N, R/2]
+  const float2* phase;   // [pos_rows, N, R/2] (cos, sin)
   float* partial;        // [B*H][nchunks][ndt][2R][NC]
   int* status;
   int64_t N, W, v_stride, v_col0;
@@ -39,7 +39,7 @@ struct SolveFwdArgs {
 
 struct ReadoutArgs {
   const bf16* proj;
-  const __half2* phase;
+  const float2* phase;
   const bf16* rmat;
   const float* eta_raw;
   bf16* out;
@@ -69,7 +69,7 @@ struct SolveBwdArgs {
 struct GradArgs {
   const bf16* gout;
   const bf16* proj;
-  const __half2* phase;
+  const float2* phase;
   const bf16* b1y;
   const bf16* b1c;
   const bf16* b1a;
@@ -105,7 +105,7 @@ struct ForwardBuffers {
   bf16* mixed;
   float* tape;             // nullable (inference)
   int* pivots;             // nullable (inference)
-  __half2* phase;
+  float2* phase;
   float* partial;
   float* zbuf;
   bf16* rmat;
@@ -124,7 +124,8 @@ struct BackwardBuffers {
   float* grad_base;
   float* grad_drive;
   float* grad_eta;
-  __half2* phase;
+  float2* phase;
+  __half2* phase16;  // the same phases as FP16 pairs (staged by the gradient tile kernel)
   float* partial;
   float* dbuf;
   float* lbuf;
@@ -167,11 +168,11 @@ struct LaunchScope {
 // Head-group tile kernels of the token passes (tokens.cu).  tiled_usable()
 // says whether the plan chose them and every pointer meets the TMA alignment.
 bool tiled_usable(const Plan& p, std::initializer_list<const void*> ptrs);
-cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const __half2* phase,
+cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const float2* phase,
                                  float* partial, int* status, int sm_count, cudaStream_t stream);
-cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2* phase, const bf16* rmat,
+cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* phase, const bf16* rmat,
                                  const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream);
-cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase, const bf16* b1y,
+cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase16, const bf16* b1y,
                               const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
                               float* etastat, int* status, int sm_count, cudaStream_t stream);
 

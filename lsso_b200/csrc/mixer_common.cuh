@@ -56,14 +56,15 @@ struct Plan {
 constexpr int kTileTokens = 128;
 constexpr int64_t kTileBox = kTileTokens * 128;       // one 64-feature x 128-token BF16 box
 constexpr int64_t kTileSmemBudget = 230400;           // dynamic shared memory per tile CTA
-constexpr int kTileMaxSlots = 3;
+constexpr int kTileMaxSlots = 6;
 
 // Bytes of one pipeline slot of each tile kernel (a multiple of 1024):
 // kind 0 moments forward, 1 moments backward, 2 readout, 3 gradient.  Every
-// slot holds the item's boxes, its phase rows and its operand matrices.
+// slot holds the item's boxes and operand matrices; the rotation warps read
+// FP32 phases into registers, the gradient kernel also stages FP16 phase rows.
 inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
   const int64_t nrel = hg * R / 64, nval = hg * d / 64;
-  const int64_t phase = kTileTokens * R * 2;
+  const int64_t phase = 0;
   int64_t bytes = 0;
   if (kind <= 1) {
     // R = 32: lo box + relation/hi box + values; R = 64: per-head [hi | lo] operands.
@@ -72,7 +73,8 @@ inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
   } else if (kind == 2) {
     bytes = (nrel + nval) * kTileBox + phase + hg * d * R * 2;
   } else {
-    bytes = (nrel + 2 * nval) * kTileBox + phase + hg * (3 * R * d + R * R) * 2;
+    // the gradient kernel stages the tile's FP16 phase rows for its epilogue
+    bytes = (nrel + 2 * nval) * kTileBox + kTileTokens * R * 2 + hg * (3 * R * d + R * R) * 2;
   }
   return (bytes + 1023) / 1024 * 1024;
 }
@@ -199,29 +201,42 @@ __device__ __forceinline__ float softplus20_derivative(float x) {
   return x > 20.0f ? 1.0f : 1.0f / (1.0f + expf(-x));
 }
 
-// Rotate 8 relation coordinates (4 even/odd pairs) by their FP16 phases.
-// rel holds 8 BF16 values, ph 4 half2 (cos, sin).
-__device__ __forceinline__ void rotate8(const uint4 rel, const uint4 ph, float (&a)[8]) {
+// Phase table entries: (cos, sin) of pos * 10000^(-k/(R/2)), computed in FP32,
+// rounded to FP16 like the reference and stored as FP32 pairs, so applying
+// them needs no conversion.  Phase4 holds 4 consecutive pairs (32 bytes).
+struct Phase4 {
+  float4 a, b;  // (cos0, sin0, cos1, sin1), (cos2, sin2, cos3, sin3)
+};
+__device__ __forceinline__ Phase4 phase_identity() {
+  return Phase4{make_float4(1.0f, 0.0f, 1.0f, 0.0f), make_float4(1.0f, 0.0f, 1.0f, 0.0f)};
+}
+// 4 pairs starting at p (32-byte aligned), read-only path.
+__device__ __forceinline__ Phase4 load_phase4(const float2* p) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  return Phase4{__ldg(q), __ldg(q + 1)};
+}
+
+// Rotate 8 relation coordinates (4 even/odd pairs) by their phases.
+// rel holds 8 BF16 values.
+__device__ __forceinline__ void rotate8(const uint4 rel, const Phase4& ph, float (&a)[8]) {
   const uint32_t rv[4] = {rel.x, rel.y, rel.z, rel.w};
-  const uint32_t pv[4] = {ph.x, ph.y, ph.z, ph.w};
+  const float c[4] = {ph.a.x, ph.a.z, ph.b.x, ph.b.z};
+  const float s[4] = {ph.a.y, ph.a.w, ph.b.y, ph.b.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float2 eo = unpack_bf16(rv[i]);
-    __half2 h = *reinterpret_cast<const __half2*>(&pv[i]);
-    const float2 cs = __half22float2(h);
-    a[2 * i] = eo.x * cs.x - eo.y * cs.y;
-    a[2 * i + 1] = eo.x * cs.y + eo.y * cs.x;
+    a[2 * i] = eo.x * c[i] - eo.y * s[i];
+    a[2 * i + 1] = eo.x * s[i] + eo.y * c[i];
   }
 }
 // Adjoint of rotate8 for FP32 gradients: returns 8 values.
-__device__ __forceinline__ void rotate8_transpose(const float (&g)[8], const uint4 ph, float (&out)[8]) {
-  const uint32_t pv[4] = {ph.x, ph.y, ph.z, ph.w};
+__device__ __forceinline__ void rotate8_transpose(const float (&g)[8], const Phase4& ph, float (&out)[8]) {
+  const float c[4] = {ph.a.x, ph.a.z, ph.b.x, ph.b.z};
+  const float s[4] = {ph.a.y, ph.a.w, ph.b.y, ph.b.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    __half2 h = *reinterpret_cast<const __half2*>(&pv[i]);
-    const float2 cs = __half22float2(h);
-    out[2 * i] = g[2 * i] * cs.x + g[2 * i + 1] * cs.y;
-    out[2 * i + 1] = -g[2 * i] * cs.y + g[2 * i + 1] * cs.x;
+    out[2 * i] = g[2 * i] * c[i] + g[2 * i + 1] * s[i];
+    out[2 * i + 1] = -g[2 * i] * s[i] + g[2 * i + 1] * c[i];
   }
 }
 

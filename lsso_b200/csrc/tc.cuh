@@ -18,9 +18,12 @@ enum DeviceStatus : int {
   kStatusMmaWaitTimeout = 1,
 };
 
-// About 2^26 polls of a non-blocking try_wait: far beyond any legitimate wait
-// (microseconds) yet short enough that a broken schedule ends within seconds.
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Time bound of a sleeping mbarrier wait: any legitimate wait inside one of
+// these kernels takes microseconds, so one second means a broken schedule.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+// Suspend-time hint of one sleeping try_wait: the thread wakes when the phase
+// completes or after this long, whichever comes first.
+constexpr uint32_t kSuspendHintNs = 20000u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -56,14 +59,45 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that lets the hardware suspend the thread until the phase
+// completes (or the hint runs out) instead of returning at once, so waiting
+// warps stop taking issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Bounded, sleeping wait on one phase of an mbarrier.  Gives up (returns
+// false) when *abort_flag is set by another role, or after kWaitLimitNs, in
+// which case it sets *abort_flag and records a timeout in the status word.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  if (abort_flag != nullptr) *abort_flag = 1;
+  if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
+  return false;
+}
 // Bounded wait on one phase of an mbarrier.  On timeout, raises the status
 // flag and returns false.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-  }
-  if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
-  return false;
+  return mbar_wait_bounded(bar, parity, nullptr, status);
 }
 
 // Arrive once and announce `bytes` of transaction traffic (TMA / bulk copies).
@@ -230,9 +264,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+// BF16 -> FP32 is exact: the BF16 bits are the high half of the FP32 bits.
+// Integer ops keep the conversion off the (narrow) conversion pipe.
 __device__ __forceinline__ float2 unpack_bf16(uint32_t v) {
-  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
-  return __bfloat1622float2(b);
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
 }
 __host__ __device__ constexpr uint32_t tmem_cols_for(uint32_t n) {
   return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;

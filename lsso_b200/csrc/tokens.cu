@@ -50,7 +50,8 @@ constexpr int kThreadsT = (kEWarp0 + kEWarps) * 32;
 constexpr size_t kSmemFloor = 120 * 1024;    // forces one CTA per SM (each allocates all of TMEM)
 
 struct TileArgs {
-  const __half2* phase;
+  const float2* phase;      // FP32 (cos, sin) table, read into registers by the rotation warps
+  const __half2* phase16;   // the same phases as FP16, staged per slot by the gradient kernel
   const float* eta_raw;
   const bf16* m0;  // readout: R_d;  grad: B1y
   const bf16* m1;  // grad: B1c
@@ -65,7 +66,7 @@ struct TileArgs {
   uint32_t off_aux;     // grad: dY boxes; moments: operand buffer (R = 32: the lo box)
   uint32_t off_rel;     // moments: relation boxes
   uint32_t off_mat;     // operand matrices
-  uint32_t off_ph;      // phase rows of the tile (R/2 half2 per token)
+  uint32_t off_ph;      // gradient kernel: FP16 phase rows of the tile
   uint32_t load_bytes;  // transaction bytes per slot fill, phase rows excluded
 };
 
@@ -82,13 +83,7 @@ struct TileShared {
 };
 
 __device__ __forceinline__ bool twait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && *abort_flag) return false;
-  }
-  *abort_flag = 1;
-  if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
-  return false;
+  return mbar_wait_bounded(bar, parity, abort_flag, status);
 }
 
 // 16-byte chunk c (features 8c .. 8c+7) of token row r in a 128B-swizzled box
@@ -97,17 +92,11 @@ __device__ __forceinline__ uint8_t* box_chunk(uint8_t* box, int r, int c) {
   return box + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
-// Phases of rank chunk q (ranks 8q .. 8q+7) of tile row r, from the phase rows
-// staged in the slot; tokens past N rotate by the identity.
-__device__ __forceinline__ uint4 phase8(const uint8_t* ph, int r, int tok, int N, int R, int q) {
-  if (tok >= N) return make_uint4(0x3C00u, 0x3C00u, 0x3C00u, 0x3C00u);  // cos 1, sin 0
-  return *reinterpret_cast<const uint4*>(ph + r * (R * 2) + q * 16);
-}
-
-// Bytes of the phase rows of tile rows [t0, t0 + 128) inside the sequence.
-__device__ __forceinline__ uint32_t phase_bytes(int t0, int N, int R) {
-  const int rows = min(kTT, N - t0);
-  return static_cast<uint32_t>(rows * R * 2);
+// Phases (cos, sin) of ranks 8q .. 8q+7 of token tok from the FP32 phase table
+// (L2-resident); tokens past N rotate by the identity.
+__device__ __forceinline__ Phase4 phase_at(const float2* table, int64_t prow, int tok, int N, int R, int q) {
+  if (tok >= N) return phase_identity();
+  return load_phase4(table + (prow + tok) * (R / 2) + 4 * q);
 }
 
 // Common prologue: barriers, TMEM (all 512 columns), 1024-byte aligned base.
@@ -150,33 +139,99 @@ __device__ __forceinline__ void tile_teardown(TileShared& sh, int slots, const i
   }
 }
 
-// Item decode for the per-tile kernels: tile fastest, then head group, then sample.
+// Item decode for the per-tile kernels: head group fastest, then tile, then
+// sample, so the CTAs in flight together cover whole projection rows (every
+// group's slice of the same tokens) instead of one 128-byte slice per row.
 struct TileItem {
   int b, g, t;
 };
 __device__ __forceinline__ TileItem decode_tile(int it, int ntiles, int groups) {
   TileItem x;
-  x.t = it % ntiles;
-  const int rest = it / ntiles;
-  x.g = rest % groups;
-  x.b = rest / groups;
+  x.g = it % groups;
+  const int rest = it / groups;
+  x.t = rest % ntiles;
+  x.b = rest / ntiles;
   return x;
+}
+
+// 4 (cos, sin) pairs of rank chunk q of tile row r from FP16 phase rows staged
+// in shared memory (R/2 half2 per row); tokens past N rotate by the identity.
+__device__ __forceinline__ Phase4 phase_rows16(const uint8_t* rows, int r, int tok, int N, int R, int q) {
+  if (tok >= N) return phase_identity();
+  const uint4 h = *reinterpret_cast<const uint4*>(rows + r * (R * 2) + q * 16);
+  const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+  const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+  const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&h.z));
+  const float2 p3 = __half22float2(*reinterpret_cast<const __half2*>(&h.w));
+  return Phase4{make_float4(p0.x, p0.y, p1.x, p1.y), make_float4(p2.x, p2.y, p3.x, p3.y)};
+}
+
+// Bytes of the FP16 phase rows of tile rows [t0, t0 + 128) inside the sequence.
+__device__ __forceinline__ uint32_t phase16_bytes(int t0, int N, int R) {
+  const int rows = min(kTT, N - t0);
+  return static_cast<uint32_t>(rows * R * 2);
+}
+
+// Relation chunks (8 features x 1 token) per transform thread and tile: the
+// thread owns chunks xt + k * kXThreads, k < nrel * 1024 / kXThreads (nrel <= 2).
+constexpr int kMaxChunks = 2 * kTT * 8 / kXThreads;
+
+__device__ __forceinline__ void chunk_coords(int idx, int& j, int& r, int& c) {
+  j = idx / (kTT * 8);
+  const int rem = idx % (kTT * 8);
+  r = rem >> 3;
+  c = rem & 7;
+}
+
+// The phases of this thread's relation chunks of one tile, into registers.
+// Issued before the thread waits for the tile's boxes, so the L2 latency
+// overlaps that wait instead of stalling the rotation.
+template <int R>
+__device__ __forceinline__ void fetch_phases(Phase4 (&ph)[kMaxChunks], const float2* table, int64_t prow, int tok0,
+                                             int N, int nrel, int xt) {
+  const int nch = nrel * (kTT * 8) / kXThreads;
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    if (k < nch) {
+      int j, r, c;
+      chunk_coords(xt + k * kXThreads, j, r, c);
+      ph[k] = phase_at(table, prow, tok0 + r, N, R, ((j * 64 + 8 * c) % R) >> 3);
+    }
+  }
+}
+
+// Rotate the relation boxes in place with phases from staged FP16 rows.
+template <int R>
+__device__ __forceinline__ void rotate_boxes16(uint8_t* rel, int nrel, const uint8_t* rows, int tok0, int N, int xt) {
+  const int nch = nrel * (kTT * 8) / kXThreads;
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    if (k < nch) {
+      int j, r, c;
+      chunk_coords(xt + k * kXThreads, j, r, c);
+      uint8_t* p = box_chunk(rel + j * kBox, r, c);
+      const Phase4 ph = phase_rows16(rows, r, tok0 + r, N, R, ((j * 64 + 8 * c) % R) >> 3);
+      float v[8];
+      rotate8(*reinterpret_cast<const uint4*>(p), ph, v);
+      *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
+    }
+  }
 }
 
 // Rotate the relation boxes of one slot in place (BF16 A' for the MMA).
 template <int R>
-__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const uint8_t* phs, int tok0, int N, int xt) {
-  const int total = nrel * kTT * 8;
-#pragma unroll 4
-  for (int idx = xt; idx < total; idx += kXThreads) {
-    const int j = idx / (kTT * 8), rem = idx % (kTT * 8);
-    const int r = rem >> 3, c = rem & 7;
-    const int q = ((j * 64 + 8 * c) % R) >> 3;
-    uint8_t* p = box_chunk(rel + j * kBox, r, c);
-    const uint4 ph = phase8(phs, r, tok0 + r, N, R, q);
-    float v[8];
-    rotate8(*reinterpret_cast<const uint4*>(p), ph, v);
-    *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
+__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase4 (&ph)[kMaxChunks], int xt) {
+  const int nch = nrel * (kTT * 8) / kXThreads;
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    if (k < nch) {
+      int j, r, c;
+      chunk_coords(xt + k * kXThreads, j, r, c);
+      uint8_t* p = box_chunk(rel + j * kBox, r, c);
+      float v[8];
+      rotate8(*reinterpret_cast<const uint4*>(p), ph[k], v);
+      *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
+    }
   }
 }
 
@@ -212,14 +267,14 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
   uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
-  int last_use[kMaxSlots] = {-1, -1, -1};
+  int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
 
   auto item_of = [&](int i, int& b, int& g, int& chunk, int& t0, int& nt) {
     const int it = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
-    chunk = it % a.nchunks;
-    const int rest = it / a.nchunks;
-    g = rest % a.groups;
-    b = rest / a.groups;
+    g = it % a.groups;  // head group fastest: concurrent CTAs read whole rows
+    const int rest = it / a.groups;
+    chunk = rest % a.nchunks;
+    b = rest / a.nchunks;
     t0 = chunk * a.ct;
     nt = min(a.ct, a.ntiles - t0);
   };
@@ -242,10 +297,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
           const uint32_t bar = smem_u32(&sh.full[s]);
           const int row = (t0 + tt) * kTT;
-          const uint32_t pb = phase_bytes(row, a.N, R);
-          mbar_arrive_expect_tx(bar, a.load_bytes + pb);
-          const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
-          bulk_load(smem_u32(slot + a.off_ph), a.phase + (prow + row) * (R / 2), pb, bar);
+          mbar_arrive_expect_tx(bar, a.load_bytes);
           for (int j = 0; j < a.nrel; ++j)
             tma_load_3d(smem_u32(slot + a.off_rel + j * kBox), &tm_rel, g * a.hg * R + j * 64, row, b, bar);
           const int vcol0 = (BWD ? 0 : a.H * R) + g * a.hg * d;
@@ -312,26 +364,27 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
     for (int i = 0; i < nloc && ok; ++i) {
       int b, g, chunk, t0, nt;
       item_of(i, b, g, chunk, t0, nt);
+      const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
       for (int tt = 0; tt < nt && ok; ++tt, ++k) {
         const int s = k % a.slots, u = k / a.slots;
+        Phase4 ph[kMaxChunks];
+        fetch_phases<R>(ph, a.phase, prow, (t0 + tt) * kTT, a.N, a.nrel, xt);
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
           uint8_t* rel = slot + a.off_rel;
           uint8_t* op = slot + a.off_aux;
-          const uint8_t* phs = slot + a.off_ph;
-          const int tok0 = (t0 + tt) * kTT;
-          const int total = a.nrel * kTT * 8;
-#pragma unroll 4
-          for (int idx = xt; idx < total; idx += kXThreads) {
-            const int j = idx / (kTT * 8), rem = idx % (kTT * 8);
-            const int r = rem >> 3, c = rem & 7;
+          const int nch = a.nrel * (kTT * 8) / kXThreads;
+#pragma unroll
+          for (int kk = 0; kk < kMaxChunks; ++kk) {
+            if (kk >= nch) break;
+            int j, r, c;
+            chunk_coords(xt + kk * kXThreads, j, r, c);
             const int f = j * 64 + 8 * c;
             const int hl = f / R, k0 = f % R;
-            const uint4 ph = phase8(phs, r, tok0 + r, a.N, R, k0 >> 3);
             uint8_t* src = box_chunk(rel + j * kBox, r, c);
             float v[8];
-            rotate8(*reinterpret_cast<const uint4*>(src), ph, v);
+            rotate8(*reinterpret_cast<const uint4*>(src), ph[kk], v);
             const uint4 hi = pack8_bf16(v);
             const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
             float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
@@ -425,7 +478,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
   uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
-  int last_use[kMaxSlots] = {-1, -1, -1};
+  int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
   const uint32_t mat_bytes = static_cast<uint32_t>(a.hg * d * R * 2);
 
   if (warp == 0) {
@@ -442,10 +495,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
         const uint32_t bar = smem_u32(&sh.full[s]);
         const int row = x.t * kTT;
-        const uint32_t pb = phase_bytes(row, a.N, R);
-        mbar_arrive_expect_tx(bar, a.load_bytes + pb);
-        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
-        bulk_load(smem_u32(slot + a.off_ph), a.phase + (prow + row) * (R / 2), pb, bar);
+        mbar_arrive_expect_tx(bar, a.load_bytes);
         for (int j = 0; j < a.nrel; ++j)
           tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
         for (int j = 0; j < a.nval; ++j)
@@ -488,10 +538,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
     for (int i = 0; i < nloc && ok; ++i) {
       const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
       const int s = i % a.slots, u = i / a.slots;
+      Phase4 ph[kMaxChunks];
+      fetch_phases<R>(ph, a.phase, a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0, x.t * kTT, a.N, a.nrel, xt);
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
-        uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
-        rotate_boxes<R>(slot, a.nrel, slot + a.off_ph, x.t * kTT, a.N, xt);
+        rotate_boxes<R>(smem + static_cast<size_t>(s) * a.slot_bytes, a.nrel, ph, xt);
         fence_proxy_async();
       }
       __syncwarp();
@@ -578,7 +629,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
   uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
-  int last_use[kMaxSlots] = {-1, -1, -1};
+  int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
   // Operand matrices of the group's heads, each block contiguous per head.
   const uint32_t sz_y = static_cast<uint32_t>(R * d * 2), sz_a = static_cast<uint32_t>(R * R * 2);
   const uint32_t off_y = 0, off_c = a.hg * sz_y, off_a = 2 * a.hg * sz_y, off_2 = off_a + a.hg * sz_a;
@@ -598,10 +649,10 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
         const uint32_t bar = smem_u32(&sh.full[s]);
         const int row = x.t * kTT;
-        const uint32_t pb = phase_bytes(row, a.N, R);
+        const uint32_t pb = phase16_bytes(row, a.N, R);
         mbar_arrive_expect_tx(bar, a.load_bytes + pb);
         const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
-        bulk_load(smem_u32(slot + a.off_ph), a.phase + (prow + row) * (R / 2), pb, bar);
+        bulk_load(smem_u32(slot + a.off_ph), a.phase16 + (prow + row) * (R / 2), pb, bar);
         for (int j = 0; j < a.nrel; ++j)
           tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
         for (int j = 0; j < a.nval; ++j) {
@@ -664,7 +715,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
-        rotate_boxes<R>(slot, a.nrel, slot + a.off_ph, x.t * kTT, a.N, xt);
+        rotate_boxes16<R>(slot, a.nrel, slot + a.off_ph, x.t * kTT, a.N, xt);
         fence_proxy_async();
       }
       __syncwarp();
@@ -679,12 +730,12 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
       const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
       const int s = i % a.slots, u = i / a.slots;
       const int tb = i % a.nbuf, tu = i / a.nbuf;
+      const int tok = x.t * kTT + r;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
       uint8_t* con = slot + a.off_val;
       uint8_t* dyb = slot + a.off_aux;
-      const int tok = x.t * kTT + r;
       const uint8_t* phs = slot + a.off_ph;
       if (ok) {
         for (int hl = half; hl < a.hg; hl += 2) {
@@ -697,7 +748,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int f = hl * R + r0 + 8 * q;
-              const uint4 ph = phase8(phs, r, tok, a.N, R, (r0 >> 3) + q);
+              const Phase4 ph = phase_rows16(phs, r, tok, a.N, R, (r0 >> 3) + q);
               const float gi[8] = {gv[8 * q], gv[8 * q + 1], gv[8 * q + 2], gv[8 * q + 3],
                                    gv[8 * q + 4], gv[8 * q + 5], gv[8 * q + 6], gv[8 * q + 7]};
               float o[8];
@@ -802,7 +853,7 @@ bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_c
   return items > 0;
 }
 
-TileArgs base_args(const Plan& p, const __half2* phase, const float* eta_raw, int* status) {
+TileArgs base_args(const Plan& p, const float2* phase, const float* eta_raw, int* status) {
   TileArgs a{};
   a.phase = phase;
   a.eta_raw = eta_raw;
@@ -830,7 +881,7 @@ bool tiled_usable(const Plan& p, std::initializer_list<const void*> ptrs) {
   return true;
 }
 
-cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const __half2* phase,
+cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const float2* phase,
                                  float* partial, int* status, int sm_count, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   CUtensorMap tm_rel{}, tm_val{};
@@ -847,13 +898,11 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
     a.off_aux = 0;
     a.off_rel = kBox;
     a.off_val = 2 * kBox;
-    a.off_ph = (2 + p.nval) * kBox;
   } else {
     // [relation boxes | value boxes | per-head [hi | lo] operands | phase rows]
     a.off_rel = 0;
     a.off_val = p.nrel * kBox;
     a.off_aux = (p.nrel + p.nval) * kBox;
-    a.off_ph = a.off_aux + p.hg * static_cast<uint32_t>(2 * p.R / 64) * kBox;
   }
   a.load_bytes = (p.nrel + p.nval) * kBox;
   const int cols = p.R == 32 ? (bwd ? 64 * p.nval : 64 + 64 * p.nval)
@@ -884,7 +933,7 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   return cudaGetLastError();
 }
 
-cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2* phase, const bf16* rmat,
+cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* phase, const bf16* rmat,
                                  const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   CUtensorMap tm_proj{}, tm_out{};
@@ -893,8 +942,7 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2*
   TileArgs a = base_args(p, phase, eta_raw, status);
   a.m0 = rmat;
   a.off_val = p.nrel * kBox;
-  a.off_ph = (p.nrel + p.nval) * kBox;
-  a.off_mat = a.off_ph + static_cast<uint32_t>(kTT * p.R * 2);
+  a.off_mat = (p.nrel + p.nval) * kBox;
   const uint32_t mat = static_cast<uint32_t>(p.hg * p.d * p.R * 2);
   a.load_bytes = (p.nrel + p.nval) * kBox + mat;
   const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
@@ -915,7 +963,7 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2*
   return cudaGetLastError();
 }
 
-cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase, const bf16* b1y,
+cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase16, const bf16* b1y,
                               const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
                               float* etastat, int* status, int sm_count, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
@@ -923,7 +971,8 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   if (encode_boxes(encode, &tm_proj, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_dy, gout, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_gproj, gproj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  TileArgs a = base_args(p, phase, eta_raw, status);
+  TileArgs a = base_args(p, nullptr, eta_raw, status);
+  a.phase16 = phase16;
   a.m0 = b1y;
   a.m1 = b1c;
   a.m2 = b1a;
