@@ -1253,14 +1253,16 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
   s.dt = static_cast<int>(p.dt);
   s.ndt = static_cast<int>(p.ndt);
   s.nchunks = static_cast<int>(p.nchunks);
-  const size_t ssm = solve_forward_smem<R>();
-  e = set_smem(reinterpret_cast<const void*>(&solve_forward_kernel<R>), ssm);
-  if (e != cudaSuccess) return e;
-  {
+  if (warp_solves_usable(p)) {
+    e = launch_solve_forward_warp(p, s, stream);
+  } else {
+    const size_t ssm = solve_forward_smem<R>();
+    e = set_smem(reinterpret_cast<const void*>(&solve_forward_kernel<R>), ssm);
+    if (e != cudaSuccess) return e;
     LaunchScope scope("solve_fwd", stream);
     solve_forward_kernel<R><<<static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream>>>(s);
+    e = cudaGetLastError();
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
   ReadoutArgs r{};
@@ -1345,14 +1347,16 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   s.dt = static_cast<int>(p.dt);
   s.ndt = static_cast<int>(p.ndt);
   s.nchunks = static_cast<int>(p.nchunks);
-  const size_t ssm = solve_backward_smem<R>();
-  e = set_smem(reinterpret_cast<const void*>(&solve_backward_kernel<R>), ssm);
-  if (e != cudaSuccess) return e;
-  {
+  if (warp_solves_usable(p)) {
+    e = launch_solve_backward_warp(p, s, stream);
+  } else {
+    const size_t ssm = solve_backward_smem<R>();
+    e = set_smem(reinterpret_cast<const void*>(&solve_backward_kernel<R>), ssm);
+    if (e != cudaSuccess) return e;
     LaunchScope scope("solve_bwd", stream);
     solve_backward_kernel<R><<<static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream>>>(s);
+    e = cudaGetLastError();
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
   GradArgs g{};

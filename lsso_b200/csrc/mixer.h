@@ -176,6 +176,11 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
                               const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
                               float* etastat, int* status, int sm_count, cudaStream_t stream);
 
+// Register-resident warp solves for R <= 32 (solve.cu).
+bool warp_solves_usable(const Plan& p);
+cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cudaStream_t stream);
+cudaError_t launch_solve_backward_warp(const Plan& p, const SolveBwdArgs& s, cudaStream_t stream);
+
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream);
 cudaError_t launch_backward(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream);
 

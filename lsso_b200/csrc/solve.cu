@@ -1,0 +1,619 @@
+// Per-(sample, head) r x r solves of the LSSO mixer for R <= 32 (sm_100a).
+//
+// Same algebra as solve_forward_kernel / solve_backward_kernel in mixer.cu
+// (reference lsso/ball/reference.py:411-572): Cholesky of the Gram matrix,
+// the accretive generator, LU without pivoting, and the triangular solves of
+// the forward and the analytic backward.  The difference is the execution
+// model: with R <= 32 one lane owns one matrix row, so
+//   - Cholesky and LU are R steps in one warp: the pivot row or column is
+//     broadcast (shuffle or same-address shared read) and every lane updates
+//     its own row with independent fused multiply-adds;
+//   - a triangular solve is R shuffle steps per right-hand side, four
+//     right-hand sides per warp at a time for instruction-level parallelism,
+//     replacing a thread-per-column R^2 chain; transposed solves read the
+//     matrix by columns (one column view of the packed LU serves both U^T and
+//     the unit L^T);
+//   - all d columns of the R x d operands stay in shared memory, split over
+//     the CTA's warps.
+// One CTA (four warps) per (sample, head).
+#include "mixer.h"
+#include "mixer_common.cuh"
+
+namespace lsso {
+
+namespace {
+
+constexpr int kWThreads = 256;
+constexpr int kWWarps = kWThreads / 32;
+constexpr int kNB = 4;  // right-hand sides per warp-level solve
+constexpr unsigned kFull = 0xffffffffu;
+
+// Matrices stay in shared memory; lane i works on row i.  The step loops are
+// kept rolled (unroll 2) so the code stays small: these kernels run once per
+// (sample, head), and fully unrolled R = 32 chains overflow the instruction
+// cache.  A matrix element (row, k) is read at M[row * rs + k * cs]: rs = ld,
+// cs = 1 for the matrix itself, rs = 1, cs = ld for its transpose.
+
+// Lower-triangular solve T x = b (lane i: b_i in b[q]); rdiag = 1 / T_ii on
+// lane i (ignored when UNIT).
+template <int R, bool UNIT>
+__device__ __forceinline__ void trsv_lower(const float* M, int rs, int cs, float rdiag, float (&b)[kNB]) {
+  const int lane = threadIdx.x & 31;
+  const float* row = M + (lane < R ? lane : 0) * rs;
+#pragma unroll 2
+  for (int k = 0; k < R; ++k) {
+    const float tk = lane < R ? row[k * cs] : 0.0f;
+#pragma unroll
+    for (int q = 0; q < kNB; ++q) {
+      const float xk = __shfl_sync(kFull, UNIT ? b[q] : b[q] * rdiag, k);
+      if (lane == k) {
+        b[q] = xk;
+      } else if (lane > k) {
+        b[q] = fmaf(-tk, xk, b[q]);
+      }
+    }
+  }
+}
+
+// Upper-triangular solve T x = b (entries k > i of row i used).
+template <int R, bool UNIT>
+__device__ __forceinline__ void trsv_upper(const float* M, int rs, int cs, float rdiag, float (&b)[kNB]) {
+  const int lane = threadIdx.x & 31;
+  const float* row = M + (lane < R ? lane : 0) * rs;
+#pragma unroll 2
+  for (int k = R - 1; k >= 0; --k) {
+    const float tk = lane < R ? row[k * cs] : 0.0f;
+#pragma unroll
+    for (int q = 0; q < kNB; ++q) {
+      const float xk = __shfl_sync(kFull, UNIT ? b[q] : b[q] * rdiag, k);
+      if (lane == k) {
+        b[q] = xk;
+      } else if (lane < k) {
+        b[q] = fmaf(-tk, xk, b[q]);
+      }
+    }
+  }
+}
+
+// Left-looking Cholesky of the lower triangle of the R x R shared matrix A
+// (leading dim ld) in place, by one warp.  Step k: lane i >= k forms
+// A[i][k] - sum_{p<k} L[i][p] L[k][p] (a read-only dot product: the loads
+// pipeline), lane k takes the square root, the pivot is broadcast by shuffle
+// and each lane stores its L[i][k] once.  dinv[i] = 1 / L_ii; the upper
+// triangle is zeroed.
+template <int R>
+__device__ __forceinline__ void cholesky_warp(float* A, int ld, float* dinv) {
+  const int lane = threadIdx.x & 31;
+  const int i = lane < R ? lane : 0;
+  const float* rowi = A + i * ld;
+#pragma unroll 1
+  for (int k = 0; k < R; ++k) {
+    const float* rowk = A + k * ld;
+    float s0 = 0.0f, s1 = 0.0f;
+    int p = 0;
+#pragma unroll 4
+    for (; p + 1 < k; p += 2) {
+      s0 = fmaf(rowi[p], rowk[p], s0);
+      s1 = fmaf(rowi[p + 1], rowk[p + 1], s1);
+    }
+    if (p < k) s0 = fmaf(rowi[p], rowk[p], s0);
+    const float v = rowi[k] - (s0 + s1);
+    const float piv = sqrtf(__shfl_sync(kFull, v, k));
+    __syncwarp();
+    if (lane == k) {
+      A[k * ld + k] = piv;
+      dinv[k] = 1.0f / piv;
+    } else if (lane > k && lane < R) {
+      A[i * ld + k] = v / piv;
+    }
+    __syncwarp();
+  }
+  if (lane < R) {
+    for (int j = lane + 1; j < R; ++j) A[lane * ld + j] = 0.0f;
+  }
+  __syncwarp();
+}
+
+// Doolittle LU without pivoting of the R x R shared matrix M in place, by one
+// warp, left-looking: step k computes row k of U (lane j >= k:
+// M[k][j] - sum_{p<k} L[k][p] U[p][j]) and then column k of the unit lower
+// factor (lane i > k: (M[i][k] - sum_{p<k} L[i][p] U[p][k]) / U[k][k]); both
+// are read-only dot products followed by one store per lane.  uinv[i] = 1 / U_ii.
+template <int R>
+__device__ __forceinline__ void lu_warp(float* M, int ld, float* uinv) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane < R ? lane : 0;
+#pragma unroll 1
+  for (int k = 0; k < R; ++k) {
+    // row k of U: lane j >= k
+    const float* rowk = M + k * ld;
+    float s0 = 0.0f, s1 = 0.0f;
+    int p = 0;
+#pragma unroll 4
+    for (; p + 1 < k; p += 2) {
+      s0 = fmaf(rowk[p], M[p * ld + j], s0);
+      s1 = fmaf(rowk[p + 1], M[(p + 1) * ld + j], s1);
+    }
+    if (p < k) s0 = fmaf(rowk[p], M[p * ld + j], s0);
+    const float ukj = M[k * ld + j] - (s0 + s1);
+    __syncwarp();
+    if (lane >= k && lane < R) M[k * ld + j] = ukj;
+    const float ukk = __shfl_sync(kFull, ukj, k);
+    if (lane == k) uinv[k] = 1.0f / ukk;
+    __syncwarp();
+    // column k of L: lane i > k
+    const float* rowi = M + j * ld;
+    float t0 = 0.0f, t1 = 0.0f;
+    p = 0;
+#pragma unroll 4
+    for (; p + 1 < k; p += 2) {
+      t0 = fmaf(rowi[p], M[p * ld + k], t0);
+      t1 = fmaf(rowi[p + 1], M[(p + 1) * ld + k], t1);
+    }
+    if (p < k) t0 = fmaf(rowi[p], M[p * ld + k], t0);
+    const float lik = (rowi[k] - (t0 + t1)) / ukk;
+    __syncwarp();
+    if (lane > k && lane < R) M[j * ld + k] = lik;
+    __syncwarp();
+  }
+}
+
+// Columns [c0, c0 + kNB) of the R x d operand X (row-major, leading dim xld)
+// into / out of the lane = row layout; columns past cend read as zero.
+__device__ __forceinline__ void get_cols(const float* X, int xld, int R, int c0, int cend, float (&b)[kNB]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < kNB; ++q) b[q] = (lane < R && c0 + q < cend) ? X[lane * xld + c0 + q] : 0.0f;
+}
+__device__ __forceinline__ void put_cols(float* X, int xld, int R, int c0, int cend, const float (&b)[kNB]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < kNB; ++q)
+    if (lane < R && c0 + q < cend) X[lane * xld + c0 + q] = b[q];
+}
+
+// The column range of warp w when `cols` columns are split over the CTA.
+__device__ __forceinline__ void warp_cols(int cols, int& c_begin, int& c_end) {
+  const int w = threadIdx.x >> 5;
+  const int per = (cols + kWWarps - 1) / kWWarps;
+  c_begin = min(cols, w * per);
+  c_end = min(cols, c_begin + per);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.0f;
+  for (int w = 0; w < kWWarps; ++w) s += red[w];
+  return s;
+}
+
+// ============================================================================
+// Forward: G = A'^T A'/n + I = L L^T, Z = L^{-1} S, Theta = base + Z W/sqrt(n),
+// M = I + F F^T + Omega = LU, U = M^{-1} Z, R_d = L^{-T}(2U - (1+eta) Z)/sqrt(n).
+// ============================================================================
+template <int R>
+__global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const SolveFwdArgs a) {
+  constexpr int LD = R + 1;
+  extern __shared__ __align__(16) float fsm[];
+  const int d = a.d;
+  const int XLD = d + 1;
+  float* L = fsm;              // [R][LD]
+  float* Th = L + R * LD;      // [R][LD]
+  float* Mm = Th + R * LD;     // [R][LD]
+  float* Zs = Mm + R * LD;     // [R][XLD]  S, then Z
+  float* fdiag = Zs + R * XLD; // [R]
+  float* dinv = fdiag + R;     // [R] 1 / L_ii
+  float* uinv = dinv + R;      // [R] 1 / U_ii
+  float* Ws = uinv + R;        // [d][R + 1] W_drive of this head
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t bh = blockIdx.x;
+  const int64_t b = bh / a.H;
+  const int h = static_cast<int>(bh % a.H);
+  const float n = a.counts != nullptr ? a.counts[b] : static_cast<float>(a.N);
+  const float rsn = 1.0f / sqrtf(n);
+  const int NC = R + a.dt;
+  const int64_t pstride = static_cast<int64_t>(2 * R) * NC;
+  const float* pbase = a.partial + bh * a.nchunks * a.ndt * pstride;
+  const TapeLayout tl = tape_layout(a.N, R, d);
+  float* tape = a.tape != nullptr ? a.tape + bh * a.tape_stride : nullptr;
+  float* Zg = tape != nullptr ? tape + tl.Z : a.zbuf + bh * static_cast<int64_t>(R) * d;
+
+  const float* Wd = a.drive + static_cast<int64_t>(h) * d * R;
+  for (int idx = tid; idx < d * R; idx += kWThreads) Ws[(idx / R) * LD + idx % R] = Wd[idx];
+  // 1. G (lower triangle) and S = A'^T C / sqrt(n) from the chunk partials.
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, k = idx % R;
+    if (k > i) continue;
+    float s = 0.0f;
+    for (int ch = 0; ch < a.nchunks; ++ch) {
+      const float* P = pbase + static_cast<int64_t>(ch) * a.ndt * pstride;
+      s += P[i * NC + k] + P[(R + i) * NC + k] + P[(R + k) * NC + i];
+    }
+    L[i * LD + k] = s * (rsn * rsn) + (i == k ? 1.0f : 0.0f);
+  }
+  for (int idx = tid; idx < R * d; idx += kWThreads) {
+    const int i = idx / d, col = idx % d;
+    const int jt = col / a.dt, cl = col % a.dt;
+    float s = 0.0f;
+    for (int ch = 0; ch < a.nchunks; ++ch) {
+      const float* P = pbase + (static_cast<int64_t>(ch) * a.ndt + jt) * pstride;
+      s += P[i * NC + R + cl] + P[(R + i) * NC + R + cl];
+    }
+    Zs[i * XLD + col] = s * rsn;
+  }
+  __syncthreads();
+  // 2. Cholesky (warp 0)
+  if (warp == 0) cholesky_warp<R>(L, LD, dinv);
+  __syncthreads();
+  // 3. Z = L^{-1} S (columns over the warps)
+  {
+    const float rd = lane < R ? dinv[lane] : 1.0f;
+    int cb, ce;
+    warp_cols(d, cb, ce);
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float x[kNB];
+      get_cols(Zs, XLD, R, c0, ce, x);
+      trsv_lower<R, false>(L, LD, 1, rd, x);
+      put_cols(Zs, XLD, R, c0, ce, x);
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < R * d; idx += kWThreads) {
+    const int i = idx / d, col = idx % d;
+    Zg[static_cast<int64_t>(i) * d + col] = Zs[i * XLD + col];
+  }
+  // 4. Theta = base + Z W_drive / sqrt(n);  F diagonal
+  const float* base = a.base + static_cast<int64_t>(h) * R * R;
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    float s = 0.0f;
+    for (int c = 0; c < d; ++c) s = fmaf(Zs[i * XLD + c], Ws[c * LD + jj], s);
+    Th[i * LD + jj] = base[idx] + s * rsn;
+  }
+  __syncthreads();
+  for (int i = tid; i < R; i += kWThreads) fdiag[i] = softplus20(Th[i * LD + i] + kSoftplusOneOffset);
+  __syncthreads();
+  // 5. M = I + F F^T + Omega
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    const int kmax = min(i, jj);
+    float s = 0.0f;
+    for (int k = 0; k <= kmax; ++k) {
+      const float fi = k < i ? Th[i * LD + k] : fdiag[i];
+      const float fj = k < jj ? Th[jj * LD + k] : fdiag[jj];
+      s += fi * fj;
+    }
+    const float omega = i < jj ? Th[i * LD + jj] : (i > jj ? -Th[jj * LD + i] : 0.0f);
+    Mm[i * LD + jj] = (i == jj ? 1.0f : 0.0f) + s + omega;
+  }
+  __syncthreads();
+  if (tape != nullptr) {
+    for (int idx = tid; idx < R * R; idx += kWThreads) {
+      const int i = idx / R, jj = idx % R;
+      tape[tl.L + idx] = L[i * LD + jj];
+      tape[tl.Theta + idx] = Th[i * LD + jj];
+    }
+    if (tid == 0) tape[tl.n] = n;
+  }
+  // 6. LU (warp 0)
+  if (warp == 0) lu_warp<R>(Mm, LD, uinv);
+  __syncthreads();
+  if (tape != nullptr) {
+    for (int idx = tid; idx < R * R; idx += kWThreads) tape[tl.LU + idx] = Mm[(idx / R) * LD + idx % R];
+  }
+  if (a.pivots != nullptr) {
+    for (int i = tid; i < R; i += kWThreads) a.pivots[bh * R + i] = i + 1;
+  }
+  // 7. U = M^{-1} Z;  R_d = L^{-T} (2U - (1+eta) Z) / sqrt(n)
+  const float eta = bounded_complement(a.eta_raw[h]);
+  uint8_t* rm = reinterpret_cast<uint8_t*>(a.rmat + bh * a.d_pad * R);
+  constexpr uint32_t RSBO = R * 16;
+  {
+    const float ru = lane < R ? uinv[lane] : 1.0f;
+    const float rd = lane < R ? dinv[lane] : 1.0f;
+    int cb, ce;
+    warp_cols(d, cb, ce);
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float z[kNB], u[kNB];
+      get_cols(Zs, XLD, R, c0, ce, z);
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) u[q] = z[q];
+      trsv_lower<R, true>(Mm, LD, 1, 1.0f, u);   // unit lower factor of M
+      trsv_upper<R, false>(Mm, LD, 1, ru, u);    // U
+      float x[kNB];
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) x[q] = 2.0f * u[q] - (1.0f + eta) * z[q];
+      trsv_upper<R, false>(L, 1, LD, rd, x);     // L^T
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) {
+        const int col = c0 + q;
+        if (lane < R && col < ce) {
+          if (tape != nullptr) tape[tl.U + static_cast<int64_t>(lane) * d + col] = u[q];
+          *reinterpret_cast<bf16*>(rm + kmajor_offset(col, lane, RSBO)) = __float2bfloat16_rn(x[q] * rsn);
+        }
+      }
+    }
+  }
+  for (int idx = tid; idx < (a.d_pad - d) * R; idx += kWThreads) {
+    const int col = d + idx / R, i = idx % R;
+    *reinterpret_cast<bf16*>(rm + kmajor_offset(col, i, RSBO)) = __float2bfloat16_rn(0.0f);
+  }
+}
+
+// ============================================================================
+// Backward (see solve_backward_kernel in mixer.cu for the derivation):
+//   D = L^{-1}(A'^T dY)/sqrt(n), lam = M^{-T} 2D, dK = -lam U^T, dTheta,
+//   dZ = lam - (1+eta) D + dTheta W^T/sqrt(n), E = M' D^T + dZ Z^T,
+//   R_d = L^{-T} M'/sqrt(n), R_z = L^{-T} dZ/sqrt(n), Q = L^{-T} Psi L^{-1}/n.
+// ============================================================================
+template <int R>
+__global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const SolveBwdArgs a) {
+  constexpr int LD = R + 1;
+  extern __shared__ __align__(16) float fsm[];
+  const int d = a.d;
+  const int XLD = d + 1;
+  float* L = fsm;               // [R][LD]
+  float* Mm = L + R * LD;       // [R][LD] packed LU
+  float* Th = Mm + R * LD;      // [R][LD]
+  float* dK = Th + R * LD;      // [R][LD] dK, then dTheta, then Psi
+  float* E = dK + R * LD;       // [R][LD]
+  float* X1 = E + R * LD;       // [R][XLD] D
+  float* X2 = X1 + R * XLD;     // [R][XLD] lambda, then dZ
+  float* X3 = X2 + R * XLD;     // [R][XLD] U, then M'
+  float* X4 = X3 + R * XLD;     // [R][XLD] Z
+  float* fdiag = X4 + R * XLD;  // [R]
+  float* dinv = fdiag + R;      // [R] 1 / L_ii
+  float* uinv = dinv + R;       // [R] 1 / U_ii
+  float* Ws = uinv + R;         // [d][R + 1] W_drive of this head
+  __shared__ float red[kWWarps];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t bh = blockIdx.x;
+  const int h = static_cast<int>(bh % a.H);
+  const TapeLayout tl = tape_layout(a.N, R, d);
+  const float* tape = a.tape + bh * a.tape_stride;
+  const float n = tape[tl.n];
+  const float rsn = 1.0f / sqrtf(n);
+  const float eta = bounded_complement(a.eta_raw[h]);
+  const int NC = a.dt;
+  const int64_t pstride = static_cast<int64_t>(2 * R) * NC;
+  const float* pbase = a.partial + bh * a.nchunks * a.ndt * pstride;
+  const float* Wd = a.drive + static_cast<int64_t>(h) * d * R;
+
+  for (int idx = tid; idx < d * R; idx += kWThreads) Ws[(idx / R) * LD + idx % R] = Wd[idx];
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    L[i * LD + jj] = tape[tl.L + idx];
+    Mm[i * LD + jj] = tape[tl.LU + idx];
+    Th[i * LD + jj] = tape[tl.Theta + idx];
+  }
+  for (int idx = tid; idx < R * d; idx += kWThreads) {
+    const int i = idx / d, col = idx % d;
+    const int jt = col / a.dt, cl = col % a.dt;
+    float s = 0.0f;
+    for (int ch = 0; ch < a.nchunks; ++ch) {
+      const float* P = pbase + (static_cast<int64_t>(ch) * a.ndt + jt) * pstride;
+      s += P[i * NC + cl] + P[(R + i) * NC + cl];
+    }
+    X1[i * XLD + col] = s;
+    X3[i * XLD + col] = tape[tl.U + static_cast<int64_t>(i) * d + col];
+    X4[i * XLD + col] = tape[tl.Z + static_cast<int64_t>(i) * d + col];
+  }
+  __syncthreads();
+  for (int i = tid; i < R; i += kWThreads) {
+    fdiag[i] = softplus20(Th[i * LD + i] + kSoftplusOneOffset);
+    dinv[i] = 1.0f / L[i * LD + i];
+    uinv[i] = 1.0f / Mm[i * LD + i];
+  }
+  __syncthreads();
+
+  // Pass A: D = L^{-1} X1 / sqrt(n);  lam = M^{-T} (2 D) = L_u^{-T} U^{-T} (2 D)
+  {
+    const float rd = lane < R ? dinv[lane] : 1.0f;
+    const float ru = lane < R ? uinv[lane] : 1.0f;
+    int cb, ce;
+    warp_cols(d, cb, ce);
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float x[kNB];
+      get_cols(X1, XLD, R, c0, ce, x);
+      trsv_lower<R, false>(L, LD, 1, rd, x);
+      float lam[kNB];
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) {
+        x[q] *= rsn;
+        lam[q] = 2.0f * x[q];
+      }
+      put_cols(X1, XLD, R, c0, ce, x);
+      // columns of the packed LU: U^T (entries j <= i), unit L^T (entries j > i)
+      trsv_lower<R, false>(Mm, 1, LD, ru, lam);  // U^T y = 2D
+      trsv_upper<R, true>(Mm, 1, LD, 1.0f, lam); // L_u^T lam = y
+      put_cols(X2, XLD, R, c0, ce, lam);
+    }
+  }
+  __syncthreads();
+  float dz_dot = 0.0f;
+  for (int idx = tid; idx < R * d; idx += kWThreads) {
+    const int i = idx / d, col = idx % d;
+    dz_dot = fmaf(X1[i * XLD + col], X4[i * XLD + col], dz_dot);
+  }
+  // dK = -lam U^T
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    float s = 0.0f;
+    for (int c = 0; c < d; ++c) s = fmaf(X2[i * XLD + c], X3[jj * XLD + c], s);
+    dK[i * LD + jj] = -s;
+  }
+  __syncthreads();
+  // dTheta through K = F F^T + Omega (into E, then back into dK)
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    float v;
+    if (i < jj) {
+      v = dK[i * LD + jj] - dK[jj * LD + i];
+    } else {
+      float s = 0.0f;
+      for (int k = jj; k < R; ++k) {
+        const float f = k == jj ? fdiag[jj] : Th[k * LD + jj];
+        s += (dK[i * LD + k] + dK[k * LD + i]) * f;
+      }
+      v = i == jj ? s * softplus20_derivative(Th[i * LD + i] + kSoftplusOneOffset) : s;
+    }
+    E[i * LD + jj] = v;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    const float v = E[i * LD + jj];
+    dK[i * LD + jj] = v;
+    a.gbase[bh * R * R + idx] = v;
+  }
+  __syncthreads();
+  // Pass B: dZ (X2), M' = 2U - (1+eta) Z (X3), drive-gradient partial Z^T dTheta / sqrt(n)
+  for (int idx = tid; idx < R * d; idx += kWThreads) {
+    const int i = idx / d, col = idx % d;
+    const float* wrow = Ws + col * LD;
+    float s = 0.0f;
+    for (int jj = 0; jj < R; ++jj) s = fmaf(dK[i * LD + jj], wrow[jj], s);
+    X2[i * XLD + col] = X2[i * XLD + col] - (1.0f + eta) * X1[i * XLD + col] + s * rsn;
+    X3[i * XLD + col] = 2.0f * X3[i * XLD + col] - (1.0f + eta) * X4[i * XLD + col];
+  }
+  for (int idx = tid; idx < d * R; idx += kWThreads) {
+    const int col = idx / R, jj = idx % R;
+    float s = 0.0f;
+    for (int i = 0; i < R; ++i) s = fmaf(X4[i * XLD + col], dK[i * LD + jj], s);
+    a.gdrive[(bh * d + col) * R + jj] = s * rsn;
+  }
+  __syncthreads();
+  // E = M' D^T + dZ Z^T
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, k = idx % R;
+    float s = 0.0f;
+    for (int c = 0; c < d; ++c) s += X3[i * XLD + c] * X1[k * XLD + c] + X2[i * XLD + c] * X4[k * XLD + c];
+    E[i * LD + k] = s;
+  }
+  // R_d = L^{-T} M' / sqrt(n) -> B1y,  R_z = L^{-T} dZ / sqrt(n) -> B1c and B2
+  uint8_t* b1y = reinterpret_cast<uint8_t*>(a.b1y + bh * R * a.d_pad);
+  uint8_t* b1c = reinterpret_cast<uint8_t*>(a.b1c + bh * R * a.d_pad);
+  uint8_t* b2 = reinterpret_cast<uint8_t*>(a.b2 + bh * a.d_pad * R);
+  const uint32_t SBO_Y = static_cast<uint32_t>(a.d_pad) * 16;
+  constexpr uint32_t SBO_R = R * 16;
+  {
+    const float rd = lane < R ? dinv[lane] : 1.0f;
+    int cb, ce;
+    warp_cols(d, cb, ce);
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float xm[kNB], xz[kNB];
+      get_cols(X3, XLD, R, c0, ce, xm);
+      get_cols(X2, XLD, R, c0, ce, xz);
+      trsv_upper<R, false>(L, 1, LD, rd, xm);
+      trsv_upper<R, false>(L, 1, LD, rd, xz);
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) {
+        const int col = c0 + q;
+        if (lane < R && col < ce) {
+          *reinterpret_cast<bf16*>(b1y + kmajor_offset(lane, col, SBO_Y)) = __float2bfloat16_rn(xm[q] * rsn);
+          const bf16 rz = __float2bfloat16_rn(xz[q] * rsn);
+          *reinterpret_cast<bf16*>(b1c + kmajor_offset(lane, col, SBO_Y)) = rz;
+          *reinterpret_cast<bf16*>(b2 + kmajor_offset(col, lane, SBO_R)) = rz;
+        }
+      }
+    }
+  }
+  for (int idx = tid; idx < (a.d_pad - d) * R; idx += kWThreads) {
+    const int col = d + idx / R, i = idx % R;
+    const bf16 z = __float2bfloat16_rn(0.0f);
+    *reinterpret_cast<bf16*>(b1y + kmajor_offset(i, col, SBO_Y)) = z;
+    *reinterpret_cast<bf16*>(b1c + kmajor_offset(i, col, SBO_Y)) = z;
+    *reinterpret_cast<bf16*>(b2 + kmajor_offset(col, i, SBO_R)) = z;
+  }
+  __syncthreads();
+  // Q = L^{-T} Psi L^{-1} / n with Psi = tril(E) + tril(E,-1)^T (symmetric):
+  // X = L^{-T} Psi column by column, then Q^T = L^{-T} X^T.
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, k = idx % R;
+    dK[i * LD + k] = i >= k ? E[i * LD + k] : E[k * LD + i];
+  }
+  __syncthreads();
+  {
+    const float rd = lane < R ? dinv[lane] : 1.0f;
+    int cb, ce;
+    warp_cols(R, cb, ce);
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float x[kNB];
+      get_cols(dK, LD, R, c0, ce, x);
+      trsv_upper<R, false>(L, 1, LD, rd, x);
+      // store transposed: E[c][i] = X[i][c]
+#pragma unroll
+      for (int q = 0; q < kNB; ++q)
+        if (lane < R && c0 + q < ce) E[(c0 + q) * LD + lane] = x[q];
+    }
+    __syncthreads();
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float x[kNB];
+      get_cols(E, LD, R, c0, ce, x);
+      trsv_upper<R, false>(L, 1, LD, rd, x);
+      put_cols(dK, LD, R, c0, ce, x);
+    }
+  }
+  __syncthreads();
+  // dK now holds Q^T; B1a[n = i][k = j] = -Q[j][i] / n = -dK[i][j] / n
+  uint8_t* b1a = reinterpret_cast<uint8_t*>(a.b1a + bh * R * R);
+  const float inv_n = rsn * rsn;
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, jj = idx % R;
+    *reinterpret_cast<bf16*>(b1a + kmajor_offset(i, jj, SBO_R)) = __float2bfloat16_rn(-dK[i * LD + jj] * inv_n);
+  }
+  const float s = block_sum(dz_dot, red);
+  if (tid == 0) a.etadot[bh] = s;
+}
+
+template <int R>
+size_t fwd_smem(int d) {
+  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1));
+}
+template <int R>
+size_t bwd_smem(int d) {
+  return sizeof(float) * (5 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
+}
+
+}  // namespace
+
+bool warp_solves_usable(const Plan& p) {
+  return (p.R == 16 || p.R == 32) && bwd_smem<32>(static_cast<int>(p.d)) <= 200 * 1024;
+}
+
+cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cudaStream_t stream) {
+  const int d = static_cast<int>(p.d);
+  const size_t smem = p.R == 16 ? fwd_smem<16>(d) : fwd_smem<32>(d);
+  const void* fn = p.R == 16 ? reinterpret_cast<const void*>(&solve_forward_warp_kernel<16>)
+                             : reinterpret_cast<const void*>(&solve_forward_warp_kernel<32>);
+  cudaError_t e = allow_smem(fn, smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope("solve_fwd", stream);
+  if (p.R == 16) {
+    solve_forward_warp_kernel<16><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
+  } else {
+    solve_forward_warp_kernel<32><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_solve_backward_warp(const Plan& p, const SolveBwdArgs& s, cudaStream_t stream) {
+  const int d = static_cast<int>(p.d);
+  const size_t smem = p.R == 16 ? bwd_smem<16>(d) : bwd_smem<32>(d);
+  const void* fn = p.R == 16 ? reinterpret_cast<const void*>(&solve_backward_warp_kernel<16>)
+                             : reinterpret_cast<const void*>(&solve_backward_warp_kernel<32>);
+  cudaError_t e = allow_smem(fn, smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope("solve_bwd", stream);
+  if (p.R == 16) {
+    solve_backward_warp_kernel<16><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
+  } else {
+    solve_backward_warp_kernel<32><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace lsso
