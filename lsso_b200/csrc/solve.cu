@@ -75,87 +75,69 @@ __device__ __forceinline__ void trsv_upper(const float* M, int rs, int cs, float
   }
 }
 
-// Left-looking Cholesky of the lower triangle of the R x R shared matrix A
-// (leading dim ld) in place, by one warp.  Step k: lane i >= k forms
-// A[i][k] - sum_{p<k} L[i][p] L[k][p] (a read-only dot product: the loads
-// pipeline), lane k takes the square root, the pivot is broadcast by shuffle
-// and each lane stores its L[i][k] once.  dinv[i] = 1 / L_ii; the upper
-// triangle is zeroed.
+// Right-looking Cholesky of the lower triangle of the R x R shared matrix A
+// (leading dim ld) in place, spread over the whole CTA with one barrier per
+// step: step k subtracts A[i][k] A[j][k] / A[k][k] from the trailing lower
+// triangle (it only reads column k, which no thread writes during the step);
+// the columns are scaled to L[i][k] = A[i][k] / sqrt(A[k][k]) at the end.
+// dinv[i] = 1 / L_ii; the upper triangle is zeroed.  All threads call it.
 template <int R>
-__device__ __forceinline__ void cholesky_warp(float* A, int ld, float* dinv) {
-  const int lane = threadIdx.x & 31;
-  const int i = lane < R ? lane : 0;
-  const float* rowi = A + i * ld;
+__device__ __forceinline__ void cholesky_block(float* A, int ld, float* dinv) {
+  const int tid = threadIdx.x;
+  __syncthreads();
 #pragma unroll 1
-  for (int k = 0; k < R; ++k) {
-    const float* rowk = A + k * ld;
-    float s0 = 0.0f, s1 = 0.0f;
-    int p = 0;
-#pragma unroll 4
-    for (; p + 1 < k; p += 2) {
-      s0 = fmaf(rowi[p], rowk[p], s0);
-      s1 = fmaf(rowi[p + 1], rowk[p + 1], s1);
+  for (int k = 0; k < R - 1; ++k) {
+    const float rkk = 1.0f / A[k * ld + k];
+    const int m = R - 1 - k;
+    for (int e = tid; e < m * m; e += kWThreads) {
+      const int ii = e / m, jj = e - ii * m;
+      if (jj <= ii) {
+        const int i = k + 1 + ii, j = k + 1 + jj;
+        A[i * ld + j] = fmaf(-A[i * ld + k] * rkk, A[j * ld + k], A[i * ld + j]);
+      }
     }
-    if (p < k) s0 = fmaf(rowi[p], rowk[p], s0);
-    const float v = rowi[k] - (s0 + s1);
-    const float piv = sqrtf(__shfl_sync(kFull, v, k));
-    __syncwarp();
-    if (lane == k) {
-      A[k * ld + k] = piv;
-      dinv[k] = 1.0f / piv;
-    } else if (lane > k && lane < R) {
-      A[i * ld + k] = v / piv;
-    }
-    __syncwarp();
+    __syncthreads();
   }
-  if (lane < R) {
-    for (int j = lane + 1; j < R; ++j) A[lane * ld + j] = 0.0f;
+  for (int e = tid; e < R * R; e += kWThreads) {
+    const int i = e / R, j = e - i * R;
+    if (j < i) A[i * ld + j] = A[i * ld + j] / sqrtf(A[j * ld + j]);
+    if (j > i) A[i * ld + j] = 0.0f;
   }
-  __syncwarp();
+  __syncthreads();
+  for (int i = tid; i < R; i += kWThreads) {
+    const float piv = sqrtf(A[i * ld + i]);
+    A[i * ld + i] = piv;
+    dinv[i] = 1.0f / piv;
+  }
+  __syncthreads();
 }
 
-// Doolittle LU without pivoting of the R x R shared matrix M in place, by one
-// warp, left-looking: step k computes row k of U (lane j >= k:
-// M[k][j] - sum_{p<k} L[k][p] U[p][j]) and then column k of the unit lower
-// factor (lane i > k: (M[i][k] - sum_{p<k} L[i][p] U[p][k]) / U[k][k]); both
-// are read-only dot products followed by one store per lane.  uinv[i] = 1 / U_ii.
+// Doolittle LU without pivoting of the R x R shared matrix M in place, spread
+// over the CTA with one barrier per step: step k subtracts
+// M[i][k] M[k][j] / M[k][k] from the trailing block (reading only row and
+// column k, which no thread writes during the step); the unit lower factor
+// M[i][k] / M[k][k] is formed at the end.  uinv[i] = 1 / U_ii.  All threads call it.
 template <int R>
-__device__ __forceinline__ void lu_warp(float* M, int ld, float* uinv) {
-  const int lane = threadIdx.x & 31;
-  const int j = lane < R ? lane : 0;
+__device__ __forceinline__ void lu_block(float* M, int ld, float* uinv) {
+  const int tid = threadIdx.x;
+  __syncthreads();
 #pragma unroll 1
-  for (int k = 0; k < R; ++k) {
-    // row k of U: lane j >= k
-    const float* rowk = M + k * ld;
-    float s0 = 0.0f, s1 = 0.0f;
-    int p = 0;
-#pragma unroll 4
-    for (; p + 1 < k; p += 2) {
-      s0 = fmaf(rowk[p], M[p * ld + j], s0);
-      s1 = fmaf(rowk[p + 1], M[(p + 1) * ld + j], s1);
+  for (int k = 0; k < R - 1; ++k) {
+    const float rkk = 1.0f / M[k * ld + k];
+    const int m = R - 1 - k;
+    for (int e = tid; e < m * m; e += kWThreads) {
+      const int ii = e / m, jj = e - ii * m;
+      const int i = k + 1 + ii, j = k + 1 + jj;
+      M[i * ld + j] = fmaf(-M[i * ld + k] * rkk, M[k * ld + j], M[i * ld + j]);
     }
-    if (p < k) s0 = fmaf(rowk[p], M[p * ld + j], s0);
-    const float ukj = M[k * ld + j] - (s0 + s1);
-    __syncwarp();
-    if (lane >= k && lane < R) M[k * ld + j] = ukj;
-    const float ukk = __shfl_sync(kFull, ukj, k);
-    if (lane == k) uinv[k] = 1.0f / ukk;
-    __syncwarp();
-    // column k of L: lane i > k
-    const float* rowi = M + j * ld;
-    float t0 = 0.0f, t1 = 0.0f;
-    p = 0;
-#pragma unroll 4
-    for (; p + 1 < k; p += 2) {
-      t0 = fmaf(rowi[p], M[p * ld + k], t0);
-      t1 = fmaf(rowi[p + 1], M[(p + 1) * ld + k], t1);
-    }
-    if (p < k) t0 = fmaf(rowi[p], M[p * ld + k], t0);
-    const float lik = (rowi[k] - (t0 + t1)) / ukk;
-    __syncwarp();
-    if (lane > k && lane < R) M[j * ld + k] = lik;
-    __syncwarp();
+    __syncthreads();
   }
+  for (int e = tid; e < R * R; e += kWThreads) {
+    const int i = e / R, k = e - i * R;
+    if (i > k) M[i * ld + k] = M[i * ld + k] / M[k * ld + k];
+  }
+  for (int i = tid; i < R; i += kWThreads) uinv[i] = 1.0f / M[i * ld + i];
+  __syncthreads();
 }
 
 // Columns [c0, c0 + kNB) of the R x d operand X (row-major, leading dim xld)
@@ -178,6 +160,24 @@ __device__ __forceinline__ void warp_cols(int cols, int& c_begin, int& c_end) {
   const int per = (cols + kWWarps - 1) / kWWarps;
   c_begin = min(cols, w * per);
   c_end = min(cols, c_begin + per);
+}
+
+// Ps[m] = sum over chunks of P[ch * stride + m], m < stride (a multiple of 4),
+// in float4 steps: every load is coalesced and independent of the others.
+__device__ __forceinline__ void sum_partials(const float* P, int nchunks, int64_t stride, float* Ps) {
+  const int n4 = static_cast<int>(stride / 4);
+  const float4* P4 = reinterpret_cast<const float4*>(P);
+  for (int e = threadIdx.x; e < n4; e += kWThreads) {
+    float4 acc = __ldg(P4 + e);
+    for (int ch = 1; ch < nchunks; ++ch) {
+      const float4 v = __ldg(P4 + static_cast<int64_t>(ch) * n4 + e);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    reinterpret_cast<float4*>(Ps)[e] = acc;
+  }
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -208,7 +208,8 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
   float* dinv = fdiag + R;     // [R] 1 / L_ii
   float* uinv = dinv + R;      // [R] 1 / U_ii
   float* Ws = uinv + R;        // [d][R + 1] W_drive of this head
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* Ps = fsm + ((static_cast<int>(Ws - fsm) + d * LD + 3) & ~3);  // [2R][R + dt] summed partials
+  const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
   const int64_t b = bh / a.H;
   const int h = static_cast<int>(bh % a.H);
@@ -223,31 +224,23 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
 
   const float* Wd = a.drive + static_cast<int64_t>(h) * d * R;
   for (int idx = tid; idx < d * R; idx += kWThreads) Ws[(idx / R) * LD + idx % R] = Wd[idx];
-  // 1. G (lower triangle) and S = A'^T C / sqrt(n) from the chunk partials.
+  // 1. Sum the chunk partials (coalesced float4 reads, ndt == 1), then
+  //    G = (hh + lh + lh^T)/n + I (lower triangle) and S = (hC + lC)/sqrt(n).
+  sum_partials(pbase, a.nchunks, pstride, Ps);
+  __syncthreads();
   for (int idx = tid; idx < R * R; idx += kWThreads) {
     const int i = idx / R, k = idx % R;
     if (k > i) continue;
-    float s = 0.0f;
-    for (int ch = 0; ch < a.nchunks; ++ch) {
-      const float* P = pbase + static_cast<int64_t>(ch) * a.ndt * pstride;
-      s += P[i * NC + k] + P[(R + i) * NC + k] + P[(R + k) * NC + i];
-    }
+    const float s = Ps[i * NC + k] + Ps[(R + i) * NC + k] + Ps[(R + k) * NC + i];
     L[i * LD + k] = s * (rsn * rsn) + (i == k ? 1.0f : 0.0f);
   }
   for (int idx = tid; idx < R * d; idx += kWThreads) {
     const int i = idx / d, col = idx % d;
-    const int jt = col / a.dt, cl = col % a.dt;
-    float s = 0.0f;
-    for (int ch = 0; ch < a.nchunks; ++ch) {
-      const float* P = pbase + (static_cast<int64_t>(ch) * a.ndt + jt) * pstride;
-      s += P[i * NC + R + cl] + P[(R + i) * NC + R + cl];
-    }
-    Zs[i * XLD + col] = s * rsn;
+    Zs[i * XLD + col] = (Ps[i * NC + R + col] + Ps[(R + i) * NC + R + col]) * rsn;
   }
   __syncthreads();
-  // 2. Cholesky (warp 0)
-  if (warp == 0) cholesky_warp<R>(L, LD, dinv);
-  __syncthreads();
+  // 2. Cholesky
+  cholesky_block<R>(L, LD, dinv);
   // 3. Z = L^{-1} S (columns over the warps)
   {
     const float rd = lane < R ? dinv[lane] : 1.0f;
@@ -298,9 +291,8 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     }
     if (tid == 0) tape[tl.n] = n;
   }
-  // 6. LU (warp 0)
-  if (warp == 0) lu_warp<R>(Mm, LD, uinv);
-  __syncthreads();
+  // 6. LU
+  lu_block<R>(Mm, LD, uinv);
   if (tape != nullptr) {
     for (int idx = tid; idx < R * R; idx += kWThreads) tape[tl.LU + idx] = Mm[(idx / R) * LD + idx % R];
   }
@@ -368,6 +360,7 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   float* dinv = fdiag + R;      // [R] 1 / L_ii
   float* uinv = dinv + R;       // [R] 1 / U_ii
   float* Ws = uinv + R;         // [d][R + 1] W_drive of this head
+  float* Ps = fsm + ((static_cast<int>(Ws - fsm) + d * LD + 3) & ~3);  // [2R][dt] summed partials
   __shared__ float red[kWWarps];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
@@ -389,15 +382,11 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
     Mm[i * LD + jj] = tape[tl.LU + idx];
     Th[i * LD + jj] = tape[tl.Theta + idx];
   }
+  sum_partials(pbase, a.nchunks, pstride, Ps);
+  __syncthreads();
   for (int idx = tid; idx < R * d; idx += kWThreads) {
     const int i = idx / d, col = idx % d;
-    const int jt = col / a.dt, cl = col % a.dt;
-    float s = 0.0f;
-    for (int ch = 0; ch < a.nchunks; ++ch) {
-      const float* P = pbase + (static_cast<int64_t>(ch) * a.ndt + jt) * pstride;
-      s += P[i * NC + cl] + P[(R + i) * NC + cl];
-    }
-    X1[i * XLD + col] = s;
+    X1[i * XLD + col] = Ps[i * NC + col] + Ps[(R + i) * NC + col];
     X3[i * XLD + col] = tape[tl.U + static_cast<int64_t>(i) * d + col];
     X4[i * XLD + col] = tape[tl.Z + static_cast<int64_t>(i) * d + col];
   }
@@ -569,24 +558,39 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   if (tid == 0) a.etadot[bh] = s;
 }
 
+// Shared-memory floats before the partial-sum block, rounded up to 4 floats.
 template <int R>
-size_t fwd_smem(int d) {
-  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1));
+int fwd_head(int d) {
+  return (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + 3) / 4 * 4;
 }
 template <int R>
-size_t bwd_smem(int d) {
-  return sizeof(float) * (5 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
+int bwd_head(int d) {
+  return (5 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1) + 3) / 4 * 4;
+}
+// The partial-sum block holds one whole chunk partial: 2R rows of R + dt
+// (forward) or dt (backward) columns, dt = d_pad >= d.
+template <int R>
+size_t fwd_smem(int d, int dt) {
+  return sizeof(float) * (fwd_head<R>(d) + 2 * R * (R + dt));
+}
+template <int R>
+size_t bwd_smem(int d, int dt) {
+  return sizeof(float) * (bwd_head<R>(d) + 2 * R * dt);
 }
 
 }  // namespace
 
 bool warp_solves_usable(const Plan& p) {
-  return (p.R == 16 || p.R == 32) && bwd_smem<32>(static_cast<int>(p.d)) <= 200 * 1024;
+  // One content tile per chunk partial (d_pad <= 128), shared memory well inside one SM.
+  const int d = static_cast<int>(p.d), dt = static_cast<int>(p.dt);
+  return (p.R == 16 || p.R == 32) && p.ndt == 1 && fwd_smem<32>(d, dt) <= 160 * 1024 &&
+         bwd_smem<32>(d, dt) <= 160 * 1024;
 }
 
 cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cudaStream_t stream) {
   const int d = static_cast<int>(p.d);
-  const size_t smem = p.R == 16 ? fwd_smem<16>(d) : fwd_smem<32>(d);
+  const int dt = static_cast<int>(p.dt);
+  const size_t smem = p.R == 16 ? fwd_smem<16>(d, dt) : fwd_smem<32>(d, dt);
   const void* fn = p.R == 16 ? reinterpret_cast<const void*>(&solve_forward_warp_kernel<16>)
                              : reinterpret_cast<const void*>(&solve_forward_warp_kernel<32>);
   cudaError_t e = allow_smem(fn, smem);
@@ -602,7 +606,8 @@ cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cuda
 
 cudaError_t launch_solve_backward_warp(const Plan& p, const SolveBwdArgs& s, cudaStream_t stream) {
   const int d = static_cast<int>(p.d);
-  const size_t smem = p.R == 16 ? bwd_smem<16>(d) : bwd_smem<32>(d);
+  const int dt = static_cast<int>(p.dt);
+  const size_t smem = p.R == 16 ? bwd_smem<16>(d, dt) : bwd_smem<32>(d, dt);
   const void* fn = p.R == 16 ? reinterpret_cast<const void*>(&solve_backward_warp_kernel<16>)
                              : reinterpret_cast<const void*>(&solve_backward_warp_kernel<32>);
   cudaError_t e = allow_smem(fn, smem);
