@@ -37,7 +37,7 @@ PUBLISHED_FWD_BWD = 64 * 4096 / 29.160e-3  # RTX 5070 Ti, native co
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=64, help="samples per GPU")
@@ -123,7 +123,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_id: str | None) -> None:
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
         if gpu_id:
             cmd += ["-i", gpu_id]
         try:
@@ -284,6 +284,16 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     for _ in range(max(3, args.warmup)):
         fwd_step(x)
 
+    # Clocks and throttle reasons are sampled across every timed region below.
+    gpu_uuid = None
+    try:
+        gpu_uuid = str(torch.cuda.get_device_properties(device).uuid)
+        gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else "GPU-" + gpu_uuid
+    except Exception:  # noqa: BLE001
+        gpu_uuid = None
+    sampler = ClockSampler(gpu_uuid)
+    time.sleep(0.3)  # let nvidia-smi start sampling
+
     # ---- eager pass with per-kernel CUDA events (kernel table, roofline, launch count)
     _native.profile_start()
     eager_ms = timed(lambda: train_step(x), args.steps)
@@ -299,15 +309,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     for _ in range(args.warmup):
         graph_train_step()
-    gpu_uuid = None
-    try:
-        gpu_uuid = str(torch.cuda.get_device_properties(device).uuid)
-        gpu_uuid = gpu_uuid if gpu_uuid.startswith("GPU-") else "GPU-" + gpu_uuid
-    except Exception:  # noqa: BLE001
-        gpu_uuid = None
-    sampler = ClockSampler(gpu_uuid)
     train_ms = timed(graph_train_step, args.steps)
-    clocks = sampler.stop()
 
     fwd_eager_ms = timed(lambda: fwd_step(x), args.steps)
     with torch.inference_mode():
@@ -355,6 +357,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     timed(e2e_run, 1)
     e2e_ms = timed(e2e_run, 1)
+    clocks = sampler.stop()
     status = cuda.device_status(reset=False)
     del train_graph, fwd_graph, graphs
 
