@@ -138,7 +138,8 @@ LSSO_API int lsso_linear(const void* a, int a_dtype, int64_t M, int64_t K, const
                          void* stream);
 
 /* Workspace bytes of lsso_linear_wgrad for T tokens, Nout outputs, K inputs
- * (per-split FP32 partial tiles); 0 if unsupported (Nout and K must be
+ * (per-split FP32 partial tiles, enough for either operand orientation the
+ * kernel picks from the dtypes); 0 if unsupported (Nout and K must be
  * positive multiples of 8). */
 LSSO_API size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_t K);
 
@@ -147,7 +148,8 @@ LSSO_API size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_
  *   dw[n, k] = sum_t bf16(g[t, n]) * bf16(x[t, k])  over tokens with row_mask[t] != 0,
  * FP32 accumulation, deterministic (fixed-order reduction of per-split
  * partials, no atomics).  g [T, Nout] and x [T, K] row-major, dtype 0 = BF16,
- * 1 = FP16 (rounded to BF16); dw FP32 [Nout, K]; both inputs 16-byte aligned. */
+ * 1 = FP16 (rounded to BF16); dw FP32 [Nout, K]; g, x, dw and the workspace
+ * 16-byte aligned.  The workspace size does not depend on the dtypes. */
 LSSO_API int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask,
                                int64_t T, int64_t Nout, int64_t K, float* dw, void* workspace,
                                size_t workspace_bytes, void* stream);

@@ -278,7 +278,10 @@ size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_t K) {
   int device = 0, sms = 0;
   int* status = nullptr;
   if (device_info(&device, &sms, &status) != LSSO_OK) return 0;
-  return lsso::make_wgrad_plan(T, Nout, K, sms).partial_bytes;
+  // The operand orientation depends on the dtypes: cover both.
+  const size_t plain = lsso::make_wgrad_plan(T, Nout, K, sms, 0, 0).partial_bytes;
+  const size_t swapped = lsso::make_wgrad_plan(T, Nout, K, sms, 0, 1).partial_bytes;
+  return plain > swapped ? plain : swapped;
 }
 
 int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask, int64_t T,
@@ -296,14 +299,14 @@ int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, co
   if ((g_dtype != 0 && g_dtype != 1) || (x_dtype != 0 && x_dtype != 1)) {
     return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: dtypes must be 0 (BF16) or 1 (FP16)");
   }
-  if (!aligned16(g) || !aligned16(x) || !aligned16(workspace)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: g, x and workspace must be 16-byte aligned");
+  if (!aligned16(g) || !aligned16(x) || !aligned16(dw) || !aligned16(workspace)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: g, x, dw and workspace must be 16-byte aligned");
   }
   int device = 0, sms = 0;
   int* status = nullptr;
   int rc = device_info(&device, &sms, &status);
   if (rc != LSSO_OK) return rc;
-  const lsso::WgradPlan plan = lsso::make_wgrad_plan(T, Nout, K, sms);
+  const lsso::WgradPlan plan = lsso::make_wgrad_plan(T, Nout, K, sms, g_dtype, x_dtype);
   if (workspace_bytes < plan.partial_bytes) {
     return fail(LSSO_ERR_WORKSPACE, "lsso_linear_wgrad: workspace of %zu bytes is smaller than the required %zu",
                 workspace_bytes, plan.partial_bytes);

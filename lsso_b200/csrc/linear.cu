@@ -398,33 +398,38 @@ __global__ void prep_weight_kernel(const float* __restrict__ w, int64_t Nout, in
 
 // ============================================================================
 // Weight gradient: dW[n, k] = sum_t bf16(G[t, n]) * bf16(X[t, k]) over tokens
-// whose row_mask is set, FP32 (reference.py:229-234).  GEMM with M = n (128
-// per tile), N = k (BNW, a multiple of 64, up to 256), K = tokens; both
-// operands MN-major SW128: each stage holds 64 tokens, one 8 KB TMA box per
-// 64 features.  The token axis is split over CTAs; each CTA accumulates one
+// whose row_mask is set, FP32 (reference.py:229-234).  The kernel computes
+// C[m, c] = sum_t A[t, m] B[t, c] with M = 128 features of A per tile, N = BNW
+// features of B (a multiple of 64, up to 512: two N = 256 MMAs per K-step),
+// K = tokens; both operands MN-major SW128, each stage 64 tokens, one 8 KB TMA
+// box per 64 features.  The plan puts an FP16 operand on the A side when only
+// one operand is FP16, so each of its elements is rounded to BF16 once (the
+// B side is re-read by every A tile); C is then dW^T and the reduce writes it
+// transposed.  The token axis is split over CTAs; each CTA accumulates one
 // 128 x BNW tile in TMEM and writes an FP32 partial; wgrad_reduce sums the
 // partials in split order (deterministic, no atomics).
 // ============================================================================
 constexpr int kWT = 64;  // tokens per stage
-constexpr int kWStages = 4;
+constexpr int kWMaxStages = 4;
 constexpr uint32_t kWBox = 64 * kWT * 2;  // 8 KB: 64 tokens x 64 features
 
 struct WgradArgs {
   const uint8_t* row_mask;  // nullable [T]
   float* partial;           // [splits][tiles][128][BNW]
-  int T, Nout, K, BNW, mtiles, ntilesw, splits, tokens_per_split, g_fp16, x_fp16;
+  int T, BNW, mtiles, ntilesw, splits, tokens_per_split, a_fp16, b_fp16, stages;
   int* status;
 };
 
-__global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constant__ CUtensorMap tmap_g,
-                                                            const __grid_constant__ CUtensorMap tmap_x,
+__global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                            const __grid_constant__ CUtensorMap tmap_b,
                                                             const WgradArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int BNW = a.BNW;
-  const uint32_t ga_bytes = 2 * kWBox;                                // 128 features
-  const uint32_t xb_bytes = static_cast<uint32_t>(BNW / 64) * kWBox;  // BNW features
-  const uint32_t stage_bytes = ga_bytes + xb_bytes;
-  __shared__ __align__(8) uint64_t full[kWStages], empty[kWStages], conv[kWStages], done;
+  const int S = a.stages;
+  const uint32_t a_bytes = 2 * kWBox;                                // 128 features
+  const uint32_t b_bytes = static_cast<uint32_t>(BNW / 64) * kWBox;  // BNW features
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  __shared__ __align__(8) uint64_t full[kWMaxStages], empty[kWMaxStages], conv[kWMaxStages], done;
   __shared__ uint32_t tmem_s;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
@@ -436,11 +441,12 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
   const int t_begin = split * a.tokens_per_split;
   const int t_end = min(a.T, t_begin + a.tokens_per_split);
   const int nst = t_begin < t_end ? (t_end - t_begin + kWT - 1) / kWT : 0;
-  const bool need_conv = a.g_fp16 || a.x_fp16 || a.row_mask != nullptr;
+  const bool masked = a.row_mask != nullptr;
+  const bool need_conv = a.a_fp16 || a.b_fp16 || masked;
   const uint32_t tcols = tmem_cols_for(BNW);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kWStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
       mbar_init(smem_u32(&conv[s]), kConvWarps);
@@ -457,30 +463,29 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
 
   if (warp == 0) {
     if (lane == 0) {
-      prefetch_tmap(&tmap_g);
-      prefetch_tmap(&tmap_x);
+      prefetch_tmap(&tmap_a);
+      prefetch_tmap(&tmap_b);
     }
     bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
-      const int s = i % kWStages, u = i / kWStages;
+      const int s = i % S, u = i / S;
       ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
       if (ok && lane == 0) {
         const uint32_t dst = smem_u32(smem + s * stage_bytes);
         const int t0 = t_begin + i * kWT;
         mbar_arrive_expect_tx(smem_u32(&full[s]), stage_bytes);
-        tma_load_2d(dst, &tmap_g, mt * 128, t0, smem_u32(&full[s]));
-        tma_load_2d(dst + kWBox, &tmap_g, mt * 128 + 64, t0, smem_u32(&full[s]));
+        tma_load_2d(dst, &tmap_a, mt * 128, t0, smem_u32(&full[s]));
+        tma_load_2d(dst + kWBox, &tmap_a, mt * 128 + 64, t0, smem_u32(&full[s]));
         for (int g = 0; g < BNW / 64; ++g) {
-          tma_load_2d(dst + ga_bytes + g * kWBox, &tmap_x, ntw * BNW + g * 64, t0, smem_u32(&full[s]));
+          tma_load_2d(dst + a_bytes + g * kWBox, &tmap_b, ntw * BNW + g * 64, t0, smem_u32(&full[s]));
         }
       }
       __syncwarp();
     }
   } else if (warp == 1) {
-    const uint32_t idesc = make_idesc(128, BNW, true, true);
     bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
-      const int s = i % kWStages, u = i / kWStages;
+      const int s = i % S, u = i / S;
       ok = lwait(smem_u32(need_conv ? &conv[s] : &full[s]), u & 1, abort_v, a.status);
       tc_fence_after();
       if (ok && lane == 0) {
@@ -488,8 +493,11 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
 #pragma unroll
         for (int ks = 0; ks < kWT / 16; ++ks) {
           const uint64_t ad = make_desc_sw128(base + ks * 2048, kWBox, 1024);
-          const uint64_t bd = make_desc_sw128(base + ga_bytes + ks * 2048, kWBox, 1024);
-          mma_bf16(tmem, ad, bd, idesc, (i | ks) != 0 ? 1u : 0u);
+          for (int nb = 0; nb < BNW; nb += 256) {
+            const int n = min(256, BNW - nb);
+            const uint64_t bd = make_desc_sw128(base + a_bytes + (nb / 64) * kWBox + ks * 2048, kWBox, 1024);
+            mma_bf16(tmem + static_cast<uint32_t>(nb), ad, bd, make_idesc(128, n, true, true), (i | ks) != 0 ? 1u : 0u);
+          }
         }
         mma_commit(smem_u32(&empty[s]));
       }
@@ -505,21 +513,27 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
     __syncwarp();
   } else if (warp < 2 + kConvWarps) {
     if (need_conv) {
+      // Only the regions that need work: an FP16 operand (rounded to BF16) or,
+      // with a row mask, every chunk (masked tokens zeroed).
       const int ct = threadIdx.x - 64;
+      const int a_chunks = static_cast<int>(a_bytes / 16), total = static_cast<int>(stage_bytes / 16);
+      const int j0 = (masked || a.a_fp16) ? 0 : a_chunks;
+      const int j1 = (masked || a.b_fp16) ? total : a_chunks;
       bool ok = true;
       for (int i = 0; i < nst && ok; ++i) {
-        const int s = i % kWStages, u = i / kWStages;
+        const int s = i % S, u = i / S;
         ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint4* p = reinterpret_cast<uint4*>(smem + s * stage_bytes);
           const int t0 = t_begin + i * kWT;
-          const int gchunks = static_cast<int>(ga_bytes / 16), total = static_cast<int>(stage_bytes / 16);
-          for (int j = ct; j < total; j += kConvThreads) {
-            const bool is_g = j < gchunks;
-            const int t = t0 + ((j % 512) >> 3);  // each 128-byte row of a box is one token
+          for (int j = j0 + ct; j < j1; j += kConvThreads) {
+            const bool is_a = j < a_chunks;
             uint4 v = p[j];
-            if ((is_g && a.g_fp16) || (!is_g && a.x_fp16)) v = half8_to_bf16(v);
-            if (a.row_mask != nullptr && (t >= a.T || a.row_mask[t] == 0)) v = make_uint4(0u, 0u, 0u, 0u);
+            if (is_a ? a.a_fp16 : a.b_fp16) v = half8_to_bf16(v);
+            if (masked) {
+              const int t = t0 + ((j % 512) >> 3);  // each 128-byte row of a box is one token
+              if (t >= a.T || a.row_mask[t] == 0) v = make_uint4(0u, 0u, 0u, 0u);
+            }
             p[j] = v;
           }
           fence_proxy_async();
@@ -531,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
   } else {
     const int sub = warp & 3;
     const int half = (warp - (2 + kConvWarps)) >> 2;
-    const int row = 32 * sub + lane;  // feature n within the tile
+    const int row = 32 * sub + lane;  // feature m within the tile
     bool ok = lwait(smem_u32(&done), 0, abort_v, a.status);
     tc_fence_after();
     float* out = a.partial + (static_cast<size_t>(split) * tiles + tile) * 128 * BNW + static_cast<size_t>(row) * BNW;
@@ -557,18 +571,38 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
   }
 }
 
-// dW[n, k] = sum over splits (ascending) of the partial tiles.
+// C[m, c] = sum over splits (ascending) of the partial tiles, four adjacent
+// columns per thread with float4 reads in partial order (coalesced, and the
+// unrolled split loop keeps several loads in flight); written to dw[m, c]
+// ([Mdim, Ndim]) or, when the operands were swapped, to dw[c, m].
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int mtiles, int ntilesw, int BNW,
-                                    int Nout, int K, float* __restrict__ dw) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<int64_t>(Nout) * K) return;
-  const int n = static_cast<int>(idx / K), k = static_cast<int>(idx % K);
+                                    int Mdim, int Ndim, int swapped, float* __restrict__ dw) {
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= static_cast<int64_t>(Mdim) * Ndim / 4) return;
+  const int64_t idx = 4 * q;
+  const int m = static_cast<int>(idx / Ndim), c = static_cast<int>(idx % Ndim);  // Ndim % 4 == 0
   const int tiles = mtiles * ntilesw;
-  const int tile = (n / 128) * ntilesw + k / BNW;
-  const size_t inner = static_cast<size_t>(n % 128) * BNW + (k % BNW);
-  float s = 0.0f;
-  for (int sp = 0; sp < splits; ++sp) s += partial[(static_cast<size_t>(sp) * tiles + tile) * 128 * BNW + inner];
-  dw[idx] = s;
+  const int tile = (m / 128) * ntilesw + c / BNW;
+  const size_t inner = static_cast<size_t>(m % 128) * BNW + (c % BNW);
+  const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(tile) * 128 * BNW + inner);
+  const size_t stride4 = static_cast<size_t>(tiles) * 128 * BNW / 4;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+  for (int sp = 0; sp < splits; ++sp) {
+    const float4 v = __ldg(src + sp * stride4);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  if (swapped) {
+    dw[static_cast<int64_t>(c) * Mdim + m] = acc.x;
+    dw[static_cast<int64_t>(c + 1) * Mdim + m] = acc.y;
+    dw[static_cast<int64_t>(c + 2) * Mdim + m] = acc.z;
+    dw[static_cast<int64_t>(c + 3) * Mdim + m] = acc.w;
+  } else {
+    *reinterpret_cast<float4*>(dw + idx) = acc;
+  }
 }
 
 // Row-major [rows, cols] 16-bit tensor, 64-column x box_rows boxes, 128-byte swizzle.
@@ -621,15 +655,23 @@ LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
 
 bool linear_shape_supported(int64_t K) { return K % 8 == 0 && K > 0 && K <= 1024; }
 
-WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count) {
+WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int g_fp16, int x_fp16) {
   WgradPlan p{};
   p.T = T;
   p.Nout = Nout;
   p.K = K;
-  // A multiple of 64: MN-major operands come in 64-feature TMA boxes.
-  p.BNW = K >= 256 ? 256 : static_cast<int>((K + 63) / 64 * 64);
-  p.mtiles = static_cast<int>((Nout + 127) / 128);
-  p.ntilesw = static_cast<int>((K + p.BNW - 1) / p.BNW);
+  // An FP16 operand goes on the A (M) side, where each element is rounded once.
+  p.swapped = (x_fp16 && !g_fp16) ? 1 : 0;
+  p.Mdim = p.swapped ? K : Nout;
+  p.Ndim = p.swapped ? Nout : K;
+  // A multiple of 64: MN-major operands come in 64-feature TMA boxes; up to
+  // the 512 TMEM columns in one tile.
+  p.BNW = p.Ndim <= 512 ? static_cast<int>((p.Ndim + 63) / 64 * 64) : 256;
+  p.mtiles = static_cast<int>((p.Mdim + 127) / 128);
+  p.ntilesw = static_cast<int>((p.Ndim + p.BNW - 1) / p.BNW);
+  const size_t stage = static_cast<size_t>(2 + p.BNW / 64) * kWBox;
+  p.stages = static_cast<int>((200 * 1024) / stage);
+  if (p.stages > kWMaxStages) p.stages = kWMaxStages;
   const int tiles = p.mtiles * p.ntilesw;
   const int sms = sm_count > 0 ? sm_count : 148;
   int splits = sms / tiles;
@@ -641,7 +683,7 @@ WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count) {
   p.tokens_per_split = static_cast<int>(per);
   p.splits = static_cast<int>((T + per - 1) / per);
   p.grid = p.splits * tiles;
-  p.smem = static_cast<size_t>(kWStages) * (2 * kWBox + static_cast<size_t>(p.BNW / 64) * kWBox);
+  p.smem = static_cast<size_t>(p.stages) * stage;
   p.partial_bytes = static_cast<size_t>(p.splits) * tiles * 128 * p.BNW * sizeof(float);
   return p;
 }
@@ -712,35 +754,39 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
 cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return cudaErrorNotSupported;
-  CUtensorMap mg{}, mx{};
-  if (encode_rows(encode, &mg, c.g, p.T, p.Nout, c.g_fp16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (encode_rows(encode, &mx, c.x, p.T, p.K, c.x_fp16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  const void* pa = p.swapped ? c.x : c.g;
+  const void* pb = p.swapped ? c.g : c.x;
+  const int a16 = p.swapped ? c.x_fp16 : c.g_fp16;
+  const int b16 = p.swapped ? c.g_fp16 : c.x_fp16;
+  CUtensorMap ma{}, mb{};
+  if (encode_rows(encode, &ma, pa, p.T, p.Mdim, a16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (encode_rows(encode, &mb, pb, p.T, p.Ndim, b16, kWT) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   WgradArgs a{};
   a.row_mask = c.row_mask;
   a.partial = c.partial;
   a.T = static_cast<int>(p.T);
-  a.Nout = static_cast<int>(p.Nout);
-  a.K = static_cast<int>(p.K);
   a.BNW = p.BNW;
   a.mtiles = p.mtiles;
   a.ntilesw = p.ntilesw;
   a.splits = p.splits;
   a.tokens_per_split = p.tokens_per_split;
-  a.g_fp16 = c.g_fp16;
-  a.x_fp16 = c.x_fp16;
+  a.a_fp16 = a16;
+  a.b_fp16 = b16;
+  a.stages = p.stages;
   a.status = c.status;
   cudaError_t e = allow_smem(reinterpret_cast<const void*>(&wgrad_kernel), p.smem);
   if (e != cudaSuccess) return e;
   {
     LaunchScope scope("wgrad", stream);
-    wgrad_kernel<<<p.grid, kThreads, p.smem, stream>>>(mg, mx, a);
+    wgrad_kernel<<<p.grid, kThreads, p.smem, stream>>>(ma, mb, a);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const int64_t total = p.Nout * p.K;
+  const int64_t quads = p.Mdim * p.Ndim / 4;
   LaunchScope scope("wgrad_reduce", stream);
-  wgrad_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-      c.partial, p.splits, p.mtiles, p.ntilesw, p.BNW, static_cast<int>(p.Nout), static_cast<int>(p.K), c.dw);
+  wgrad_reduce_kernel<<<static_cast<unsigned>((quads + 255) / 256), 256, 0, stream>>>(
+      c.partial, p.splits, p.mtiles, p.ntilesw, p.BNW, static_cast<int>(p.Mdim), static_cast<int>(p.Ndim), p.swapped,
+      c.dw);
   return cudaGetLastError();
 }
 

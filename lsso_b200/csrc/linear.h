@@ -31,7 +31,9 @@ struct LinearCall {
 
 struct WgradPlan {
   int64_t T, Nout, K;
-  int BNW, mtiles, ntilesw, splits, tokens_per_split, grid;
+  int64_t Mdim, Ndim;  // GEMM M (A-side features) and N (B-side features)
+  int swapped;         // A = X and B = G (the kernel computes dW^T)
+  int BNW, mtiles, ntilesw, splits, tokens_per_split, stages, grid;
   size_t smem, partial_bytes;
 };
 
@@ -49,7 +51,7 @@ struct WgradCall {
 // cuTensorMapEncodeTiled through the runtime's driver entry point (null if unavailable).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
-WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count);
+WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int g_fp16, int x_fp16);
 cudaError_t launch_wgrad(const WgradPlan& plan, const WgradCall& call, cudaStream_t stream);
 
 LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count);
