@@ -52,6 +52,9 @@ struct LinearArgs {
   int out_dtype;            // 0 BF16, 1 FP16, 2 FP32
   int M, Nout, K_pad, BN, NT, a_fp16;
   int tma_out;              // output written by TMA tensor stores (else direct stores)
+  int b_stream;             // weight k-blocks ride in the stages instead of staying resident
+  int stages;               // pipeline stages (<= kStages)
+  uint32_t stage_bytes;     // A box (16 KB) [+ streamed weight k-block]
   int* status;
 };
 
@@ -165,9 +168,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
                                                              const __grid_constant__ CUtensorMap tmap_out,
                                                              const LinearArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  // Resident weight: [weight tile | stages | epilogue staging]; streamed: [stages | staging].
   uint8_t* sB = smem;
-  uint8_t* sA = smem + static_cast<size_t>(a.BN) * a.K_pad * 2;  // a multiple of 1024
-  uint8_t* sOut = sA + kStages * kStageBytes;
+  uint8_t* sA = a.b_stream ? smem : smem + static_cast<size_t>(a.BN) * a.K_pad * 2;  // a multiple of 1024
+  const uint32_t SB = a.stage_bytes;
+  const int S = a.stages;
+  uint8_t* sOut = sA + S * SB;
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], conv[kStages], tfull[2], tempty[2], bbar;
   __shared__ uint32_t tmem_s;
   __shared__ int abort_flag;
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   const uint32_t tcols = tmem_cols_for(2 * BN);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
       mbar_init(smem_u32(&conv[s]), kConvWarps);
@@ -212,14 +218,17 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
 
   if (warp == 0) {
     // ---------------- producer
+    const uint32_t bbytes = static_cast<uint32_t>(BN) * a.K_pad * 2;
+    const uint8_t* bsrc = a.bprep + static_cast<size_t>(nt) * bbytes;
+    const uint32_t b_region = static_cast<uint32_t>(BN) * 128;  // one 64-wide K region of the weight tile
     if (lane == 0) {
       prefetch_tmap(&tmap_a);
-      const uint32_t bbytes = static_cast<uint32_t>(BN) * a.K_pad * 2;
-      mbar_arrive_expect_tx(smem_u32(&bbar), bbytes);
-      const uint8_t* src = a.bprep + static_cast<size_t>(nt) * bbytes;
-      for (uint32_t off = 0; off < bbytes; off += 32768u) {
-        const uint32_t chunk = min(32768u, bbytes - off);
-        bulk_load(smem_u32(sB + off), src + off, chunk, smem_u32(&bbar));
+      if (!a.b_stream) {
+        mbar_arrive_expect_tx(smem_u32(&bbar), bbytes);
+        for (uint32_t off = 0; off < bbytes; off += 32768u) {
+          const uint32_t chunk = min(32768u, bbytes - off);
+          bulk_load(smem_u32(sB + off), bsrc + off, chunk, smem_u32(&bbar));
+        }
       }
     }
     __syncwarp();
@@ -228,18 +237,21 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int m = mstart + i * mstep;
       for (int kb = 0; kb < KB && ok; ++kb, ++it) {
-        const int s = it % kStages, u = it / kStages;
+        const int s = it % S, u = it / S;
         ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
         if (ok && lane == 0) {
-          mbar_arrive_expect_tx(smem_u32(&full[s]), kStageBytes);
-          tma_load_2d(smem_u32(sA + s * kStageBytes), &tmap_a, kb * kBK, m * kBM, smem_u32(&full[s]));
+          uint8_t* stage = sA + s * SB;
+          mbar_arrive_expect_tx(smem_u32(&full[s]), SB);
+          tma_load_2d(smem_u32(stage), &tmap_a, kb * kBK, m * kBM, smem_u32(&full[s]));
+          // Streamed weight: k-block kb of this N tile (L2-resident, reused by every M tile).
+          if (a.b_stream) bulk_load(smem_u32(stage + kStageBytes), bsrc + kb * b_region, b_region, smem_u32(&full[s]));
         }
         __syncwarp();
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
-    bool ok = lwait(smem_u32(&bbar), 0, abort_v, a.status);
+    bool ok = a.b_stream ? true : lwait(smem_u32(&bbar), 0, abort_v, a.status);
     const uint32_t idesc = make_idesc(kBM, BN, false, false);
     const uint32_t sa0 = smem_u32(sA), sb0 = smem_u32(sB);
     const uint32_t b_region = static_cast<uint32_t>(BN) * 128;  // one 64-wide K region of the weight tile
@@ -250,14 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       tc_fence_after();
       const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
       for (int kb = 0; kb < KB && ok; ++kb, ++it) {
-        const int s = it % kStages, u = it / kStages;
+        const int s = it % S, u = it / S;
         ok = lwait(smem_u32(a.a_fp16 ? &conv[s] : &full[s]), u & 1, abort_v, a.status);
         tc_fence_after();
         if (ok && lane == 0) {
+          const uint32_t stage = sa0 + s * SB;
+          const uint32_t bk = a.b_stream ? stage + kStageBytes : sb0 + kb * b_region;
 #pragma unroll
           for (int ks = 0; ks < kBK / 16; ++ks) {
-            const uint64_t ad = make_desc_sw128(sa0 + s * kStageBytes + ks * 32, 16, 1024);
-            const uint64_t bd = make_desc_sw128(sb0 + kb * b_region + ks * 32, 16, 1024);
+            const uint64_t ad = make_desc_sw128(stage + ks * 32, 16, 1024);
+            const uint64_t bd = make_desc_sw128(bk + ks * 32, 16, 1024);
             mma_bf16(d, ad, bd, idesc, (kb | ks) != 0 ? 1u : 0u);
           }
           mma_commit(smem_u32(&empty[s]));
@@ -275,10 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       bool ok = true;
       for (int i = 0; i < ntile_local && ok; ++i) {
         for (int kb = 0; kb < KB && ok; ++kb, ++it) {
-          const int s = it % kStages, u = it / kStages;
+          const int s = it % S, u = it / S;
           ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
           if (ok) {
-            uint4* p = reinterpret_cast<uint4*>(sA + s * kStageBytes);
+            uint4* p = reinterpret_cast<uint4*>(sA + s * SB);  // the A box (first 16 KB of the stage)
 #pragma unroll 2
             for (int j = ct; j < static_cast<int>(kStageBytes / 16); j += kConvThreads) p[j] = half8_to_bf16(p[j]);
             fence_proxy_async();
@@ -641,6 +655,13 @@ LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
   const int64_t n16 = (Nout + 15) / 16 * 16;
   int bn = 256;
   while (bn > 16 && (static_cast<int64_t>(bn) * p.K_pad * 2 > 128 * 1024 || bn / 2 >= n16)) bn /= 2;
+  // When keeping the weight tile resident would force a narrower tile (long K),
+  // stream its k-blocks through the stages instead and keep the wide tile: the
+  // A tile then goes through fewer, wider MMAs and is read once per N tile less.
+  int bn_wide = 256;
+  while (bn_wide > 16 && bn_wide / 2 >= n16) bn_wide /= 2;
+  p.b_stream = bn_wide > bn ? 1 : 0;
+  if (p.b_stream) bn = bn_wide;
   p.BN = bn;
   p.NT = static_cast<int>((Nout + bn - 1) / bn);
   const int64_t mtiles = (M + kBM - 1) / kBM;
@@ -648,7 +669,17 @@ LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
   if (groups < 1) groups = 1;
   if (groups > mtiles) groups = mtiles;
   p.grid = static_cast<int>(groups * p.NT);
-  p.smem = static_cast<size_t>(bn) * p.K_pad * 2 + kStages * kStageBytes + kEpiWarps * kEpiStage;
+  if (p.b_stream) {
+    p.stage_bytes = kStageBytes + static_cast<uint32_t>(bn) * 128;
+    const size_t room = 230400 - 1024 - static_cast<size_t>(kEpiWarps) * kEpiStage;
+    p.stages = static_cast<int>(room / p.stage_bytes);
+    if (p.stages > kStages) p.stages = kStages;
+    p.smem = static_cast<size_t>(p.stages) * p.stage_bytes + kEpiWarps * kEpiStage;
+  } else {
+    p.stage_bytes = kStageBytes;
+    p.stages = kStages;
+    p.smem = static_cast<size_t>(bn) * p.K_pad * 2 + kStages * kStageBytes + kEpiWarps * kEpiStage;
+  }
   p.prep_bytes = static_cast<size_t>(p.NT) * bn * p.K_pad * 2;
   return p;
 }
@@ -718,6 +749,9 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   }
   LinearArgs a{};
   a.tma_out = tma_out ? 1 : 0;
+  a.b_stream = p.b_stream;
+  a.stages = p.stages;
+  a.stage_bytes = p.stage_bytes;
   a.bprep = c.prep;
   a.bias = c.bias;
   a.row_mask = c.row_mask;

@@ -12,6 +12,9 @@ namespace lsso {
 struct LinearPlan {
   int64_t M, K, Nout, K_pad;
   int BN, NT, grid;
+  int b_stream;          // weight k-blocks streamed with the activation stages
+  int stages;
+  uint32_t stage_bytes;
   size_t smem, prep_bytes;
 };
 
