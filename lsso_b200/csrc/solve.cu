@@ -85,16 +85,15 @@ template <int R>
 __device__ __forceinline__ void cholesky_block(float* A, int ld, float* dinv) {
   const int tid = threadIdx.x;
   __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
 #pragma unroll 1
   for (int k = 0; k < R - 1; ++k) {
     const float rkk = 1.0f / A[k * ld + k];
-    const int m = R - 1 - k;
-    for (int e = tid; e < m * m; e += kWThreads) {
-      const int ii = e / m, jj = e - ii * m;
-      if (jj <= ii) {
-        const int i = k + 1 + ii, j = k + 1 + jj;
-        A[i * ld + j] = fmaf(-A[i * ld + k] * rkk, A[j * ld + k], A[i * ld + j]);
-      }
+    // rows over warps, columns over lanes (R <= 32: one column pass)
+    const int j = k + 1 + lane;
+    const float ajk = j < R ? A[j * ld + k] : 0.0f;
+    for (int i = k + 1 + warp; i < R; i += kWWarps) {
+      if (j <= i) A[i * ld + j] = fmaf(-A[i * ld + k] * rkk, ajk, A[i * ld + j]);
     }
     __syncthreads();
   }
@@ -121,14 +120,15 @@ template <int R>
 __device__ __forceinline__ void lu_block(float* M, int ld, float* uinv) {
   const int tid = threadIdx.x;
   __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
 #pragma unroll 1
   for (int k = 0; k < R - 1; ++k) {
     const float rkk = 1.0f / M[k * ld + k];
-    const int m = R - 1 - k;
-    for (int e = tid; e < m * m; e += kWThreads) {
-      const int ii = e / m, jj = e - ii * m;
-      const int i = k + 1 + ii, j = k + 1 + jj;
-      M[i * ld + j] = fmaf(-M[i * ld + k] * rkk, M[k * ld + j], M[i * ld + j]);
+    // rows over warps, columns over lanes (R <= 32: one column pass)
+    const int j = k + 1 + lane;
+    const float ukj = j < R ? M[k * ld + j] : 0.0f;
+    for (int i = k + 1 + warp; i < R; i += kWWarps) {
+      if (j < R) M[i * ld + j] = fmaf(-M[i * ld + k] * rkk, ukj, M[i * ld + j]);
     }
     __syncthreads();
   }

@@ -11,10 +11,10 @@
 //                 as zero), plus bulk copies of the per-(b, h) operand
 //                 matrices the solves produced;
 //   warp 1        tcgen05 MMA issuer (one lane);
-//   warps 2-5     Rank-Rotary rotation of the relation boxes in place (and,
-//                 for the moment pass, the BF16 hi/lo split into the
-//                 MN-major operand buffer);
-//   warps 6-13    epilogue: TMEM -> registers, combine with the staged
+//   warps 2-9     Rank-Rotary rotation of the relation boxes in place (the
+//                 moment pass uses warps 2-13, adding the BF16 hi/lo split
+//                 into the MN-major operand buffer);
+//   warps 10-17   epilogue (moment pass: warps 14-17): TMEM -> registers, combine with the staged
 //                 content / dY boxes, write the result back into the boxes
 //                 and store them with TMA tensor stores (tokens past N are
 //                 clipped), or drain moment accumulators to the partials.
@@ -47,6 +47,13 @@ constexpr int kXWarp0 = 2, kXWarps = 8;      // rotation / split warps
 constexpr int kEWarp0 = 10, kEWarps = 8;      // epilogue warps (two per TMEM sub-partition)
 constexpr int kXThreads = kXWarps * 32;
 constexpr int kThreadsT = (kEWarp0 + kEWarps) * 32;
+// The moment pass drains TMEM only at the end of a chunk, so it gives most of
+// its warps to the rotation / hi-lo split: 12 of them, and 4 drain warps (one
+// per TMEM sub-partition).
+constexpr int kMXWarps = 12, kMEWarp0 = kXWarp0 + kMXWarps, kMEWarps = 4;
+constexpr int kMXThreads = kMXWarps * 32;
+constexpr int kMThreads = (kMEWarp0 + kMEWarps) * 32;
+constexpr int kMMaxChunks = (2 * kTileTokens * 8 + kMXThreads - 1) / kMXThreads;  // nrel <= 2
 constexpr size_t kSmemFloor = 120 * 1024;    // forces one CTA per SM (each allocates all of TMEM)
 
 struct TileArgs {
@@ -101,17 +108,17 @@ __device__ __forceinline__ Phase4 phase_at(const float2* table, int64_t prow, in
 
 // Common prologue: barriers, TMEM (all 512 columns), 1024-byte aligned base.
 __device__ __forceinline__ uint8_t* tile_setup(TileShared& sh, uint8_t* raw, int slots, int nbuf, int tcount_mma,
-                                               int tcount_free) {
+                                               int tcount_free, int xwarps, int ewarps) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < slots; ++s) {
       mbar_init(smem_u32(&sh.full[s]), 1);
-      mbar_init(smem_u32(&sh.xdone[s]), kXWarps);
+      mbar_init(smem_u32(&sh.xdone[s]), xwarps);
       mbar_init(smem_u32(&sh.sfree[s]), tcount_free);
-      mbar_init(smem_u32(&sh.edone[s]), kEWarps);
+      mbar_init(smem_u32(&sh.edone[s]), ewarps);
     }
     for (int b = 0; b < nbuf; ++b) {
       mbar_init(smem_u32(&sh.tfull[b]), tcount_mma);
-      mbar_init(smem_u32(&sh.tempty[b]), kEWarps);
+      mbar_init(smem_u32(&sh.tempty[b]), ewarps);
     }
     sh.abort_flag = 0;
     fence_mbar_init();
@@ -252,7 +259,7 @@ __device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase
 // (forward) or  D += [hi|lo]^T dY (backward).
 // ============================================================================
 template <int R, bool BWD>
-__global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid_constant__ CUtensorMap tm_rel,
+__global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid_constant__ CUtensorMap tm_rel,
                                                                      const __grid_constant__ CUtensorMap tm_val,
                                                                      const TileArgs a) {
   constexpr bool kFused = R == 32;
@@ -264,7 +271,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.d;
   const int NC = (BWD ? 0 : R) + d;
-  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
+  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1, kMXWarps, kMEWarps);
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
   int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
@@ -356,30 +363,60 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
         __syncwarp();
       }
     }
-  } else if (warp < kXWarp0 + kXWarps) {
+  } else if (warp < kXWarp0 + kMXWarps) {
     // ------------------------------------------------------------ rotate + hi/lo split
+    // The phases of tile k + 1 are fetched (from the L2-resident table) while
+    // tile k is transformed, so their latency is off the critical path.
+    constexpr int NCH = ((R == 32 ? 1 : 2) * kTT * 8 + kMXThreads - 1) / kMXThreads;  // chunks per thread
     const int xt = threadIdx.x - kXWarp0 * 32;
+    const int total = a.nrel * kTT * 8;
+    auto fetch = [&](int ii, int tt, Phase4 (&ph)[NCH]) {
+      int b, g, chunk, t0, nt;
+      item_of(ii, b, g, chunk, t0, nt);
+      const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
+      const int tok0 = (t0 + tt) * kTT;
+#pragma unroll
+      for (int kk = 0; kk < NCH; ++kk) {
+        const int idx = xt + kk * kMXThreads;
+        if (idx < total) {
+          int j, r, c;
+          chunk_coords(idx, j, r, c);
+          ph[kk] = phase_at(a.phase, prow, tok0 + r, a.N, R, ((j * 64 + 8 * c) % R) >> 3);
+        }
+      }
+    };
+    // One tile ahead at R = 32 (three chunks per thread); at R = 64 a second
+    // register set would spill, so the phases are fetched just before the wait.
+    constexpr bool kAhead = R == 32;
+    Phase4 ph[NCH], phn[kAhead ? NCH : 1];
+    if (kAhead && nloc > 0) fetch(0, 0, ph);
     int k = 0;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
       int b, g, chunk, t0, nt;
       item_of(i, b, g, chunk, t0, nt);
-      const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
       for (int tt = 0; tt < nt && ok; ++tt, ++k) {
         const int s = k % a.slots, u = k / a.slots;
-        Phase4 ph[kMaxChunks];
-        fetch_phases<R>(ph, a.phase, prow, (t0 + tt) * kTT, a.N, a.nrel, xt);
+        if constexpr (kAhead) {
+          if (tt + 1 < nt) {
+            fetch(i, tt + 1, phn);
+          } else if (i + 1 < nloc) {
+            fetch(i + 1, 0, phn);
+          }
+        } else {
+          fetch(i, tt, ph);
+        }
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
           uint8_t* rel = slot + a.off_rel;
           uint8_t* op = slot + a.off_aux;
-          const int nch = a.nrel * (kTT * 8) / kXThreads;
 #pragma unroll
-          for (int kk = 0; kk < kMaxChunks; ++kk) {
-            if (kk >= nch) break;
+          for (int kk = 0; kk < NCH; ++kk) {
+            const int idx = xt + kk * kMXThreads;
+            if (idx >= total) break;
             int j, r, c;
-            chunk_coords(xt + kk * kXThreads, j, r, c);
+            chunk_coords(idx, j, r, c);
             const int f = j * 64 + 8 * c;
             const int hl = f / R, k0 = f % R;
             uint8_t* src = box_chunk(rel + j * kBox, r, c);
@@ -403,11 +440,15 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
+        if constexpr (kAhead) {
+#pragma unroll
+          for (int kk = 0; kk < NCH; ++kk) ph[kk] = phn[kk];
+        }
       }
     }
   } else {
-    // ------------------------------------------------------------ drain accumulators
-    const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
+    // ------------------------------------------------------------ drain accumulators (one warp per sub-partition)
+    const int sub = warp & 3;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
@@ -423,7 +464,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
           const int row = (sub < 2 ? R : 0) + lane;
           const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hh;
           float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + row) * static_cast<int64_t>(NC);
-          for (int c0 = 32 * half; c0 < NC; c0 += 64) {
+          for (int c0 = 0; c0 < NC; c0 += 32) {
             const int tc = BWD ? hh * d + c0 : (c0 < R ? 32 * hh + c0 : 64 + hh * d + (c0 - R));
             float v[32];
             tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
@@ -434,11 +475,11 @@ __global__ void __launch_bounds__(kThreadsT, 1) moments_tile_kernel(const __grid
           }
         } else {
           const bool m64 = M2 == 64;
-          const int m = m64 ? 16 * sub + lane : 32 * sub + lane;
+          const int mrow = m64 ? 16 * sub + lane : 32 * sub + lane;
           const bool valid = !m64 || lane < 16;
-          for (int hl = half; hl < a.hg; hl += 2) {
+          for (int hl = 0; hl < a.hg; ++hl) {
             const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
-            float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + m) * static_cast<int64_t>(NC);
+            float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + mrow) * static_cast<int64_t>(NC);
             for (int c0 = 0; c0 < NC; c0 += 32) {
               float v[32];
               tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC + c0), v);
@@ -475,7 +516,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
   volatile int* abort_v = &sh.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.d;
-  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
+  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1, kXWarps, kEWarps);
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
   int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
@@ -626,7 +667,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.d;
   const int NC = R + d;
-  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1);
+  uint8_t* smem = tile_setup(sh, smem_raw, a.slots, a.nbuf, 1, 1, kXWarps, kEWarps);
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
   int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
@@ -924,11 +965,11 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   if (e != cudaSuccess) return e;
   LaunchScope scope(bwd ? "moments_bwd" : "moments_fwd", stream);
   if (p.R == 32) {
-    if (bwd) moments_tile_kernel<32, true><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
-    else moments_tile_kernel<32, false><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
+    if (bwd) moments_tile_kernel<32, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    else moments_tile_kernel<32, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
   } else {
-    if (bwd) moments_tile_kernel<64, true><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
-    else moments_tile_kernel<64, false><<<grid, kThreadsT, smem, stream>>>(tm_rel, tm_val, a);
+    if (bwd) moments_tile_kernel<64, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    else moments_tile_kernel<64, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
   }
   return cudaGetLastError();
 }
