@@ -1,21 +1,23 @@
-// Per-(sample, head) r x r solves of the LSSO mixer for R <= 32 (sm_100a).
+// Per-(sample, head) r x r solves of the LSSO mixer (sm_100a), r in {16, 32, 48, 64}.
 //
 // Same algebra as solve_forward_kernel / solve_backward_kernel in mixer.cu
 // (reference lsso/ball/reference.py:411-572): Cholesky of the Gram matrix,
 // the accretive generator, LU without pivoting, and the triangular solves of
 // the forward and the analytic backward.  The difference is the execution
-// model: with R <= 32 one lane owns one matrix row, so
-//   - Cholesky and LU are R steps in one warp: the pivot row or column is
-//     broadcast (shuffle or same-address shared read) and every lane updates
-//     its own row with independent fused multiply-adds;
+// model: lane l of a warp owns matrix rows l, l + 32, ... (P = ceil(R/32)
+// register slots), so
 //   - a triangular solve is R shuffle steps per right-hand side, four
 //     right-hand sides per warp at a time for instruction-level parallelism,
 //     replacing a thread-per-column R^2 chain; transposed solves read the
 //     matrix by columns (one column view of the packed LU serves both U^T and
 //     the unit L^T);
+//   - Cholesky and LU are right-looking over the whole CTA, one barrier per
+//     step (rows over warps, columns over lanes);
 //   - all d columns of the R x d operands stay in shared memory, split over
-//     the CTA's warps.
-// One CTA (four warps) per (sample, head).
+//     the CTA's warps;
+//   - the chunk partials of the moment pass are summed with coalesced float4
+//     loads straight into the matrices that use them.
+// One CTA (eight warps) per (sample, head).
 #include "mixer.h"
 #include "mixer_common.cuh"
 
@@ -27,29 +29,49 @@ constexpr int kWThreads = 256;
 constexpr int kWWarps = kWThreads / 32;
 constexpr int kNB = 4;  // right-hand sides per warp-level solve
 constexpr unsigned kFull = 0xffffffffu;
+constexpr size_t kWarpSolveSmemLimit = 200 * 1024;
 
-// Matrices stay in shared memory; lane i works on row i.  The step loops are
-// kept rolled (unroll 2) so the code stays small: these kernels run once per
-// (sample, head), and fully unrolled R = 32 chains overflow the instruction
+// Rows per lane.
+template <int R>
+__host__ __device__ constexpr int rows_per_lane() {
+  return (R + 31) / 32;
+}
+
+// Matrices stay in shared memory; lane l works on rows 32 p + l.  The step
+// loops are kept rolled (unroll 2) so the code stays small: these kernels run
+// once per (sample, head), and fully unrolled chains overflow the instruction
 // cache.  A matrix element (row, k) is read at M[row * rs + k * cs]: rs = ld,
 // cs = 1 for the matrix itself, rs = 1, cs = ld for its transpose.
 
-// Lower-triangular solve T x = b (lane i: b_i in b[q]); rdiag = 1 / T_ii on
-// lane i (ignored when UNIT).
+// Lower-triangular solve T x = b (lane l, slot p: b_{32p+l} in b[p][q]);
+// rdiag[p] = 1 / T_ii of the lane's row i in slot p (ignored when UNIT).
 template <int R, bool UNIT>
-__device__ __forceinline__ void trsv_lower(const float* M, int rs, int cs, float rdiag, float (&b)[kNB]) {
+__device__ __forceinline__ void trsv_lower(const float* M, int rs, int cs, const float (&rdiag)[rows_per_lane<R>()],
+                                           float (&b)[rows_per_lane<R>()][kNB]) {
+  constexpr int P = rows_per_lane<R>();
   const int lane = threadIdx.x & 31;
-  const float* row = M + (lane < R ? lane : 0) * rs;
-#pragma unroll 2
-  for (int k = 0; k < R; ++k) {
-    const float tk = lane < R ? row[k * cs] : 0.0f;
+  const float* row[P];
 #pragma unroll
-    for (int q = 0; q < kNB; ++q) {
-      const float xk = __shfl_sync(kFull, UNIT ? b[q] : b[q] * rdiag, k);
-      if (lane == k) {
-        b[q] = xk;
-      } else if (lane > k) {
-        b[q] = fmaf(-tk, xk, b[q]);
+  for (int p = 0; p < P; ++p) row[p] = M + (32 * p + lane < R ? 32 * p + lane : 0) * rs;
+#pragma unroll
+  for (int s = 0; s < P; ++s) {
+    const int kend = 32 * s + 32 < R ? 32 * s + 32 : R;
+#pragma unroll 2
+    for (int k = 32 * s; k < kend; ++k) {
+      const int src = k - 32 * s;
+      float tk[P];
+#pragma unroll
+      for (int p = s; p < P; ++p) tk[p] = 32 * p + lane < R ? row[p][k * cs] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) {
+        const float xk = __shfl_sync(kFull, UNIT ? b[s][q] : b[s][q] * rdiag[s], src);
+        if (lane == src) {
+          b[s][q] = xk;
+        } else if (lane > src) {
+          b[s][q] = fmaf(-tk[s], xk, b[s][q]);
+        }
+#pragma unroll
+        for (int p = s + 1; p < P; ++p) b[p][q] = fmaf(-tk[p], xk, b[p][q]);
       }
     }
   }
@@ -57,46 +79,107 @@ __device__ __forceinline__ void trsv_lower(const float* M, int rs, int cs, float
 
 // Upper-triangular solve T x = b (entries k > i of row i used).
 template <int R, bool UNIT>
-__device__ __forceinline__ void trsv_upper(const float* M, int rs, int cs, float rdiag, float (&b)[kNB]) {
+__device__ __forceinline__ void trsv_upper(const float* M, int rs, int cs, const float (&rdiag)[rows_per_lane<R>()],
+                                           float (&b)[rows_per_lane<R>()][kNB]) {
+  constexpr int P = rows_per_lane<R>();
   const int lane = threadIdx.x & 31;
-  const float* row = M + (lane < R ? lane : 0) * rs;
-#pragma unroll 2
-  for (int k = R - 1; k >= 0; --k) {
-    const float tk = lane < R ? row[k * cs] : 0.0f;
+  const float* row[P];
 #pragma unroll
-    for (int q = 0; q < kNB; ++q) {
-      const float xk = __shfl_sync(kFull, UNIT ? b[q] : b[q] * rdiag, k);
-      if (lane == k) {
-        b[q] = xk;
-      } else if (lane < k) {
-        b[q] = fmaf(-tk, xk, b[q]);
+  for (int p = 0; p < P; ++p) row[p] = M + (32 * p + lane < R ? 32 * p + lane : 0) * rs;
+#pragma unroll
+  for (int s = P - 1; s >= 0; --s) {
+    const int kend = 32 * s + 32 < R ? 32 * s + 32 : R;
+#pragma unroll 2
+    for (int k = kend - 1; k >= 32 * s; --k) {
+      const int src = k - 32 * s;
+      float tk[P];
+#pragma unroll
+      for (int p = 0; p <= s; ++p) tk[p] = 32 * p + lane < R ? row[p][k * cs] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < kNB; ++q) {
+        const float xk = __shfl_sync(kFull, UNIT ? b[s][q] : b[s][q] * rdiag[s], src);
+        if (lane == src) {
+          b[s][q] = xk;
+        } else if (lane < src) {
+          b[s][q] = fmaf(-tk[s], xk, b[s][q]);
+        }
+#pragma unroll
+        for (int p = 0; p < s; ++p) b[p][q] = fmaf(-tk[p], xk, b[p][q]);
       }
     }
   }
 }
 
-// Right-looking Cholesky of the lower triangle of the R x R shared matrix A
-// (leading dim ld) in place, spread over the whole CTA with one barrier per
-// step: step k subtracts A[i][k] A[j][k] / A[k][k] from the trailing lower
-// triangle (it only reads column k, which no thread writes during the step);
-// the columns are scaled to L[i][k] = A[i][k] / sqrt(A[k][k]) at the end.
-// dinv[i] = 1 / L_ii; the upper triangle is zeroed.  All threads call it.
+// rd[p] = v[32 p + lane] (1 past R).
 template <int R>
-__device__ __forceinline__ void cholesky_block(float* A, int ld, float* dinv) {
+__device__ __forceinline__ void lane_rows(const float* v, float (&rd)[rows_per_lane<R>()]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int p = 0; p < rows_per_lane<R>(); ++p) rd[p] = 32 * p + lane < R ? v[32 * p + lane] : 1.0f;
+}
+
+// Register tiles: thread (ty, tx) of the CTA's 16 x 16 grid owns the
+// elements (ty + 16 a, tx + 16 b), a, b < R / 16, of an R x R matrix.
+template <int R>
+__device__ __forceinline__ void tile_load(const float* A, int ld, float (&g)[R / 16][R / 16], bool lower_only) {
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+  for (int a = 0; a < R / 16; ++a)
+#pragma unroll
+    for (int b = 0; b < R / 16; ++b) {
+      const int i = ty + 16 * a, j = tx + 16 * b;
+      g[a][b] = (!lower_only || j <= i) ? A[i * ld + j] : 0.0f;
+    }
+}
+template <int R>
+__device__ __forceinline__ void tile_store(float* A, int ld, const float (&g)[R / 16][R / 16]) {
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+  for (int a = 0; a < R / 16; ++a)
+#pragma unroll
+    for (int b = 0; b < R / 16; ++b) A[(ty + 16 * a) * ld + tx + 16 * b] = g[a][b];
+}
+
+// Right-looking Cholesky of the lower triangle of the R x R shared matrix A
+// (leading dim ld) in place, with the matrix in register tiles: step k
+// publishes column k (its owners write it to a double-buffered shared
+// vector, one barrier) and every thread subtracts A[i][k] A[j][k] / A[k][k]
+// from its trailing elements; column k is final after step k, and the
+// columns are scaled to L[i][k] = A[i][k] / sqrt(A[k][k]) at the end (0 above
+// the diagonal).  dinv[i] = 1 / L_ii.  buf holds 2 R floats.  All threads call it.
+template <int R>
+__device__ __forceinline__ void cholesky_block(float* A, int ld, float* dinv, float* buf) {
+  constexpr int T = R / 16;
   const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
   __syncthreads();
-  const int warp = tid >> 5, lane = tid & 31;
+  float g[T][T];
+  tile_load<R>(A, ld, g, true);
 #pragma unroll 1
   for (int k = 0; k < R - 1; ++k) {
-    const float rkk = 1.0f / A[k * ld + k];
-    // rows over warps, columns over lanes (R <= 32: one column pass)
-    const int j = k + 1 + lane;
-    const float ajk = j < R ? A[j * ld + k] : 0.0f;
-    for (int i = k + 1 + warp; i < R; i += kWWarps) {
-      if (j <= i) A[i * ld + j] = fmaf(-A[i * ld + k] * rkk, ajk, A[i * ld + j]);
+    float* col = buf + (k & 1) * R;
+    const int kb = k >> 4, kr = k & 15;
+    if (tx == kr) {
+#pragma unroll
+      for (int b = 0; b < T; ++b)
+        if (b == kb)
+#pragma unroll
+          for (int a = 0; a < T; ++a) col[ty + 16 * a] = g[a][b];
     }
     __syncthreads();
+    const float rkk = 1.0f / col[k];
+    float l[T], w[T];
+#pragma unroll
+    for (int a = 0; a < T; ++a) l[a] = ty + 16 * a > k ? col[ty + 16 * a] * rkk : 0.0f;
+#pragma unroll
+    for (int b = 0; b < T; ++b) w[b] = tx + 16 * b > k ? col[tx + 16 * b] : 0.0f;
+#pragma unroll
+    for (int a = 0; a < T; ++a)
+#pragma unroll
+      for (int b = 0; b < T; ++b) g[a][b] = fmaf(-l[a], w[b], g[a][b]);
   }
+  tile_store<R>(A, ld, g);
+  __syncthreads();
   for (int e = tid; e < R * R; e += kWThreads) {
     const int i = e / R, j = e - i * R;
     if (j < i) A[i * ld + j] = A[i * ld + j] / sqrtf(A[j * ld + j]);
@@ -111,27 +194,53 @@ __device__ __forceinline__ void cholesky_block(float* A, int ld, float* dinv) {
   __syncthreads();
 }
 
-// Doolittle LU without pivoting of the R x R shared matrix M in place, spread
-// over the CTA with one barrier per step: step k subtracts
-// M[i][k] M[k][j] / M[k][k] from the trailing block (reading only row and
-// column k, which no thread writes during the step); the unit lower factor
-// M[i][k] / M[k][k] is formed at the end.  uinv[i] = 1 / U_ii.  All threads call it.
+// Doolittle LU without pivoting of the R x R shared matrix M in place, with
+// the matrix in register tiles: step k publishes column k and row k
+// (double-buffered, one barrier) and every thread subtracts
+// M[i][k] M[k][j] / M[k][k] from its trailing elements; column k is final
+// after step k, and the unit lower factor M[i][k] / M[k][k] is formed at the
+// end.  uinv[i] = 1 / U_ii.  buf holds 4 R floats.  All threads call it.
 template <int R>
-__device__ __forceinline__ void lu_block(float* M, int ld, float* uinv) {
+__device__ __forceinline__ void lu_block(float* M, int ld, float* uinv, float* buf) {
+  constexpr int T = R / 16;
   const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
   __syncthreads();
-  const int warp = tid >> 5, lane = tid & 31;
+  float m[T][T];
+  tile_load<R>(M, ld, m, false);
 #pragma unroll 1
   for (int k = 0; k < R - 1; ++k) {
-    const float rkk = 1.0f / M[k * ld + k];
-    // rows over warps, columns over lanes (R <= 32: one column pass)
-    const int j = k + 1 + lane;
-    const float ukj = j < R ? M[k * ld + j] : 0.0f;
-    for (int i = k + 1 + warp; i < R; i += kWWarps) {
-      if (j < R) M[i * ld + j] = fmaf(-M[i * ld + k] * rkk, ukj, M[i * ld + j]);
+    float* col = buf + (k & 1) * 2 * R;
+    float* row = col + R;
+    const int kb = k >> 4, kr = k & 15;
+    if (tx == kr) {
+#pragma unroll
+      for (int b = 0; b < T; ++b)
+        if (b == kb)
+#pragma unroll
+          for (int a = 0; a < T; ++a) col[ty + 16 * a] = m[a][b];
+    }
+    if (ty == kr) {
+#pragma unroll
+      for (int a = 0; a < T; ++a)
+        if (a == kb)
+#pragma unroll
+          for (int b = 0; b < T; ++b) row[tx + 16 * b] = m[a][b];
     }
     __syncthreads();
+    const float rkk = 1.0f / row[k];
+    float l[T], u[T];
+#pragma unroll
+    for (int a = 0; a < T; ++a) l[a] = ty + 16 * a > k ? col[ty + 16 * a] * rkk : 0.0f;
+#pragma unroll
+    for (int b = 0; b < T; ++b) u[b] = tx + 16 * b > k ? row[tx + 16 * b] : 0.0f;
+#pragma unroll
+    for (int a = 0; a < T; ++a)
+#pragma unroll
+      for (int b = 0; b < T; ++b) m[a][b] = fmaf(-l[a], u[b], m[a][b]);
   }
+  tile_store<R>(M, ld, m);
+  __syncthreads();
   for (int e = tid; e < R * R; e += kWThreads) {
     const int i = e / R, k = e - i * R;
     if (i > k) M[i * ld + k] = M[i * ld + k] / M[k * ld + k];
@@ -140,18 +249,77 @@ __device__ __forceinline__ void lu_block(float* M, int ld, float* uinv) {
   __syncthreads();
 }
 
+// out(i, j) = sum_k a(i, k) b(k, j) for the R rows and `ncols` columns, as
+// register tiles (rows ty + 16 a, columns c0 + tx + 16 b in passes of 16 NB
+// columns), k ascending; store(i, j, acc) receives each result.
+// With SYNC the CTA synchronises before the stores (single pass only), so the
+// result may overwrite an operand.
+template <int R, int NB, bool SYNC = false, typename FA, typename FB, typename FS>
+__device__ __forceinline__ void tile_gemm(int ncols, int kdim, FA a_at, FB b_at, FS store) {
+  constexpr int T = R / 16;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  for (int c0 = 0; c0 < ncols; c0 += 16 * NB) {
+    float acc[T][NB];
+#pragma unroll
+    for (int a = 0; a < T; ++a)
+#pragma unroll
+      for (int b = 0; b < NB; ++b) acc[a][b] = 0.0f;
+#pragma unroll 2
+    for (int k = 0; k < kdim; ++k) {
+      float av[T], bv[NB];
+#pragma unroll
+      for (int a = 0; a < T; ++a) av[a] = a_at(ty + 16 * a, k);
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const int j = c0 + tx + 16 * b;
+        bv[b] = j < ncols ? b_at(k, j) : 0.0f;
+      }
+#pragma unroll
+      for (int a = 0; a < T; ++a)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+    }
+    if (SYNC) __syncthreads();
+#pragma unroll
+    for (int a = 0; a < T; ++a)
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const int j = c0 + tx + 16 * b;
+        if (j < ncols) store(ty + 16 * a, j, acc[a][b]);
+      }
+  }
+}
+
+// Columns per register-tile pass: R x R products use all R columns at once.
+template <int R>
+__host__ __device__ constexpr int square_nb() {
+  return R / 16;
+}
+
 // Columns [c0, c0 + kNB) of the R x d operand X (row-major, leading dim xld)
 // into / out of the lane = row layout; columns past cend read as zero.
-__device__ __forceinline__ void get_cols(const float* X, int xld, int R, int c0, int cend, float (&b)[kNB]) {
+template <int R>
+__device__ __forceinline__ void get_cols(const float* X, int xld, int c0, int cend,
+                                         float (&b)[rows_per_lane<R>()][kNB]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int q = 0; q < kNB; ++q) b[q] = (lane < R && c0 + q < cend) ? X[lane * xld + c0 + q] : 0.0f;
+  for (int p = 0; p < rows_per_lane<R>(); ++p) {
+    const int row = 32 * p + lane;
+#pragma unroll
+    for (int q = 0; q < kNB; ++q) b[p][q] = (row < R && c0 + q < cend) ? X[row * xld + c0 + q] : 0.0f;
+  }
 }
-__device__ __forceinline__ void put_cols(float* X, int xld, int R, int c0, int cend, const float (&b)[kNB]) {
+template <int R>
+__device__ __forceinline__ void put_cols(float* X, int xld, int c0, int cend,
+                                         const float (&b)[rows_per_lane<R>()][kNB]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int q = 0; q < kNB; ++q)
-    if (lane < R && c0 + q < cend) X[lane * xld + c0 + q] = b[q];
+  for (int p = 0; p < rows_per_lane<R>(); ++p) {
+    const int row = 32 * p + lane;
+#pragma unroll
+    for (int q = 0; q < kNB; ++q)
+      if (row < R && c0 + q < cend) X[row * xld + c0 + q] = b[p][q];
+  }
 }
 
 // The column range of warp w when `cols` columns are split over the CTA.
@@ -162,21 +330,32 @@ __device__ __forceinline__ void warp_cols(int cols, int& c_begin, int& c_end) {
   c_end = min(cols, c_begin + per);
 }
 
-// Ps[m] = sum over chunks of P[ch * stride + m], m < stride (a multiple of 4),
-// in float4 steps: every load is coalesced and independent of the others.
-__device__ __forceinline__ void sum_partials(const float* P, int nchunks, int64_t stride, float* Ps) {
-  const int n4 = static_cast<int>(stride / 4);
-  const float4* P4 = reinterpret_cast<const float4*>(P);
-  for (int e = threadIdx.x; e < n4; e += kWThreads) {
-    float4 acc = __ldg(P4 + e);
+__device__ __forceinline__ void add4(float4& a, const float4 b) {
+  a.x += b.x;
+  a.y += b.y;
+  a.z += b.z;
+  a.w += b.w;
+}
+
+// Chunk partials [nchunks][2R][cols] (rows R.. hold the low halves): element
+// e of the first R rows summed over the chunks, high and low rows separately,
+// in float4 steps (every load coalesced and independent of the others).
+// fn(row, col, hi4, lo4) receives the four columns starting at col.
+template <int R, typename Fn>
+__device__ __forceinline__ void sum_chunks(const float* partial, int nchunks, int cols, Fn fn) {
+  const int c4 = cols / 4;
+  const int64_t lo = static_cast<int64_t>(R) * c4;
+  const int64_t stride = 2 * lo;
+  const float4* P4 = reinterpret_cast<const float4*>(partial);
+  for (int e = threadIdx.x; e < R * c4; e += kWThreads) {
+    float4 hi = __ldg(P4 + e);
+    float4 lw = __ldg(P4 + lo + e);
     for (int ch = 1; ch < nchunks; ++ch) {
-      const float4 v = __ldg(P4 + static_cast<int64_t>(ch) * n4 + e);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+      add4(hi, __ldg(P4 + ch * stride + e));
+      add4(lw, __ldg(P4 + ch * stride + lo + e));
     }
-    reinterpret_cast<float4*>(Ps)[e] = acc;
+    const int row = e / c4;
+    fn(row, (e - row * c4) * 4, hi, lw);
   }
 }
 
@@ -197,18 +376,19 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 template <int R>
 __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const SolveFwdArgs a) {
   constexpr int LD = R + 1;
+  constexpr int P = rows_per_lane<R>();
   extern __shared__ __align__(16) float fsm[];
   const int d = a.d;
   const int XLD = d + 1;
   float* L = fsm;              // [R][LD]
-  float* Th = L + R * LD;      // [R][LD]
+  float* Th = L + R * LD;      // [R][LD] low Gram half, then Theta
   float* Mm = Th + R * LD;     // [R][LD]
   float* Zs = Mm + R * LD;     // [R][XLD]  S, then Z
   float* fdiag = Zs + R * XLD; // [R]
   float* dinv = fdiag + R;     // [R] 1 / L_ii
   float* uinv = dinv + R;      // [R] 1 / U_ii
   float* Ws = uinv + R;        // [d][R + 1] W_drive of this head
-  float* Ps = fsm + ((static_cast<int>(Ws - fsm) + d * LD + 3) & ~3);  // [2R][R + dt] summed partials
+  float* buf = Ws + d * LD;    // [4R] pivot broadcast of the factorisations
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
   const int64_t b = bh / a.H;
@@ -224,33 +404,41 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
 
   const float* Wd = a.drive + static_cast<int64_t>(h) * d * R;
   for (int idx = tid; idx < d * R; idx += kWThreads) Ws[(idx / R) * LD + idx % R] = Wd[idx];
-  // 1. Sum the chunk partials (coalesced float4 reads, ndt == 1), then
-  //    G = (hh + lh + lh^T)/n + I (lower triangle) and S = (hC + lC)/sqrt(n).
-  sum_partials(pbase, a.nchunks, pstride, Ps);
+  // 1. Sum the chunk partials (ndt == 1): L <- hh + lh, Th <- lh, S = (hC + lC)/sqrt(n);
+  //    then G = (hh + lh + lh^T)/n + I on the lower triangle.
+  sum_chunks<R>(pbase, a.nchunks, NC, [&](int i, int c, float4 hi, float4 lo) {
+    const float hv[4] = {hi.x, hi.y, hi.z, hi.w};
+    const float lv[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int cc = c + u;
+      if (cc < R) {
+        L[i * LD + cc] = hv[u] + lv[u];
+        Th[i * LD + cc] = lv[u];
+      } else if (cc - R < d) {
+        Zs[i * XLD + cc - R] = (hv[u] + lv[u]) * rsn;
+      }
+    }
+  });
   __syncthreads();
   for (int idx = tid; idx < R * R; idx += kWThreads) {
     const int i = idx / R, k = idx % R;
     if (k > i) continue;
-    const float s = Ps[i * NC + k] + Ps[(R + i) * NC + k] + Ps[(R + k) * NC + i];
-    L[i * LD + k] = s * (rsn * rsn) + (i == k ? 1.0f : 0.0f);
+    L[i * LD + k] = (L[i * LD + k] + Th[k * LD + i]) * (rsn * rsn) + (i == k ? 1.0f : 0.0f);
   }
-  for (int idx = tid; idx < R * d; idx += kWThreads) {
-    const int i = idx / d, col = idx % d;
-    Zs[i * XLD + col] = (Ps[i * NC + R + col] + Ps[(R + i) * NC + R + col]) * rsn;
-  }
-  __syncthreads();
   // 2. Cholesky
-  cholesky_block<R>(L, LD, dinv);
+  cholesky_block<R>(L, LD, dinv, buf);
   // 3. Z = L^{-1} S (columns over the warps)
   {
-    const float rd = lane < R ? dinv[lane] : 1.0f;
+    float rd[P];
+    lane_rows<R>(dinv, rd);
     int cb, ce;
     warp_cols(d, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[kNB];
-      get_cols(Zs, XLD, R, c0, ce, x);
+      float x[P][kNB];
+      get_cols<R>(Zs, XLD, c0, ce, x);
       trsv_lower<R, false>(L, LD, 1, rd, x);
-      put_cols(Zs, XLD, R, c0, ce, x);
+      put_cols<R>(Zs, XLD, c0, ce, x);
     }
   }
   __syncthreads();
@@ -260,28 +448,25 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
   }
   // 4. Theta = base + Z W_drive / sqrt(n);  F diagonal
   const float* base = a.base + static_cast<int64_t>(h) * R * R;
-  for (int idx = tid; idx < R * R; idx += kWThreads) {
-    const int i = idx / R, jj = idx % R;
-    float s = 0.0f;
-    for (int c = 0; c < d; ++c) s = fmaf(Zs[i * XLD + c], Ws[c * LD + jj], s);
-    Th[i * LD + jj] = base[idx] + s * rsn;
-  }
+  tile_gemm<R, square_nb<R>()>(
+      R, d, [&](int i, int c) { return Zs[i * XLD + c]; }, [&](int c, int j) { return Ws[c * LD + j]; },
+      [&](int i, int j, float acc) { Th[i * LD + j] = base[i * R + j] + acc * rsn; });
   __syncthreads();
   for (int i = tid; i < R; i += kWThreads) fdiag[i] = softplus20(Th[i * LD + i] + kSoftplusOneOffset);
   __syncthreads();
   // 5. M = I + F F^T + Omega
+  //    (F: strict lower triangle of Theta, softplus diagonal, zero above; built in Mm first)
   for (int idx = tid; idx < R * R; idx += kWThreads) {
-    const int i = idx / R, jj = idx % R;
-    const int kmax = min(i, jj);
-    float s = 0.0f;
-    for (int k = 0; k <= kmax; ++k) {
-      const float fi = k < i ? Th[i * LD + k] : fdiag[i];
-      const float fj = k < jj ? Th[jj * LD + k] : fdiag[jj];
-      s += fi * fj;
-    }
-    const float omega = i < jj ? Th[i * LD + jj] : (i > jj ? -Th[jj * LD + i] : 0.0f);
-    Mm[i * LD + jj] = (i == jj ? 1.0f : 0.0f) + s + omega;
+    const int i = idx / R, k = idx % R;
+    Mm[i * LD + k] = k < i ? Th[i * LD + k] : (k == i ? fdiag[i] : 0.0f);
   }
+  __syncthreads();
+  tile_gemm<R, square_nb<R>(), true>(
+      R, R, [&](int i, int k) { return Mm[i * LD + k]; }, [&](int k, int j) { return Mm[j * LD + k]; },
+      [&](int i, int j, float acc) {
+        const float omega = i < j ? Th[i * LD + j] : (i > j ? -Th[j * LD + i] : 0.0f);
+        Mm[i * LD + j] = (i == j ? 1.0f : 0.0f) + acc + omega;
+      });
   __syncthreads();
   if (tape != nullptr) {
     for (int idx = tid; idx < R * R; idx += kWThreads) {
@@ -292,7 +477,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     if (tid == 0) tape[tl.n] = n;
   }
   // 6. LU
-  lu_block<R>(Mm, LD, uinv);
+  lu_block<R>(Mm, LD, uinv, buf);
   if (tape != nullptr) {
     for (int idx = tid; idx < R * R; idx += kWThreads) tape[tl.LU + idx] = Mm[(idx / R) * LD + idx % R];
   }
@@ -304,27 +489,38 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
   uint8_t* rm = reinterpret_cast<uint8_t*>(a.rmat + bh * a.d_pad * R);
   constexpr uint32_t RSBO = R * 16;
   {
-    const float ru = lane < R ? uinv[lane] : 1.0f;
-    const float rd = lane < R ? dinv[lane] : 1.0f;
+    float ru[P], rd[P], one[P];
+    lane_rows<R>(uinv, ru);
+    lane_rows<R>(dinv, rd);
+#pragma unroll
+    for (int p = 0; p < P; ++p) one[p] = 1.0f;
     int cb, ce;
     warp_cols(d, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float z[kNB], u[kNB];
-      get_cols(Zs, XLD, R, c0, ce, z);
+      float z[P][kNB], u[P][kNB];
+      get_cols<R>(Zs, XLD, c0, ce, z);
 #pragma unroll
-      for (int q = 0; q < kNB; ++q) u[q] = z[q];
-      trsv_lower<R, true>(Mm, LD, 1, 1.0f, u);   // unit lower factor of M
-      trsv_upper<R, false>(Mm, LD, 1, ru, u);    // U
-      float x[kNB];
+      for (int p = 0; p < P; ++p)
 #pragma unroll
-      for (int q = 0; q < kNB; ++q) x[q] = 2.0f * u[q] - (1.0f + eta) * z[q];
-      trsv_upper<R, false>(L, 1, LD, rd, x);     // L^T
+        for (int q = 0; q < kNB; ++q) u[p][q] = z[p][q];
+      trsv_lower<R, true>(Mm, LD, 1, one, u);   // unit lower factor of M
+      trsv_upper<R, false>(Mm, LD, 1, ru, u);   // U
+      float x[P][kNB];
 #pragma unroll
-      for (int q = 0; q < kNB; ++q) {
-        const int col = c0 + q;
-        if (lane < R && col < ce) {
-          if (tape != nullptr) tape[tl.U + static_cast<int64_t>(lane) * d + col] = u[q];
-          *reinterpret_cast<bf16*>(rm + kmajor_offset(col, lane, RSBO)) = __float2bfloat16_rn(x[q] * rsn);
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) x[p][q] = 2.0f * u[p][q] - (1.0f + eta) * z[p][q];
+      trsv_upper<R, false>(L, 1, LD, rd, x);    // L^T
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const int row = 32 * p + lane;
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) {
+          const int col = c0 + q;
+          if (row < R && col < ce) {
+            if (tape != nullptr) tape[tl.U + static_cast<int64_t>(row) * d + col] = u[p][q];
+            *reinterpret_cast<bf16*>(rm + kmajor_offset(col, row, RSBO)) = __float2bfloat16_rn(x[p][q] * rsn);
+          }
         }
       }
     }
@@ -344,15 +540,16 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
 template <int R>
 __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const SolveBwdArgs a) {
   constexpr int LD = R + 1;
+  constexpr int P = rows_per_lane<R>();
   extern __shared__ __align__(16) float fsm[];
   const int d = a.d;
   const int XLD = d + 1;
   float* L = fsm;               // [R][LD]
-  float* Mm = L + R * LD;       // [R][LD] packed LU
+  float* Mm = L + R * LD;       // [R][LD] packed LU; after pass A dTheta, then E, then X^T
   float* Th = Mm + R * LD;      // [R][LD]
   float* dK = Th + R * LD;      // [R][LD] dK, then dTheta, then Psi
-  float* E = dK + R * LD;       // [R][LD]
-  float* X1 = E + R * LD;       // [R][XLD] D
+  float* E = Mm;
+  float* X1 = dK + R * LD;      // [R][XLD] D
   float* X2 = X1 + R * XLD;     // [R][XLD] lambda, then dZ
   float* X3 = X2 + R * XLD;     // [R][XLD] U, then M'
   float* X4 = X3 + R * XLD;     // [R][XLD] Z
@@ -360,7 +557,6 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   float* dinv = fdiag + R;      // [R] 1 / L_ii
   float* uinv = dinv + R;       // [R] 1 / U_ii
   float* Ws = uinv + R;         // [d][R + 1] W_drive of this head
-  float* Ps = fsm + ((static_cast<int>(Ws - fsm) + d * LD + 3) & ~3);  // [2R][dt] summed partials
   __shared__ float red[kWWarps];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
@@ -382,11 +578,15 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
     Mm[i * LD + jj] = tape[tl.LU + idx];
     Th[i * LD + jj] = tape[tl.Theta + idx];
   }
-  sum_partials(pbase, a.nchunks, pstride, Ps);
-  __syncthreads();
+  // X1 = A'^T dY summed over the chunks (high + low halves)
+  sum_chunks<R>(pbase, a.nchunks, NC, [&](int i, int c, float4 hi, float4 lo) {
+    const float v[4] = {hi.x + lo.x, hi.y + lo.y, hi.z + lo.z, hi.w + lo.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c + u < d) X1[i * XLD + c + u] = v[u];
+  });
   for (int idx = tid; idx < R * d; idx += kWThreads) {
     const int i = idx / d, col = idx % d;
-    X1[i * XLD + col] = Ps[i * NC + col] + Ps[(R + i) * NC + col];
     X3[i * XLD + col] = tape[tl.U + static_cast<int64_t>(i) * d + col];
     X4[i * XLD + col] = tape[tl.Z + static_cast<int64_t>(i) * d + col];
   }
@@ -400,25 +600,30 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
 
   // Pass A: D = L^{-1} X1 / sqrt(n);  lam = M^{-T} (2 D) = L_u^{-T} U^{-T} (2 D)
   {
-    const float rd = lane < R ? dinv[lane] : 1.0f;
-    const float ru = lane < R ? uinv[lane] : 1.0f;
+    float rd[P], ru[P], one[P];
+    lane_rows<R>(dinv, rd);
+    lane_rows<R>(uinv, ru);
+#pragma unroll
+    for (int p = 0; p < P; ++p) one[p] = 1.0f;
     int cb, ce;
     warp_cols(d, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[kNB];
-      get_cols(X1, XLD, R, c0, ce, x);
+      float x[P][kNB];
+      get_cols<R>(X1, XLD, c0, ce, x);
       trsv_lower<R, false>(L, LD, 1, rd, x);
-      float lam[kNB];
+      float lam[P][kNB];
 #pragma unroll
-      for (int q = 0; q < kNB; ++q) {
-        x[q] *= rsn;
-        lam[q] = 2.0f * x[q];
-      }
-      put_cols(X1, XLD, R, c0, ce, x);
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) {
+          x[p][q] *= rsn;
+          lam[p][q] = 2.0f * x[p][q];
+        }
+      put_cols<R>(X1, XLD, c0, ce, x);
       // columns of the packed LU: U^T (entries j <= i), unit L^T (entries j > i)
       trsv_lower<R, false>(Mm, 1, LD, ru, lam);  // U^T y = 2D
-      trsv_upper<R, true>(Mm, 1, LD, 1.0f, lam); // L_u^T lam = y
-      put_cols(X2, XLD, R, c0, ce, lam);
+      trsv_upper<R, true>(Mm, 1, LD, one, lam);  // L_u^T lam = y
+      put_cols<R>(X2, XLD, c0, ce, lam);
     }
   }
   __syncthreads();
@@ -428,29 +633,28 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
     dz_dot = fmaf(X1[i * XLD + col], X4[i * XLD + col], dz_dot);
   }
   // dK = -lam U^T
+  tile_gemm<R, square_nb<R>()>(
+      R, d, [&](int i, int c) { return X2[i * XLD + c]; }, [&](int c, int j) { return X3[j * XLD + c]; },
+      [&](int i, int j, float acc) { dK[i * LD + j] = -acc; });
+  __syncthreads();
+  // dTheta through K = F F^T + Omega (into E, then back into dK):
+  //   i < j: dK_ij - dK_ji;  i >= j: sum_{k >= j} (dK_ik + dK_ki) F_kj (times softplus' on the diagonal)
   for (int idx = tid; idx < R * R; idx += kWThreads) {
-    const int i = idx / R, jj = idx % R;
-    float s = 0.0f;
-    for (int c = 0; c < d; ++c) s = fmaf(X2[i * XLD + c], X3[jj * XLD + c], s);
-    dK[i * LD + jj] = -s;
+    const int k = idx / R, j = idx % R;
+    E[k * LD + j] = k > j ? Th[k * LD + j] : (k == j ? fdiag[j] : 0.0f);
   }
   __syncthreads();
-  // dTheta through K = F F^T + Omega (into E, then back into dK)
-  for (int idx = tid; idx < R * R; idx += kWThreads) {
-    const int i = idx / R, jj = idx % R;
-    float v;
-    if (i < jj) {
-      v = dK[i * LD + jj] - dK[jj * LD + i];
-    } else {
-      float s = 0.0f;
-      for (int k = jj; k < R; ++k) {
-        const float f = k == jj ? fdiag[jj] : Th[k * LD + jj];
-        s += (dK[i * LD + k] + dK[k * LD + i]) * f;
-      }
-      v = i == jj ? s * softplus20_derivative(Th[i * LD + i] + kSoftplusOneOffset) : s;
-    }
-    E[i * LD + jj] = v;
-  }
+  tile_gemm<R, square_nb<R>(), true>(
+      R, R, [&](int i, int k) { return dK[i * LD + k] + dK[k * LD + i]; }, [&](int k, int j) { return E[k * LD + j]; },
+      [&](int i, int j, float acc) {
+        float v;
+        if (i < j) {
+          v = dK[i * LD + j] - dK[j * LD + i];
+        } else {
+          v = i == j ? acc * softplus20_derivative(Th[i * LD + i] + kSoftplusOneOffset) : acc;
+        }
+        E[i * LD + j] = v;
+      });
   __syncthreads();
   for (int idx = tid; idx < R * R; idx += kWThreads) {
     const int i = idx / R, jj = idx % R;
@@ -460,28 +664,22 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   }
   __syncthreads();
   // Pass B: dZ (X2), M' = 2U - (1+eta) Z (X3), drive-gradient partial Z^T dTheta / sqrt(n)
-  for (int idx = tid; idx < R * d; idx += kWThreads) {
-    const int i = idx / d, col = idx % d;
-    const float* wrow = Ws + col * LD;
-    float s = 0.0f;
-    for (int jj = 0; jj < R; ++jj) s = fmaf(dK[i * LD + jj], wrow[jj], s);
-    X2[i * XLD + col] = X2[i * XLD + col] - (1.0f + eta) * X1[i * XLD + col] + s * rsn;
-    X3[i * XLD + col] = 2.0f * X3[i * XLD + col] - (1.0f + eta) * X4[i * XLD + col];
-  }
-  for (int idx = tid; idx < d * R; idx += kWThreads) {
-    const int col = idx / R, jj = idx % R;
-    float s = 0.0f;
-    for (int i = 0; i < R; ++i) s = fmaf(X4[i * XLD + col], dK[i * LD + jj], s);
-    a.gdrive[(bh * d + col) * R + jj] = s * rsn;
-  }
+  tile_gemm<R, 2>(
+      d, R, [&](int i, int jj) { return dK[i * LD + jj]; }, [&](int jj, int col) { return Ws[col * LD + jj]; },
+      [&](int i, int col, float acc) {
+        X2[i * XLD + col] = X2[i * XLD + col] - (1.0f + eta) * X1[i * XLD + col] + acc * rsn;
+        X3[i * XLD + col] = 2.0f * X3[i * XLD + col] - (1.0f + eta) * X4[i * XLD + col];
+      });
+  tile_gemm<R, 2>(
+      d, R, [&](int jj, int i) { return dK[i * LD + jj]; }, [&](int i, int col) { return X4[i * XLD + col]; },
+      [&](int jj, int col, float acc) { a.gdrive[(bh * d + col) * R + jj] = acc * rsn; });
   __syncthreads();
-  // E = M' D^T + dZ Z^T
-  for (int idx = tid; idx < R * R; idx += kWThreads) {
-    const int i = idx / R, k = idx % R;
-    float s = 0.0f;
-    for (int c = 0; c < d; ++c) s += X3[i * XLD + c] * X1[k * XLD + c] + X2[i * XLD + c] * X4[k * XLD + c];
-    E[i * LD + k] = s;
-  }
+  // E = M' D^T + dZ Z^T  (k < d: the first product, k >= d: the second)
+  tile_gemm<R, square_nb<R>()>(
+      R, 2 * d,
+      [&](int i, int k) { return k < d ? X3[i * XLD + k] : X2[i * XLD + k - d]; },
+      [&](int k, int j) { return k < d ? X1[j * XLD + k] : X4[j * XLD + k - d]; },
+      [&](int i, int j, float acc) { E[i * LD + j] = acc; });
   // R_d = L^{-T} M' / sqrt(n) -> B1y,  R_z = L^{-T} dZ / sqrt(n) -> B1c and B2
   uint8_t* b1y = reinterpret_cast<uint8_t*>(a.b1y + bh * R * a.d_pad);
   uint8_t* b1c = reinterpret_cast<uint8_t*>(a.b1c + bh * R * a.d_pad);
@@ -489,23 +687,28 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   const uint32_t SBO_Y = static_cast<uint32_t>(a.d_pad) * 16;
   constexpr uint32_t SBO_R = R * 16;
   {
-    const float rd = lane < R ? dinv[lane] : 1.0f;
+    float rd[P];
+    lane_rows<R>(dinv, rd);
     int cb, ce;
     warp_cols(d, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float xm[kNB], xz[kNB];
-      get_cols(X3, XLD, R, c0, ce, xm);
-      get_cols(X2, XLD, R, c0, ce, xz);
+      float xm[P][kNB], xz[P][kNB];
+      get_cols<R>(X3, XLD, c0, ce, xm);
+      get_cols<R>(X2, XLD, c0, ce, xz);
       trsv_upper<R, false>(L, 1, LD, rd, xm);
       trsv_upper<R, false>(L, 1, LD, rd, xz);
 #pragma unroll
-      for (int q = 0; q < kNB; ++q) {
-        const int col = c0 + q;
-        if (lane < R && col < ce) {
-          *reinterpret_cast<bf16*>(b1y + kmajor_offset(lane, col, SBO_Y)) = __float2bfloat16_rn(xm[q] * rsn);
-          const bf16 rz = __float2bfloat16_rn(xz[q] * rsn);
-          *reinterpret_cast<bf16*>(b1c + kmajor_offset(lane, col, SBO_Y)) = rz;
-          *reinterpret_cast<bf16*>(b2 + kmajor_offset(col, lane, SBO_R)) = rz;
+      for (int p = 0; p < P; ++p) {
+        const int row = 32 * p + lane;
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) {
+          const int col = c0 + q;
+          if (row < R && col < ce) {
+            *reinterpret_cast<bf16*>(b1y + kmajor_offset(row, col, SBO_Y)) = __float2bfloat16_rn(xm[p][q] * rsn);
+            const bf16 rz = __float2bfloat16_rn(xz[p][q] * rsn);
+            *reinterpret_cast<bf16*>(b1c + kmajor_offset(row, col, SBO_Y)) = rz;
+            *reinterpret_cast<bf16*>(b2 + kmajor_offset(col, row, SBO_R)) = rz;
+          }
         }
       }
     }
@@ -526,24 +729,27 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   }
   __syncthreads();
   {
-    const float rd = lane < R ? dinv[lane] : 1.0f;
+    float rd[P];
+    lane_rows<R>(dinv, rd);
     int cb, ce;
     warp_cols(R, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[kNB];
-      get_cols(dK, LD, R, c0, ce, x);
+      float x[P][kNB];
+      get_cols<R>(dK, LD, c0, ce, x);
       trsv_upper<R, false>(L, 1, LD, rd, x);
       // store transposed: E[c][i] = X[i][c]
 #pragma unroll
-      for (int q = 0; q < kNB; ++q)
-        if (lane < R && c0 + q < ce) E[(c0 + q) * LD + lane] = x[q];
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < kNB; ++q)
+          if (32 * p + lane < R && c0 + q < ce) E[(c0 + q) * LD + 32 * p + lane] = x[p][q];
     }
     __syncthreads();
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[kNB];
-      get_cols(E, LD, R, c0, ce, x);
+      float x[P][kNB];
+      get_cols<R>(E, LD, c0, ce, x);
       trsv_upper<R, false>(L, 1, LD, rd, x);
-      put_cols(dK, LD, R, c0, ce, x);
+      put_cols<R>(dK, LD, c0, ce, x);
     }
   }
   __syncthreads();
@@ -558,67 +764,73 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   if (tid == 0) a.etadot[bh] = s;
 }
 
-// Shared-memory floats before the partial-sum block, rounded up to 4 floats.
 template <int R>
-int fwd_head(int d) {
-  return (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + 3) / 4 * 4;
+size_t fwd_smem(int d) {
+  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + 4 * R);
 }
 template <int R>
-int bwd_head(int d) {
-  return (5 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1) + 3) / 4 * 4;
+size_t bwd_smem(int d) {
+  return sizeof(float) * (4 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
 }
-// The partial-sum block holds one whole chunk partial: 2R rows of R + dt
-// (forward) or dt (backward) columns, dt = d_pad >= d.
+
 template <int R>
-size_t fwd_smem(int d, int dt) {
-  return sizeof(float) * (fwd_head<R>(d) + 2 * R * (R + dt));
+cudaError_t launch_fwd(const SolveFwdArgs& s, int64_t systems, cudaStream_t stream) {
+  const size_t smem = fwd_smem<R>(s.d);
+  cudaError_t e = allow_smem(reinterpret_cast<const void*>(&solve_forward_warp_kernel<R>), smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope("solve_fwd", stream);
+  solve_forward_warp_kernel<R><<<static_cast<unsigned>(systems), kWThreads, smem, stream>>>(s);
+  return cudaGetLastError();
 }
+
 template <int R>
-size_t bwd_smem(int d, int dt) {
-  return sizeof(float) * (bwd_head<R>(d) + 2 * R * dt);
+cudaError_t launch_bwd(const SolveBwdArgs& s, int64_t systems, cudaStream_t stream) {
+  const size_t smem = bwd_smem<R>(s.d);
+  cudaError_t e = allow_smem(reinterpret_cast<const void*>(&solve_backward_warp_kernel<R>), smem);
+  if (e != cudaSuccess) return e;
+  LaunchScope scope("solve_bwd", stream);
+  solve_backward_warp_kernel<R><<<static_cast<unsigned>(systems), kWThreads, smem, stream>>>(s);
+  return cudaGetLastError();
+}
+
+template <int R>
+bool fits(int d) {
+  return fwd_smem<R>(d) <= kWarpSolveSmemLimit && bwd_smem<R>(d) <= kWarpSolveSmemLimit;
 }
 
 }  // namespace
 
 bool warp_solves_usable(const Plan& p) {
-  // One content tile per chunk partial (d_pad <= 128), shared memory well inside one SM.
-  const int d = static_cast<int>(p.d), dt = static_cast<int>(p.dt);
-  return (p.R == 16 || p.R == 32) && p.ndt == 1 && fwd_smem<32>(d, dt) <= 160 * 1024 &&
-         bwd_smem<32>(d, dt) <= 160 * 1024;
+  // One content tile per chunk partial (ndt == 1), shared memory inside one SM.
+  if (p.ndt != 1) return false;
+  const int d = static_cast<int>(p.d);
+  switch (p.R) {
+    case 16: return fits<16>(d);
+    case 32: return fits<32>(d);
+    case 48: return fits<48>(d);
+    case 64: return fits<64>(d);
+    default: return false;
+  }
 }
 
 cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cudaStream_t stream) {
-  const int d = static_cast<int>(p.d);
-  const int dt = static_cast<int>(p.dt);
-  const size_t smem = p.R == 16 ? fwd_smem<16>(d, dt) : fwd_smem<32>(d, dt);
-  const void* fn = p.R == 16 ? reinterpret_cast<const void*>(&solve_forward_warp_kernel<16>)
-                             : reinterpret_cast<const void*>(&solve_forward_warp_kernel<32>);
-  cudaError_t e = allow_smem(fn, smem);
-  if (e != cudaSuccess) return e;
-  LaunchScope scope("solve_fwd", stream);
-  if (p.R == 16) {
-    solve_forward_warp_kernel<16><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
-  } else {
-    solve_forward_warp_kernel<32><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
+  switch (p.R) {
+    case 16: return launch_fwd<16>(s, p.BH, stream);
+    case 32: return launch_fwd<32>(s, p.BH, stream);
+    case 48: return launch_fwd<48>(s, p.BH, stream);
+    case 64: return launch_fwd<64>(s, p.BH, stream);
+    default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_solve_backward_warp(const Plan& p, const SolveBwdArgs& s, cudaStream_t stream) {
-  const int d = static_cast<int>(p.d);
-  const int dt = static_cast<int>(p.dt);
-  const size_t smem = p.R == 16 ? bwd_smem<16>(d, dt) : bwd_smem<32>(d, dt);
-  const void* fn = p.R == 16 ? reinterpret_cast<const void*>(&solve_backward_warp_kernel<16>)
-                             : reinterpret_cast<const void*>(&solve_backward_warp_kernel<32>);
-  cudaError_t e = allow_smem(fn, smem);
-  if (e != cudaSuccess) return e;
-  LaunchScope scope("solve_bwd", stream);
-  if (p.R == 16) {
-    solve_backward_warp_kernel<16><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
-  } else {
-    solve_backward_warp_kernel<32><<<static_cast<unsigned>(p.BH), kWThreads, smem, stream>>>(s);
+  switch (p.R) {
+    case 16: return launch_bwd<16>(s, p.BH, stream);
+    case 32: return launch_bwd<32>(s, p.BH, stream);
+    case 48: return launch_bwd<48>(s, p.BH, stream);
+    case 64: return launch_bwd<64>(s, p.BH, stream);
+    default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace lsso
