@@ -135,22 +135,22 @@ __device__ __forceinline__ void stage_row32(uint8_t* box, int r, const float (&v
       *reinterpret_cast<float4*>(box + r * 128 + ((c ^ (r & 7)) << 4)) =
           make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
     }
-    return;
-  }
+  } else {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int j = 8 * c;
-    uint4 w;
-    if (OUT == 0) {
-      w = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]), pack_bf16(v[j + 4], v[j + 5]),
-                     pack_bf16(v[j + 6], v[j + 7]));
-    } else {
-      __half2 h0 = __floats2half2_rn(v[j], v[j + 1]), h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
-      __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]), h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
-      w = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
-                     *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+    for (int c = 0; c < 4; ++c) {
+      const int j = 8 * c;
+      uint4 w;
+      if (OUT == 0) {
+        w = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]), pack_bf16(v[j + 4], v[j + 5]),
+                       pack_bf16(v[j + 6], v[j + 7]));
+      } else {
+        __half2 h0 = __floats2half2_rn(v[j], v[j + 1]), h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
+        __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]), h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
+        w = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                       *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+      }
+      *reinterpret_cast<uint4*>(box + r * 64 + ((c ^ ((r >> 1) & 3)) << 4)) = w;
     }
-    *reinterpret_cast<uint4*>(box + r * 64 + ((c ^ ((r >> 1) & 3)) << 4)) = w;
   }
 }
 
@@ -306,7 +306,6 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     // ---------------- epilogue: two warps per TMEM sub-partition
     const int sub = warp & 3;
     const int half = (warp - (2 + kConvWarps)) >> 2;
-    const int row = 32 * sub + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * sub) << 16);
     const bool vec = (a.ldo % (OUT == 2 ? 4 : 8)) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0;
     uint8_t* stage = sOut + (warp - (2 + kConvWarps)) * kEpiStage;

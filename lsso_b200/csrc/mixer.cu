@@ -1382,8 +1382,8 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   g.ntiles = static_cast<int>(p.ntiles);
   g.pos_batched = pos_batched;
   g.vec = bb.vec;
-  if (tiled) {
-    e = launch_grad_tiled(p, bb.grad_output, bb.projected, bb.phase16, bb.b1y, bb.b1c, bb.b1a, bb.b2, bb.eta_raw,
+  if (tiled && p.tiled_grad) {
+    e = launch_grad_tiled(p, bb.grad_output, bb.projected, bb.phase16, bb.b1y, bb.b1c, bb.b1a, bb.eta_raw,
                           bb.grad_projected, bb.etastat, bb.status, p.sms, stream);
   } else {
     const size_t gsm = grad_smem<R>(static_cast<int>(p.nb));

@@ -173,7 +173,7 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
 cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* phase, const bf16* rmat,
                                  const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream);
 cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase16, const bf16* b1y,
-                              const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
+                              const bf16* b1c, const bf16* b1a, const float* eta_raw, bf16* gproj,
                               float* etastat, int* status, int sm_count, cudaStream_t stream);
 
 // Register-resident warp solves for R <= 32 (solve.cu).

@@ -49,6 +49,7 @@ struct Plan {
   // whole 64-feature boxes (nrel / nval boxes); the moment pass sums `ct`
   // tiles per chunk.
   bool tiled;
+  bool tiled_grad;               // the gradient pass too (its slot is the largest)
   int hg, groups, nrel, nval, ct;
   int sms;                       // SM count the plan was made for
 };
@@ -73,8 +74,9 @@ inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
   } else if (kind == 2) {
     bytes = (nrel + nval) * kTileBox + phase + hg * d * R * 2;
   } else {
-    // the gradient kernel stages the tile's FP16 phase rows for its epilogue
-    bytes = (nrel + 2 * nval) * kTileBox + kTileTokens * R * 2 + hg * (3 * R * d + R * R) * 2;
+    // the gradient kernel stages the tile's FP16 phase rows for its epilogue and
+    // the per-head B1y, B1c (also read transposed, as B2) and B1a matrices
+    bytes = (nrel + 2 * nval) * kTileBox + kTileTokens * R * 2 + hg * (2 * R * d + R * R) * 2;
   }
   return (bytes + 1023) / 1024 * 1024;
 }
@@ -88,13 +90,15 @@ inline int tile_slots(int64_t slot_bytes) {
 // per-head kernels of mixer.cu).
 inline void plan_tiles(Plan& p, int sm_count) {
   p.tiled = false;
+  p.tiled_grad = false;
   const bool r_ok = p.R == 32 || p.R == 64;
   const bool d_ok = p.d == 32 || p.d == 64;
   if (!r_ok || !d_ok || (p.W % 8) != 0 || p.D != p.H * p.d) return;
   const int hg = static_cast<int>(64 / (p.R < p.d ? p.R : p.d));
   if (p.H % hg != 0) return;
-  for (int kind = 0; kind < 4; ++kind)
+  for (int kind = 0; kind < 3; ++kind)
     if (tile_slots(tile_slot_bytes(kind, p.R, p.d, hg)) < 2) return;
+  p.tiled_grad = tile_slots(tile_slot_bytes(3, p.R, p.d, hg)) >= 2;
   p.hg = hg;
   p.groups = static_cast<int>(p.H / hg);
   p.nrel = static_cast<int>(hg * p.R / 64);

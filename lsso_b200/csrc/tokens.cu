@@ -24,7 +24,8 @@
 //   moments_tile_kernel<R, false>  G/S partials  [hi|lo]^T [hi | C] per chunk of tiles
 //   moments_tile_kernel<R, true>   A'^T dY partials [hi|lo]^T dY
 //   readout_tile_kernel<R>         Y = eta C + A' R_d
-//   grad_tile_kernel<R>            dA' = dY B1y + C B1c + A' B1a (rotated back), dC = eta dY + A' B2,
+//   grad_tile_kernel<R>            dA' = dY B1y + C B1c + A' B1a (rotated back), dC = eta dY + A' B2
+//                                  (B2 = B1c^T, read from the B1c matrix as an MN-major operand),
 //                                  and the per-tile complement statistic sum(dY * C)
 //
 // Every wait is bounded (the status word records a timeout and all roles
@@ -53,7 +54,6 @@ constexpr int kThreadsT = (kEWarp0 + kEWarps) * 32;
 constexpr int kMXWarps = 12, kMEWarp0 = kXWarp0 + kMXWarps, kMEWarps = 4;
 constexpr int kMXThreads = kMXWarps * 32;
 constexpr int kMThreads = (kMEWarp0 + kMEWarps) * 32;
-constexpr int kMMaxChunks = (2 * kTileTokens * 8 + kMXThreads - 1) / kMXThreads;  // nrel <= 2
 constexpr size_t kSmemFloor = 120 * 1024;    // forces one CTA per SM (each allocates all of TMEM)
 
 struct TileArgs {
@@ -63,7 +63,6 @@ struct TileArgs {
   const bf16* m0;  // readout: R_d;  grad: B1y
   const bf16* m1;  // grad: B1c
   const bf16* m2;  // grad: B1a
-  const bf16* m3;  // grad: B2
   float* partial;  // moment partials [B*H][nchunks][2R][NC]
   float* etastat;  // [B*H][ntiles]
   int* status;
@@ -671,9 +670,12 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
   const int nloc = (a.items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                    static_cast<int>(gridDim.x);
   int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
-  // Operand matrices of the group's heads, each block contiguous per head.
+  // Operand matrices of the group's heads, each block contiguous per head.  B2
+  // (d x R, K-major) is B1c (R x d, K-major canonical) read as an MN-major
+  // operand: element (n, k) of B2 is element (k, n) of B1c, whose 8 x 8 core
+  // matrices are n-adjacent at 128 bytes and k-adjacent at d * 16 bytes.
   const uint32_t sz_y = static_cast<uint32_t>(R * d * 2), sz_a = static_cast<uint32_t>(R * R * 2);
-  const uint32_t off_y = 0, off_c = a.hg * sz_y, off_a = 2 * a.hg * sz_y, off_2 = off_a + a.hg * sz_a;
+  const uint32_t off_y = 0, off_c = a.hg * sz_y, off_a = 2 * a.hg * sz_y;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -706,14 +708,13 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
         bulk_load(smem_u32(mat + off_y), a.m0 + bh0 * R * d, a.hg * sz_y, bar);
         bulk_load(smem_u32(mat + off_c), a.m1 + bh0 * R * d, a.hg * sz_y, bar);
         bulk_load(smem_u32(mat + off_a), a.m2 + bh0 * R * R, a.hg * sz_a, bar);
-        bulk_load(smem_u32(mat + off_2), a.m3 + bh0 * d * R, a.hg * sz_y, bar);
         last_use[s] = u;
       }
       __syncwarp();
     }
   } else if (warp == 1) {
     const uint32_t idesc_r = make_idesc(128, R, false, false);
-    const uint32_t idesc_d = make_idesc(128, d, false, false);
+    const uint32_t idesc_d = make_idesc(128, d, false, true);
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
       const int s = i % a.slots, u = i / a.slots;
@@ -739,7 +740,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
             const int f = hl * R + 16 * ks;
             const uint64_t ad = make_desc_sw128(slot + (f >> 6) * kBox + (f & 63) * 2, 16, 1024);
             mma_bf16(da, ad, make_desc(mat + off_a + hl * sz_a + ks * 256, 128, R * 16), idesc_r, 1u);
-            mma_bf16(da + R, ad, make_desc(mat + off_2 + hl * sz_y + ks * 256, 128, R * 16), idesc_d,
+            mma_bf16(da + R, ad, make_desc(mat + off_c + hl * sz_y + ks * 32 * d, d * 16, 128), idesc_d,
                      ks > 0 ? 1u : 0u);
           }
         }
@@ -1005,7 +1006,7 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* 
 }
 
 cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase16, const bf16* b1y,
-                              const bf16* b1c, const bf16* b1a, const bf16* b2, const float* eta_raw, bf16* gproj,
+                              const bf16* b1c, const bf16* b1a, const float* eta_raw, bf16* gproj,
                               float* etastat, int* status, int sm_count, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   CUtensorMap tm_proj{}, tm_dy{}, tm_gproj{};
@@ -1017,13 +1018,12 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   a.m0 = b1y;
   a.m1 = b1c;
   a.m2 = b1a;
-  a.m3 = b2;
   a.etastat = etastat;
   a.off_val = p.nrel * kBox;
   a.off_aux = (p.nrel + p.nval) * kBox;
   a.off_ph = (p.nrel + 2 * p.nval) * kBox;
   a.off_mat = a.off_ph + static_cast<uint32_t>(kTT * p.R * 2);
-  const uint32_t mat = static_cast<uint32_t>(p.hg * (3 * p.R * p.d + p.R * p.R) * 2);
+  const uint32_t mat = static_cast<uint32_t>(p.hg * (2 * p.R * p.d + p.R * p.R) * 2);
   a.load_bytes = (p.nrel + 2 * p.nval) * kBox + mat;
   const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
   size_t smem = 0;

@@ -82,6 +82,8 @@ EXPANDED = [
     (1, 48, 2, 96, 33), (1, 64, 1, 33, 33), (1, 64, 1, 257, 33), (1, 16, 1, 17, 2048), (1, 32, 1, 17, 2048),
     (1, 48, 1, 17, 2048), (1, 64, 1, 17, 2048), (1, 16, 1, 17, 2017), (1, 64, 1, 17, 2017), (1, 64, 1, 17, 4096),
     (1, 32, 8, 32, 4096), (1, 16, 4, 32, 4776), (1, 32, 1, 17, 8193), (2, 64, 2, 384, 40), (1, 48, 3, 256, 70),
+    # head-group tile kernels: r = 64 with d = 32 (gradient pass per head), r = 64 / d = 64, r = 32 / d = 64
+    (2, 64, 2, 32, 300), (1, 64, 2, 64, 300), (1, 32, 2, 64, 300), (1, 64, 4, 32, 1100),
 ]
 
 
