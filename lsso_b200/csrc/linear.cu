@@ -391,19 +391,21 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
 // canonical tiles of BN rows: 64-wide K regions of BN rows x 128 bytes; row n
 // at (n/8)*1024 + (n%8)*128, its 16-byte chunk c stored at chunk c ^ (n%8).
 // Zero outside [Nout, K].
-__global__ void prep_weight_kernel(const float* __restrict__ w, int64_t Nout, int64_t K, int transposed, int BN,
-                                   int K_pad, int NT, uint8_t* __restrict__ out) {
-  const int64_t total = static_cast<int64_t>(NT) * BN * K_pad;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+__global__ void prep_weight_kernel(const float* __restrict__ w, int Nout, int K, int transposed, int BN, int K_pad,
+                                   int NT, uint8_t* __restrict__ out) {
+  // 32-bit index arithmetic: a weight tile set is far below 2^31 elements.
+  const int total = NT * BN * K_pad;
+  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;
-  const int64_t j = idx / (static_cast<int64_t>(BN) * K_pad);
-  const int64_t rem = idx % (static_cast<int64_t>(BN) * K_pad);
-  const int nl = static_cast<int>(rem / K_pad), k = static_cast<int>(rem % K_pad);
-  const int64_t n = j * BN + nl;
+  const int tile = BN * K_pad;
+  const int j = idx / tile;
+  const int rem = idx - j * tile;
+  const int nl = rem / K_pad, k = rem - nl * K_pad;
+  const int n = j * BN + nl;
   float v = 0.0f;
-  if (n < Nout && k < K) v = transposed ? w[static_cast<int64_t>(k) * Nout + n] : w[n * K + k];
+  if (n < Nout && k < K) v = transposed ? w[static_cast<int64_t>(k) * Nout + n] : w[static_cast<int64_t>(n) * K + k];
   const int kk = k % kBK;
-  const size_t off = static_cast<size_t>(j) * BN * K_pad * 2 + static_cast<size_t>(k / kBK) * BN * 128 +
+  const size_t off = static_cast<size_t>(j) * tile * 2 + static_cast<size_t>(k / kBK) * BN * 128 +
                      static_cast<size_t>(nl / 8) * 1024 + (nl % 8) * 128 + ((((kk * 2) / 16) ^ (nl % 8)) * 16) +
                      (kk * 2) % 16;
   *reinterpret_cast<__nv_bfloat16*>(out + off) = __float2bfloat16_rn(v);
@@ -724,8 +726,10 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   {
     const int64_t total = static_cast<int64_t>(p.NT) * p.BN * p.K_pad;
     LaunchScope scope("prep_weight", stream);
+    if (total >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
     prep_weight_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        c.weight, p.Nout, p.K, c.weight_transposed, p.BN, static_cast<int>(p.K_pad), p.NT, c.prep);
+        c.weight, static_cast<int>(p.Nout), static_cast<int>(p.K), c.weight_transposed, p.BN,
+        static_cast<int>(p.K_pad), p.NT, c.prep);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

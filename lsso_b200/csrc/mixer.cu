@@ -33,20 +33,24 @@ struct InvFreq {
   float v[32];
 };
 
-__global__ void phase_kernel(const float* __restrict__ pos, int64_t rows, int64_t N, int half, InvFreq f,
+// One thread per (token, frequency) of position rows blockIdx.y, + gridDim.y, ...; the
+// frequency table stays in parameter space (__grid_constant__), so indexing it
+// with the thread's frequency does not copy it to local memory.
+__global__ void phase_kernel(const float* __restrict__ pos, int64_t rows, int N, int half,
+                             const __grid_constant__ InvFreq f,
                              float2* __restrict__ out, __half2* __restrict__ out16) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = rows * N * half;
-  if (i >= total) return;
-  const int k = static_cast<int>(i % half);
-  const int64_t rt = i / half;  // row * N + t
-  const int64_t t = rt % N;
-  const float p = pos != nullptr ? pos[rt] : static_cast<float>(t) - 0.5f * static_cast<float>(N - 1);
-  float s, c;
-  sincosf(p * f.v[k], &s, &c);
-  const __half2 h = __floats2half2_rn(c, s);
-  out[i] = __half22float2(h);
-  if (out16 != nullptr) out16[i] = h;
+  const int i = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;  // t * half + k within the row
+  if (i >= N * half) return;
+  const int t = i / half, k = i - t * half;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const float p = pos != nullptr ? pos[row * N + t] : static_cast<float>(t) - 0.5f * static_cast<float>(N - 1);
+    float s, c;
+    sincosf(p * f.v[k], &s, &c);
+    const __half2 h = __floats2half2_rn(c, s);
+    const int64_t o = row * N * half + i;
+    out[o] = __half22float2(h);
+    if (out16 != nullptr) out16[o] = h;
+  }
 }
 
 // ============================================================================
@@ -1184,11 +1188,12 @@ static InvFreq inverse_frequencies(int R) {
 static cudaError_t launch_phase(const Plan& p, const float* pos, float2* table, __half2* table16,
                                 cudaStream_t stream) {
   const int half = static_cast<int>(p.R / 2);
-  const int64_t total = p.pos_rows * p.N * half;
   const int threads = 256;
+  const dim3 grid(static_cast<unsigned>(ceil_div(p.N * half, threads)),
+                  static_cast<unsigned>(p.pos_rows < 65535 ? p.pos_rows : 65535));
   LaunchScope scope("phase", stream);
-  phase_kernel<<<static_cast<unsigned>(ceil_div(total, threads)), threads, 0, stream>>>(pos, p.pos_rows, p.N, half,
-                                                                                         inverse_frequencies(static_cast<int>(p.R)), table, table16);
+  phase_kernel<<<grid, threads, 0, stream>>>(pos, p.pos_rows, static_cast<int>(p.N), half,
+                                             inverse_frequencies(static_cast<int>(p.R)), table, table16);
   return cudaGetLastError();
 }
 
