@@ -586,15 +586,19 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
   }
 }
 
-// C[m, c] = sum over splits (ascending) of the partial tiles, four adjacent
-// columns per thread with float4 reads in partial order (coalesced, and the
-// unrolled split loop keeps several loads in flight); written to dw[m, c]
-// ([Mdim, Ndim]) or, when the operands were swapped, to dw[c, m].
+// C[m, c] = sum over splits of the partial tiles, four adjacent columns per
+// group of kSplitLanes lanes: lane g sums splits g, g + 8, ... (float4 reads,
+// all independent, so a lane keeps its whole share in flight), then the eight
+// lane sums are combined by a fixed butterfly (deterministic order).  Written
+// to dw[m, c] ([Mdim, Ndim]) or, when the operands were swapped, to dw[c, m].
+constexpr int kSplitLanes = 8;
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int mtiles, int ntilesw, int BNW,
                                     int Mdim, int Ndim, int swapped, float* __restrict__ dw) {
-  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (q >= static_cast<int64_t>(Mdim) * Ndim / 4) return;
-  const int64_t idx = 4 * q;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t q = t / kSplitLanes;
+  const int g = static_cast<int>(t % kSplitLanes);
+  const bool live = q < static_cast<int64_t>(Mdim) * Ndim / 4;  // whole lane groups share this
+  const int64_t idx = 4 * (live ? q : 0);
   const int m = static_cast<int>(idx / Ndim), c = static_cast<int>(idx % Ndim);  // Ndim % 4 == 0
   const int tiles = mtiles * ntilesw;
   const int tile = (m / 128) * ntilesw + c / BNW;
@@ -602,14 +606,24 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int split
   const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(tile) * 128 * BNW + inner);
   const size_t stride4 = static_cast<size_t>(tiles) * 128 * BNW / 4;
   float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 8
-  for (int sp = 0; sp < splits; ++sp) {
-    const float4 v = __ldg(src + sp * stride4);
-    acc.x += v.x;
-    acc.y += v.y;
-    acc.z += v.z;
-    acc.w += v.w;
+  if (live) {
+#pragma unroll 4
+    for (int sp = g; sp < splits; sp += kSplitLanes) {
+      const float4 v = __ldg(src + sp * stride4);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
   }
+#pragma unroll
+  for (int o = 1; o < kSplitLanes; o <<= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+    acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+    acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+  }
+  if (!live || g != 0) return;
   if (swapped) {
     dw[static_cast<int64_t>(c) * Mdim + m] = acc.x;
     dw[static_cast<int64_t>(c + 1) * Mdim + m] = acc.y;
@@ -819,9 +833,9 @@ cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t st
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const int64_t quads = p.Mdim * p.Ndim / 4;
+  const int64_t lanes = p.Mdim * p.Ndim / 4 * kSplitLanes;
   LaunchScope scope("wgrad_reduce", stream);
-  wgrad_reduce_kernel<<<static_cast<unsigned>((quads + 255) / 256), 256, 0, stream>>>(
+  wgrad_reduce_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
       c.partial, p.splits, p.mtiles, p.ntilesw, p.BNW, static_cast<int>(p.Mdim), static_cast<int>(p.Ndim), p.swapped,
       c.dw);
   return cudaGetLastError();

@@ -210,16 +210,28 @@ __device__ __forceinline__ void fetch_phases(Phase4 (&ph)[kMaxChunks], const flo
 template <int R>
 __device__ __forceinline__ void rotate_boxes16(uint8_t* rel, int nrel, const uint8_t* rows, int tok0, int N, int xt) {
   const int nch = nrel * (kTT * 8) / kXThreads;
+  // In batches of four chunks, each read before any of it is written back.
 #pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    if (k < nch) {
-      int j, r, c;
-      chunk_coords(xt + k * kXThreads, j, r, c);
-      uint8_t* p = box_chunk(rel + j * kBox, r, c);
-      const Phase4 ph = phase_rows16(rows, r, tok0 + r, N, R, ((j * 64 + 8 * c) % R) >> 3);
-      float v[8];
-      rotate8(*reinterpret_cast<const uint4*>(p), ph, v);
-      *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
+  for (int k0 = 0; k0 < kMaxChunks; k0 += 4) {
+    uint4 in[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k0 + k < nch) {
+        int j, r, c;
+        chunk_coords(xt + (k0 + k) * kXThreads, j, r, c);
+        in[k] = *reinterpret_cast<const uint4*>(box_chunk(rel + j * kBox, r, c));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k0 + k < nch) {
+        int j, r, c;
+        chunk_coords(xt + (k0 + k) * kXThreads, j, r, c);
+        const Phase4 ph = phase_rows16(rows, r, tok0 + r, N, R, ((j * 64 + 8 * c) % R) >> 3);
+        float v[8];
+        rotate8(in[k], ph, v);
+        *reinterpret_cast<uint4*>(box_chunk(rel + j * kBox, r, c)) = pack8_bf16(v);
+      }
     }
   }
 }
@@ -228,15 +240,27 @@ __device__ __forceinline__ void rotate_boxes16(uint8_t* rel, int nrel, const uin
 template <int R>
 __device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase4 (&ph)[kMaxChunks], int xt) {
   const int nch = nrel * (kTT * 8) / kXThreads;
+  // In batches of four chunks, each read before any of it is written back.
 #pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    if (k < nch) {
-      int j, r, c;
-      chunk_coords(xt + k * kXThreads, j, r, c);
-      uint8_t* p = box_chunk(rel + j * kBox, r, c);
-      float v[8];
-      rotate8(*reinterpret_cast<const uint4*>(p), ph[k], v);
-      *reinterpret_cast<uint4*>(p) = pack8_bf16(v);
+  for (int k0 = 0; k0 < kMaxChunks; k0 += 4) {
+    uint4 in[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k0 + k < nch) {
+        int j, r, c;
+        chunk_coords(xt + (k0 + k) * kXThreads, j, r, c);
+        in[k] = *reinterpret_cast<const uint4*>(box_chunk(rel + j * kBox, r, c));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k0 + k < nch) {
+        int j, r, c;
+        chunk_coords(xt + (k0 + k) * kXThreads, j, r, c);
+        float v[8];
+        rotate8(in[k], ph[k0 + k], v);
+        *reinterpret_cast<uint4*>(box_chunk(rel + j * kBox, r, c)) = pack8_bf16(v);
+      }
     }
   }
 }
@@ -410,29 +434,45 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
           uint8_t* rel = slot + a.off_rel;
           uint8_t* op = slot + a.off_aux;
+          // In batches of three chunks, each read before any of it is written,
+          // so the shared-memory loads overlap instead of waiting behind stores.
 #pragma unroll
-          for (int kk = 0; kk < NCH; ++kk) {
-            const int idx = xt + kk * kMXThreads;
-            if (idx >= total) break;
-            int j, r, c;
-            chunk_coords(idx, j, r, c);
-            const int f = j * 64 + 8 * c;
-            const int hl = f / R, k0 = f % R;
-            uint8_t* src = box_chunk(rel + j * kBox, r, c);
-            float v[8];
-            rotate8(*reinterpret_cast<const uint4*>(src), ph[kk], v);
-            const uint4 hi = pack8_bf16(v);
-            const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
-            float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
-                           v[4] - h2.x, v[5] - h2.y, v[6] - h3.x, v[7] - h3.y};
-            if constexpr (kFused) {
-              *reinterpret_cast<uint4*>(src) = hi;                                        // hi in place
-              *reinterpret_cast<uint4*>(box_chunk(op + j * kBox, r, c)) = pack8_bf16(lo);  // lo, same position
-            } else {
-              uint8_t* ob = op + hl * kHead;
-              const int mh = k0, ml = R + k0;
-              *reinterpret_cast<uint4*>(box_chunk(ob + (mh >> 6) * kBox, r, (mh & 63) >> 3)) = hi;
-              *reinterpret_cast<uint4*>(box_chunk(ob + (ml >> 6) * kBox, r, (ml & 63) >> 3)) = pack8_bf16(lo);
+          for (int b0 = 0; b0 < NCH; b0 += 3) {
+            uint4 in[3];
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+              const int idx = xt + (b0 + q) * kMXThreads;
+              if (b0 + q < NCH && idx < total) {
+                int j, r, c;
+                chunk_coords(idx, j, r, c);
+                in[q] = *reinterpret_cast<const uint4*>(box_chunk(rel + j * kBox, r, c));
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+              const int kk = b0 + q;
+              const int idx = xt + kk * kMXThreads;
+              if (kk >= NCH || idx >= total) break;
+              int j, r, c;
+              chunk_coords(idx, j, r, c);
+              const int f = j * 64 + 8 * c;
+              const int hl = f / R, k0 = f % R;
+              uint8_t* src = box_chunk(rel + j * kBox, r, c);
+              float v[8];
+              rotate8(in[q], ph[kk], v);
+              const uint4 hi = pack8_bf16(v);
+              const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
+              float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
+                             v[4] - h2.x, v[5] - h2.y, v[6] - h3.x, v[7] - h3.y};
+              if constexpr (kFused) {
+                *reinterpret_cast<uint4*>(src) = hi;                                        // hi in place
+                *reinterpret_cast<uint4*>(box_chunk(op + j * kBox, r, c)) = pack8_bf16(lo);  // lo, same position
+              } else {
+                uint8_t* ob = op + hl * kHead;
+                const int mh = k0, ml = R + k0;
+                *reinterpret_cast<uint4*>(box_chunk(ob + (mh >> 6) * kBox, r, (mh & 63) >> 3)) = hi;
+                *reinterpret_cast<uint4*>(box_chunk(ob + (ml >> 6) * kBox, r, (ml & 63) >> 3)) = pack8_bf16(lo);
+              }
             }
           }
           fence_proxy_async();
