@@ -182,6 +182,58 @@ LSSO_API int lsso_forward_inference_noalloc(const void* projected, const float* 
                                             const float* valid_counts, int64_t B, int64_t N, int64_t H,
                                             int64_t D, int64_t R, void* mixed, void* stream);
 
+/* ---- Sequence-parallel halves (no counterpart in the reference).
+ *
+ * One sample's tokens may be split over several GPUs ("ranks"): the mixer's
+ * only cross-token quantities are the per-(sample, head) moment sums, so
+ * each rank runs the moment pass over its own tokens, the caller sums the
+ * moment buffers over the ranks (one all-reduce), and every rank then runs
+ * the solves and its own tokens' readout / gradient pass.  Every rank passes
+ * its own N (tokens it holds), the centered positions of those tokens taken
+ * from the whole sequence (required), and, to the finish calls, the counts of
+ * valid tokens over the whole sequence (required).  The workspace is the one
+ * of lsso_forward / lsso_backward for the rank's sizes.
+ *
+ * Elements (FP32) of the moment buffer: B*H*ndt*2R*(R + dt) forward,
+ * B*H*ndt*2R*dt backward (ndt, dt from the content width; independent of N,
+ * so equal on every rank holding the same samples). */
+LSSO_API size_t lsso_moment_elements(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int backward);
+
+/* Phase table and forward moment pass of this rank's tokens; writes the
+ * rank's moment sums to `moments` (16-byte aligned). */
+LSSO_API int lsso_forward_moments(const void* projected, const float* centered_positions, int positions_batched,
+                                  int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, float* moments,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Solves from the moment sums of all ranks and the readout of this rank's
+ * tokens; arguments otherwise as in lsso_forward (tape and pivots optional,
+ * together). */
+LSSO_API int lsso_forward_finish(const void* projected, const float* core_base_raw,
+                                 const float* core_drive_weight, const float* eta_raw,
+                                 const float* centered_positions, int positions_batched, const float* valid_counts,
+                                 int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, const float* moments,
+                                 void* mixed, float* tape, int32_t* pivots, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Backward moment pass of this rank's tokens (A'^T dY sums into `moments`). */
+LSSO_API int lsso_backward_moments(const void* grad_output, const void* projected, const float* centered_positions,
+                                   int positions_batched, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                                   float* moments, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward solves from the moment sums of all ranks, this rank's gradient
+ * pass and the parameter gradients.  The terms every rank computes
+ * identically from the shared moments (the whole gradient of core_base_raw
+ * and core_drive_weight, and the solve's part of eta_raw's) are multiplied by
+ * `redundant`: pass 1 on one rank and 0 on the others, so that the sum of the
+ * parameter gradients over the ranks counts them once.  Arguments otherwise
+ * as in lsso_backward. */
+LSSO_API int lsso_backward_finish(const void* grad_output, const void* projected, const float* core_drive_weight,
+                                  const float* eta_raw, const float* tape, const float* centered_positions,
+                                  int positions_batched, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                                  const float* moments, float redundant, void* grad_projected,
+                                  float* grad_core_base_raw, float* grad_core_drive_weight, float* grad_eta_raw,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* Per-kernel timing (no counterpart in the reference; instrumentation only).
  * lsso_profile_start() makes every subsequent kernel launch of the library
  * record a CUDA event pair on its launch stream; lsso_profile_stop()

@@ -24,6 +24,8 @@ EXPORTED_SYMBOLS = (
     "lsso_tape_stride", "lsso_forward_workspace_size", "lsso_forward", "lsso_backward_workspace_size",
     "lsso_backward", "lsso_profile_start", "lsso_profile_stop", "lsso_forward_inference_noalloc",
     "lsso_linear_workspace_size", "lsso_linear", "lsso_linear_wgrad_workspace_size", "lsso_linear_wgrad",
+    "lsso_moment_elements", "lsso_forward_moments", "lsso_forward_finish", "lsso_backward_moments",
+    "lsso_backward_finish",
 )
 
 _LIBRARY: "NativeLibrary | None" = None
@@ -54,6 +56,13 @@ class NativeLibrary:
             "lsso_linear_wgrad_workspace_size": (sz, [i64, i64, i64]),
             "lsso_linear_wgrad": (ci, [vp, ci, vp, ci, vp, i64, i64, i64, vp, vp, sz, vp]),
             "lsso_forward_inference_noalloc": (ci, [vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp]),
+            "lsso_moment_elements": (sz, [i64, i64, i64, i64, i64, ci]),
+            "lsso_forward_moments": (ci, [vp, vp, ci, i64, i64, i64, i64, i64, vp, vp, sz, vp]),
+            "lsso_forward_finish": (ci, [vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp,
+                                         sz, vp]),
+            "lsso_backward_moments": (ci, [vp, vp, vp, ci, i64, i64, i64, i64, i64, vp, vp, sz, vp]),
+            "lsso_backward_finish": (ci, [vp, vp, vp, vp, vp, vp, ci, i64, i64, i64, i64, i64, vp, c.c_float, vp,
+                                          vp, vp, vp, vp, sz, vp]),
             "lsso_profile_start": (ci, []),
             "lsso_profile_stop": (ci, [ci, c.c_char_p, c.POINTER(c.c_float), c.POINTER(c.c_int)]),
         }
@@ -228,6 +237,138 @@ def backward(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, 
             heads, dim, rank, _ptr(grad_projected), _ptr(grad_base), _ptr(grad_drive), _ptr(grad_eta),
             _ptr(workspace), size, _stream(device)))
     return grad_projected, grad_base, grad_drive, grad_eta
+
+
+# ---------------------------------------------------------------------------- sequence-parallel halves
+def _sequence_inputs(projected, centered_positions, valid_counts, need_counts: bool):
+    if centered_positions is None:
+        raise RuntimeError("the sequence-parallel mixer needs the centered positions of this rank's tokens")
+    if need_counts and valid_counts is None:
+        raise RuntimeError("the sequence-parallel mixer needs the valid-token counts of the whole sequence")
+    return centered_positions.dim() == 2
+
+
+def moment_elements(batch, length, heads, dim, rank, *, backward: bool) -> int:
+    lib = library()
+    count = lib.lib.lsso_moment_elements(batch, length, heads, dim, rank, int(backward))
+    if count == 0:
+        lib.check(1)
+    return int(count)
+
+
+def forward_moments(projected, core_base_raw, core_drive_weight, eta_raw, centered_positions):
+    """This rank's forward moment sums (FP32, flat); sum them over the ranks before forward_finish."""
+    lib = library()
+    batch, length, heads, dim, rank = validate_fast_inputs(
+        projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, None)
+    batched = _sequence_inputs(projected, centered_positions, None, False)
+    device = projected.device
+    with torch.cuda.device(device):
+        moments = torch.empty((moment_elements(batch, length, heads, dim, rank, backward=False),),
+                              dtype=torch.float32, device=device)
+        size = lib.lib.lsso_forward_workspace_size(batch, length, heads, dim, rank, int(batched), 1)
+        if size == 0:
+            lib.check(1)
+        workspace = torch.empty((size,), dtype=torch.uint8, device=device)
+        lib.check(lib.lib.lsso_forward_moments(
+            _ptr(projected), _ptr(centered_positions), int(batched), batch, length, heads, dim, rank, _ptr(moments),
+            _ptr(workspace), size, _stream(device)))
+    return moments
+
+
+def forward_finish(projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts, moments,
+                   *, train: bool):
+    """Solves from the summed moments and this rank's readout; returns (mixed, tape, pivots)."""
+    lib = library()
+    batch, length, heads, dim, rank = validate_fast_inputs(
+        projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts)
+    batched = _sequence_inputs(projected, centered_positions, valid_counts, True)
+    _check_moments(moments, projected, moment_elements(batch, length, heads, dim, rank, backward=False))
+    device = projected.device
+    with torch.cuda.device(device):
+        mixed = torch.empty((batch, length, dim), dtype=torch.bfloat16, device=device)
+        tape = pivots = None
+        if train:
+            stride = lib.lib.lsso_tape_stride(length, heads, dim, rank)
+            tape = torch.empty((batch * heads, stride), dtype=torch.float32, device=device)
+            pivots = torch.empty((batch * heads, rank), dtype=torch.int32, device=device)
+        size = lib.lib.lsso_forward_workspace_size(batch, length, heads, dim, rank, int(batched), int(train))
+        if size == 0:
+            lib.check(1)
+        workspace = torch.empty((size,), dtype=torch.uint8, device=device)
+        lib.check(lib.lib.lsso_forward_finish(
+            _ptr(projected), _ptr(core_base_raw), _ptr(core_drive_weight), _ptr(eta_raw), _ptr(centered_positions),
+            int(batched), _ptr(valid_counts), batch, length, heads, dim, rank, _ptr(moments), _ptr(mixed), _ptr(tape),
+            _ptr(pivots), _ptr(workspace), size, _stream(device)))
+    return mixed, tape, pivots
+
+
+def backward_moments(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, centered_positions):
+    """This rank's backward moment sums (FP32, flat); sum them over the ranks before backward_finish."""
+    lib = library()
+    batch, length, heads, dim, rank = validate_fast_inputs(
+        projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, None)
+    batched = _sequence_inputs(projected, centered_positions, None, False)
+    _check_grad_output(grad_output, projected, batch, length, dim)
+    device = projected.device
+    with torch.cuda.device(device):
+        moments = torch.empty((moment_elements(batch, length, heads, dim, rank, backward=True),),
+                              dtype=torch.float32, device=device)
+        size = lib.lib.lsso_backward_workspace_size(batch, length, heads, dim, rank, int(batched))
+        if size == 0:
+            lib.check(1)
+        workspace = torch.empty((size,), dtype=torch.uint8, device=device)
+        lib.check(lib.lib.lsso_backward_moments(
+            _ptr(grad_output), _ptr(projected), _ptr(centered_positions), int(batched), batch, length, heads, dim,
+            rank, _ptr(moments), _ptr(workspace), size, _stream(device)))
+    return moments
+
+
+def backward_finish(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, tape, centered_positions,
+                    moments, redundant: float):
+    """Backward solves from the summed moments, this rank's gradient pass and the parameter gradients."""
+    lib = library()
+    batch, length, heads, dim, rank = validate_fast_inputs(
+        projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, None)
+    batched = _sequence_inputs(projected, centered_positions, None, False)
+    _check_grad_output(grad_output, projected, batch, length, dim)
+    _check_moments(moments, projected, moment_elements(batch, length, heads, dim, rank, backward=True))
+    stride = lib.lib.lsso_tape_stride(length, heads, dim, rank)
+    _same_device(tape, projected, "tape")
+    if tape.dtype != torch.float32 or not tape.is_contiguous() or tuple(tape.shape) != (batch * heads, stride):
+        raise RuntimeError(f"tape has an incompatible shape or dtype {list(tape.shape)} {tape.dtype}")
+    device = projected.device
+    with torch.cuda.device(device):
+        grad_projected = torch.empty_like(projected)
+        grad_base = torch.empty_like(core_base_raw)
+        grad_drive = torch.empty_like(core_drive_weight)
+        grad_eta = torch.empty_like(eta_raw)
+        size = lib.lib.lsso_backward_workspace_size(batch, length, heads, dim, rank, int(batched))
+        if size == 0:
+            lib.check(1)
+        workspace = torch.empty((size,), dtype=torch.uint8, device=device)
+        lib.check(lib.lib.lsso_backward_finish(
+            _ptr(grad_output), _ptr(projected), _ptr(core_drive_weight), _ptr(eta_raw), _ptr(tape),
+            _ptr(centered_positions), int(batched), batch, length, heads, dim, rank, _ptr(moments), float(redundant),
+            _ptr(grad_projected), _ptr(grad_base), _ptr(grad_drive), _ptr(grad_eta), _ptr(workspace), size,
+            _stream(device)))
+    return grad_projected, grad_base, grad_drive, grad_eta
+
+
+def _check_moments(moments, projected, count: int) -> None:
+    _same_device(moments, projected, "moments")
+    if moments.dtype != torch.float32 or not moments.is_contiguous() or moments.numel() != count:
+        raise RuntimeError(f"moments must be a contiguous float32 buffer of {count} elements")
+
+
+def _check_grad_output(grad_output, projected, batch, length, dim) -> None:
+    _same_device(grad_output, projected, "grad_output")
+    if not grad_output.is_contiguous():
+        raise RuntimeError("grad_output must be contiguous")
+    if grad_output.dtype != torch.bfloat16:
+        raise RuntimeError("grad_output must use bfloat16")
+    if tuple(grad_output.shape) != (batch, length, dim):
+        raise RuntimeError(f"grad_output must have shape [B, N, D], got {list(grad_output.shape)}")
 
 
 # ---------------------------------------------------------------------------- operator registration

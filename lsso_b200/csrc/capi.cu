@@ -579,4 +579,191 @@ int lsso_backward(const void* grad_output, const void* projected, const float* c
   return LSSO_OK;
 }
 
+size_t lsso_moment_elements(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int backward) {
+  g_last_error.clear();
+  lsso::Plan p{};
+  if (plan_for(B, N, H, D, R, 0, &p) != LSSO_OK) return 0;
+  return static_cast<size_t>(lsso::moment_elements(p, backward != 0));
+}
+
+int lsso_forward_moments(const void* projected, const float* centered_positions, int positions_batched, int64_t B,
+                         int64_t N, int64_t H, int64_t D, int64_t R, float* moments, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (projected == nullptr || centered_positions == nullptr || moments == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT,
+                "lsso_forward_moments: projected, centered_positions and moments are required");
+  }
+  if (!aligned16(moments)) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward_moments: moments must be 16-byte aligned");
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, positions_batched != 0 ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const ForwardLayout l = forward_layout(p, true);
+  if (workspace_bytes < l.total || workspace == nullptr) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_forward_moments: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, l.total);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  lsso::ForwardBuffers fb{};
+  fb.projected = static_cast<const lsso::bf16*>(projected);
+  fb.positions = centered_positions;
+  fb.positions_batched = positions_batched != 0 ? 1 : 0;
+  fb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  fb.partial = reinterpret_cast<float*>(ws + l.partial);
+  fb.status = status;
+  fb.vec = p.vec && aligned16(projected);
+  const cudaError_t e = lsso::launch_forward_moments(p, fb, moments, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_forward_moments");
+  return LSSO_OK;
+}
+
+int lsso_forward_finish(const void* projected, const float* core_base_raw, const float* core_drive_weight,
+                        const float* eta_raw, const float* centered_positions, int positions_batched,
+                        const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                        const float* moments, void* mixed, float* tape, int32_t* pivots, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (projected == nullptr || core_base_raw == nullptr || core_drive_weight == nullptr || eta_raw == nullptr ||
+      centered_positions == nullptr || valid_counts == nullptr || moments == nullptr || mixed == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward_finish: a required pointer is NULL (centered_positions and "
+                                           "valid_counts are required)");
+  }
+  if ((tape == nullptr) != (pivots == nullptr)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward_finish: tape and pivots must be given together");
+  }
+  if (!aligned16(moments)) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_forward_finish: moments must be 16-byte aligned");
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, positions_batched != 0 ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const bool train = tape != nullptr;
+  const ForwardLayout l = forward_layout(p, train);
+  if (workspace_bytes < l.total || workspace == nullptr) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_forward_finish: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, l.total);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  lsso::ForwardBuffers fb{};
+  fb.projected = static_cast<const lsso::bf16*>(projected);
+  fb.base = core_base_raw;
+  fb.drive = core_drive_weight;
+  fb.eta_raw = eta_raw;
+  fb.positions = centered_positions;
+  fb.positions_batched = positions_batched != 0 ? 1 : 0;
+  fb.counts = valid_counts;
+  fb.mixed = static_cast<lsso::bf16*>(mixed);
+  fb.tape = tape;
+  fb.pivots = pivots;
+  fb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  fb.partial = reinterpret_cast<float*>(ws + l.partial);
+  fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.zbuf);
+  fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
+  fb.status = status;
+  fb.vec = p.vec && aligned16(projected) && aligned16(mixed);
+  const cudaError_t e = lsso::launch_forward_finish(p, fb, moments, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_forward_finish");
+  return LSSO_OK;
+}
+
+int lsso_backward_moments(const void* grad_output, const void* projected, const float* centered_positions,
+                          int positions_batched, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, float* moments,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (grad_output == nullptr || projected == nullptr || centered_positions == nullptr || moments == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT,
+                "lsso_backward_moments: grad_output, projected, centered_positions and moments are required");
+  }
+  if (!aligned16(moments)) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_backward_moments: moments must be 16-byte aligned");
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, positions_batched != 0 ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const BackwardLayout l = backward_layout(p);
+  if (workspace_bytes < l.total || workspace == nullptr) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_backward_moments: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, l.total);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  lsso::BackwardBuffers bb{};
+  bb.grad_output = static_cast<const lsso::bf16*>(grad_output);
+  bb.projected = static_cast<const lsso::bf16*>(projected);
+  bb.positions = centered_positions;
+  bb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  bb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
+  bb.partial = reinterpret_cast<float*>(ws + l.partial);
+  bb.status = status;
+  bb.vec = p.vec && aligned16(projected) && aligned16(grad_output);
+  const cudaError_t e = lsso::launch_backward_moments(p, bb, moments, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_backward_moments");
+  return LSSO_OK;
+}
+
+int lsso_backward_finish(const void* grad_output, const void* projected, const float* core_drive_weight,
+                         const float* eta_raw, const float* tape, const float* centered_positions,
+                         int positions_batched, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                         const float* moments, float redundant, void* grad_projected, float* grad_core_base_raw,
+                         float* grad_core_drive_weight, float* grad_eta_raw, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (grad_output == nullptr || projected == nullptr || core_drive_weight == nullptr || eta_raw == nullptr ||
+      tape == nullptr || centered_positions == nullptr || moments == nullptr || grad_projected == nullptr ||
+      grad_core_base_raw == nullptr || grad_core_drive_weight == nullptr || grad_eta_raw == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_backward_finish: a required pointer is NULL");
+  }
+  if (!aligned16(moments)) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_backward_finish: moments must be 16-byte aligned");
+  lsso::Plan p{};
+  int rc = plan_for(B, N, H, D, R, positions_batched != 0 ? 1 : 0, &p);
+  if (rc != LSSO_OK) return rc;
+  const BackwardLayout l = backward_layout(p);
+  if (workspace_bytes < l.total || workspace == nullptr) {
+    return fail(LSSO_ERR_WORKSPACE, "lsso_backward_finish: workspace of %zu bytes is smaller than the required %zu",
+                workspace_bytes, l.total);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  lsso::BackwardBuffers bb{};
+  bb.grad_output = static_cast<const lsso::bf16*>(grad_output);
+  bb.projected = static_cast<const lsso::bf16*>(projected);
+  bb.drive = core_drive_weight;
+  bb.eta_raw = eta_raw;
+  bb.tape = tape;
+  bb.positions = centered_positions;
+  bb.grad_projected = static_cast<lsso::bf16*>(grad_projected);
+  bb.grad_base = grad_core_base_raw;
+  bb.grad_drive = grad_core_drive_weight;
+  bb.grad_eta = grad_eta_raw;
+  bb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  bb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
+  bb.partial = reinterpret_cast<float*>(ws + l.partial);
+  bb.dbuf = reinterpret_cast<float*>(ws + l.dbuf);
+  bb.lbuf = reinterpret_cast<float*>(ws + l.lbuf);
+  bb.b1y = reinterpret_cast<lsso::bf16*>(ws + l.b1y);
+  bb.b1c = reinterpret_cast<lsso::bf16*>(ws + l.b1c);
+  bb.b1a = reinterpret_cast<lsso::bf16*>(ws + l.b1a);
+  bb.b2 = reinterpret_cast<lsso::bf16*>(ws + l.b2);
+  bb.gbase = reinterpret_cast<float*>(ws + l.gbase);
+  bb.gdrive = reinterpret_cast<float*>(ws + l.gdrive);
+  bb.etastat = reinterpret_cast<float*>(ws + l.etastat);
+  bb.etadot = reinterpret_cast<float*>(ws + l.etadot);
+  bb.status = status;
+  bb.vec = p.vec && aligned16(projected) && aligned16(grad_output) && aligned16(grad_projected);
+  const cudaError_t e =
+      lsso::launch_backward_finish(p, bb, moments, redundant, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_backward_finish");
+  return LSSO_OK;
+}
+
 }  // extern "C"

@@ -1113,7 +1113,7 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
       s3 += src[(b + 3) * stride];
     }
     for (; b < a.B; ++b) s0 += src[b * stride];
-    const float total = (s0 + s1) + (s2 + s3);
+    const float total = ((s0 + s1) + (s2 + s3)) * a.redundant;
     if (is_base) {
       a.grad_base[k] = total;
     } else {
@@ -1128,7 +1128,7 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
     const int64_t b = i / a.ntiles, t = i % a.ntiles;
     s += a.etastat[(b * H + h) * a.ntiles + t];
   }
-  for (int64_t b = threadIdx.x; b < a.B; b += kReduceThreads) s -= a.etadot[b * H + h];
+  for (int64_t b = threadIdx.x; b < a.B; b += kReduceThreads) s -= a.redundant * a.etadot[b * H + h];
   part[threadIdx.x] = s;
   __syncthreads();
   for (int w = kReduceThreads / 2; w > 0; w >>= 1) {
@@ -1210,8 +1210,9 @@ static cudaError_t launch_moments(const Plan& p, MomentArgs args, cudaStream_t s
   return cudaGetLastError();
 }
 
+// Phase table and the forward moment pass (chunk partials into fb.partial).
 template <int R>
-static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {
+static cudaError_t forward_moments_r(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {
   cudaError_t e = launch_phase(p, fb.positions, fb.phase, nullptr, stream);
   if (e != cudaSuccess) return e;
   MomentArgs m{};
@@ -1232,16 +1233,20 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
   m.chunk_len = static_cast<int>(p.chunk_len);
   m.pos_batched = p.pos_rows > 1 ? 1 : 0;
   m.vec = fb.vec;
-  const bool tiled = tiled_usable(p, {fb.projected, fb.mixed});
-  if (tiled) {
-    e = launch_moments_tiled(p, false, fb.projected, nullptr, fb.phase, fb.partial, fb.status, p.sms, stream);
-  } else {
-    e = launch_moments<R, false>(p, m, stream);
+  if (tiled_usable(p, {fb.projected})) {
+    return launch_moments_tiled(p, false, fb.projected, nullptr, fb.phase, fb.partial, fb.status, p.sms, stream);
   }
-  if (e != cudaSuccess) return e;
+  return launch_moments<R, false>(p, m, stream);
+}
 
+// Solves (over `nchunks` partials per (b, h)) and the readout; the phase table
+// is already in fb.phase.
+template <int R>
+static cudaError_t forward_finish_r(const Plan& p, const ForwardBuffers& fb, const float* partial, int64_t nchunks,
+                                    cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
   SolveFwdArgs s{};
-  s.partial = fb.partial;
+  s.partial = partial;
   s.base = fb.base;
   s.drive = fb.drive;
   s.eta_raw = fb.eta_raw;
@@ -1257,7 +1262,7 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
   s.d_pad = static_cast<int>(p.d_pad);
   s.dt = static_cast<int>(p.dt);
   s.ndt = static_cast<int>(p.ndt);
-  s.nchunks = static_cast<int>(p.nchunks);
+  s.nchunks = static_cast<int>(nchunks);
   if (warp_solves_usable(p)) {
     e = launch_solve_forward_warp(p, s, stream);
   } else {
@@ -1286,9 +1291,9 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
   r.nb = static_cast<int>(p.nb);
   r.njd = static_cast<int>(p.njd);
   r.ntiles = static_cast<int>(p.ntiles);
-  r.pos_batched = m.pos_batched;
+  r.pos_batched = p.pos_rows > 1 ? 1 : 0;
   r.vec = fb.vec;
-  if (tiled) {
+  if (tiled_usable(p, {fb.projected, fb.mixed})) {
     return launch_readout_tiled(p, fb.projected, fb.phase, fb.rmat, fb.eta_raw, fb.mixed, fb.status, p.sms, stream);
   }
   const size_t rsm = readout_smem<R>(static_cast<int>(p.nb));
@@ -1300,7 +1305,15 @@ static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream
 }
 
 template <int R>
-static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream) {
+static cudaError_t forward_r(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {
+  const cudaError_t e = forward_moments_r<R>(p, fb, stream);
+  if (e != cudaSuccess) return e;
+  return forward_finish_r<R>(p, fb, fb.partial, p.nchunks, stream);
+}
+
+// Phase tables and the backward moment pass (chunk partials into bb.partial).
+template <int R>
+static cudaError_t backward_moments_r(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream) {
   cudaError_t e = launch_phase(p, bb.positions, bb.phase, bb.phase16, stream);
   if (e != cudaSuccess) return e;
   const int pos_batched = p.pos_rows > 1 ? 1 : 0;
@@ -1322,16 +1335,22 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   m.chunk_len = static_cast<int>(p.chunk_len);
   m.pos_batched = pos_batched;
   m.vec = bb.vec;
-  const bool tiled = tiled_usable(p, {bb.projected, bb.grad_output, bb.grad_projected});
-  if (tiled) {
-    e = launch_moments_tiled(p, true, bb.projected, bb.grad_output, bb.phase, bb.partial, bb.status, p.sms, stream);
-  } else {
-    e = launch_moments<R, true>(p, m, stream);
+  if (tiled_usable(p, {bb.projected, bb.grad_output})) {
+    return launch_moments_tiled(p, true, bb.projected, bb.grad_output, bb.phase, bb.partial, bb.status, p.sms,
+                                stream);
   }
-  if (e != cudaSuccess) return e;
+  return launch_moments<R, true>(p, m, stream);
+}
 
+// Backward solves (over `nchunks` partials per (b, h)), the gradient pass and
+// the parameter reduction; the phase tables are already in bb.
+template <int R>
+static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, const float* partial, int64_t nchunks,
+                                     float redundant, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
+  const int pos_batched = p.pos_rows > 1 ? 1 : 0;
   SolveBwdArgs s{};
-  s.partial = bb.partial;
+  s.partial = partial;
   s.tape = bb.tape;
   s.drive = bb.drive;
   s.eta_raw = bb.eta_raw;
@@ -1351,7 +1370,7 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   s.d_pad = static_cast<int>(p.d_pad);
   s.dt = static_cast<int>(p.dt);
   s.ndt = static_cast<int>(p.ndt);
-  s.nchunks = static_cast<int>(p.nchunks);
+  s.nchunks = static_cast<int>(nchunks);
   if (warp_solves_usable(p)) {
     e = launch_solve_backward_warp(p, s, stream);
   } else {
@@ -1387,7 +1406,7 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   g.ntiles = static_cast<int>(p.ntiles);
   g.pos_batched = pos_batched;
   g.vec = bb.vec;
-  if (tiled && p.tiled_grad) {
+  if (p.tiled_grad && tiled_usable(p, {bb.projected, bb.grad_output, bb.grad_projected})) {
     e = launch_grad_tiled(p, bb.grad_output, bb.projected, bb.phase16, bb.b1y, bb.b1c, bb.b1a, bb.eta_raw,
                           bb.grad_projected, bb.etastat, bb.status, p.sms, stream);
   } else {
@@ -1414,10 +1433,102 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
   pr.R = p.R;
   pr.d = p.d;
   pr.ntiles = p.ntiles;
+  pr.redundant = redundant;
   const int64_t main_blocks = ceil_div(p.H * p.R * p.R + p.H * p.d * p.R, kReduceThreads);
   LaunchScope scope("param_reduce", stream);
   param_reduce_kernel<<<static_cast<unsigned>(main_blocks + p.H), kReduceThreads, 0, stream>>>(pr);
   return cudaGetLastError();
+}
+
+template <int R>
+static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream) {
+  const cudaError_t e = backward_moments_r<R>(p, bb, stream);
+  if (e != cudaSuccess) return e;
+  return backward_finish_r<R>(p, bb, bb.partial, p.nchunks, 1.0f, stream);
+}
+
+// Sum of the chunk partials of every (b, h): out[bh][e] = sum_ch partial[bh][ch][e]
+// (ascending chunks), float4 per thread.
+__global__ void chunk_sum_kernel(const float4* __restrict__ partial, int64_t BH, int nchunks, int64_t per4,
+                                 float4* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= BH * per4) return;
+  const int64_t bh = i / per4, e = i - bh * per4;
+  const float4* src = partial + bh * nchunks * per4 + e;
+  float4 acc = src[0];
+  for (int ch = 1; ch < nchunks; ++ch) {
+    const float4 v = src[ch * per4];
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  out[i] = acc;
+}
+
+static cudaError_t sum_chunks(const Plan& p, bool bwd, const float* partial, float* moments, cudaStream_t stream) {
+  const int64_t per = moment_elements(p, bwd) / p.BH;  // a multiple of 4 (R and dt are multiples of 16)
+  const int64_t total4 = p.BH * per / 4;
+  LaunchScope scope("chunk_sum", stream);
+  chunk_sum_kernel<<<static_cast<unsigned>(ceil_div(total4, 256)), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(partial), p.BH, static_cast<int>(p.nchunks), per / 4,
+      reinterpret_cast<float4*>(moments));
+  return cudaGetLastError();
+}
+
+int64_t moment_elements(const Plan& p, bool bwd) {
+  return p.BH * p.ndt * 2 * p.R * ((bwd ? 0 : p.R) + p.dt);
+}
+
+cudaError_t launch_forward_moments(const Plan& p, const ForwardBuffers& fb, float* moments, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
+  switch (p.R) {
+    case 16: e = forward_moments_r<16>(p, fb, stream); break;
+    case 32: e = forward_moments_r<32>(p, fb, stream); break;
+    case 48: e = forward_moments_r<48>(p, fb, stream); break;
+    case 64: e = forward_moments_r<64>(p, fb, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  return sum_chunks(p, false, fb.partial, moments, stream);
+}
+
+cudaError_t launch_forward_finish(const Plan& p, const ForwardBuffers& fb, const float* moments, cudaStream_t stream) {
+  const cudaError_t e = launch_phase(p, fb.positions, fb.phase, nullptr, stream);
+  if (e != cudaSuccess) return e;
+  switch (p.R) {
+    case 16: return forward_finish_r<16>(p, fb, moments, 1, stream);
+    case 32: return forward_finish_r<32>(p, fb, moments, 1, stream);
+    case 48: return forward_finish_r<48>(p, fb, moments, 1, stream);
+    case 64: return forward_finish_r<64>(p, fb, moments, 1, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_backward_moments(const Plan& p, const BackwardBuffers& bb, float* moments, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
+  switch (p.R) {
+    case 16: e = backward_moments_r<16>(p, bb, stream); break;
+    case 32: e = backward_moments_r<32>(p, bb, stream); break;
+    case 48: e = backward_moments_r<48>(p, bb, stream); break;
+    case 64: e = backward_moments_r<64>(p, bb, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  return sum_chunks(p, true, bb.partial, moments, stream);
+}
+
+cudaError_t launch_backward_finish(const Plan& p, const BackwardBuffers& bb, const float* moments, float redundant,
+                                   cudaStream_t stream) {
+  const cudaError_t e = launch_phase(p, bb.positions, bb.phase, bb.phase16, stream);
+  if (e != cudaSuccess) return e;
+  switch (p.R) {
+    case 16: return backward_finish_r<16>(p, bb, moments, 1, redundant, stream);
+    case 32: return backward_finish_r<32>(p, bb, moments, 1, redundant, stream);
+    case 48: return backward_finish_r<48>(p, bb, moments, 1, redundant, stream);
+    case 64: return backward_finish_r<64>(p, bb, moments, 1, redundant, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {

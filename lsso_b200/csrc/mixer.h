@@ -92,6 +92,7 @@ struct ParamReduceArgs {
   float* grad_drive;
   float* grad_eta;
   int64_t B, H, R, d, ntiles;
+  float redundant;  // weight of the solve-computed terms (gbase, gdrive, etadot); 1 unless sequence-parallel
 };
 
 struct ForwardBuffers {
@@ -183,5 +184,21 @@ cudaError_t launch_solve_backward_warp(const Plan& p, const SolveBwdArgs& s, cud
 
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream);
 cudaError_t launch_backward(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream);
+
+// Sequence-parallel halves.  The moment halves run the phase table and the
+// token moment pass over this rank's tokens and sum the chunk partials into
+// `moments` ([B*H][ndt][2R][R + dt] forward, [B*H][ndt][2R][dt] backward,
+// moment_elements); the caller sums `moments` over the ranks holding the
+// other tokens, then the finish halves recompute the phase table and run the
+// solves and the readout (forward) or the gradient pass and the parameter
+// reduction (backward), with the solve-computed parameter terms weighted by
+// `redundant` (1 on one rank, 0 on the others, so that summing the
+// parameter gradients over the ranks counts them once).
+int64_t moment_elements(const Plan& p, bool bwd);
+cudaError_t launch_forward_moments(const Plan& p, const ForwardBuffers& fb, float* moments, cudaStream_t stream);
+cudaError_t launch_forward_finish(const Plan& p, const ForwardBuffers& fb, const float* moments, cudaStream_t stream);
+cudaError_t launch_backward_moments(const Plan& p, const BackwardBuffers& bb, float* moments, cudaStream_t stream);
+cudaError_t launch_backward_finish(const Plan& p, const BackwardBuffers& bb, const float* moments, float redundant,
+                                   cudaStream_t stream);
 
 }  // namespace lsso

@@ -90,3 +90,67 @@ def test_a_rank_leaving_ends_the_collective_with_an_error(tmp_path) -> None:
     path = tmp_path / "outcome.txt"
     mp.spawn(_failing_worker, args=(2, _free_port(), str(path)), nprocs=2, join=True)
     assert path.read_text().startswith("error")
+
+
+# ---------------------------------------------------------------------------- sequence-parallel positions
+_SEQ_CASES = ("plain", "mask", "mask_ids", "shared_ids", "float_ids")
+_SEQ_CUTS = (0, 7, 19)  # two unequal slices of a 19-token sequence
+
+
+def _seq_inputs(case: str):
+    batch, length = 3, _SEQ_CUTS[-1]
+    g = torch.Generator().manual_seed(5)
+    mask = None
+    ids = None
+    if case in ("mask", "mask_ids"):
+        mask = torch.rand(batch, length, generator=g) > 0.3
+        mask[1] = False  # a sample with no valid token
+    if case == "mask_ids":
+        ids = torch.randint(0, 50, (batch, length), generator=g)
+    if case == "shared_ids":
+        ids = torch.arange(length) * 3 + 5
+    if case == "float_ids":
+        ids = torch.linspace(-2.0, 7.5, length, dtype=torch.float32)
+    return batch, length, mask, ids
+
+
+def _seq_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    from lsso_b200.ball.sequence_parallel import sequence_positions
+
+    a, b = _SEQ_CUTS[rank], _SEQ_CUTS[rank + 1]
+    result = {}
+    for case in _SEQ_CASES:
+        batch, _, mask, ids = _seq_inputs(case)
+        m = None if mask is None else mask[:, a:b]
+        i = None if ids is None else ids[..., a:b]
+        result[case] = sequence_positions(batch, b - a, m, i, device=torch.device("cpu"))
+    torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sequence_parallel_positions_are_slices_of_the_whole_sequence(tmp_path) -> None:
+    from lsso import LSSO
+
+    mp.spawn(_seq_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    ranks = [torch.load(tmp_path / f"rank{r}.pt") for r in range(2)]
+    for case in _SEQ_CASES:
+        batch, length, mask, ids = _seq_inputs(case)
+        all_valid = mask is None
+        if all_valid and ids is None:
+            full = torch.arange(length, dtype=torch.float32) - 0.5 * (length - 1)
+        else:
+            centered = LSSO._center_positions(ids, mask, dtype=torch.float32, all_valid=all_valid, batch=batch,
+                                              length=length, device=torch.device("cpu"))
+            full = centered[0] if (all_valid and (ids is None or ids.dim() == 1)) else centered
+        counts = (torch.full((batch,), float(length)) if all_valid
+                  else mask.sum(-1).float().clamp_min(1.0))
+        for r in range(2):
+            positions, got_counts, offset, total = ranks[r][case]
+            a, b = _SEQ_CUTS[r], _SEQ_CUTS[r + 1]
+            assert (offset, total) == (a, length), case
+            assert torch.equal(positions, full[..., a:b].contiguous()), case
+            assert torch.equal(got_counts, counts), case
