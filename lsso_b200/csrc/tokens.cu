@@ -15,9 +15,10 @@
 //                 moment pass uses warps 2-13, adding the BF16 hi/lo split
 //                 into the MN-major operand buffer);
 //   warps 10-17   epilogue (moment pass: warps 14-17): TMEM -> registers, combine with the staged
-//                 content / dY boxes, write the result back into the boxes
-//                 and store them with TMA tensor stores (tokens past N are
-//                 clipped), or drain moment accumulators to the partials.
+//                 content / dY boxes and write the result back into the boxes,
+//                 or drain moment accumulators to the partials;
+//   warp 18       (readout and gradient passes) storer: TMA tensor stores of
+//                 the finished boxes (tokens past N are clipped), slot release.
 //
 // Kernels (same algebra as the per-head kernels of mixer.cu; reference
 // lsso/ball/reference.py:411-572,691-724, lsso/ball/model.py:245-268):
@@ -47,7 +48,11 @@ constexpr int kMaxSlots = kTileMaxSlots;
 constexpr int kXWarp0 = 2, kXWarps = 8;      // rotation / split warps
 constexpr int kEWarp0 = 10, kEWarps = 8;      // epilogue warps (two per TMEM sub-partition)
 constexpr int kXThreads = kXWarps * 32;
-constexpr int kThreadsT = (kEWarp0 + kEWarps) * 32;
+// Readout and gradient passes add one storer warp: it waits for a tile's
+// epilogue, issues the TMA stores and frees the slot once they have read it,
+// so no epilogue warp blocks on store completion.
+constexpr int kSWarp = kEWarp0 + kEWarps;
+constexpr int kThreadsS = (kSWarp + 1) * 32;
 // The moment pass drains TMEM only at the end of a chunk, so it gives most of
 // its warps to the rotation / hi-lo split: 12 of them, and 4 drain warps (one
 // per TMEM sub-partition).
@@ -547,7 +552,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
 // eta C + acc over the content box and stores it to the mixed output.
 // ============================================================================
 template <int R>
-__global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
+__global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
                                                                      const __grid_constant__ CUtensorMap tm_out,
                                                                      const TileArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -628,14 +633,14 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
     }
-  } else {
+  } else if (warp < kSWarp) {
     const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
     const int r = 32 * sub + lane;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
       const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots, u = i / a.slots;
+      const int s = i % a.slots;
       const int tb = i % a.nbuf, tu = i / a.nbuf;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
@@ -670,9 +675,17 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
         mbar_arrive(smem_u32(&sh.tempty[tb]));
         if (ok) mbar_arrive(smem_u32(&sh.edone[s]));
       }
-      if (ok && warp == kEWarp0 && lane == 0) {
+    }
+  } else {
+    // ------------------------------------------------------------ storer
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nloc && ok; ++i) {
+        const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+        const int s = i % a.slots, u = i / a.slots;
         ok = twait(smem_u32(&sh.edone[s]), u & 1, abort_v, a.status);
         if (ok) {
+          uint8_t* con = smem + static_cast<size_t>(s) * a.slot_bytes + a.off_val;
           for (int j = 0; j < a.nval; ++j)
             tma_store_3d(&tm_out, smem_u32(con + j * kBox), x.g * a.hg * d + j * 64, x.t * kTT, x.b);
           bulk_commit();
@@ -680,9 +693,9 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
           mbar_arrive(smem_u32(&sh.sfree[s]));
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      bulk_wait<0>();
     }
-    if (warp == kEWarp0 && lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
   tile_teardown(sh, a.slots, last_use, a.status);
 }
@@ -696,7 +709,7 @@ __global__ void __launch_bounds__(kThreadsT, 1) readout_tile_kernel(const __grid
 // statistic sum(dY * C) is taken), both stored to the packed gradient.
 // ============================================================================
 template <int R>
-__global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
+__global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
                                                                   const __grid_constant__ CUtensorMap tm_dy,
                                                                   const __grid_constant__ CUtensorMap tm_gproj,
                                                                   const TileArgs a) {
@@ -803,14 +816,14 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
     }
-  } else {
+  } else if (warp < kSWarp) {
     const int sub = warp & 3, half = (warp - kEWarp0) >> 2;
     const int r = 32 * sub + lane;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
       const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots, u = i / a.slots;
+      const int s = i % a.slots;
       const int tb = i % a.nbuf, tu = i / a.nbuf;
       const int tok = x.t * kTT + r;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
@@ -877,9 +890,18 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
         mbar_arrive(smem_u32(&sh.tempty[tb]));
         if (ok) mbar_arrive(smem_u32(&sh.edone[s]));
       }
-      if (ok && warp == kEWarp0 && lane == 0) {
+    }
+  } else {
+    // ------------------------------------------------------------ storer
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nloc && ok; ++i) {
+        const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
+        const int s = i % a.slots, u = i / a.slots;
         ok = twait(smem_u32(&sh.edone[s]), u & 1, abort_v, a.status);
         if (ok) {
+          uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+          uint8_t* con = slot + a.off_val;
           for (int j = 0; j < a.nrel; ++j)
             tma_store_3d(&tm_gproj, smem_u32(slot + j * kBox), x.g * a.hg * R + j * 64, x.t * kTT, x.b);
           for (int j = 0; j < a.nval; ++j)
@@ -893,9 +915,9 @@ __global__ void __launch_bounds__(kThreadsT, 1) grad_tile_kernel(const __grid_co
           mbar_arrive(smem_u32(&sh.sfree[s]));
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      bulk_wait<0>();
     }
-    if (warp == kEWarp0 && lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
   tile_teardown(sh, a.slots, last_use, a.status);
 }
@@ -1038,9 +1060,9 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* 
   if (e != cudaSuccess) return e;
   LaunchScope scope("readout", stream);
   if (p.R == 32) {
-    readout_tile_kernel<32><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_out, a);
+    readout_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
   } else {
-    readout_tile_kernel<64><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_out, a);
+    readout_tile_kernel<64><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
   }
   return cudaGetLastError();
 }
@@ -1077,9 +1099,9 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   if (e != cudaSuccess) return e;
   LaunchScope scope("grad", stream);
   if (p.R == 32) {
-    grad_tile_kernel<32><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+    grad_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
   } else {
-    grad_tile_kernel<64><<<grid, kThreadsT, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+    grad_tile_kernel<64><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
   }
   return cudaGetLastError();
 }
