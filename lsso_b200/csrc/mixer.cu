@@ -1113,7 +1113,7 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
       s3 += src[(b + 3) * stride];
     }
     for (; b < a.B; ++b) s0 += src[b * stride];
-    const float total = ((s0 + s1) + (s2 + s3)) * a.redundant;
+    const float total = (s0 + s1) + (s2 + s3);
     if (is_base) {
       a.grad_base[k] = total;
     } else {
@@ -1128,7 +1128,7 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
     const int64_t b = i / a.ntiles, t = i % a.ntiles;
     s += a.etastat[(b * H + h) * a.ntiles + t];
   }
-  for (int64_t b = threadIdx.x; b < a.B; b += kReduceThreads) s -= a.redundant * a.etadot[b * H + h];
+  for (int64_t b = threadIdx.x; b < a.B; b += kReduceThreads) s -= a.etadot[b * H + h];
   part[threadIdx.x] = s;
   __syncthreads();
   for (int w = kReduceThreads / 2; w > 0; w >>= 1) {
@@ -1136,6 +1136,24 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
     __syncthreads();
   }
   if (threadIdx.x == 0) a.grad_eta[h] = part[0] * bounded_complement_derivative(a.eta_raw[h]);
+}
+
+// x *= w over the three per-(b, h) buffers the solve writes for the parameter
+// gradients (concatenated index space).
+__global__ void param_scale_kernel(float* __restrict__ g0, int64_t n0, float* __restrict__ g1, int64_t n1,
+                                   float* __restrict__ g2, int64_t n2, float w) {
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n0) {
+    g0[i] *= w;
+    return;
+  }
+  i -= n0;
+  if (i < n1) {
+    g1[i] *= w;
+    return;
+  }
+  i -= n1;
+  if (i < n2) g2[i] *= w;
 }
 
 // ============================================================================
@@ -1433,7 +1451,15 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
   pr.R = p.R;
   pr.d = p.d;
   pr.ntiles = p.ntiles;
-  pr.redundant = redundant;
+  if (redundant != 1.0f) {
+    // Sequence-parallel ranks: weight the solve-computed terms before they are reduced.
+    const int64_t n = p.BH * (p.R * p.R + p.d * p.R + 1);
+    LaunchScope scope("param_scale", stream);
+    param_scale_kernel<<<static_cast<unsigned>(ceil_div(n, kReduceThreads)), kReduceThreads, 0, stream>>>(
+        bb.gbase, p.BH * p.R * p.R, bb.gdrive, p.BH * p.d * p.R, bb.etadot, p.BH, redundant);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   const int64_t main_blocks = ceil_div(p.H * p.R * p.R + p.H * p.d * p.R, kReduceThreads);
   LaunchScope scope("param_reduce", stream);
   param_reduce_kernel<<<static_cast<unsigned>(main_blocks + p.H), kReduceThreads, 0, stream>>>(pr);

@@ -92,7 +92,6 @@ struct ParamReduceArgs {
   float* grad_drive;
   float* grad_eta;
   int64_t B, H, R, d, ntiles;
-  float redundant;  // weight of the solve-computed terms (gbase, gdrive, etadot); 1 unless sequence-parallel
 };
 
 struct ForwardBuffers {
