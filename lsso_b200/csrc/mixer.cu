@@ -1104,16 +1104,27 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
     const int64_t h = k / per, e = k % per;
     const float* src = (is_base ? a.gbase : a.gdrive) + h * per + e;
     const int64_t stride = H * per;
-    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    // Sixteen partial sums (sample b goes to sum b % 16), so sixteen loads are
+    // in flight per thread; combined by a fixed pairwise tree.
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
     int64_t b = 0;
-    for (; b + 4 <= a.B; b += 4) {
-      s0 += src[b * stride];
-      s1 += src[(b + 1) * stride];
-      s2 += src[(b + 2) * stride];
-      s3 += src[(b + 3) * stride];
+    for (; b + 16 <= a.B; b += 16) {
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __ldg(src + (b + j) * stride);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] += v[j];
     }
-    for (; b < a.B; ++b) s0 += src[b * stride];
-    const float total = (s0 + s1) + (s2 + s3);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (b + j < a.B) acc[j] += src[(b + j) * stride];
+#pragma unroll
+    for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j) acc[j] += acc[j + w];
+    const float total = acc[0];
     if (is_base) {
       a.grad_base[k] = total;
     } else {

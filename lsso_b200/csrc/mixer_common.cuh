@@ -68,9 +68,9 @@ inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
   const int64_t phase = 0;
   int64_t bytes = 0;
   if (kind <= 1) {
-    // R = 32: lo box + relation/hi box + values; R = 64: per-head [hi | lo] operands.
-    const int64_t ops = R == 32 ? nrel : hg * (2 * R / 64);
-    bytes = (nrel + nval + ops) * kTileBox + phase;
+    // one relation box per item (64 / R heads): lo box + relation/hi box + the value boxes of those heads
+    const int64_t hm = 64 / R;
+    bytes = (2 + (hm * d + 63) / 64) * kTileBox + phase;
   } else if (kind == 2) {
     bytes = (nrel + nval) * kTileBox + phase + hg * d * R * 2;
   } else {

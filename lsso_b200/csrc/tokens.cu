@@ -275,24 +275,21 @@ __device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase
 // per tile, accumulated in TMEM over the chunk; at its end the epilogue drains
 // partial[(b*H + h)][chunk][2R][NC] (rows [0, R) hi products, [R, 2R) lo).
 //
-// R = 32 (two heads per group, fused): slot = [lo box | relation box, rotated
-// to hi in place | value boxes | phase rows].  Per K-step ONE MMA covers both
-// heads: A = [lo | hi] (M = 128: lo_0, lo_1, hi_0, hi_1), B = [hi | values]
-// (forward: N = 64 + hg d: hi_0, hi_1, C_0, C_1) or B = dY (backward); the
-// two 64-feature groups of each operand are consecutive boxes (LBO = 16 KB).
-// The cross-head blocks of the product are computed and ignored.
-//
-// R = 64: per head an MN-major operand [hi | lo] (two groups) in its own
-// buffer and per K-step  D[:, 0:R) += [hi|lo]^T hi,  D[:, R:) += [hi|lo]^T C
-// (forward) or  D += [hi|lo]^T dY (backward).
+// The item's relation features fill one 64-feature box (two heads at R = 32,
+// one head at R = 64): slot = [lo box | relation box, rotated to hi in place |
+// value box].  Per K-step ONE MMA covers the box: A = [lo | hi] (M = 128:
+// the 64 lo rows, then the 64 hi rows), B = [hi | values] (forward: N = 128)
+// or B = dY (backward: N = 64); the two 64-feature groups of each operand are
+// consecutive boxes (LBO = 16 KB).  The value / dY box is the 64-feature box
+// holding the item's heads (at R = 64, d = 32 it also holds the neighbouring
+// head, whose columns are computed and ignored, as are the cross-head blocks
+// at R = 32).
 // ============================================================================
 template <int R, bool BWD>
 __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid_constant__ CUtensorMap tm_rel,
                                                                      const __grid_constant__ CUtensorMap tm_val,
                                                                      const TileArgs a) {
-  constexpr bool kFused = R == 32;
   constexpr int M2 = 2 * R;                       // rows of one head's partial
-  constexpr uint32_t kHead = (M2 / 64) * kBox;    // unfused operand bytes per head
   extern __shared__ uint8_t smem_raw[];
   __shared__ TileShared sh;
   volatile int* abort_v = &sh.abort_flag;
@@ -335,7 +332,8 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
           mbar_arrive_expect_tx(bar, a.load_bytes);
           for (int j = 0; j < a.nrel; ++j)
             tma_load_3d(smem_u32(slot + a.off_rel + j * kBox), &tm_rel, g * a.hg * R + j * 64, row, b, bar);
-          const int vcol0 = (BWD ? 0 : a.H * R) + g * a.hg * d;
+          // the 64-feature boxes holding the item's heads (their first feature rounded down)
+          const int vcol0 = (BWD ? 0 : a.H * R) + ((g * a.hg * d) & ~63);
           for (int j = 0; j < a.nval; ++j)
             tma_load_3d(smem_u32(slot + a.off_val + j * kBox), &tm_val, vcol0 + j * 64, row, b, bar);
           last_use[s] = u;
@@ -346,8 +344,6 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_f = make_idesc(128, BWD ? 64 * a.nval : 64 + 64 * a.nval, true, true);
-    const uint32_t idesc_r = make_idesc(M2, R, true, true);
-    const uint32_t idesc_v = make_idesc(M2, d, true, true);
     int k = 0;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
@@ -362,28 +358,12 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
         tc_fence_after();
         if (ok && lane == 0) {
           const uint32_t slot = smem_u32(smem + static_cast<size_t>(s) * a.slot_bytes);
-          if constexpr (kFused) {
-            const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols);
-            const uint32_t bsrc = slot + (BWD ? a.off_val : a.off_rel);
+          const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols);
+          const uint32_t bsrc = slot + (BWD ? a.off_val : a.off_rel);
 #pragma unroll
-            for (int ks = 0; ks < kTT / 16; ++ks) {
-              mma_bf16(dcol, make_desc_sw128(slot + a.off_aux + ks * 2048, kBox, 1024),
-                       make_desc_sw128(bsrc + ks * 2048, kBox, 1024), idesc_f, (tt > 0 || ks > 0) ? 1u : 0u);
-            }
-          } else {
-            for (int hl = 0; hl < a.hg; ++hl) {
-              const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols + hl * NC);
-              const uint32_t op = slot + a.off_aux + hl * kHead;
-              const int fv = hl * d;
-              const uint32_t vb = slot + a.off_val + (fv >> 6) * kBox + (fv & 63) * 2;
-#pragma unroll
-              for (int ks = 0; ks < kTT / 16; ++ks) {
-                const uint32_t acc = (tt > 0 || ks > 0) ? 1u : 0u;
-                const uint64_t ad = make_desc_sw128(op + ks * 2048, kBox, 1024);
-                if (!BWD) mma_bf16(dcol, ad, ad, idesc_r, acc);
-                mma_bf16(dcol + (BWD ? 0 : R), ad, make_desc_sw128(vb + ks * 2048, kBox, 1024), idesc_v, acc);
-              }
-            }
+          for (int ks = 0; ks < kTT / 16; ++ks) {
+            mma_bf16(dcol, make_desc_sw128(slot + a.off_aux + ks * 2048, kBox, 1024),
+                     make_desc_sw128(bsrc + ks * 2048, kBox, 1024), idesc_f, (tt > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(smem_u32(&sh.sfree[s]));
           if (tt == nt - 1) mma_commit(smem_u32(&sh.tfull[tb]));
@@ -395,7 +375,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     // ------------------------------------------------------------ rotate + hi/lo split
     // The phases of tile k + 1 are fetched (from the L2-resident table) while
     // tile k is transformed, so their latency is off the critical path.
-    constexpr int NCH = ((R == 32 ? 1 : 2) * kTT * 8 + kMXThreads - 1) / kMXThreads;  // chunks per thread
+    constexpr int NCH = (kTT * 8 + kMXThreads - 1) / kMXThreads;  // chunks per thread (one relation box)
     const int xt = threadIdx.x - kXWarp0 * 32;
     const int total = a.nrel * kTT * 8;
     auto fetch = [&](int ii, int tt, Phase4 (&ph)[NCH]) {
@@ -413,11 +393,9 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
         }
       }
     };
-    // One tile ahead at R = 32 (three chunks per thread); at R = 64 a second
-    // register set would spill, so the phases are fetched just before the wait.
-    constexpr bool kAhead = R == 32;
-    Phase4 ph[NCH], phn[kAhead ? NCH : 1];
-    if (kAhead && nloc > 0) fetch(0, 0, ph);
+    // One tile ahead (three chunks per thread).
+    Phase4 ph[NCH], phn[NCH];
+    if (nloc > 0) fetch(0, 0, ph);
     int k = 0;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i) {
@@ -425,14 +403,10 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
       item_of(i, b, g, chunk, t0, nt);
       for (int tt = 0; tt < nt && ok; ++tt, ++k) {
         const int s = k % a.slots, u = k / a.slots;
-        if constexpr (kAhead) {
-          if (tt + 1 < nt) {
-            fetch(i, tt + 1, phn);
-          } else if (i + 1 < nloc) {
-            fetch(i + 1, 0, phn);
-          }
-        } else {
-          fetch(i, tt, ph);
+        if (tt + 1 < nt) {
+          fetch(i, tt + 1, phn);
+        } else if (i + 1 < nloc) {
+          fetch(i + 1, 0, phn);
         }
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) {
@@ -460,8 +434,6 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
               if (kk >= NCH || idx >= total) break;
               int j, r, c;
               chunk_coords(idx, j, r, c);
-              const int f = j * 64 + 8 * c;
-              const int hl = f / R, k0 = f % R;
               uint8_t* src = box_chunk(rel + j * kBox, r, c);
               float v[8];
               rotate8(in[q], ph[kk], v);
@@ -469,25 +441,16 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
               const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
               float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
                              v[4] - h2.x, v[5] - h2.y, v[6] - h3.x, v[7] - h3.y};
-              if constexpr (kFused) {
-                *reinterpret_cast<uint4*>(src) = hi;                                        // hi in place
-                *reinterpret_cast<uint4*>(box_chunk(op + j * kBox, r, c)) = pack8_bf16(lo);  // lo, same position
-              } else {
-                uint8_t* ob = op + hl * kHead;
-                const int mh = k0, ml = R + k0;
-                *reinterpret_cast<uint4*>(box_chunk(ob + (mh >> 6) * kBox, r, (mh & 63) >> 3)) = hi;
-                *reinterpret_cast<uint4*>(box_chunk(ob + (ml >> 6) * kBox, r, (ml & 63) >> 3)) = pack8_bf16(lo);
-              }
+              *reinterpret_cast<uint4*>(src) = hi;                                        // hi in place
+              *reinterpret_cast<uint4*>(box_chunk(op + j * kBox, r, c)) = pack8_bf16(lo);  // lo, same position
             }
           }
           fence_proxy_async();
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
-        if constexpr (kAhead) {
 #pragma unroll
-          for (int kk = 0; kk < NCH; ++kk) ph[kk] = phn[kk];
-        }
+        for (int kk = 0; kk < NCH; ++kk) ph[kk] = phn[kk];
       }
     }
   } else {
@@ -502,39 +465,22 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
-        if constexpr (kFused) {
-          // TMEM lanes: sub 0 lo_0, 1 lo_1, 2 hi_0, 3 hi_1; columns hi_0, hi_1 | values of head 0, head 1.
-          const int hh = sub & 1;
-          const int row = (sub < 2 ? R : 0) + lane;
-          const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hh;
-          float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + row) * static_cast<int64_t>(NC);
-          for (int c0 = 0; c0 < NC; c0 += 32) {
-            const int tc = BWD ? hh * d + c0 : (c0 < R ? 32 * hh + c0 : 64 + hh * d + (c0 - R));
-            float v[32];
-            tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
-            tmem_ld_wait();
+        // TMEM lane = (lo ? 0 : 64) + f for feature f of the relation box:
+        // feature f = 32 (sub & 1) + lane is rank f % R of the item's head f / R.
+        const int f = 32 * (sub & 1) + lane;
+        const int hl = f / R;
+        const int row = (sub < 2 ? R : 0) + f % R;
+        const int voff = (g * a.hg * d) & 63;  // the item's first head inside the value box
+        const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
+        float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + row) * static_cast<int64_t>(NC);
+        for (int c0 = 0; c0 < NC; c0 += 32) {
+          const int tc = BWD ? voff + hl * d + c0 : (c0 < R ? hl * R + c0 : 64 + voff + hl * d + (c0 - R));
+          float v[32];
+          tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
+          tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          }
-        } else {
-          const bool m64 = M2 == 64;
-          const int mrow = m64 ? 16 * sub + lane : 32 * sub + lane;
-          const bool valid = !m64 || lane < 16;
-          for (int hl = 0; hl < a.hg; ++hl) {
-            const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
-            float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + mrow) * static_cast<int64_t>(NC);
-            for (int c0 = 0; c0 < NC; c0 += 32) {
-              float v[32];
-              tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC + c0), v);
-              tmem_ld_wait();
-              if (valid) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                  *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-              }
-            }
-          }
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         }
       }
       tc_fence_before();
@@ -997,24 +943,22 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   }
   TileArgs a = base_args(p, phase, nullptr, status);
   a.partial = partial;
-  if (p.R == 32) {
-    // [lo box | relation box (hi in place) | value boxes | phase rows]
-    a.off_aux = 0;
-    a.off_rel = kBox;
-    a.off_val = 2 * kBox;
-  } else {
-    // [relation boxes | value boxes | per-head [hi | lo] operands | phase rows]
-    a.off_rel = 0;
-    a.off_val = p.nrel * kBox;
-    a.off_aux = (p.nrel + p.nval) * kBox;
-  }
-  a.load_bytes = (p.nrel + p.nval) * kBox;
-  const int cols = p.R == 32 ? (bwd ? 64 * p.nval : 64 + 64 * p.nval)
-                             : p.hg * static_cast<int>((bwd ? 0 : p.R) + p.d);
-  const int items = static_cast<int>(p.B * p.groups * p.nchunks);
+  // One relation box per item: two heads at R = 32, one at R = 64, and the
+  // value boxes holding those heads.  Slot: [lo box | relation box (hi in
+  // place) | value boxes].
+  a.hg = static_cast<int>(64 / p.R);
+  a.groups = static_cast<int>(p.H / a.hg);
+  a.nrel = 1;
+  a.nval = static_cast<int>(ceil_div(a.hg * p.d, 64));
+  a.off_aux = 0;
+  a.off_rel = kBox;
+  a.off_val = 2 * kBox;
+  a.load_bytes = (1 + a.nval) * kBox;
+  const int cols = bwd ? 64 * a.nval : 64 + 64 * a.nval;
+  const int items = static_cast<int>(p.B * a.groups * p.nchunks);
   size_t smem = 0;
   int grid = 0;
-  const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(bwd ? 1 : 0, p.R, p.d, p.hg));
+  const uint32_t slot = static_cast<uint32_t>((2 + a.nval) * kBox);
   if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
   const void* fn = nullptr;
   if (p.R == 32) {
