@@ -140,6 +140,140 @@ __device__ __forceinline__ void tile_store(float* A, int ld, const float (&g)[R 
     for (int b = 0; b < R / 16; ++b) A[(ty + 16 * a) * ld + tx + 16 * b] = g[a][b];
 }
 
+// Panel versions for R <= 32 (one warp covers every row): the factorisation
+// advances kPanel columns at a time.  Warp 0 factorises the column panel in
+// registers (lane i holds row i's kPanel panel entries; the panel's steps are
+// unrolled, pivots and multipliers broadcast by shuffles, no barrier), then the
+// CTA applies the panel's kPanel rank-1 updates to the trailing block in step
+// order, so every element receives exactly the operations, in exactly the
+// order, of the one-step-per-barrier algorithm, with 2 (Cholesky) or 3 (LU)
+// barriers per panel instead of one per step.  P ([R][kPanel] floats of buf)
+// holds the panel's multipliers A[i][k] / A[k][k].
+constexpr int kPanel = 8;
+
+template <int R>
+__device__ __forceinline__ void cholesky_panels(float* A, int ld, float* dinv, float* P) {
+  static_assert(R <= 32, "one warp per panel");
+  const int tid = threadIdx.x, lane = tid & 31;
+  __syncthreads();
+#pragma unroll 1
+  for (int k0 = 0; k0 < R - 1; k0 += kPanel) {
+    const int pw = min(kPanel, R - 1 - k0);  // steps in this panel
+    if (tid < 32) {
+      const int i = lane;
+      float x[kPanel];
+#pragma unroll
+      for (int c = 0; c < kPanel; ++c) x[c] = (i < R && k0 + c < R) ? A[i * ld + k0 + c] : 0.0f;
+#pragma unroll
+      for (int t = 0; t < kPanel; ++t) {
+        if (t < pw) {
+          const float rkk = 1.0f / __shfl_sync(kFull, x[t], k0 + t);
+          const float l = x[t] * rkk;
+#pragma unroll
+          for (int c = t + 1; c < kPanel; ++c) {
+            const float ajk = __shfl_sync(kFull, x[t], (k0 + c) & 31);  // A[k0+c][k0+t]
+            if (i > k0 + t) x[c] = fmaf(-l, ajk, x[c]);
+          }
+          if (i < R) P[i * kPanel + t] = i > k0 + t ? l : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kPanel; ++c)
+        if (i < R && k0 + c < R) A[i * ld + k0 + c] = x[c];
+    }
+    __syncthreads();
+    const int j0 = k0 + kPanel, n = R - j0;
+    for (int e = tid; e < n * n; e += kWThreads) {
+      const int ii = j0 + e / n, jj = j0 + e % n;
+      if (jj > ii) continue;
+      float acc = A[ii * ld + jj];
+#pragma unroll
+      for (int t = 0; t < kPanel; ++t)
+        if (t < pw) acc = fmaf(-P[ii * kPanel + t], A[jj * ld + k0 + t], acc);
+      A[ii * ld + jj] = acc;
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < R * R; e += kWThreads) {
+    const int i = e / R, j = e - i * R;
+    if (j < i) A[i * ld + j] = A[i * ld + j] / sqrtf(A[j * ld + j]);
+    if (j > i) A[i * ld + j] = 0.0f;
+  }
+  __syncthreads();
+  for (int i = tid; i < R; i += kWThreads) {
+    const float piv = sqrtf(A[i * ld + i]);
+    A[i * ld + i] = piv;
+    dinv[i] = 1.0f / piv;
+  }
+  __syncthreads();
+}
+
+template <int R>
+__device__ __forceinline__ void lu_panels(float* M, int ld, float* uinv, float* P) {
+  static_assert(R <= 32, "one warp per panel");
+  const int tid = threadIdx.x, lane = tid & 31;
+  __syncthreads();
+#pragma unroll 1
+  for (int k0 = 0; k0 < R - 1; k0 += kPanel) {
+    const int pw = min(kPanel, R - 1 - k0);
+    if (tid < 32) {
+      const int i = lane;
+      float x[kPanel];
+#pragma unroll
+      for (int c = 0; c < kPanel; ++c) x[c] = (i < R && k0 + c < R) ? M[i * ld + k0 + c] : 0.0f;
+#pragma unroll
+      for (int t = 0; t < kPanel; ++t) {
+        if (t < pw) {
+          const float rkk = 1.0f / __shfl_sync(kFull, x[t], k0 + t);
+          const float l = x[t] * rkk;
+#pragma unroll
+          for (int c = t + 1; c < kPanel; ++c) {
+            const float ukj = __shfl_sync(kFull, x[c], k0 + t);  // M[k0+t][k0+c]
+            if (i > k0 + t) x[c] = fmaf(-l, ukj, x[c]);
+          }
+          if (i < R) P[i * kPanel + t] = i > k0 + t ? l : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kPanel; ++c)
+        if (i < R && k0 + c < R) M[i * ld + k0 + c] = x[c];
+    }
+    __syncthreads();
+    // the panel rows right of the panel: row k0+t receives the steps k0 .. k0+t-1, in order
+    const int j0 = k0 + kPanel, n = R - j0;
+    for (int jj = tid; jj < n; jj += kWThreads) {
+      const int j = j0 + jj;
+      float u[kPanel];
+#pragma unroll
+      for (int t = 0; t < kPanel; ++t) u[t] = k0 + t < R ? M[(k0 + t) * ld + j] : 0.0f;
+#pragma unroll
+      for (int t = 1; t < kPanel; ++t)
+#pragma unroll
+        for (int q = 0; q < t; ++q)
+          if (q < pw) u[t] = fmaf(-P[(k0 + t) * kPanel + q], u[q], u[t]);
+#pragma unroll
+      for (int t = 1; t < kPanel; ++t)
+        if (k0 + t < R) M[(k0 + t) * ld + j] = u[t];
+    }
+    __syncthreads();
+    for (int e = tid; e < n * n; e += kWThreads) {
+      const int ii = j0 + e / n, jj = j0 + e % n;
+      float acc = M[ii * ld + jj];
+#pragma unroll
+      for (int t = 0; t < kPanel; ++t)
+        if (t < pw) acc = fmaf(-P[ii * kPanel + t], M[(k0 + t) * ld + jj], acc);
+      M[ii * ld + jj] = acc;
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < R * R; e += kWThreads) {
+    const int i = e / R, k = e - i * R;
+    if (i > k) M[i * ld + k] = M[i * ld + k] / M[k * ld + k];
+  }
+  for (int i = tid; i < R; i += kWThreads) uinv[i] = 1.0f / M[i * ld + i];
+  __syncthreads();
+}
+
 // Right-looking Cholesky of the lower triangle of the R x R shared matrix A
 // (leading dim ld) in place, with the matrix in register tiles: step k
 // publishes column k (its owners write it to a double-buffered shared
@@ -388,7 +522,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
   float* dinv = fdiag + R;     // [R] 1 / L_ii
   float* uinv = dinv + R;      // [R] 1 / U_ii
   float* Ws = uinv + R;        // [d][R + 1] W_drive of this head
-  float* buf = Ws + d * LD;    // [4R] pivot broadcast of the factorisations
+  float* buf = Ws + d * LD;    // [R * kPanel] panel multipliers / [4R] pivot broadcast of the factorisations
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
   const int64_t b = bh / a.H;
@@ -427,7 +561,11 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     L[i * LD + k] = (L[i * LD + k] + Th[k * LD + i]) * (rsn * rsn) + (i == k ? 1.0f : 0.0f);
   }
   // 2. Cholesky
-  cholesky_block<R>(L, LD, dinv, buf);
+  if constexpr (R <= 32) {
+    cholesky_panels<R>(L, LD, dinv, buf);
+  } else {
+    cholesky_block<R>(L, LD, dinv, buf);
+  }
   // 3. Z = L^{-1} S (columns over the warps)
   {
     float rd[P];
@@ -477,7 +615,11 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     if (tid == 0) tape[tl.n] = n;
   }
   // 6. LU
-  lu_block<R>(Mm, LD, uinv, buf);
+  if constexpr (R <= 32) {
+    lu_panels<R>(Mm, LD, uinv, buf);
+  } else {
+    lu_block<R>(Mm, LD, uinv, buf);
+  }
   if (tape != nullptr) {
     for (int idx = tid; idx < R * R; idx += kWThreads) tape[tl.LU + idx] = Mm[(idx / R) * LD + idx % R];
   }
@@ -766,7 +908,7 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
 
 template <int R>
 size_t fwd_smem(int d) {
-  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + 4 * R);
+  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + (R <= 32 ? kPanel : 4) * R);
 }
 template <int R>
 size_t bwd_smem(int d) {
