@@ -11,8 +11,11 @@
 //     replacing a thread-per-column R^2 chain; transposed solves read the
 //     matrix by columns (one column view of the packed LU serves both U^T and
 //     the unit L^T);
-//   - Cholesky and LU are right-looking over the whole CTA, one barrier per
-//     step (rows over warps, columns over lanes);
+//   - Cholesky and LU advance eight columns per panel: warp 0 factorises the
+//     panel in registers with shuffles, the CTA applies the panel's updates to
+//     the trailing block (2-3 barriers per panel);
+//   - the r x r and r x d products are register-blocked over a 16 x 16 thread
+//     grid;
 //   - all d columns of the R x d operands stay in shared memory, split over
 //     the CTA's warps;
 //   - the chunk partials of the moment pass are summed with coalesced float4
@@ -118,68 +121,71 @@ __device__ __forceinline__ void lane_rows(const float* v, float (&rd)[rows_per_l
   for (int p = 0; p < rows_per_lane<R>(); ++p) rd[p] = 32 * p + lane < R ? v[32 * p + lane] : 1.0f;
 }
 
-// Register tiles: thread (ty, tx) of the CTA's 16 x 16 grid owns the
-// elements (ty + 16 a, tx + 16 b), a, b < R / 16, of an R x R matrix.
-template <int R>
-__device__ __forceinline__ void tile_load(const float* A, int ld, float (&g)[R / 16][R / 16], bool lower_only) {
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-#pragma unroll
-  for (int a = 0; a < R / 16; ++a)
-#pragma unroll
-    for (int b = 0; b < R / 16; ++b) {
-      const int i = ty + 16 * a, j = tx + 16 * b;
-      g[a][b] = (!lower_only || j <= i) ? A[i * ld + j] : 0.0f;
-    }
-}
-template <int R>
-__device__ __forceinline__ void tile_store(float* A, int ld, const float (&g)[R / 16][R / 16]) {
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-#pragma unroll
-  for (int a = 0; a < R / 16; ++a)
-#pragma unroll
-    for (int b = 0; b < R / 16; ++b) A[(ty + 16 * a) * ld + tx + 16 * b] = g[a][b];
-}
-
-// Panel versions for R <= 32 (one warp covers every row): the factorisation
-// advances kPanel columns at a time.  Warp 0 factorises the column panel in
-// registers (lane i holds row i's kPanel panel entries; the panel's steps are
-// unrolled, pivots and multipliers broadcast by shuffles, no barrier), then the
-// CTA applies the panel's kPanel rank-1 updates to the trailing block in step
-// order, so every element receives exactly the operations, in exactly the
-// order, of the one-step-per-barrier algorithm, with 2 (Cholesky) or 3 (LU)
-// barriers per panel instead of one per step.  P ([R][kPanel] floats of buf)
-// holds the panel's multipliers A[i][k] / A[k][k].
+// Panel factorisations: the factorisation advances kPanel columns at a time.
+// Warp 0 factorises the column panel in registers (lane l holds the panel
+// entries of rows l and l + 32; the panel's steps are unrolled, pivots and
+// multipliers broadcast by shuffles, no barrier), then the CTA applies the
+// panel's rank-1 updates to the trailing block in step order, so every
+// element receives exactly the operations, in exactly the order, of the
+// one-step-per-barrier algorithm, with 2 (Cholesky) or 3 (LU) barriers per
+// panel instead of one per step.  Pn ([R][kPanel] floats) holds the panel's
+// multipliers A[i][k] / A[k][k].
 constexpr int kPanel = 8;
 
+// Value of row `row` (panel register slot row >> 5) held by lane row & 31,
+// broadcast to the warp.
+template <int P>
+__device__ __forceinline__ float row_value(const float (&x)[P][kPanel], int row, int c) {
+  const float v = (P > 1 && (row >> 5) != 0) ? x[P - 1][c] : x[0][c];
+  return __shfl_sync(kFull, v, row & 31);
+}
+
 template <int R>
-__device__ __forceinline__ void cholesky_panels(float* A, int ld, float* dinv, float* P) {
-  static_assert(R <= 32, "one warp per panel");
+__device__ __forceinline__ void cholesky_panels(float* A, int ld, float* dinv, float* Pn) {
+  constexpr int P = rows_per_lane<R>();
   const int tid = threadIdx.x, lane = tid & 31;
   __syncthreads();
 #pragma unroll 1
   for (int k0 = 0; k0 < R - 1; k0 += kPanel) {
     const int pw = min(kPanel, R - 1 - k0);  // steps in this panel
     if (tid < 32) {
-      const int i = lane;
-      float x[kPanel];
+      float x[P][kPanel];
 #pragma unroll
-      for (int c = 0; c < kPanel; ++c) x[c] = (i < R && k0 + c < R) ? A[i * ld + k0 + c] : 0.0f;
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int c = 0; c < kPanel; ++c) {
+          const int row = 32 * p + lane;
+          x[p][c] = (row < R && k0 + c < R) ? A[row * ld + k0 + c] : 0.0f;
+        }
 #pragma unroll
       for (int t = 0; t < kPanel; ++t) {
         if (t < pw) {
-          const float rkk = 1.0f / __shfl_sync(kFull, x[t], k0 + t);
-          const float l = x[t] * rkk;
+          const int kt = k0 + t;
+          const float rkk = 1.0f / row_value<P>(x, kt, t);
+          float l[P];
+#pragma unroll
+          for (int p = 0; p < P; ++p) l[p] = x[p][t] * rkk;
 #pragma unroll
           for (int c = t + 1; c < kPanel; ++c) {
-            const float ajk = __shfl_sync(kFull, x[t], (k0 + c) & 31);  // A[k0+c][k0+t]
-            if (i > k0 + t) x[c] = fmaf(-l, ajk, x[c]);
+            const float ajk = row_value<P>(x, (k0 + c) < R ? k0 + c : R - 1, t);  // A[k0+c][kt]
+#pragma unroll
+            for (int p = 0; p < P; ++p)
+              if (32 * p + lane > kt) x[p][c] = fmaf(-l[p], ajk, x[p][c]);
           }
-          if (i < R) P[i * kPanel + t] = i > k0 + t ? l : 0.0f;
+#pragma unroll
+          for (int p = 0; p < P; ++p) {
+            const int row = 32 * p + lane;
+            if (row < R) Pn[row * kPanel + t] = row > kt ? l[p] : 0.0f;
+          }
         }
       }
 #pragma unroll
-      for (int c = 0; c < kPanel; ++c)
-        if (i < R && k0 + c < R) A[i * ld + k0 + c] = x[c];
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int c = 0; c < kPanel; ++c) {
+          const int row = 32 * p + lane;
+          if (row < R && k0 + c < R) A[row * ld + k0 + c] = x[p][c];
+        }
     }
     __syncthreads();
     const int j0 = k0 + kPanel, n = R - j0;
@@ -189,7 +195,7 @@ __device__ __forceinline__ void cholesky_panels(float* A, int ld, float* dinv, f
       float acc = A[ii * ld + jj];
 #pragma unroll
       for (int t = 0; t < kPanel; ++t)
-        if (t < pw) acc = fmaf(-P[ii * kPanel + t], A[jj * ld + k0 + t], acc);
+        if (t < pw) acc = fmaf(-Pn[ii * kPanel + t], A[jj * ld + k0 + t], acc);
       A[ii * ld + jj] = acc;
     }
     __syncthreads();
@@ -209,34 +215,51 @@ __device__ __forceinline__ void cholesky_panels(float* A, int ld, float* dinv, f
 }
 
 template <int R>
-__device__ __forceinline__ void lu_panels(float* M, int ld, float* uinv, float* P) {
-  static_assert(R <= 32, "one warp per panel");
+__device__ __forceinline__ void lu_panels(float* M, int ld, float* uinv, float* Pn) {
+  constexpr int P = rows_per_lane<R>();
   const int tid = threadIdx.x, lane = tid & 31;
   __syncthreads();
 #pragma unroll 1
   for (int k0 = 0; k0 < R - 1; k0 += kPanel) {
     const int pw = min(kPanel, R - 1 - k0);
     if (tid < 32) {
-      const int i = lane;
-      float x[kPanel];
+      float x[P][kPanel];
 #pragma unroll
-      for (int c = 0; c < kPanel; ++c) x[c] = (i < R && k0 + c < R) ? M[i * ld + k0 + c] : 0.0f;
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int c = 0; c < kPanel; ++c) {
+          const int row = 32 * p + lane;
+          x[p][c] = (row < R && k0 + c < R) ? M[row * ld + k0 + c] : 0.0f;
+        }
 #pragma unroll
       for (int t = 0; t < kPanel; ++t) {
         if (t < pw) {
-          const float rkk = 1.0f / __shfl_sync(kFull, x[t], k0 + t);
-          const float l = x[t] * rkk;
+          const int kt = k0 + t;
+          const float rkk = 1.0f / row_value<P>(x, kt, t);
+          float l[P];
+#pragma unroll
+          for (int p = 0; p < P; ++p) l[p] = x[p][t] * rkk;
 #pragma unroll
           for (int c = t + 1; c < kPanel; ++c) {
-            const float ukj = __shfl_sync(kFull, x[c], k0 + t);  // M[k0+t][k0+c]
-            if (i > k0 + t) x[c] = fmaf(-l, ukj, x[c]);
+            const float ukj = row_value<P>(x, kt, c);  // M[kt][k0+c]
+#pragma unroll
+            for (int p = 0; p < P; ++p)
+              if (32 * p + lane > kt) x[p][c] = fmaf(-l[p], ukj, x[p][c]);
           }
-          if (i < R) P[i * kPanel + t] = i > k0 + t ? l : 0.0f;
+#pragma unroll
+          for (int p = 0; p < P; ++p) {
+            const int row = 32 * p + lane;
+            if (row < R) Pn[row * kPanel + t] = row > kt ? l[p] : 0.0f;
+          }
         }
       }
 #pragma unroll
-      for (int c = 0; c < kPanel; ++c)
-        if (i < R && k0 + c < R) M[i * ld + k0 + c] = x[c];
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int c = 0; c < kPanel; ++c) {
+          const int row = 32 * p + lane;
+          if (row < R && k0 + c < R) M[row * ld + k0 + c] = x[p][c];
+        }
     }
     __syncthreads();
     // the panel rows right of the panel: row k0+t receives the steps k0 .. k0+t-1, in order
@@ -250,7 +273,7 @@ __device__ __forceinline__ void lu_panels(float* M, int ld, float* uinv, float* 
       for (int t = 1; t < kPanel; ++t)
 #pragma unroll
         for (int q = 0; q < t; ++q)
-          if (q < pw) u[t] = fmaf(-P[(k0 + t) * kPanel + q], u[q], u[t]);
+          if (q < pw) u[t] = fmaf(-Pn[(k0 + t) * kPanel + q], u[q], u[t]);
 #pragma unroll
       for (int t = 1; t < kPanel; ++t)
         if (k0 + t < R) M[(k0 + t) * ld + j] = u[t];
@@ -261,120 +284,11 @@ __device__ __forceinline__ void lu_panels(float* M, int ld, float* uinv, float* 
       float acc = M[ii * ld + jj];
 #pragma unroll
       for (int t = 0; t < kPanel; ++t)
-        if (t < pw) acc = fmaf(-P[ii * kPanel + t], M[(k0 + t) * ld + jj], acc);
+        if (t < pw) acc = fmaf(-Pn[ii * kPanel + t], M[(k0 + t) * ld + jj], acc);
       M[ii * ld + jj] = acc;
     }
     __syncthreads();
   }
-  for (int e = tid; e < R * R; e += kWThreads) {
-    const int i = e / R, k = e - i * R;
-    if (i > k) M[i * ld + k] = M[i * ld + k] / M[k * ld + k];
-  }
-  for (int i = tid; i < R; i += kWThreads) uinv[i] = 1.0f / M[i * ld + i];
-  __syncthreads();
-}
-
-// Right-looking Cholesky of the lower triangle of the R x R shared matrix A
-// (leading dim ld) in place, with the matrix in register tiles: step k
-// publishes column k (its owners write it to a double-buffered shared
-// vector, one barrier) and every thread subtracts A[i][k] A[j][k] / A[k][k]
-// from its trailing elements; column k is final after step k, and the
-// columns are scaled to L[i][k] = A[i][k] / sqrt(A[k][k]) at the end (0 above
-// the diagonal).  dinv[i] = 1 / L_ii.  buf holds 2 R floats.  All threads call it.
-template <int R>
-__device__ __forceinline__ void cholesky_block(float* A, int ld, float* dinv, float* buf) {
-  constexpr int T = R / 16;
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  __syncthreads();
-  float g[T][T];
-  tile_load<R>(A, ld, g, true);
-#pragma unroll 1
-  for (int k = 0; k < R - 1; ++k) {
-    float* col = buf + (k & 1) * R;
-    const int kb = k >> 4, kr = k & 15;
-    if (tx == kr) {
-#pragma unroll
-      for (int b = 0; b < T; ++b)
-        if (b == kb)
-#pragma unroll
-          for (int a = 0; a < T; ++a) col[ty + 16 * a] = g[a][b];
-    }
-    __syncthreads();
-    const float rkk = 1.0f / col[k];
-    float l[T], w[T];
-#pragma unroll
-    for (int a = 0; a < T; ++a) l[a] = ty + 16 * a > k ? col[ty + 16 * a] * rkk : 0.0f;
-#pragma unroll
-    for (int b = 0; b < T; ++b) w[b] = tx + 16 * b > k ? col[tx + 16 * b] : 0.0f;
-#pragma unroll
-    for (int a = 0; a < T; ++a)
-#pragma unroll
-      for (int b = 0; b < T; ++b) g[a][b] = fmaf(-l[a], w[b], g[a][b]);
-  }
-  tile_store<R>(A, ld, g);
-  __syncthreads();
-  for (int e = tid; e < R * R; e += kWThreads) {
-    const int i = e / R, j = e - i * R;
-    if (j < i) A[i * ld + j] = A[i * ld + j] / sqrtf(A[j * ld + j]);
-    if (j > i) A[i * ld + j] = 0.0f;
-  }
-  __syncthreads();
-  for (int i = tid; i < R; i += kWThreads) {
-    const float piv = sqrtf(A[i * ld + i]);
-    A[i * ld + i] = piv;
-    dinv[i] = 1.0f / piv;
-  }
-  __syncthreads();
-}
-
-// Doolittle LU without pivoting of the R x R shared matrix M in place, with
-// the matrix in register tiles: step k publishes column k and row k
-// (double-buffered, one barrier) and every thread subtracts
-// M[i][k] M[k][j] / M[k][k] from its trailing elements; column k is final
-// after step k, and the unit lower factor M[i][k] / M[k][k] is formed at the
-// end.  uinv[i] = 1 / U_ii.  buf holds 4 R floats.  All threads call it.
-template <int R>
-__device__ __forceinline__ void lu_block(float* M, int ld, float* uinv, float* buf) {
-  constexpr int T = R / 16;
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  __syncthreads();
-  float m[T][T];
-  tile_load<R>(M, ld, m, false);
-#pragma unroll 1
-  for (int k = 0; k < R - 1; ++k) {
-    float* col = buf + (k & 1) * 2 * R;
-    float* row = col + R;
-    const int kb = k >> 4, kr = k & 15;
-    if (tx == kr) {
-#pragma unroll
-      for (int b = 0; b < T; ++b)
-        if (b == kb)
-#pragma unroll
-          for (int a = 0; a < T; ++a) col[ty + 16 * a] = m[a][b];
-    }
-    if (ty == kr) {
-#pragma unroll
-      for (int a = 0; a < T; ++a)
-        if (a == kb)
-#pragma unroll
-          for (int b = 0; b < T; ++b) row[tx + 16 * b] = m[a][b];
-    }
-    __syncthreads();
-    const float rkk = 1.0f / row[k];
-    float l[T], u[T];
-#pragma unroll
-    for (int a = 0; a < T; ++a) l[a] = ty + 16 * a > k ? col[ty + 16 * a] * rkk : 0.0f;
-#pragma unroll
-    for (int b = 0; b < T; ++b) u[b] = tx + 16 * b > k ? row[tx + 16 * b] : 0.0f;
-#pragma unroll
-    for (int a = 0; a < T; ++a)
-#pragma unroll
-      for (int b = 0; b < T; ++b) m[a][b] = fmaf(-l[a], u[b], m[a][b]);
-  }
-  tile_store<R>(M, ld, m);
-  __syncthreads();
   for (int e = tid; e < R * R; e += kWThreads) {
     const int i = e / R, k = e - i * R;
     if (i > k) M[i * ld + k] = M[i * ld + k] / M[k * ld + k];
@@ -522,7 +436,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
   float* dinv = fdiag + R;     // [R] 1 / L_ii
   float* uinv = dinv + R;      // [R] 1 / U_ii
   float* Ws = uinv + R;        // [d][R + 1] W_drive of this head
-  float* buf = Ws + d * LD;    // [R * kPanel] panel multipliers / [4R] pivot broadcast of the factorisations
+  float* buf = Ws + d * LD;    // [R * kPanel] panel multipliers of the factorisations
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
   const int64_t b = bh / a.H;
@@ -561,11 +475,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     L[i * LD + k] = (L[i * LD + k] + Th[k * LD + i]) * (rsn * rsn) + (i == k ? 1.0f : 0.0f);
   }
   // 2. Cholesky
-  if constexpr (R <= 32) {
-    cholesky_panels<R>(L, LD, dinv, buf);
-  } else {
-    cholesky_block<R>(L, LD, dinv, buf);
-  }
+  cholesky_panels<R>(L, LD, dinv, buf);
   // 3. Z = L^{-1} S (columns over the warps)
   {
     float rd[P];
@@ -615,11 +525,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     if (tid == 0) tape[tl.n] = n;
   }
   // 6. LU
-  if constexpr (R <= 32) {
-    lu_panels<R>(Mm, LD, uinv, buf);
-  } else {
-    lu_block<R>(Mm, LD, uinv, buf);
-  }
+  lu_panels<R>(Mm, LD, uinv, buf);
   if (tape != nullptr) {
     for (int idx = tid; idx < R * R; idx += kWThreads) tape[tl.LU + idx] = Mm[(idx / R) * LD + idx % R];
   }
@@ -908,7 +814,7 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
 
 template <int R>
 size_t fwd_smem(int d) {
-  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + (R <= 32 ? kPanel : 4) * R);
+  return sizeof(float) * (3 * R * (R + 1) + R * (d + 1) + 3 * R + d * (R + 1) + kPanel * R);
 }
 template <int R>
 size_t bwd_smem(int d) {
