@@ -64,7 +64,7 @@ constexpr int kTileMaxSlots = 6;
 // slot holds the item's boxes and operand matrices; the rotation warps read
 // FP32 phases into registers, the gradient kernel also stages FP16 phase rows.
 inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
-  const int64_t nrel = hg * R / 64, nval = hg * d / 64;
+  const int64_t nrel = (hg * R + 63) / 64, nval = hg * d / 64;  // relation boxes: hg*R features from hg*R*g
   const int64_t phase = 0;
   int64_t bytes = 0;
   if (kind <= 1) {
@@ -91,7 +91,7 @@ inline int tile_slots(int64_t slot_bytes) {
 inline void plan_tiles(Plan& p, int sm_count) {
   p.tiled = false;
   p.tiled_grad = false;
-  const bool r_ok = p.R == 32 || p.R == 64;
+  const bool r_ok = p.R == 32 || p.R == 48 || p.R == 64;
   const bool d_ok = p.d == 32 || p.d == 64;
   if (!r_ok || !d_ok || (p.W % 8) != 0 || p.D != p.H * p.d) return;
   const int hg = static_cast<int>(64 / (p.R < p.d ? p.R : p.d));
@@ -101,7 +101,7 @@ inline void plan_tiles(Plan& p, int sm_count) {
   p.tiled_grad = tile_slots(tile_slot_bytes(3, p.R, p.d, hg)) >= 2;
   p.hg = hg;
   p.groups = static_cast<int>(p.H / hg);
-  p.nrel = static_cast<int>(hg * p.R / 64);
+  p.nrel = static_cast<int>((hg * p.R + 63) / 64);
   p.nval = static_cast<int>(hg * p.d / 64);
   const int64_t ntiles = (p.N + kTileTokens - 1) / kTileTokens;
   const int64_t pairs = p.B * p.groups;

@@ -69,9 +69,12 @@ struct TileArgs {
   const bf16* m1;  // grad: B1c
   const bf16* m2;  // grad: B1a
   float* partial;  // moment partials [B*H][nchunks][2R][NC]
+  bf16* gproj;     // gradient pass: packed gradient [B][N][W], for relation features outside whole boxes
   float* etastat;  // [B*H][ntiles]
   int* status;
   int N, H, d, hg, groups, nrel, nval, ntiles, ct, nchunks, items, pos_batched, slots, nbuf, cols;
+  int rel_tma;          // gradient pass: relation boxes wholly inside the group (stored by TMA)
+  int W;                // packed width
   uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
   uint32_t off_val;     // content (or dY) boxes
   uint32_t off_aux;     // grad: dY boxes; moments: operand buffer (R = 32: the lo box)
@@ -467,20 +470,28 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
       if (ok) {
         // TMEM lane = (lo ? 0 : 64) + f for feature f of the relation box:
         // feature f = 32 (sub & 1) + lane is rank f % R of the item's head f / R.
+        // (at R = 48 the box's last 16 features belong to the next head: computed, not stored)
         const int f = 32 * (sub & 1) + lane;
         const int hl = f / R;
+        const bool mine = hl < a.hg;
         const int row = (sub < 2 ? R : 0) + f % R;
         const int voff = (g * a.hg * d) & 63;  // the item's first head inside the value box
-        const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + hl;
+        const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + (mine ? hl : 0);
         float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + row) * static_cast<int64_t>(NC);
+        // Gram columns (forward only), in pieces of at most 32, then the value columns
         for (int c0 = 0; c0 < NC; c0 += 32) {
-          const int tc = BWD ? voff + hl * d + c0 : (c0 < R ? hl * R + c0 : 64 + voff + hl * d + (c0 - R));
+          const bool gram = !BWD && c0 < R;
+          const int n = gram ? min(32, R - c0) : 32;
+          const int tc = BWD ? voff + hl * d + c0 : (gram ? hl * R + c0 : 64 + voff + hl * d + (c0 - R));
           float v[32];
           tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
           tmem_ld_wait();
+          if (mine) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            for (int j = 0; j < 32; j += 4)
+              if (j < n) *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+          if (gram && n < 32) c0 -= 32 - n;  // the value columns start right after the Gram columns
         }
       }
       tc_fence_before();
@@ -781,20 +792,30 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
       if (ok) {
         for (int hl = half; hl < a.hg; hl += 2) {
           const uint32_t tcol = lane_base + static_cast<uint32_t>(tb * a.cols + hl * NC);
-          // relation gradient: rotate dA' back and overwrite the relation box
+          // relation gradient: rotate dA' back and overwrite the relation box (features
+          // in a box the group only partly owns, at R = 48, go straight to global memory)
           for (int r0 = 0; r0 < R; r0 += 32) {
             float gv[32];
             tmem_ld32(tcol + r0, gv);
             tmem_ld_wait();
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
+              if constexpr (R % 32 != 0) {
+                if (r0 + 8 * q >= R) break;
+              }
               const int f = hl * R + r0 + 8 * q;
               const Phase4 ph = phase_rows16(phs, r, tok, a.N, R, (r0 >> 3) + q);
               const float gi[8] = {gv[8 * q], gv[8 * q + 1], gv[8 * q + 2], gv[8 * q + 3],
                                    gv[8 * q + 4], gv[8 * q + 5], gv[8 * q + 6], gv[8 * q + 7]};
               float o[8];
               rotate8_transpose(gi, ph, o);
-              *reinterpret_cast<uint4*>(box_chunk(slot + (f >> 6) * kBox, r, (f & 63) >> 3)) = pack8_bf16(o);
+              const uint4 packed = pack8_bf16(o);
+              if (R % 32 == 0 || (f >> 6) < a.rel_tma) {  // R = 32, 64: every box wholly the group's
+                *reinterpret_cast<uint4*>(box_chunk(slot + (f >> 6) * kBox, r, (f & 63) >> 3)) = packed;
+              } else if (tok < a.N) {
+                *reinterpret_cast<uint4*>(a.gproj + (static_cast<int64_t>(x.b) * a.N + tok) * a.W +
+                                          x.g * a.hg * R + f) = packed;
+              }
             }
           }
           // content gradient eta dY + dC, and the statistic sum(dY * C)
@@ -848,7 +869,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
         if (ok) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
           uint8_t* con = slot + a.off_val;
-          for (int j = 0; j < a.nrel; ++j)
+          for (int j = 0; j < a.rel_tma; ++j)
             tma_store_3d(&tm_gproj, smem_u32(slot + j * kBox), x.g * a.hg * R + j * 64, x.t * kTT, x.b);
           for (int j = 0; j < a.nval; ++j)
             tma_store_3d(&tm_gproj, smem_u32(con + j * kBox), a.H * R + x.g * a.hg * d + j * 64, x.t * kTT, x.b);
@@ -919,6 +940,8 @@ TileArgs base_args(const Plan& p, const float2* phase, const float* eta_raw, int
   a.ct = p.ct;
   a.nchunks = static_cast<int>(p.nchunks);
   a.pos_batched = p.pos_rows > 1 ? 1 : 0;
+  a.W = static_cast<int>(p.W);
+  a.rel_tma = static_cast<int>(p.hg * p.R / 64);
   return a;
 }
 
@@ -961,12 +984,14 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   const uint32_t slot = static_cast<uint32_t>((2 + a.nval) * kBox);
   if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
   const void* fn = nullptr;
-  if (p.R == 32) {
-    fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<32, true>)
-             : reinterpret_cast<const void*>(&moments_tile_kernel<32, false>);
-  } else {
-    fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<64, true>)
-             : reinterpret_cast<const void*>(&moments_tile_kernel<64, false>);
+  switch (p.R) {
+    case 32: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<32, true>)
+                      : reinterpret_cast<const void*>(&moments_tile_kernel<32, false>); break;
+    case 48: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<48, true>)
+                      : reinterpret_cast<const void*>(&moments_tile_kernel<48, false>); break;
+    case 64: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<64, true>)
+                      : reinterpret_cast<const void*>(&moments_tile_kernel<64, false>); break;
+    default: return cudaErrorInvalidValue;
   }
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
@@ -974,6 +999,9 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   if (p.R == 32) {
     if (bwd) moments_tile_kernel<32, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
     else moments_tile_kernel<32, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+  } else if (p.R == 48) {
+    if (bwd) moments_tile_kernel<48, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    else moments_tile_kernel<48, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
   } else {
     if (bwd) moments_tile_kernel<64, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
     else moments_tile_kernel<64, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
@@ -998,13 +1026,16 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* 
   int grid = 0;
   const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(2, p.R, p.d, p.hg));
   if (!finish_args(a, slot, p.hg * static_cast<int>(p.d), items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
-  const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
-                             : reinterpret_cast<const void*>(&readout_tile_kernel<64>);
+  const void* fn = p.R == 32   ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
+                   : p.R == 48 ? reinterpret_cast<const void*>(&readout_tile_kernel<48>)
+                               : reinterpret_cast<const void*>(&readout_tile_kernel<64>);
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("readout", stream);
   if (p.R == 32) {
     readout_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
+  } else if (p.R == 48) {
+    readout_tile_kernel<48><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
   } else {
     readout_tile_kernel<64><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
   }
@@ -1025,6 +1056,7 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   a.m1 = b1c;
   a.m2 = b1a;
   a.etastat = etastat;
+  a.gproj = gproj;
   a.off_val = p.nrel * kBox;
   a.off_aux = (p.nrel + p.nval) * kBox;
   a.off_ph = (p.nrel + 2 * p.nval) * kBox;
@@ -1037,13 +1069,16 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(3, p.R, p.d, p.hg));
   if (!finish_args(a, slot, p.hg * static_cast<int>(p.R + p.d), items, sm_count, &smem, &grid))
     return cudaErrorInvalidValue;
-  const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
-                             : reinterpret_cast<const void*>(&grad_tile_kernel<64>);
+  const void* fn = p.R == 32   ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
+                   : p.R == 48 ? reinterpret_cast<const void*>(&grad_tile_kernel<48>)
+                               : reinterpret_cast<const void*>(&grad_tile_kernel<64>);
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("grad", stream);
   if (p.R == 32) {
     grad_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+  } else if (p.R == 48) {
+    grad_tile_kernel<48><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
   } else {
     grad_tile_kernel<64><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
   }

@@ -84,6 +84,8 @@ EXPANDED = [
     (1, 32, 8, 32, 4096), (1, 16, 4, 32, 4776), (1, 32, 1, 17, 8193), (2, 64, 2, 384, 40), (1, 48, 3, 256, 70),
     # head-group tile kernels: r = 64 with d = 32 (gradient pass per head), r = 64 / d = 64, r = 32 / d = 64
     (2, 64, 2, 32, 300), (1, 64, 2, 64, 300), (1, 32, 2, 64, 300), (1, 64, 4, 32, 1100),
+    # r = 48 tiles: two heads per group (relation boxes partly owned), and one head per group at d = 64
+    (2, 48, 2, 32, 300), (1, 48, 4, 32, 1100), (1, 48, 2, 64, 333), (1, 48, 8, 32, 4096),
 ]
 
 
@@ -97,7 +99,8 @@ def test_expanded_shapes_match_oracle(batch, rank, heads, head_dim, length) -> N
 
 
 @pytest.mark.parametrize(("rank", "head_dim", "length"),
-                         [(16, 17, 35), (32, 64, 35), (48, 96, 35), (64, 257, 35), (16, 17, 2048), (64, 17, 2017)])
+                         [(16, 17, 35), (32, 64, 35), (48, 96, 35), (64, 257, 35), (16, 17, 2048), (64, 17, 2017),
+                          (48, 32, 513), (32, 32, 513)])
 def test_masked_batch_specific_positions_match_oracle(rank, head_dim, length) -> None:
     pattern = torch.tensor([True, False, True, True, False, True, True])
     first = pattern.repeat((length + 6) // 7)[:length]
