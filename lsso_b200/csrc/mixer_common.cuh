@@ -91,11 +91,13 @@ inline int tile_slots(int64_t slot_bytes) {
 inline void plan_tiles(Plan& p, int sm_count) {
   p.tiled = false;
   p.tiled_grad = false;
-  const bool r_ok = p.R == 32 || p.R == 48 || p.R == 64;
+  const bool r_ok = p.R == 16 || p.R == 32 || p.R == 48 || p.R == 64;
   const bool d_ok = p.d == 32 || p.d == 64;
   if (!r_ok || !d_ok || (p.W % 8) != 0 || p.D != p.H * p.d) return;
   const int hg = static_cast<int>(64 / (p.R < p.d ? p.R : p.d));
   if (p.H % hg != 0) return;
+  // the moment pass's fused MMA has N = 64 + the value boxes of 64 / R heads (at most 256)
+  if (64 + 64 * (((64 / p.R) * p.d + 63) / 64) > 256) return;
   for (int kind = 0; kind < 3; ++kind)
     if (tile_slots(tile_slot_bytes(kind, p.R, p.d, hg)) < 2) return;
   p.tiled_grad = tile_slots(tile_slot_bytes(3, p.R, p.d, hg)) >= 2;

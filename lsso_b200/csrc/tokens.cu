@@ -470,28 +470,34 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
       if (ok) {
         // TMEM lane = (lo ? 0 : 64) + f for feature f of the relation box:
         // feature f = 32 (sub & 1) + lane is rank f % R of the item's head f / R.
-        // (at R = 48 the box's last 16 features belong to the next head: computed, not stored)
-        const int f = 32 * (sub & 1) + lane;
+        // (at R = 48 the box's last 16 features belong to the next head: computed, not
+        // stored).  A TMEM load takes one column address per warp, so a warp whose
+        // 32 lanes span two heads (R = 16) loads once per head.
+        const int f0 = 32 * (sub & 1);
+        const int f = f0 + lane;
         const int hl = f / R;
         const bool mine = hl < a.hg;
         const int row = (sub < 2 ? R : 0) + f % R;
         const int voff = (g * a.hg * d) & 63;  // the item's first head inside the value box
         const int64_t bh = static_cast<int64_t>(b) * a.H + g * a.hg + (mine ? hl : 0);
         float* out = a.partial + ((bh * a.nchunks + chunk) * M2 + row) * static_cast<int64_t>(NC);
-        // Gram columns (forward only), in pieces of at most 32, then the value columns
-        for (int c0 = 0; c0 < NC; c0 += 32) {
-          const bool gram = !BWD && c0 < R;
-          const int n = gram ? min(32, R - c0) : 32;
-          const int tc = BWD ? voff + hl * d + c0 : (gram ? hl * R + c0 : 64 + voff + hl * d + (c0 - R));
-          float v[32];
-          tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
-          tmem_ld_wait();
-          if (mine) {
+        const int hw_last = min(a.hg - 1, (f0 + 31) / R);
+        for (int hw = f0 / R; hw <= hw_last; ++hw) {
+          // Gram columns (forward only), in pieces of at most 32, then the value columns
+          for (int c0 = 0; c0 < NC; c0 += 32) {
+            const bool gram = !BWD && c0 < R;
+            const int n = gram ? min(32, R - c0) : 32;
+            const int tc = BWD ? voff + hw * d + c0 : (gram ? hw * R + c0 : 64 + voff + hw * d + (c0 - R));
+            float v[32];
+            tmem_ld32(lane_base + static_cast<uint32_t>(tb * a.cols + tc), v);
+            tmem_ld_wait();
+            if (mine && hl == hw) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              if (j < n) *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              for (int j = 0; j < 32; j += 4)
+                if (j < n) *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+            if (gram && n < 32) c0 -= 32 - n;  // the value columns start right after the Gram columns
           }
-          if (gram && n < 32) c0 -= 32 - n;  // the value columns start right after the Gram columns
         }
       }
       tc_fence_before();
@@ -810,7 +816,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
               float o[8];
               rotate8_transpose(gi, ph, o);
               const uint4 packed = pack8_bf16(o);
-              if (R % 32 == 0 || (f >> 6) < a.rel_tma) {  // R = 32, 64: every box wholly the group's
+              if (R != 48 || (f >> 6) < a.rel_tma) {  // R = 16, 32, 64: every box wholly the group's
                 *reinterpret_cast<uint4*>(box_chunk(slot + (f >> 6) * kBox, r, (f & 63) >> 3)) = packed;
               } else if (tok < a.N) {
                 *reinterpret_cast<uint4*>(a.gproj + (static_cast<int64_t>(x.b) * a.N + tok) * a.W +
@@ -985,6 +991,8 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
   const void* fn = nullptr;
   switch (p.R) {
+    case 16: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<16, true>)
+                      : reinterpret_cast<const void*>(&moments_tile_kernel<16, false>); break;
     case 32: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<32, true>)
                       : reinterpret_cast<const void*>(&moments_tile_kernel<32, false>); break;
     case 48: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<48, true>)
@@ -996,7 +1004,10 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope(bwd ? "moments_bwd" : "moments_fwd", stream);
-  if (p.R == 32) {
+  if (p.R == 16) {
+    if (bwd) moments_tile_kernel<16, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    else moments_tile_kernel<16, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+  } else if (p.R == 32) {
     if (bwd) moments_tile_kernel<32, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
     else moments_tile_kernel<32, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
   } else if (p.R == 48) {
@@ -1026,13 +1037,16 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* 
   int grid = 0;
   const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(2, p.R, p.d, p.hg));
   if (!finish_args(a, slot, p.hg * static_cast<int>(p.d), items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
-  const void* fn = p.R == 32   ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
+  const void* fn = p.R == 16   ? reinterpret_cast<const void*>(&readout_tile_kernel<16>)
+                   : p.R == 32 ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
                    : p.R == 48 ? reinterpret_cast<const void*>(&readout_tile_kernel<48>)
                                : reinterpret_cast<const void*>(&readout_tile_kernel<64>);
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("readout", stream);
-  if (p.R == 32) {
+  if (p.R == 16) {
+    readout_tile_kernel<16><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
+  } else if (p.R == 32) {
     readout_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
   } else if (p.R == 48) {
     readout_tile_kernel<48><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
@@ -1069,13 +1083,16 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(3, p.R, p.d, p.hg));
   if (!finish_args(a, slot, p.hg * static_cast<int>(p.R + p.d), items, sm_count, &smem, &grid))
     return cudaErrorInvalidValue;
-  const void* fn = p.R == 32   ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
+  const void* fn = p.R == 16   ? reinterpret_cast<const void*>(&grad_tile_kernel<16>)
+                   : p.R == 32 ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
                    : p.R == 48 ? reinterpret_cast<const void*>(&grad_tile_kernel<48>)
                                : reinterpret_cast<const void*>(&grad_tile_kernel<64>);
   cudaError_t e = allow_smem(fn, smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("grad", stream);
-  if (p.R == 32) {
+  if (p.R == 16) {
+    grad_tile_kernel<16><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+  } else if (p.R == 32) {
     grad_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
   } else if (p.R == 48) {
     grad_tile_kernel<48><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);

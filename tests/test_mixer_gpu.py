@@ -86,6 +86,8 @@ EXPANDED = [
     (2, 64, 2, 32, 300), (1, 64, 2, 64, 300), (1, 32, 2, 64, 300), (1, 64, 4, 32, 1100),
     # r = 48 tiles: two heads per group (relation boxes partly owned), and one head per group at d = 64
     (2, 48, 2, 32, 300), (1, 48, 4, 32, 1100), (1, 48, 2, 64, 333), (1, 48, 8, 32, 4096),
+    # r = 16 tiles: four heads per group
+    (2, 16, 4, 32, 300), (1, 16, 8, 32, 2049),
 ]
 
 
