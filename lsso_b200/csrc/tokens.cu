@@ -74,6 +74,7 @@ struct TileArgs {
   int* status;
   int N, H, d, hg, groups, nrel, nval, ntiles, ct, nchunks, items, pos_batched, slots, nbuf, cols;
   int rel_tma;          // gradient pass: relation boxes wholly inside the group (stored by TMA)
+  int wdg, wdm, wdb;    // the grid stride as (group, tile or chunk, sample) steps of the item walk
   int W;                // packed width
   uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
   uint32_t off_val;     // content (or dY) boxes
@@ -168,6 +169,42 @@ __device__ __forceinline__ TileItem decode_tile(int it, int ntiles, int groups) 
   return x;
 }
 
+// The items of one persistent CTA, it = blockIdx.x + i * gridDim.x, as
+// (g fastest, then m, then b), advanced by one CTA stride without division
+// (the stride's own decomposition comes precomputed in the arguments): the
+// integer divisions run once per role, not once per tile.
+struct ItemWalk {
+  int g, m, b;
+  __device__ __forceinline__ void start(int groups, int mids) {
+    const TileItem x = decode_tile(static_cast<int>(blockIdx.x), mids, groups);
+    g = x.g;
+    m = x.t;
+    b = x.b;
+  }
+  // (dg, dm, db): gridDim.x decomposed the same way.
+  __device__ __forceinline__ void next(int groups, int mids, int dg, int dm, int db) {
+    g += dg;
+    int c = g >= groups ? 1 : 0;
+    g -= c * groups;
+    m += dm + c;
+    c = m >= mids ? 1 : 0;
+    m -= c * mids;
+    b += db + c;
+  }
+  __device__ __forceinline__ TileItem item() const { return TileItem{b, g, m}; }
+};
+
+// Position (entry s, pass u) in a ring of n entries, advanced one step at a time.
+struct RingPos {
+  int s = 0, u = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++s == n) {
+      s = 0;
+      ++u;
+    }
+  }
+};
+
 // 4 (cos, sin) pairs of rank chunk q of tile row r from FP16 phase rows staged
 // in shared memory (R/2 half2 per row); tokens past N rotate by the identity.
 __device__ __forceinline__ Phase4 phase_rows16(const uint8_t* rows, int r, int tok, int N, int R, int q) {
@@ -189,6 +226,11 @@ __device__ __forceinline__ uint32_t phase16_bytes(int t0, int N, int R) {
 // Relation chunks (8 features x 1 token) per transform thread and tile: the
 // thread owns chunks xt + k * kXThreads, k < nrel * 1024 / kXThreads (nrel <= 2).
 constexpr int kMaxChunks = 2 * kTT * 8 / kXThreads;
+// Chunks per thread: at most one relation box per head group at R <= 32, two above.
+template <int R>
+__host__ __device__ constexpr int chunks_of() {
+  return (R <= 32 ? 1 : 2) * kTT * 8 / kXThreads;
+}
 
 __device__ __forceinline__ void chunk_coords(int idx, int& j, int& r, int& c) {
   j = idx / (kTT * 8);
@@ -201,11 +243,11 @@ __device__ __forceinline__ void chunk_coords(int idx, int& j, int& r, int& c) {
 // Issued before the thread waits for the tile's boxes, so the L2 latency
 // overlaps that wait instead of stalling the rotation.
 template <int R>
-__device__ __forceinline__ void fetch_phases(Phase4 (&ph)[kMaxChunks], const float2* table, int64_t prow, int tok0,
-                                             int N, int nrel, int xt) {
+__device__ __forceinline__ void fetch_phases(Phase4 (&ph)[chunks_of<R>()], const float2* table, int64_t prow,
+                                             int tok0, int N, int nrel, int xt) {
   const int nch = nrel * (kTT * 8) / kXThreads;
 #pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
+  for (int k = 0; k < chunks_of<R>(); ++k) {
     if (k < nch) {
       int j, r, c;
       chunk_coords(xt + k * kXThreads, j, r, c);
@@ -246,11 +288,11 @@ __device__ __forceinline__ void rotate_boxes16(uint8_t* rel, int nrel, const uin
 
 // Rotate the relation boxes of one slot in place (BF16 A' for the MMA).
 template <int R>
-__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase4 (&ph)[kMaxChunks], int xt) {
+__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase4 (&ph)[chunks_of<R>()], int xt) {
   const int nch = nrel * (kTT * 8) / kXThreads;
   // In batches of four chunks, each read before any of it is written back.
 #pragma unroll
-  for (int k0 = 0; k0 < kMaxChunks; k0 += 4) {
+  for (int k0 = 0; k0 < chunks_of<R>(); k0 += 4) {
     uint4 in[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -304,29 +346,20 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
                    static_cast<int>(gridDim.x);
   int last_use[kMaxSlots] = {-1, -1, -1, -1, -1, -1};
 
-  auto item_of = [&](int i, int& b, int& g, int& chunk, int& t0, int& nt) {
-    const int it = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
-    g = it % a.groups;  // head group fastest: concurrent CTAs read whole rows
-    const int rest = it / a.groups;
-    chunk = rest % a.nchunks;
-    b = rest / a.nchunks;
-    t0 = chunk * a.ct;
-    nt = min(a.ct, a.ntiles - t0);
-  };
-
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tm_rel);
       prefetch_tmap(&tm_val);
     }
-    int k = 0;
+    ItemWalk w;
+    w.start(a.groups, a.nchunks);
+    RingPos sp;
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      int b, g, chunk, t0, nt;
-      item_of(i, b, g, chunk, t0, nt);
-      for (int tt = 0; tt < nt && ok; ++tt, ++k) {
-        const int s = k % a.slots, u = k / a.slots;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
+      const int b = w.b, g = w.g, t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots)) {
+        const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
         if (ok && lane == 0) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
@@ -347,16 +380,17 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_f = make_idesc(128, BWD ? 64 * a.nval : 64 + 64 * a.nval, true, true);
-    int k = 0;
+    ItemWalk w;
+    w.start(a.groups, a.nchunks);
+    RingPos sp, bp;
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      int b, g, chunk, t0, nt;
-      item_of(i, b, g, chunk, t0, nt);
-      const int tb = i % a.nbuf, tu = i / a.nbuf;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb), bp.next(a.nbuf)) {
+      const int t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
+      const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
       tc_fence_after();
-      for (int tt = 0; tt < nt && ok; ++tt, ++k) {
-        const int s = k % a.slots, u = k / a.slots;
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots)) {
+        const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
         tc_fence_after();
         if (ok && lane == 0) {
@@ -381,11 +415,9 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     constexpr int NCH = (kTT * 8 + kMXThreads - 1) / kMXThreads;  // chunks per thread (one relation box)
     const int xt = threadIdx.x - kXWarp0 * 32;
     const int total = a.nrel * kTT * 8;
-    auto fetch = [&](int ii, int tt, Phase4 (&ph)[NCH]) {
-      int b, g, chunk, t0, nt;
-      item_of(ii, b, g, chunk, t0, nt);
+    auto fetch = [&](int b, int tile, Phase4 (&ph)[NCH]) {
       const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
-      const int tok0 = (t0 + tt) * kTT;
+      const int tok0 = tile * kTT;
 #pragma unroll
       for (int kk = 0; kk < NCH; ++kk) {
         const int idx = xt + kk * kMXThreads;
@@ -398,18 +430,21 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     };
     // One tile ahead (three chunks per thread).
     Phase4 ph[NCH], phn[NCH];
-    if (nloc > 0) fetch(0, 0, ph);
-    int k = 0;
+    ItemWalk w;
+    w.start(a.groups, a.nchunks);
+    if (nloc > 0) fetch(w.b, w.m * a.ct, ph);
+    RingPos sp;
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      int b, g, chunk, t0, nt;
-      item_of(i, b, g, chunk, t0, nt);
-      for (int tt = 0; tt < nt && ok; ++tt, ++k) {
-        const int s = k % a.slots, u = k / a.slots;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
+      const int b = w.b, t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots)) {
+        const int s = sp.s, u = sp.u;
         if (tt + 1 < nt) {
-          fetch(i, tt + 1, phn);
+          fetch(b, t0 + tt + 1, phn);
         } else if (i + 1 < nloc) {
-          fetch(i + 1, 0, phn);
+          ItemWalk wn = w;
+          wn.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb);
+          fetch(wn.b, wn.m * a.ct, phn);
         }
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) {
@@ -460,11 +495,13 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     // ------------------------------------------------------------ drain accumulators (one warp per sub-partition)
     const int sub = warp & 3;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
+    ItemWalk w;
+    w.start(a.groups, a.nchunks);
+    RingPos bp;
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      int b, g, chunk, t0, nt;
-      item_of(i, b, g, chunk, t0, nt);
-      const int tb = i % a.nbuf, tu = i / a.nbuf;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb), bp.next(a.nbuf)) {
+      const int b = w.b, g = w.g, chunk = w.m;
+      const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
@@ -535,9 +572,12 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
       prefetch_tmap(&tm_out);
     }
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots, u = i / a.slots;
+    ItemWalk w;
+    w.start(a.groups, a.ntiles);
+    RingPos sp;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
+      const TileItem x = w.item();
+      const int s = sp.s, u = sp.u;
       ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
       if (ok && lane == 0) {
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
@@ -558,9 +598,10 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
   } else if (warp == 1) {
     const uint32_t idesc = make_idesc(128, d, false, false);
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const int s = i % a.slots, u = i / a.slots;
-      const int tb = i % a.nbuf, tu = i / a.nbuf;
+    RingPos sp, bp;
+    for (int i = 0; i < nloc && ok; ++i, sp.next(a.slots), bp.next(a.nbuf)) {
+      const int s = sp.s, u = sp.u;
+      const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
       if (ok) ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
       tc_fence_after();
@@ -583,10 +624,13 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
   } else if (warp < kXWarp0 + kXWarps) {
     const int xt = threadIdx.x - kXWarp0 * 32;
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots, u = i / a.slots;
-      Phase4 ph[kMaxChunks];
+    ItemWalk w;
+    w.start(a.groups, a.ntiles);
+    RingPos sp;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
+      const TileItem x = w.item();
+      const int s = sp.s, u = sp.u;
+      Phase4 ph[chunks_of<R>()];
       fetch_phases<R>(ph, a.phase, a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0, x.t * kTT, a.N, a.nrel, xt);
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
@@ -601,10 +645,13 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     const int r = 32 * sub + lane;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots;
-      const int tb = i % a.nbuf, tu = i / a.nbuf;
+    ItemWalk w;
+    w.start(a.groups, a.ntiles);
+    RingPos sp, bp;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots), bp.next(a.nbuf)) {
+      const TileItem x = w.item();
+      const int s = sp.s;
+      const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       uint8_t* con = smem + static_cast<size_t>(s) * a.slot_bytes + a.off_val;
@@ -643,9 +690,12 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     // ------------------------------------------------------------ storer
     if (lane == 0) {
       bool ok = true;
-      for (int i = 0; i < nloc && ok; ++i) {
-        const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-        const int s = i % a.slots, u = i / a.slots;
+      ItemWalk w;
+      w.start(a.groups, a.ntiles);
+      RingPos sp;
+      for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
+        const TileItem x = w.item();
+        const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.edone[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint8_t* con = smem + static_cast<size_t>(s) * a.slot_bytes + a.off_val;
@@ -700,9 +750,12 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
       prefetch_tmap(&tm_gproj);
     }
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots, u = i / a.slots;
+    ItemWalk w;
+    w.start(a.groups, a.ntiles);
+    RingPos sp;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
+      const TileItem x = w.item();
+      const int s = sp.s, u = sp.u;
       ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
       if (ok && lane == 0) {
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
@@ -732,9 +785,10 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     const uint32_t idesc_r = make_idesc(128, R, false, false);
     const uint32_t idesc_d = make_idesc(128, d, false, true);
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const int s = i % a.slots, u = i / a.slots;
-      const int tb = i % a.nbuf, tu = i / a.nbuf;
+    RingPos sp, bp;
+    for (int i = 0; i < nloc && ok; ++i, sp.next(a.slots), bp.next(a.nbuf)) {
+      const int s = sp.s, u = sp.u;
+      const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
       if (ok) ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
       tc_fence_after();
@@ -767,9 +821,12 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
   } else if (warp < kXWarp0 + kXWarps) {
     const int xt = threadIdx.x - kXWarp0 * 32;
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots, u = i / a.slots;
+    ItemWalk w;
+    w.start(a.groups, a.ntiles);
+    RingPos sp;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
+      const TileItem x = w.item();
+      const int s = sp.s, u = sp.u;
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
@@ -784,10 +841,13 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     const int r = 32 * sub + lane;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i) {
-      const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-      const int s = i % a.slots;
-      const int tb = i % a.nbuf, tu = i / a.nbuf;
+    ItemWalk w;
+    w.start(a.groups, a.ntiles);
+    RingPos sp, bp;
+    for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots), bp.next(a.nbuf)) {
+      const TileItem x = w.item();
+      const int s = sp.s;
+      const int tb = bp.s, tu = bp.u;
       const int tok = x.t * kTT + r;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
@@ -868,9 +928,12 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     // ------------------------------------------------------------ storer
     if (lane == 0) {
       bool ok = true;
-      for (int i = 0; i < nloc && ok; ++i) {
-        const TileItem x = decode_tile(static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x), a.ntiles, a.groups);
-        const int s = i % a.slots, u = i / a.slots;
+      ItemWalk w;
+      w.start(a.groups, a.ntiles);
+      RingPos sp;
+      for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
+        const TileItem x = w.item();
+        const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.edone[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
@@ -928,6 +991,14 @@ bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_c
   const int sms = sm_count > 0 ? sm_count : 148;
   *grid = items < sms ? items : sms;
   return items > 0;
+}
+
+// The item walk's stride: gridDim.x as (group, middle index, sample) steps.
+void set_walk(TileArgs& a, int grid, int mids) {
+  a.wdg = grid % a.groups;
+  const int rest = grid / a.groups;
+  a.wdm = rest % mids;
+  a.wdb = rest / mids;
 }
 
 TileArgs base_args(const Plan& p, const float2* phase, const float* eta_raw, int* status) {
@@ -989,6 +1060,7 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   int grid = 0;
   const uint32_t slot = static_cast<uint32_t>((2 + a.nval) * kBox);
   if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
+  set_walk(a, grid, a.nchunks);
   const void* fn = nullptr;
   switch (p.R) {
     case 16: fn = bwd ? reinterpret_cast<const void*>(&moments_tile_kernel<16, true>)
@@ -1037,6 +1109,7 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* 
   int grid = 0;
   const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(2, p.R, p.d, p.hg));
   if (!finish_args(a, slot, p.hg * static_cast<int>(p.d), items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
+  set_walk(a, grid, a.ntiles);
   const void* fn = p.R == 16   ? reinterpret_cast<const void*>(&readout_tile_kernel<16>)
                    : p.R == 32 ? reinterpret_cast<const void*>(&readout_tile_kernel<32>)
                    : p.R == 48 ? reinterpret_cast<const void*>(&readout_tile_kernel<48>)
@@ -1083,6 +1156,7 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   const uint32_t slot = static_cast<uint32_t>(tile_slot_bytes(3, p.R, p.d, p.hg));
   if (!finish_args(a, slot, p.hg * static_cast<int>(p.R + p.d), items, sm_count, &smem, &grid))
     return cudaErrorInvalidValue;
+  set_walk(a, grid, a.ntiles);
   const void* fn = p.R == 16   ? reinterpret_cast<const void*>(&grad_tile_kernel<16>)
                    : p.R == 32 ? reinterpret_cast<const void*>(&grad_tile_kernel<32>)
                    : p.R == 48 ? reinterpret_cast<const void*>(&grad_tile_kernel<48>)
