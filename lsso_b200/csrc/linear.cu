@@ -232,12 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       }
     }
     __syncwarp();
-    int it = 0;
+    RingPos rp;
     bool ok = true;
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int m = mstart + i * mstep;
-      for (int kb = 0; kb < KB && ok; ++kb, ++it) {
-        const int s = it % S, u = it / S;
+      for (int kb = 0; kb < KB && ok; ++kb, rp.next(S)) {
+        const int s = rp.s, u = rp.u;
         ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
         if (ok && lane == 0) {
           uint8_t* stage = sA + s * SB;
@@ -255,14 +255,14 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     const uint32_t idesc = make_idesc(kBM, BN, false, false);
     const uint32_t sa0 = smem_u32(sA), sb0 = smem_u32(sB);
     const uint32_t b_region = static_cast<uint32_t>(BN) * 128;  // one 64-wide K region of the weight tile
-    int it = 0;
+    RingPos rp;
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int b = i & 1, v = i >> 1;
       ok = lwait(smem_u32(&tempty[b]), (v & 1) ^ 1, abort_v, a.status);
       tc_fence_after();
       const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
-      for (int kb = 0; kb < KB && ok; ++kb, ++it) {
-        const int s = it % S, u = it / S;
+      for (int kb = 0; kb < KB && ok; ++kb, rp.next(S)) {
+        const int s = rp.s, u = rp.u;
         ok = lwait(smem_u32(a.a_fp16 ? &conv[s] : &full[s]), u & 1, abort_v, a.status);
         tc_fence_after();
         if (ok && lane == 0) {
@@ -285,11 +285,11 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     // ---------------- FP16 -> BF16 rounding in shared memory
     if (a.a_fp16) {
       const int ct = threadIdx.x - 64;
-      int it = 0;
+      RingPos rp;
       bool ok = true;
       for (int i = 0; i < ntile_local && ok; ++i) {
-        for (int kb = 0; kb < KB && ok; ++kb, ++it) {
-          const int s = it % S, u = it / S;
+        for (int kb = 0; kb < KB && ok; ++kb, rp.next(S)) {
+          const int s = rp.s, u = rp.u;
           ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
           if (ok) {
             uint4* p = reinterpret_cast<uint4*>(sA + s * SB);  // the A box (first 16 KB of the stage)
@@ -482,8 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
       prefetch_tmap(&tmap_b);
     }
     bool ok = true;
-    for (int i = 0; i < nst && ok; ++i) {
-      const int s = i % S, u = i / S;
+    RingPos rp;
+    for (int i = 0; i < nst && ok; ++i, rp.next(S)) {
+      const int s = rp.s, u = rp.u;
       ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
       if (ok && lane == 0) {
         const uint32_t dst = smem_u32(smem + s * stage_bytes);
@@ -499,8 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
     }
   } else if (warp == 1) {
     bool ok = true;
-    for (int i = 0; i < nst && ok; ++i) {
-      const int s = i % S, u = i / S;
+    RingPos rp;
+    for (int i = 0; i < nst && ok; ++i, rp.next(S)) {
+      const int s = rp.s, u = rp.u;
       ok = lwait(smem_u32(need_conv ? &conv[s] : &full[s]), u & 1, abort_v, a.status);
       tc_fence_after();
       if (ok && lane == 0) {
@@ -535,8 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
       const int j0 = (masked || a.a_fp16) ? 0 : a_chunks;
       const int j1 = (masked || a.b_fp16) ? total : a_chunks;
       bool ok = true;
-      for (int i = 0; i < nst && ok; ++i) {
-        const int s = i % S, u = i / S;
+      RingPos rp;
+      for (int i = 0; i < nst && ok; ++i, rp.next(S)) {
+        const int s = rp.s, u = rp.u;
         ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
         if (ok) {
           uint4* p = reinterpret_cast<uint4*>(smem + s * stage_bytes);

@@ -273,4 +273,15 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(uint32_t n) {
   return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
 }
 
+// Position (entry s, pass u) in a ring of n entries, advanced one step at a time.
+struct RingPos {
+  int s = 0, u = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++s == n) {
+      s = 0;
+      ++u;
+    }
+  }
+};
+
 }  // namespace lsso

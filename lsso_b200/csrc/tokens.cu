@@ -194,16 +194,6 @@ struct ItemWalk {
   __device__ __forceinline__ TileItem item() const { return TileItem{b, g, m}; }
 };
 
-// Position (entry s, pass u) in a ring of n entries, advanced one step at a time.
-struct RingPos {
-  int s = 0, u = 0;
-  __device__ __forceinline__ void next(int n) {
-    if (++s == n) {
-      s = 0;
-      ++u;
-    }
-  }
-};
 
 // 4 (cos, sin) pairs of rank chunk q of tile row r from FP16 phase rows staged
 // in shared memory (R/2 half2 per row); tokens past N rotate by the identity.
