@@ -32,27 +32,22 @@ def allreduce_gradients(parameters: Iterable[torch.nn.Parameter], *, group=None,
     total = sum(p.numel() for p in params)
     if buffer is None or buffer.numel() != total or buffer.device != device:
         buffer = torch.empty(total, dtype=torch.float32, device=device)
-    offset = 0
-    for p in params:
-        n = p.numel()
-        view = buffer[offset:offset + n]
-        if p.grad is None:
-            view.zero_()
-        else:
-            view.copy_(p.grad.reshape(-1))
-        offset += n
+    # One gather kernel into the flat buffer, one collective, one scatter kernel
+    # back (multi-tensor copy), instead of a copy launch per parameter each way.
+    grads = [p.grad.reshape(-1) if p.grad is not None else torch.zeros(p.numel(), device=device,
+                                                                       dtype=torch.float32) for p in params]
+    torch.cat([g.to(torch.float32) for g in grads], out=buffer)
     dist.all_reduce(buffer, op=dist.ReduceOp.SUM, group=group)
     if average:
         buffer.div_(world)
-    offset = 0
-    for p in params:
-        n = p.numel()
-        flat = buffer[offset:offset + n].view_as(p)
-        if p.grad is None:
-            p.grad = flat.to(p.dtype).clone()
-        else:
-            p.grad.copy_(flat)
-        offset += n
+    views = list(buffer.split([p.numel() for p in params]))
+    missing = [i for i, p in enumerate(params) if p.grad is None]
+    for i in missing:
+        params[i].grad = views[i].view_as(params[i]).to(params[i].dtype).clone()
+    present = [i for i, p in enumerate(params) if p.grad is not None and i not in missing]
+    if present:
+        torch._foreach_copy_([params[i].grad for i in present],
+                             [views[i].view_as(params[i]).to(params[i].grad.dtype) for i in present])
     return buffer
 
 
