@@ -293,8 +293,20 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           ok = lwait(smem_u32(&full[s]), u & 1, abort_v, a.status);
           if (ok) {
             uint4* p = reinterpret_cast<uint4*>(sA + s * SB);  // the A box (first 16 KB of the stage)
-#pragma unroll 2
-            for (int j = ct; j < static_cast<int>(kStageBytes / 16); j += kConvThreads) p[j] = half8_to_bf16(p[j]);
+            // every chunk of the thread read before any is written back, so the
+            // shared-memory loads overlap instead of waiting behind the stores
+            constexpr int kPer = (kStageBytes / 16 + kConvThreads - 1) / kConvThreads;
+            uint4 v[kPer];
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) {
+              const int j = ct + q * kConvThreads;
+              if (j < static_cast<int>(kStageBytes / 16)) v[q] = p[j];
+            }
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) {
+              const int j = ct + q * kConvThreads;
+              if (j < static_cast<int>(kStageBytes / 16)) p[j] = half8_to_bf16(v[q]);
+            }
             fence_proxy_async();
           }
           __syncwarp();
@@ -544,15 +556,27 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
         if (ok) {
           uint4* p = reinterpret_cast<uint4*>(smem + s * stage_bytes);
           const int t0 = t_begin + i * kWT;
-          for (int j = j0 + ct; j < j1; j += kConvThreads) {
-            const bool is_a = j < a_chunks;
-            uint4 v = p[j];
-            if (is_a ? a.a_fp16 : a.b_fp16) v = half8_to_bf16(v);
-            if (masked) {
-              const int t = t0 + ((j % 512) >> 3);  // each 128-byte row of a box is one token
-              if (t >= a.T || a.row_mask[t] == 0) v = make_uint4(0u, 0u, 0u, 0u);
+          // in batches of four chunks, each read before any of it is written back
+          for (int jb = j0 + ct; jb < j1; jb += 4 * kConvThreads) {
+            uint4 v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int j = jb + q * kConvThreads;
+              if (j < j1) v[q] = p[j];
             }
-            p[j] = v;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int j = jb + q * kConvThreads;
+              if (j >= j1) break;
+              const bool is_a = j < a_chunks;
+              uint4 w = v[q];
+              if (is_a ? a.a_fp16 : a.b_fp16) w = half8_to_bf16(w);
+              if (masked) {
+                const int t = t0 + ((j % 512) >> 3);  // each 128-byte row of a box is one token
+                if (t >= a.T || a.row_mask[t] == 0) w = make_uint4(0u, 0u, 0u, 0u);
+              }
+              p[j] = w;
+            }
           }
           fence_proxy_async();
         }
