@@ -9,7 +9,10 @@ with several GPUs, one NCCL all-reduce of the flat gradient buffer.
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
 prints one JSON line (rank 0).  ``--impl reference`` times the CPU oracle
-restatement of the reference algorithm on the host cores instead.
+restatement of the reference algorithm on the host cores instead.  The shape
+options (``--dim --heads --rank --batch --seq --bf16 --masked``) measure the
+other BASELINE configs and ranks the same way; their lines carry no
+``vs_baseline`` (the published figure is for the headline shape only).
 """
 
 from __future__ import annotations
@@ -43,7 +46,20 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=64, help="samples per GPU")
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    # Other shapes (the defaults are the headline workload; these reproduce the other BASELINE configs
+    # and ranks as throughput lines, e.g. --rank 64 --batch 32 --seq 2048 --bf16 --masked for config 3).
+    ap.add_argument("--dim", type=int, default=DIM)
+    ap.add_argument("--heads", type=int, default=HEADS)
+    ap.add_argument("--rank", type=int, default=RANK, choices=(16, 32, 48, 64))
+    ap.add_argument("--bf16", action="store_true", help="BF16 activations (default FP16)")
+    ap.add_argument("--masked", action="store_true",
+                    help="per-sample valid prefix ~U[L/4, L], position ids arange(valid) then zeros (config 3)")
     return ap.parse_args()
+
+
+def headline(args) -> bool:
+    return (args.dim, args.heads, args.rank, args.seq, args.bf16, args.masked) == (DIM, HEADS, RANK, 4096, False,
+                                                                                    False)
 
 
 def dist_env():
@@ -54,10 +70,14 @@ def dist_env():
 
 
 def workload(args, world: int) -> dict:
+    name = "BASELINE config 2 (mixer bench shape)" if (args.dim, args.heads, args.rank) == (DIM, HEADS, RANK) \
+        and not (args.bf16 or args.masked) else "LSSO mixer"
     return {
-        "workload": f"BASELINE config 2 (mixer bench shape) at L={args.seq}: LSSO(dim={DIM}, heads={HEADS}, "
-                    f"rank={RANK}) DYNAMIC + Rank-Rotary, x [B={args.batch} per GPU, {args.seq}, {DIM}] FP16, shared "
-                    "positions, fwd+bwd with loss=y.float().square().mean()",
+        "workload": f"{name} at L={args.seq}: LSSO(dim={args.dim}, heads={args.heads}, "
+                    f"rank={args.rank}) DYNAMIC + Rank-Rotary, x [B={args.batch} per GPU, {args.seq}, {args.dim}] "
+                    f"{'BF16' if args.bf16 else 'FP16'}, "
+                    f"{'per-sample valid prefixes and positions' if args.masked else 'shared positions'}, "
+                    "fwd+bwd with loss=y.float().square().mean()",
         "global_batch": args.batch * world,
         "seq_len": args.seq,
         "parallelism": f"dp{world}",
@@ -66,17 +86,18 @@ def workload(args, world: int) -> dict:
 
 
 # ---------------------------------------------------------------------------- CPU legs
-def cpu_fwd_bwd_tokens_per_s(seq: int, budget_s: float, steps: int | None = None, warmup: int = 1):
+def cpu_fwd_bwd_tokens_per_s(seq: int, budget_s: float, steps: int | None = None, warmup: int = 1,
+                             dim: int = DIM, heads: int = HEADS, rank: int = RANK):
     """Oracle restatement (FP32 reference CPU path) on one sample of the workload."""
     import numpy as np
 
     from oracle import lsso_oracle as O
 
-    params = O.init_params(DIM, HEADS, RANK, seed=0)
-    x = np.random.default_rng(0).standard_normal((1, seq, DIM)).astype(np.float32)
+    params = O.init_params(dim, heads, rank, seed=0)
+    x = np.random.default_rng(0).standard_normal((1, seq, dim)).astype(np.float32)
 
     def one():
-        y, state = O.module_forward(params, x, None, None, heads=HEADS, rank=RANK, dtype=np.float32,
+        y, state = O.module_forward(params, x, None, None, heads=heads, rank=rank, dtype=np.float32,
                                     return_state=True)
         O.module_backward(2.0 * y / y.size, state)
 
@@ -100,7 +121,8 @@ def reference_arm(args, rank: int, world: int) -> int:
     if rank != 0:
         return 0
     cores = os.cpu_count() or 1
-    value, n, median = cpu_fwd_bwd_tokens_per_s(args.seq, args.cpu_seconds, steps=args.steps, warmup=args.warmup)
+    value, n, median = cpu_fwd_bwd_tokens_per_s(args.seq, args.cpu_seconds, steps=args.steps, warmup=args.warmup,
+                                                dim=args.dim, heads=args.heads, rank=args.rank)
     sample = f"1 sample x {args.seq} tokens per step (bench shape), median of {n} steps"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
@@ -160,9 +182,10 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- GPU arm
-def algorithmic_bytes(kernel: str, B: int, N: int) -> float | None:
+def algorithmic_bytes(kernel: str, B: int, N: int, dim: int = DIM, heads: int = HEADS,
+                      rank: int = RANK) -> float | None:
     """Compulsory HBM bytes of one launch of our kernels at this workload (2-byte elements)."""
-    D, W, HR = DIM, HEADS * RANK + DIM, HEADS * RANK
+    D, W, HR = dim, heads * rank + dim, heads * rank
     T = B * N
     table = {
         "moments_fwd": 2 * W * T,            # read the packed projection once
@@ -204,11 +227,19 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     cuda.load(device=local)
     torch.manual_seed(0)
-    layer = LSSO(LSSOConfig(DIM, HEADS, RANK)).to(device)
+    layer = LSSO(LSSOConfig(args.dim, args.heads, args.rank)).to(device)
     params = list(layer.parameters())
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     B, N = args.batch, args.seq
-    x = torch.randn(B, N, DIM, device=device, generator=gen).half().requires_grad_()
+    act = torch.bfloat16 if args.bf16 else torch.float16
+    x = torch.randn(B, N, args.dim, device=device, generator=gen).to(act).requires_grad_()
+    mask = ids = None
+    if args.masked:
+        lens = torch.randint(N // 4, N + 1, (B,), device=device, generator=gen)
+        pos = torch.arange(N, device=device)
+        mask = pos[None, :] < lens[:, None]
+        ids = torch.where(mask, pos[None, :].expand(B, N), torch.zeros_like(pos)[None, :])
+    ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank)  # noqa: E731
     from lsso_b200.ball.distributed import allreduce_gradients
 
     flat = torch.empty(sum(p.numel() for p in params), device=device, dtype=torch.float32)
@@ -219,8 +250,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     def fwd_bwd(xx):
         # cache_enabled=False: autocast's weight-cast cache must not outlive a graph capture.
-        with torch.autocast("cuda", dtype=torch.float16, cache_enabled=False):
-            loss = layer(xx, implementation="cuda").float().square().mean()
+        with torch.autocast("cuda", dtype=act, cache_enabled=False):
+            loss = layer(xx, mask, ids, implementation="cuda").float().square().mean()
         loss.backward()
         return loss.detach()
 
@@ -236,8 +267,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         return loss
 
     def fwd_step(xx):
-        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.float16, cache_enabled=False):
-            return layer(xx, implementation="cuda")
+        with torch.inference_mode(), torch.autocast("cuda", dtype=act, cache_enabled=False):
+            return layer(xx, mask, ids, implementation="cuda")
 
     def timed(fn, steps: int) -> float:
         if world > 1:
@@ -366,33 +397,33 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     line = None
     if rank == 0:
         peaks = measured_peaks()
-        ours = {k: v for k, v in kernels.items() if algorithmic_bytes(k, B, N) is not None}
+        ours = {k: v for k, v in kernels.items() if ab(k) is not None}
         dominant = max(ours, key=lambda k: ours[k][0]) if ours else None
         roofline = None
         if dominant is not None:
             total_ms, launches = ours[dominant]
             per_launch_s = total_ms / launches / 1e3
-            alg = algorithmic_bytes(dominant, B, N)
+            alg = ab(dominant)
             achieved = alg / per_launch_s / 1e9
-            traffic = traffic_record().get(dominant)
+            traffic = traffic_record().get(dominant) if headline(args) and B == 64 else None
             roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                         "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
                         "algorithmic_bytes_per_launch": alg, "avg_launch_ms": total_ms / launches}
         step_kernels = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps,
-                            **({} if algorithmic_bytes(k, B, N) is None else
-                               {"gbs": algorithmic_bytes(k, B, N) / (v[0] / v[1] / 1e3) / 1e9})}
+                            **({} if ab(k) is None else {"gbs": ab(k) / (v[0] / v[1] / 1e3) / 1e9})}
                         for k, v in kernels.items()}
         cpu = None
         if world == 1:
-            cpu_value, n, median = cpu_fwd_bwd_tokens_per_s(N, args.cpu_seconds)
+            cpu_value, n, median = cpu_fwd_bwd_tokens_per_s(N, args.cpu_seconds, dim=args.dim, heads=args.heads,
+                                                            rank=args.rank)
             cpu = {"value": cpu_value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                    "sample": f"1 sample x {N} tokens fwd+bwd (bench shape), median of {n} steps, NumPy oracle "
                              "(FP32 reference-path rounding) on all host threads"}
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": train_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": value / PUBLISHED_FWD_BWD,
+            "scaling": "weak", "vs_baseline": value / PUBLISHED_FWD_BWD if headline(args) else None,
             "vs_baseline_note": "BASELINE.md fwd+bwd at N=4096 (8.99 M tokens/s, RTX 5070 Ti, one GPU)",
             "dtype": "bf16", "data": "synthetic", "config": workload(args, world),
             "fwd": {"value": tokens * args.steps / (fwd_ms / 1e3), "unit": "tokens/s",
