@@ -106,7 +106,9 @@ inline void plan_tiles(Plan& p, int sm_count) {
   p.nrel = static_cast<int>((hg * p.R + 63) / 64);
   p.nval = static_cast<int>(hg * p.d / 64);
   const int64_t ntiles = (p.N + kTileTokens - 1) / kTileTokens;
-  const int64_t pairs = p.B * p.groups;
+  // the moment pass's items hold one relation box: 64 / R heads (one head at R = 48, 64)
+  const int64_t hm = p.R <= 64 && 64 / p.R > 0 ? 64 / p.R : 1;
+  const int64_t pairs = p.B * (p.H / hm);
   const int64_t sms = sm_count > 0 ? sm_count : 148;
   // Largest chunk (fewest partials) whose item count still balances over the SMs.
   int best = 1;
