@@ -183,18 +183,24 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------- GPU arm
 def algorithmic_bytes(kernel: str, B: int, N: int, dim: int = DIM, heads: int = HEADS,
-                      rank: int = RANK) -> float | None:
-    """Compulsory HBM bytes of one launch of our kernels at this workload (2-byte elements)."""
+                      rank: int = RANK, fused: bool = False) -> float | None:
+    """Compulsory HBM bytes of one launch of our kernels at this workload (2-byte elements).
+
+    ``fused``: the input projection runs inside the fused projection + moment
+    pass (``proj_moments``), so the projection GEMMs are the other three.
+    """
     D, W, HR = dim, heads * rank + dim, heads * rank
     T = B * N
     table = {
         "moments_fwd": 2 * W * T,            # read the packed projection once
+        "proj_moments": (2 * D + 2 * W) * T,  # read x, write the packed projection
         "readout": (2 * W + 2 * D) * T,      # read projection, write mixed coordinates
         "moments_bwd": (2 * HR + 2 * D) * T,  # read relation and the upstream gradient
         "grad": (2 * D + 4 * W) * T,         # read dY and projection, write the packed gradient
         # projection GEMMs, averaged over the launches of one step: x->projected, mixed->y,
-        # dy->dmixed, dprojected->dx (4 launches) and the two weight gradients (read g and x)
-        "linear": (12 * D + 4 * W) * T / 4,
+        # dy->dmixed, dprojected->dx (4 launches; 3 without x->projected) and the two weight
+        # gradients (read g and x)
+        "linear": (10 * D + 2 * W) * T / 3 if fused else (12 * D + 4 * W) * T / 4,
         "wgrad": (2 * W + 6 * D) * T / 2,
     }
     return table.get(kernel)
@@ -239,7 +245,10 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         pos = torch.arange(N, device=device)
         mask = pos[None, :] < lens[:, None]
         ids = torch.where(mask, pos[None, :].expand(B, N), torch.zeros_like(pos)[None, :])
-    ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank)  # noqa: E731
+    from lsso_b200.ball import projection
+
+    fused = projection.fused_input_covers(x, args.heads, args.rank)
+    ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank, fused)  # noqa: E731
     from lsso_b200.ball.distributed import allreduce_gradients
 
     flat = torch.empty(sum(p.numel() for p in params), device=device, dtype=torch.float32)
@@ -406,6 +415,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             alg = ab(dominant)
             achieved = alg / per_launch_s / 1e9
             traffic = traffic_record().get(dominant) if headline(args) and B == 64 else None
+            if traffic is not None and dominant == "linear" and bool(traffic.get("input_fused")) != fused:
+                traffic = None  # measured over the other launch mix of the projection GEMMs
             roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                         "traffic": None if traffic is None else traffic.get("bytes_per_launch"),

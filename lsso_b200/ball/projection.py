@@ -104,24 +104,97 @@ class _ProjectionFunction(torch.autograd.Function):
     @once_differentiable
     def backward(ctx, grad_output):
         value, weight, row_mask = ctx.saved_tensors
-        g = grad_output
-        if g.dtype not in (torch.float16, torch.bfloat16):
-            g = g.to(torch.bfloat16)
-        g = g.contiguous()
-        grad_value = grad_weight = grad_bias = None
-        # Masked rows: the input-gradient GEMM writes them as zero and the
-        # weight-gradient kernel skips them, so only the bias sum masks here.
-        if ctx.needs_input_grad[0]:
-            grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True)
-        if ctx.needs_input_grad[1]:
-            grad_weight = weight_gradient(g, value, row_mask)
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            dims = tuple(range(grad_output.ndim - 1))
-            src = grad_output if row_mask is None else torch.where(row_mask[..., None], grad_output,
-                                                                   torch.zeros_like(grad_output))
-            total = src.sum(dim=dims, dtype=torch.float32) if dims else src.float()
-            grad_bias = total.to(device=ctx.bias_meta[1], dtype=ctx.bias_meta[0])
-        return grad_value, grad_weight, grad_bias, None, None
+        grads = _linear_vjp(grad_output, value, weight, row_mask, ctx.needs_input_grad[:3],
+                            ctx.bias_meta if ctx.has_bias else None)
+        return (*grads, None, None)
+
+
+def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta):
+    """(grad_value, grad_weight, grad_bias) of ``value W^T + bias`` (reference.py:170-247)."""
+    g = grad_output
+    if g.dtype not in (torch.float16, torch.bfloat16):
+        g = g.to(torch.bfloat16)
+    g = g.contiguous()
+    grad_value = grad_weight = grad_bias = None
+    # Masked rows: the input-gradient GEMM writes them as zero and the
+    # weight-gradient kernel skips them, so only the bias sum masks here.
+    if needs[0]:
+        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True)
+    if needs[1]:
+        grad_weight = weight_gradient(g, value, row_mask)
+    if bias_meta is not None and needs[2]:
+        dims = tuple(range(grad_output.ndim - 1))
+        src = grad_output if row_mask is None else torch.where(row_mask[..., None], grad_output,
+                                                               torch.zeros_like(grad_output))
+        total = src.sum(dim=dims, dtype=torch.float32) if dims else src.float()
+        grad_bias = total.to(device=bias_meta[1], dtype=bias_meta[0])
+    return grad_value, grad_weight, grad_bias
+
+
+class _FusedInputMix(torch.autograd.Function):
+    """Input projection + mixer with the projection fused into the moment pass (lsso_fused_forward).
+
+    Forward: ``projected = bf16(x) bf16(W_bc)^T + b`` (masked rows zero) and the
+    mixer on it, in one native call.  Backward: the mixer's VJP
+    (``lsso_backward`` on the saved projection) followed by the projection's.
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw, centered_positions,
+                valid_counts):
+        projected, mixed, tape, pivots = _native.fused_forward(
+            x, weight, None if bias is None else bias.detach(), row_mask, core_base_raw, core_drive_weight, eta_raw,
+            centered_positions, valid_counts, train=True)
+        ctx.save_for_backward(x, weight, row_mask, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
+                              centered_positions, valid_counts)
+        ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
+        return mixed
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_mixed):
+        (x, weight, row_mask, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots, centered_positions,
+         valid_counts) = ctx.saved_tensors
+        grad_projected, grad_base, grad_drive, grad_eta = torch.ops.lsso_equilibrium.backward(
+            grad_mixed.contiguous(), projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
+            centered_positions, valid_counts)
+        grad_x, grad_w, grad_b = _linear_vjp(grad_projected, x, weight, row_mask, ctx.needs_input_grad[:3],
+                                             ctx.bias_meta)
+        return grad_x, grad_w, grad_b, None, grad_base, grad_drive, grad_eta, None, None
+
+
+# Opt-in: the fused input projection + moment pass is exact (bit-identical to
+# the separate calls) but, measured on B200 at the bench shape, slower than the
+# projection GEMM followed by the moment pass (one head group per CTA repeats
+# the x staging and conversion for every group).  Set True to use it.
+FUSED_INPUT = False
+_FUSED_SHAPES: dict[tuple[int, ...], bool] = {}
+
+
+def fused_input_covers(x: torch.Tensor, heads: int, rank: int) -> bool:
+    """Whether ``fused_input_mix`` runs for this input (library coverage, cached per shape)."""
+    if not FUSED_INPUT:
+        return False
+    key = (x.device.index or 0, *x.shape, heads, rank)
+    hit = _FUSED_SHAPES.get(key)
+    if hit is None:
+        batch, length, dim = x.shape
+        with torch.cuda.device(x.device):
+            hit = _native.fused_supported(batch, length, heads, dim, rank)
+        _FUSED_SHAPES[key] = hit
+    return hit
+
+
+def fused_input_mix(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw, centered_positions,
+                    valid_counts) -> torch.Tensor:
+    """``fast_mix(input_projection(x, ...), ...)`` through the fused native forward."""
+    if torch.is_grad_enabled() and any(
+            v is not None and v.requires_grad for v in (x, weight, bias, core_base_raw, core_drive_weight, eta_raw)):
+        return _FusedInputMix.apply(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw,
+                                    centered_positions, valid_counts)
+    _, mixed, _, _ = _native.fused_forward(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw,
+                                           centered_positions, valid_counts, train=False)
+    return mixed
 
 
 def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
@@ -137,4 +210,4 @@ def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Ten
     return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype)
 
 
-__all__ = ["input_projection", "linear", "output_projection", "weight_gradient"]
+__all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "linear", "output_projection", "weight_gradient"]

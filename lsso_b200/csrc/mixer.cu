@@ -1568,6 +1568,16 @@ cudaError_t launch_backward_finish(const Plan& p, const BackwardBuffers& bb, con
   }
 }
 
+cudaError_t launch_forward_fused(const Plan& p, const ForwardBuffers& fb, const FusedInput& in, cudaStream_t stream) {
+  if (p.R != 32 && p.R != 64) return cudaErrorInvalidValue;
+  cudaError_t e = launch_phase(p, fb.positions, fb.phase, in.phase16, stream);
+  if (e != cudaSuccess) return e;
+  e = launch_proj_moments(p, in, fb.partial, fb.status, p.sms, stream);
+  if (e != cudaSuccess) return e;
+  return p.R == 32 ? forward_finish_r<32>(p, fb, fb.partial, p.nchunks, stream)
+                   : forward_finish_r<64>(p, fb, fb.partial, p.nchunks, stream);
+}
+
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {
   switch (p.R) {
     case 16: return forward_r<16>(p, fb, stream);
