@@ -80,8 +80,9 @@ struct TileArgs {
   int W;                // packed width
   uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
   uint32_t off_val;     // content (or dY) boxes
-  uint32_t off_aux;     // grad: dY boxes; moments: operand buffer (R = 32: the lo box)
+  uint32_t off_aux;     // grad: dY boxes
   uint32_t off_rel;     // moments: relation boxes
+  uint32_t off_slots;   // moments: first slot (the lo ring, two boxes, sits below it)
   uint32_t off_mat;     // operand matrices
   uint32_t off_ph;      // gradient kernel: FP16 phase rows of the tile
   uint32_t load_bytes;  // transaction bytes per slot fill, phase rows excluded
@@ -94,6 +95,7 @@ struct TileShared {
   uint64_t edone[kMaxSlots];  // epilogue warps -> storing thread
   uint64_t tfull[4];          // MMA -> epilogue (accumulator ready)
   uint64_t tempty[4];         // epilogue -> MMA (accumulator drained)
+  uint64_t lofree[2];         // moment pass: lo box free (MMA done with it)
   uint32_t tmem;
   int abort_flag;
   float red[kMaxSlots][4][4];  // per slot, head, sub-partition: complement statistic
@@ -130,6 +132,7 @@ __device__ __forceinline__ uint8_t* tile_setup(TileShared& sh, uint8_t* raw, int
       mbar_init(smem_u32(&sh.tfull[b]), tcount_mma);
       mbar_init(smem_u32(&sh.tempty[b]), ewarps);
     }
+    for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&sh.lofree[b]), 1);
     sh.abort_flag = 0;
     fence_mbar_init();
   }
@@ -355,11 +358,13 @@ __device__ __forceinline__ void drain_moments(uint32_t taddr, int sub, int lane,
 // partial[(b*H + h)][chunk][2R][NC] (rows [0, R) hi products, [R, 2R) lo).
 //
 // The item's relation features fill one 64-feature box (two heads at R = 32,
-// one head at R = 64): slot = [lo box | relation box, rotated to hi in place |
-// value box].  Per K-step ONE MMA covers the box: A = [lo | hi] (M = 128:
-// the 64 lo rows, then the 64 hi rows), B = [hi | values] (forward: N = 128)
-// or B = dY (backward: N = 64); the two 64-feature groups of each operand are
-// consecutive boxes (LBO = 16 KB).  The value / dY box is the 64-feature box
+// one head at R = 64): slot = [relation box, rotated to hi in place | value
+// box]; the lo box comes from a ring of two below the slots, so a slot holds
+// only loaded data and more loads fit in flight.  Per K-step ONE MMA covers
+// the box: A = [lo | hi] (M = 128: the 64 lo rows, then the 64 hi rows; LBO
+// = the distance from the lo box to the slot), B = [hi | values] (forward:
+// N = 128) or B = dY (backward: N = 64), consecutive boxes (LBO = 16 KB).
+// The value / dY box is the 64-feature box
 // holding the item's heads (at R = 64, d = 32 it also holds the neighbouring
 // head, whose columns are computed and ignored, as are the cross-head blocks
 // at R = 32).
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
         const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.sfree[s]), (u & 1) ^ 1, abort_v, a.status);
         if (ok && lane == 0) {
-          uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+          uint8_t* slot = smem + a.off_slots + static_cast<size_t>(s) * a.slot_bytes;
           const uint32_t bar = smem_u32(&sh.full[s]);
           const int row = (t0 + tt) * kTT;
           mbar_arrive_expect_tx(bar, a.load_bytes);
@@ -414,27 +419,31 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     const uint32_t idesc_f = make_idesc(128, BWD ? 64 * a.nval : 64 + 64 * a.nval, true, true);
     ItemWalk w;
     w.start(a.groups, a.nchunks);
-    RingPos sp, bp;
+    RingPos sp, bp, lp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb), bp.next(a.nbuf)) {
       const int t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
       const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
       tc_fence_after();
-      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots)) {
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(2)) {
         const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
         tc_fence_after();
         if (ok && lane == 0) {
-          const uint32_t slot = smem_u32(smem + static_cast<size_t>(s) * a.slot_bytes);
+          const uint32_t slot = smem_u32(smem + a.off_slots + static_cast<size_t>(s) * a.slot_bytes);
+          const uint32_t lo = smem_u32(smem) + static_cast<uint32_t>(lp.s) * kBox;
           const uint32_t dcol = sh.tmem + static_cast<uint32_t>(tb * a.cols);
           const uint32_t bsrc = slot + (BWD ? a.off_val : a.off_rel);
+          // A = [lo | hi]: the lo box of the ring, then the slot's (rotated) relation box
+          const uint32_t lbo = slot + a.off_rel - lo;
 #pragma unroll
           for (int ks = 0; ks < kTT / 16; ++ks) {
-            mma_bf16(dcol, make_desc_sw128(slot + a.off_aux + ks * 2048, kBox, 1024),
+            mma_bf16(dcol, make_desc_sw128(lo + ks * 2048, lbo, 1024),
                      make_desc_sw128(bsrc + ks * 2048, kBox, 1024), idesc_f, (tt > 0 || ks > 0) ? 1u : 0u);
           }
           mma_commit(smem_u32(&sh.sfree[s]));
+          mma_commit(smem_u32(&sh.lofree[lp.s]));
           if (tt == nt - 1) mma_commit(smem_u32(&sh.tfull[tb]));
         }
         __syncwarp();
@@ -465,11 +474,11 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     ItemWalk w;
     w.start(a.groups, a.nchunks);
     if (nloc > 0) fetch(w.b, w.m * a.ct, ph);
-    RingPos sp;
+    RingPos sp, lp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
       const int b = w.b, t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
-      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots)) {
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(2)) {
         const int s = sp.s, u = sp.u;
         if (tt + 1 < nt) {
           fetch(b, t0 + tt + 1, phn);
@@ -479,10 +488,11 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
           fetch(wn.b, wn.m * a.ct, phn);
         }
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
+        if (ok) ok = twait(smem_u32(&sh.lofree[lp.s]), (lp.u & 1) ^ 1, abort_v, a.status);
         if (ok) {
-          uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+          uint8_t* slot = smem + a.off_slots + static_cast<size_t>(s) * a.slot_bytes;
           uint8_t* rel = slot + a.off_rel;
-          uint8_t* op = slot + a.off_aux;
+          uint8_t* op = smem + static_cast<size_t>(lp.s) * kBox;  // this tile's lo box
           // In batches of three chunks, each read before any of it is written,
           // so the shared-memory loads overlap instead of waiting behind stores.
 #pragma unroll
@@ -1504,8 +1514,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Slot layout and counts shared by the launchers.  Returns false when fewer
 // than two slots fit (the caller then uses the per-head kernels).
-bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_count, size_t* smem, int* grid) {
-  const int slots = tile_slots(slot_bytes);
+bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_count, size_t* smem, int* grid,
+                 uint32_t reserve = 0) {
+  const int slots = static_cast<int>(
+      std::min<int64_t>(kMaxSlots, (kTileSmemBudget - 1024 - static_cast<int64_t>(reserve)) / slot_bytes));
   if (slots < 2) return false;
   int pc = 32;
   while (pc < cols) pc *= 2;
@@ -1515,7 +1527,7 @@ bool finish_args(TileArgs& a, uint32_t slot_bytes, int cols, int items, int sm_c
   a.slots = slots;
   a.slot_bytes = slot_bytes;
   a.items = items;
-  size_t bytes = static_cast<size_t>(slots) * slot_bytes + 1024;
+  size_t bytes = reserve + static_cast<size_t>(slots) * slot_bytes + 1024;
   if (bytes < kSmemFloor) bytes = kSmemFloor;
   *smem = bytes;
   const int sms = sm_count > 0 ? sm_count : 148;
@@ -1574,22 +1586,24 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   TileArgs a = base_args(p, phase, nullptr, status);
   a.partial = partial;
   // One relation box per item: two heads at R = 32, one at R = 64, and the
-  // value boxes holding those heads.  Slot: [lo box | relation box (hi in
-  // place) | value boxes].
+  // value boxes holding those heads.  Slot: [relation box (hi in place) |
+  // value boxes]; the lo boxes, written by the rotation warps and read by the
+  // MMA, come from a ring of two below the slots, so the slots hold only
+  // loaded data (six slots at R = 32, d = 32).
   a.hg = static_cast<int>(64 / p.R);
   a.groups = static_cast<int>(p.H / a.hg);
   a.nrel = 1;
   a.nval = static_cast<int>(ceil_div(a.hg * p.d, 64));
-  a.off_aux = 0;
-  a.off_rel = kBox;
-  a.off_val = 2 * kBox;
+  a.off_slots = 2 * kBox;
+  a.off_rel = 0;
+  a.off_val = kBox;
   a.load_bytes = (1 + a.nval) * kBox;
   const int cols = bwd ? 64 * a.nval : 64 + 64 * a.nval;
   const int items = static_cast<int>(p.B * a.groups * p.nchunks);
   size_t smem = 0;
   int grid = 0;
-  const uint32_t slot = static_cast<uint32_t>((2 + a.nval) * kBox);
-  if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid)) return cudaErrorInvalidValue;
+  const uint32_t slot = static_cast<uint32_t>((1 + a.nval) * kBox);
+  if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid, 2 * kBox)) return cudaErrorInvalidValue;
   set_walk(a, grid, a.nchunks);
   const void* fn = nullptr;
   switch (p.R) {
