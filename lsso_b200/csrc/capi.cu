@@ -104,13 +104,15 @@ int validate_sizes(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R) {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct ForwardLayout {
-  size_t phase, partial, zbuf, rmat, total;
+  size_t phase, phase16, partial, zbuf, rmat, total;
 };
 ForwardLayout forward_layout(const lsso::Plan& p, bool train) {
   ForwardLayout l{};
   size_t off = 0;
   l.phase = off;
   off = align256(off + sizeof(float2) * p.pos_rows * p.N * (p.R / 2));
+  l.phase16 = off;
+  off = align256(off + sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
   l.partial = off;
   off = align256(off + sizeof(float) * p.BH * p.nchunks * p.ndt * 2 * p.R * (p.R + p.dt));
   l.zbuf = off;
@@ -121,18 +123,15 @@ ForwardLayout forward_layout(const lsso::Plan& p, bool train) {
   return l;
 }
 
-// lsso_fused_forward: the forward layout, then the FP16 phase table and the
-// fused kernel's BF16 weight tiles.
+// lsso_fused_forward: the forward layout, then the fused kernel's BF16 weight tiles.
 struct FusedLayout {
   ForwardLayout f;
-  size_t phase16, wprep, total;
+  size_t wprep, total;
 };
 FusedLayout fused_layout(const lsso::Plan& p, bool train) {
   FusedLayout l{};
   l.f = forward_layout(p, train);
   size_t off = l.f.total;
-  l.phase16 = off;
-  off = align256(off + sizeof(__half2) * p.pos_rows * p.N * (p.R / 2));
   l.wprep = off;
   off = align256(off + lsso::fused_weight_bytes(p));
   l.total = off;
@@ -393,6 +392,7 @@ int lsso_forward_inference_noalloc(const void* projected, const float* core_base
   fb.tape = nullptr;
   fb.pivots = nullptr;
   fb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  fb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
   fb.partial = reinterpret_cast<float*>(ws + l.partial);
   fb.zbuf = reinterpret_cast<float*>(ws + l.zbuf);
   fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
@@ -527,6 +527,7 @@ int lsso_forward(const void* projected, const float* core_base_raw, const float*
   fb.tape = tape;
   fb.pivots = pivots;
   fb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  fb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
   fb.partial = reinterpret_cast<float*>(ws + l.partial);
   fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.zbuf);
   fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);
@@ -604,6 +605,7 @@ int lsso_fused_forward(const void* x, int x_dtype, const float* w_bc, const floa
   fb.tape = tape;
   fb.pivots = pivots;
   fb.phase = reinterpret_cast<float2*>(ws + l.f.phase);
+  fb.phase16 = reinterpret_cast<__half2*>(ws + l.f.phase16);
   fb.partial = reinterpret_cast<float*>(ws + l.f.partial);
   fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.f.zbuf);
   fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.f.rmat);
@@ -617,7 +619,7 @@ int lsso_fused_forward(const void* x, int x_dtype, const float* w_bc, const floa
   in.row_mask = row_mask;
   in.projected = static_cast<lsso::bf16*>(projected);
   in.wprep = ws + l.wprep;
-  in.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
+  in.phase16 = fb.phase16;
   const cudaError_t e = lsso::launch_forward_fused(p, fb, in, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lsso_fused_forward");
   return LSSO_OK;
@@ -717,6 +719,7 @@ int lsso_forward_moments(const void* projected, const float* centered_positions,
   fb.positions = centered_positions;
   fb.positions_batched = positions_batched != 0 ? 1 : 0;
   fb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  fb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
   fb.partial = reinterpret_cast<float*>(ws + l.partial);
   fb.status = status;
   fb.vec = p.vec && aligned16(projected);
@@ -766,6 +769,7 @@ int lsso_forward_finish(const void* projected, const float* core_base_raw, const
   fb.tape = tape;
   fb.pivots = pivots;
   fb.phase = reinterpret_cast<float2*>(ws + l.phase);
+  fb.phase16 = reinterpret_cast<__half2*>(ws + l.phase16);
   fb.partial = reinterpret_cast<float*>(ws + l.partial);
   fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.zbuf);
   fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.rmat);

@@ -1242,7 +1242,7 @@ static cudaError_t launch_moments(const Plan& p, MomentArgs args, cudaStream_t s
 // Phase table and the forward moment pass (chunk partials into fb.partial).
 template <int R>
 static cudaError_t forward_moments_r(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {
-  cudaError_t e = launch_phase(p, fb.positions, fb.phase, nullptr, stream);
+  cudaError_t e = launch_phase(p, fb.positions, fb.phase, fb.phase16, stream);
   if (e != cudaSuccess) return e;
   MomentArgs m{};
   m.proj = fb.projected;
@@ -1263,7 +1263,7 @@ static cudaError_t forward_moments_r(const Plan& p, const ForwardBuffers& fb, cu
   m.pos_batched = p.pos_rows > 1 ? 1 : 0;
   m.vec = fb.vec;
   if (tiled_usable(p, {fb.projected})) {
-    return launch_moments_tiled(p, false, fb.projected, nullptr, fb.phase, fb.partial, fb.status, p.sms, stream);
+    return launch_moments_tiled(p, false, fb.projected, nullptr, fb.phase16, fb.partial, fb.status, p.sms, stream);
   }
   return launch_moments<R, false>(p, m, stream);
 }
@@ -1323,7 +1323,8 @@ static cudaError_t forward_finish_r(const Plan& p, const ForwardBuffers& fb, con
   r.pos_batched = p.pos_rows > 1 ? 1 : 0;
   r.vec = fb.vec;
   if (tiled_usable(p, {fb.projected, fb.mixed})) {
-    return launch_readout_tiled(p, fb.projected, fb.phase, fb.rmat, fb.eta_raw, fb.mixed, fb.status, p.sms, stream);
+    return launch_readout_tiled(p, fb.projected, fb.phase16, fb.rmat, fb.eta_raw, fb.mixed, fb.status, p.sms,
+                                stream);
   }
   const size_t rsm = readout_smem<R>(static_cast<int>(p.nb));
   e = set_smem(reinterpret_cast<const void*>(&readout_kernel<R>), rsm);
@@ -1365,7 +1366,7 @@ static cudaError_t backward_moments_r(const Plan& p, const BackwardBuffers& bb, 
   m.pos_batched = pos_batched;
   m.vec = bb.vec;
   if (tiled_usable(p, {bb.projected, bb.grad_output})) {
-    return launch_moments_tiled(p, true, bb.projected, bb.grad_output, bb.phase, bb.partial, bb.status, p.sms,
+    return launch_moments_tiled(p, true, bb.projected, bb.grad_output, bb.phase16, bb.partial, bb.status, p.sms,
                                 stream);
   }
   return launch_moments<R, true>(p, m, stream);
@@ -1531,7 +1532,7 @@ cudaError_t launch_forward_moments(const Plan& p, const ForwardBuffers& fb, floa
 }
 
 cudaError_t launch_forward_finish(const Plan& p, const ForwardBuffers& fb, const float* moments, cudaStream_t stream) {
-  const cudaError_t e = launch_phase(p, fb.positions, fb.phase, nullptr, stream);
+  const cudaError_t e = launch_phase(p, fb.positions, fb.phase, fb.phase16, stream);
   if (e != cudaSuccess) return e;
   switch (p.R) {
     case 16: return forward_finish_r<16>(p, fb, moments, 1, stream);
@@ -1570,7 +1571,7 @@ cudaError_t launch_backward_finish(const Plan& p, const BackwardBuffers& bb, con
 
 cudaError_t launch_forward_fused(const Plan& p, const ForwardBuffers& fb, const FusedInput& in, cudaStream_t stream) {
   if (p.R != 32 && p.R != 64) return cudaErrorInvalidValue;
-  cudaError_t e = launch_phase(p, fb.positions, fb.phase, in.phase16, stream);
+  cudaError_t e = launch_phase(p, fb.positions, fb.phase, fb.phase16, stream);
   if (e != cudaSuccess) return e;
   e = launch_proj_moments(p, in, fb.partial, fb.status, p.sms, stream);
   if (e != cudaSuccess) return e;

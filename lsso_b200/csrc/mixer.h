@@ -106,6 +106,7 @@ struct ForwardBuffers {
   float* tape;             // nullable (inference)
   int* pivots;             // nullable (inference)
   float2* phase;
+  __half2* phase16;        // the same phases as FP16 pairs (staged per tile by the tile kernels)
   float* partial;
   float* zbuf;
   bf16* rmat;
@@ -168,9 +169,9 @@ struct LaunchScope {
 // Head-group tile kernels of the token passes (tokens.cu).  tiled_usable()
 // says whether the plan chose them and every pointer meets the TMA alignment.
 bool tiled_usable(const Plan& p, std::initializer_list<const void*> ptrs);
-cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const float2* phase,
+cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const __half2* phase16,
                                  float* partial, int* status, int sm_count, cudaStream_t stream);
-cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* phase, const bf16* rmat,
+cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2* phase16, const bf16* rmat,
                                  const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream);
 cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj, const __half2* phase16, const bf16* b1y,
                               const bf16* b1c, const bf16* b1a, const float* eta_raw, bf16* gproj,

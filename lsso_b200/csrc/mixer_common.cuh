@@ -61,14 +61,15 @@ constexpr int kTileMaxSlots = 6;
 
 // Bytes of one pipeline slot of each tile kernel (a multiple of 1024):
 // kind 0 moments forward, 1 moments backward, 2 readout, 3 gradient.  Every
-// slot holds the item's boxes and operand matrices; the rotation warps read
-// FP32 phases into registers, the gradient kernel also stages FP16 phase rows.
+// slot holds the item's boxes, operand matrices and the tile's FP16 phase rows
+// (128 tokens x R/2 pairs).
 inline int64_t tile_slot_bytes(int kind, int64_t R, int64_t d, int64_t hg) {
   const int64_t nrel = (hg * R + 63) / 64, nval = hg * d / 64;  // relation boxes: hg*R features from hg*R*g
-  const int64_t phase = 0;
+  const int64_t phase = kTileTokens * R * 2;
   int64_t bytes = 0;
   if (kind <= 1) {
-    // one relation box per item (64 / R heads): lo box + relation/hi box + the value boxes of those heads
+    // one relation box per item (64 / R heads) + the value boxes of those heads, and one box
+    // for the lo ring (two lo boxes below the slots, shared by all of them)
     const int64_t hm = 64 / R;
     bytes = (2 + (hm * d + 63) / 64) * kTileBox + phase;
   } else if (kind == 2) {

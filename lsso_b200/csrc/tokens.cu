@@ -64,8 +64,7 @@ constexpr int kMThreads = (kMEWarp0 + kMEWarps) * 32;
 constexpr size_t kSmemFloor = 120 * 1024;    // forces one CTA per SM (each allocates all of TMEM)
 
 struct TileArgs {
-  const float2* phase;      // FP32 (cos, sin) table, read into registers by the rotation warps
-  const __half2* phase16;   // the same phases as FP16, staged per slot by the gradient kernel
+  const __half2* phase16;   // FP16 (cos, sin) table [pos_rows][N][R/2], staged per slot by the producer
   const float* eta_raw;
   const bf16* m0;  // readout: R_d;  grad: B1y
   const bf16* m1;  // grad: B1c
@@ -84,7 +83,7 @@ struct TileArgs {
   uint32_t off_rel;     // moments: relation boxes
   uint32_t off_slots;   // moments: first slot (the lo ring, two boxes, sits below it)
   uint32_t off_mat;     // operand matrices
-  uint32_t off_ph;      // gradient kernel: FP16 phase rows of the tile
+  uint32_t off_ph;      // the tile's FP16 phase rows
   uint32_t load_bytes;  // transaction bytes per slot fill, phase rows excluded
 };
 
@@ -109,13 +108,6 @@ __device__ __forceinline__ bool twait(uint32_t bar, uint32_t parity, volatile in
 // (1024-byte aligned): chunk c of row r lives at chunk c ^ (r % 8).
 __device__ __forceinline__ uint8_t* box_chunk(uint8_t* box, int r, int c) {
   return box + r * 128 + ((c ^ (r & 7)) << 4);
-}
-
-// Phases (cos, sin) of ranks 8q .. 8q+7 of token tok from the FP32 phase table
-// (L2-resident); tokens past N rotate by the identity.
-__device__ __forceinline__ Phase4 phase_at(const float2* table, int64_t prow, int tok, int N, int R, int q) {
-  if (tok >= N) return phase_identity();
-  return load_phase4(table + (prow + tok) * (R / 2) + 4 * q);
 }
 
 // Common prologue: barriers, TMEM (all 512 columns), 1024-byte aligned base.
@@ -221,34 +213,12 @@ __device__ __forceinline__ uint32_t phase16_bytes(int t0, int N, int R) {
 // Relation chunks (8 features x 1 token) per transform thread and tile: the
 // thread owns chunks xt + k * kXThreads, k < nrel * 1024 / kXThreads (nrel <= 2).
 constexpr int kMaxChunks = 2 * kTT * 8 / kXThreads;
-// Chunks per thread: at most one relation box per head group at R <= 32, two above.
-template <int R>
-__host__ __device__ constexpr int chunks_of() {
-  return (R <= 32 ? 1 : 2) * kTT * 8 / kXThreads;
-}
 
 __device__ __forceinline__ void chunk_coords(int idx, int& j, int& r, int& c) {
   j = idx / (kTT * 8);
   const int rem = idx % (kTT * 8);
   r = rem >> 3;
   c = rem & 7;
-}
-
-// The phases of this thread's relation chunks of one tile, into registers.
-// Issued before the thread waits for the tile's boxes, so the L2 latency
-// overlaps that wait instead of stalling the rotation.
-template <int R>
-__device__ __forceinline__ void fetch_phases(Phase4 (&ph)[chunks_of<R>()], const float2* table, int64_t prow,
-                                             int tok0, int N, int nrel, int xt) {
-  const int nch = nrel * (kTT * 8) / kXThreads;
-#pragma unroll
-  for (int k = 0; k < chunks_of<R>(); ++k) {
-    if (k < nch) {
-      int j, r, c;
-      chunk_coords(xt + k * kXThreads, j, r, c);
-      ph[k] = phase_at(table, prow, tok0 + r, N, R, ((j * 64 + 8 * c) % R) >> 3);
-    }
-  }
 }
 
 // Rotate the relation boxes in place with phases from staged FP16 rows.
@@ -275,35 +245,6 @@ __device__ __forceinline__ void rotate_boxes16(uint8_t* rel, int nrel, const uin
         const Phase4 ph = phase_rows16(rows, r, tok0 + r, N, R, ((j * 64 + 8 * c) % R) >> 3);
         float v[8];
         rotate8(in[k], ph, v);
-        *reinterpret_cast<uint4*>(box_chunk(rel + j * kBox, r, c)) = pack8_bf16(v);
-      }
-    }
-  }
-}
-
-// Rotate the relation boxes of one slot in place (BF16 A' for the MMA).
-template <int R>
-__device__ __forceinline__ void rotate_boxes(uint8_t* rel, int nrel, const Phase4 (&ph)[chunks_of<R>()], int xt) {
-  const int nch = nrel * (kTT * 8) / kXThreads;
-  // In batches of four chunks, each read before any of it is written back.
-#pragma unroll
-  for (int k0 = 0; k0 < chunks_of<R>(); k0 += 4) {
-    uint4 in[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (k0 + k < nch) {
-        int j, r, c;
-        chunk_coords(xt + (k0 + k) * kXThreads, j, r, c);
-        in[k] = *reinterpret_cast<const uint4*>(box_chunk(rel + j * kBox, r, c));
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (k0 + k < nch) {
-        int j, r, c;
-        chunk_coords(xt + (k0 + k) * kXThreads, j, r, c);
-        float v[8];
-        rotate8(in[k], ph[k0 + k], v);
         *reinterpret_cast<uint4*>(box_chunk(rel + j * kBox, r, c)) = pack8_bf16(v);
       }
     }
@@ -402,7 +343,10 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
           uint8_t* slot = smem + a.off_slots + static_cast<size_t>(s) * a.slot_bytes;
           const uint32_t bar = smem_u32(&sh.full[s]);
           const int row = (t0 + tt) * kTT;
-          mbar_arrive_expect_tx(bar, a.load_bytes);
+          const uint32_t pb = phase16_bytes(row, a.N, R);
+          mbar_arrive_expect_tx(bar, a.load_bytes + pb);
+          const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
+          bulk_load(smem_u32(slot + a.off_ph), a.phase16 + (prow + row) * (R / 2), pb, bar);
           for (int j = 0; j < a.nrel; ++j)
             tma_load_3d(smem_u32(slot + a.off_rel + j * kBox), &tm_rel, g * a.hg * R + j * 64, row, b, bar);
           // the 64-feature boxes holding the item's heads (their first feature rounded down)
@@ -451,48 +395,27 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     }
   } else if (warp < kXWarp0 + kMXWarps) {
     // ------------------------------------------------------------ rotate + hi/lo split
-    // The phases of tile k + 1 are fetched (from the L2-resident table) while
-    // tile k is transformed, so their latency is off the critical path.
+    // The phases arrive with the boxes: the producer stages the tile's FP16
+    // phase rows in the slot, so the rotation waits on no global load.
     constexpr int NCH = (kTT * 8 + kMXThreads - 1) / kMXThreads;  // chunks per thread (one relation box)
     const int xt = threadIdx.x - kXWarp0 * 32;
     const int total = a.nrel * kTT * 8;
-    auto fetch = [&](int b, int tile, Phase4 (&ph)[NCH]) {
-      const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
-      const int tok0 = tile * kTT;
-#pragma unroll
-      for (int kk = 0; kk < NCH; ++kk) {
-        const int idx = xt + kk * kMXThreads;
-        if (idx < total) {
-          int j, r, c;
-          chunk_coords(idx, j, r, c);
-          ph[kk] = phase_at(a.phase, prow, tok0 + r, a.N, R, ((j * 64 + 8 * c) % R) >> 3);
-        }
-      }
-    };
-    // One tile ahead (three chunks per thread).
-    Phase4 ph[NCH], phn[NCH];
     ItemWalk w;
     w.start(a.groups, a.nchunks);
-    if (nloc > 0) fetch(w.b, w.m * a.ct, ph);
     RingPos sp, lp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
-      const int b = w.b, t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
+      const int t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
       for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(2)) {
         const int s = sp.s, u = sp.u;
-        if (tt + 1 < nt) {
-          fetch(b, t0 + tt + 1, phn);
-        } else if (i + 1 < nloc) {
-          ItemWalk wn = w;
-          wn.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb);
-          fetch(wn.b, wn.m * a.ct, phn);
-        }
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) ok = twait(smem_u32(&sh.lofree[lp.s]), (lp.u & 1) ^ 1, abort_v, a.status);
         if (ok) {
           uint8_t* slot = smem + a.off_slots + static_cast<size_t>(s) * a.slot_bytes;
           uint8_t* rel = slot + a.off_rel;
+          const uint8_t* rows = slot + a.off_ph;
           uint8_t* op = smem + static_cast<size_t>(lp.s) * kBox;  // this tile's lo box
+          const int tok0 = (t0 + tt) * kTT;
           // In batches of three chunks, each read before any of it is written,
           // so the shared-memory loads overlap instead of waiting behind stores.
 #pragma unroll
@@ -516,7 +439,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
               chunk_coords(idx, j, r, c);
               uint8_t* src = box_chunk(rel + j * kBox, r, c);
               float v[8];
-              rotate8(in[q], ph[kk], v);
+              rotate8(in[q], phase_rows16(rows, r, tok0 + r, a.N, R, ((j * 64 + 8 * c) % R) >> 3), v);
               const uint4 hi = pack8_bf16(v);
               const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
               float lo[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
@@ -529,8 +452,6 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
         }
         __syncwarp();
         if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[s]));
-#pragma unroll
-        for (int kk = 0; kk < NCH; ++kk) ph[kk] = phn[kk];
       }
     }
   } else {
@@ -1123,7 +1044,10 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
         uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
         const uint32_t bar = smem_u32(&sh.full[s]);
         const int row = x.t * kTT;
-        mbar_arrive_expect_tx(bar, a.load_bytes);
+        const uint32_t pb = phase16_bytes(row, a.N, R);
+        mbar_arrive_expect_tx(bar, a.load_bytes + pb);
+        const int64_t prow = a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0;
+        bulk_load(smem_u32(slot + a.off_ph), a.phase16 + (prow + row) * (R / 2), pb, bar);
         for (int j = 0; j < a.nrel; ++j)
           tma_load_3d(smem_u32(slot + j * kBox), &tm_proj, x.g * a.hg * R + j * 64, row, x.b, bar);
         for (int j = 0; j < a.nval; ++j)
@@ -1170,11 +1094,10 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
       const TileItem x = w.item();
       const int s = sp.s, u = sp.u;
-      Phase4 ph[chunks_of<R>()];
-      fetch_phases<R>(ph, a.phase, a.pos_batched ? static_cast<int64_t>(x.b) * a.N : 0, x.t * kTT, a.N, a.nrel, xt);
       ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
       if (ok) {
-        rotate_boxes<R>(smem + static_cast<size_t>(s) * a.slot_bytes, a.nrel, ph, xt);
+        uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
+        rotate_boxes16<R>(slot, a.nrel, slot + a.off_ph, x.t * kTT, a.N, xt);
         fence_proxy_async();
       }
       __syncwarp();
@@ -1543,9 +1466,9 @@ void set_walk(TileArgs& a, int grid, int mids) {
   a.wdb = rest / mids;
 }
 
-TileArgs base_args(const Plan& p, const float2* phase, const float* eta_raw, int* status) {
+TileArgs base_args(const Plan& p, const __half2* phase16, const float* eta_raw, int* status) {
   TileArgs a{};
-  a.phase = phase;
+  a.phase16 = phase16;
   a.eta_raw = eta_raw;
   a.status = status;
   a.N = static_cast<int>(p.N);
@@ -1573,7 +1496,7 @@ bool tiled_usable(const Plan& p, std::initializer_list<const void*> ptrs) {
   return true;
 }
 
-cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const float2* phase,
+cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, const bf16* gout, const __half2* phase16,
                                  float* partial, int* status, int sm_count, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   CUtensorMap tm_rel{}, tm_val{};
@@ -1583,13 +1506,13 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   } else {
     tm_val = tm_rel;
   }
-  TileArgs a = base_args(p, phase, nullptr, status);
+  TileArgs a = base_args(p, phase16, nullptr, status);
   a.partial = partial;
   // One relation box per item: two heads at R = 32, one at R = 64, and the
   // value boxes holding those heads.  Slot: [relation box (hi in place) |
-  // value boxes]; the lo boxes, written by the rotation warps and read by the
-  // MMA, come from a ring of two below the slots, so the slots hold only
-  // loaded data (six slots at R = 32, d = 32).
+  // value boxes | the tile's FP16 phase rows]; the lo boxes, written by the
+  // rotation warps and read by the MMA, come from a ring of two below the
+  // slots, so the slots hold only loaded data.
   a.hg = static_cast<int>(64 / p.R);
   a.groups = static_cast<int>(p.H / a.hg);
   a.nrel = 1;
@@ -1602,7 +1525,8 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   const int items = static_cast<int>(p.B * a.groups * p.nchunks);
   size_t smem = 0;
   int grid = 0;
-  const uint32_t slot = static_cast<uint32_t>((1 + a.nval) * kBox);
+  a.off_ph = static_cast<uint32_t>((1 + a.nval) * kBox);
+  const uint32_t slot = (a.off_ph + static_cast<uint32_t>(kTT * p.R * 2) + 1023u) & ~1023u;
   if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid, 2 * kBox)) return cudaErrorInvalidValue;
   set_walk(a, grid, a.nchunks);
   const void* fn = nullptr;
@@ -1712,17 +1636,18 @@ cudaError_t launch_proj_moments(const Plan& p, const FusedInput& in, float* part
   return cudaGetLastError();
 }
 
-cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const float2* phase, const bf16* rmat,
+cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2* phase16, const bf16* rmat,
                                  const float* eta_raw, bf16* out, int* status, int sm_count, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   CUtensorMap tm_proj{}, tm_out{};
   if (encode_boxes(encode, &tm_proj, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_out, out, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  TileArgs a = base_args(p, phase, eta_raw, status);
+  TileArgs a = base_args(p, phase16, eta_raw, status);
   a.m0 = rmat;
   a.off_val = p.nrel * kBox;
   a.off_mat = (p.nrel + p.nval) * kBox;
   const uint32_t mat = static_cast<uint32_t>(p.hg * p.d * p.R * 2);
+  a.off_ph = a.off_mat + mat;  // the tile's FP16 phase rows (mat is a multiple of 16 bytes)
   a.load_bytes = (p.nrel + p.nval) * kBox + mat;
   const int items = static_cast<int>(p.B * p.groups * ceil_div(p.N, kTT));
   size_t smem = 0;
@@ -1757,8 +1682,7 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   if (encode_boxes(encode, &tm_proj, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_dy, gout, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_gproj, gproj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  TileArgs a = base_args(p, nullptr, eta_raw, status);
-  a.phase16 = phase16;
+  TileArgs a = base_args(p, phase16, eta_raw, status);
   a.m0 = b1y;
   a.m1 = b1c;
   a.m2 = b1a;
