@@ -593,11 +593,11 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   const int d = a.d;
   const int XLD = d + 1;
   float* L = fsm;               // [R][LD]
-  float* Mm = L + R * LD;       // [R][LD] packed LU; after pass A dTheta, then E, then X^T
+  float* Mm = L + R * LD;       // [R][LD] packed LU; after pass A dTheta, then E, then Psi L^{-1}
   float* Th = Mm + R * LD;      // [R][LD]
-  float* dK = Th + R * LD;      // [R][LD] dK, then dTheta, then Psi
+  float* dK = Th + R * LD;      // [R][LD] dK, then dTheta, then Psi, then Q^T
   float* E = Mm;
-  float* X1 = dK + R * LD;      // [R][XLD] D
+  float* X1 = dK + R * LD;      // [R][XLD] A'^T dY, then D
   float* X2 = X1 + R * XLD;     // [R][XLD] lambda, then dZ
   float* X3 = X2 + R * XLD;     // [R][XLD] U, then M'
   float* X4 = X3 + R * XLD;     // [R][XLD] Z
@@ -605,6 +605,8 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   float* dinv = fdiag + R;      // [R] 1 / L_ii
   float* uinv = dinv + R;       // [R] 1 / U_ii
   float* Ws = uinv + R;         // [d][R + 1] W_drive of this head
+  float* Li = Ws + d * LD;      // [R][LD] L^{-1}
+  float* Mi = Li + R * LD;      // [R][LD] M^{-1}
   __shared__ float red[kWWarps];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
@@ -646,7 +648,9 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   }
   __syncthreads();
 
-  // Pass A: D = L^{-1} X1 / sqrt(n);  lam = M^{-T} (2 D) = L_u^{-T} U^{-T} (2 D)
+  // The explicit inverses L^{-1} and M^{-1} = U^{-1} L_u^{-1} (identity columns over the
+  // warps): three triangular-solve chains, after which every solve of this kernel (D,
+  // lambda, R_d, R_z and both sides of Q) is a register-blocked product instead of a chain.
   {
     float rd[P], ru[P], one[P];
     lane_rows<R>(dinv, rd);
@@ -654,27 +658,36 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
 #pragma unroll
     for (int p = 0; p < P; ++p) one[p] = 1.0f;
     int cb, ce;
-    warp_cols(d, cb, ce);
+    warp_cols(R, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[P][kNB];
-      get_cols<R>(X1, XLD, c0, ce, x);
-      trsv_lower<R, false>(L, LD, 1, rd, x);
-      float lam[P][kNB];
+      float x[P][kNB], y[P][kNB];
 #pragma unroll
       for (int p = 0; p < P; ++p)
 #pragma unroll
-        for (int q = 0; q < kNB; ++q) {
-          x[p][q] *= rsn;
-          lam[p][q] = 2.0f * x[p][q];
-        }
-      put_cols<R>(X1, XLD, c0, ce, x);
-      // columns of the packed LU: U^T (entries j <= i), unit L^T (entries j > i)
-      trsv_lower<R, false>(Mm, 1, LD, ru, lam);  // U^T y = 2D
-      trsv_upper<R, true>(Mm, 1, LD, one, lam);  // L_u^T lam = y
-      put_cols<R>(X2, XLD, c0, ce, lam);
+        for (int q = 0; q < kNB; ++q) x[p][q] = y[p][q] = (32 * p + lane == c0 + q) ? 1.0f : 0.0f;
+      trsv_lower<R, false>(L, LD, 1, rd, x);
+      put_cols<R>(Li, LD, c0, ce, x);
+      trsv_lower<R, true>(Mm, LD, 1, one, y);  // unit lower factor of M
+      trsv_upper<R, false>(Mm, LD, 1, ru, y);  // U
+      put_cols<R>(Mi, LD, c0, ce, y);
     }
   }
   __syncthreads();
+  // Pass A: D = L^{-1} (A'^T dY) / sqrt(n) into X2, then lam = M^{-T} (2 D) into X1; the two
+  // buffers then swap names (X1 = D, X2 = lam).
+  tile_gemm<R, 2>(
+      d, R, [&](int i, int k) { return Li[i * LD + k]; }, [&](int k, int c) { return X1[k * XLD + c]; },
+      [&](int i, int c, float acc) { X2[i * XLD + c] = acc * rsn; });
+  __syncthreads();
+  tile_gemm<R, 2>(
+      d, R, [&](int i, int k) { return Mi[k * LD + i]; }, [&](int k, int c) { return X2[k * XLD + c]; },
+      [&](int i, int c, float acc) { X1[i * XLD + c] = 2.0f * acc; });
+  __syncthreads();
+  {
+    float* t = X1;
+    X1 = X2;
+    X2 = t;
+  }
   float dz_dot = 0.0f;
   for (int idx = tid; idx < R * d; idx += kWThreads) {
     const int i = idx / d, col = idx % d;
@@ -734,33 +747,18 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   uint8_t* b2 = reinterpret_cast<uint8_t*>(a.b2 + bh * a.d_pad * R);
   const uint32_t SBO_Y = static_cast<uint32_t>(a.d_pad) * 16;
   constexpr uint32_t SBO_R = R * 16;
-  {
-    float rd[P];
-    lane_rows<R>(dinv, rd);
-    int cb, ce;
-    warp_cols(d, cb, ce);
-    for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float xm[P][kNB], xz[P][kNB];
-      get_cols<R>(X3, XLD, c0, ce, xm);
-      get_cols<R>(X2, XLD, c0, ce, xz);
-      trsv_upper<R, false>(L, 1, LD, rd, xm);
-      trsv_upper<R, false>(L, 1, LD, rd, xz);
-#pragma unroll
-      for (int p = 0; p < P; ++p) {
-        const int row = 32 * p + lane;
-#pragma unroll
-        for (int q = 0; q < kNB; ++q) {
-          const int col = c0 + q;
-          if (row < R && col < ce) {
-            *reinterpret_cast<bf16*>(b1y + kmajor_offset(row, col, SBO_Y)) = __float2bfloat16_rn(xm[p][q] * rsn);
-            const bf16 rz = __float2bfloat16_rn(xz[p][q] * rsn);
-            *reinterpret_cast<bf16*>(b1c + kmajor_offset(row, col, SBO_Y)) = rz;
-            *reinterpret_cast<bf16*>(b2 + kmajor_offset(col, row, SBO_R)) = rz;
-          }
-        }
-      }
-    }
-  }
+  tile_gemm<R, 2>(
+      d, R, [&](int i, int k) { return Li[k * LD + i]; }, [&](int k, int c) { return X3[k * XLD + c]; },
+      [&](int i, int c, float acc) {
+        *reinterpret_cast<bf16*>(b1y + kmajor_offset(i, c, SBO_Y)) = __float2bfloat16_rn(acc * rsn);
+      });
+  tile_gemm<R, 2>(
+      d, R, [&](int i, int k) { return Li[k * LD + i]; }, [&](int k, int c) { return X2[k * XLD + c]; },
+      [&](int i, int c, float acc) {
+        const bf16 rz = __float2bfloat16_rn(acc * rsn);
+        *reinterpret_cast<bf16*>(b1c + kmajor_offset(i, c, SBO_Y)) = rz;
+        *reinterpret_cast<bf16*>(b2 + kmajor_offset(c, i, SBO_R)) = rz;
+      });
   for (int idx = tid; idx < (a.d_pad - d) * R; idx += kWThreads) {
     const int col = d + idx / R, i = idx % R;
     const bf16 z = __float2bfloat16_rn(0.0f);
@@ -769,37 +767,20 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
     *reinterpret_cast<bf16*>(b2 + kmajor_offset(col, i, SBO_R)) = z;
   }
   __syncthreads();
-  // Q = L^{-T} Psi L^{-1} / n with Psi = tril(E) + tril(E,-1)^T (symmetric):
-  // X = L^{-T} Psi column by column, then Q^T = L^{-T} X^T.
+  // Q = L^{-T} Psi L^{-1} / n with Psi = tril(E) + tril(E,-1)^T (symmetric): Psi L^{-1}
+  // into E, then L^{-T} (Psi L^{-1}) into dK, stored transposed.
   for (int idx = tid; idx < R * R; idx += kWThreads) {
     const int i = idx / R, k = idx % R;
     dK[i * LD + k] = i >= k ? E[i * LD + k] : E[k * LD + i];
   }
   __syncthreads();
-  {
-    float rd[P];
-    lane_rows<R>(dinv, rd);
-    int cb, ce;
-    warp_cols(R, cb, ce);
-    for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[P][kNB];
-      get_cols<R>(dK, LD, c0, ce, x);
-      trsv_upper<R, false>(L, 1, LD, rd, x);
-      // store transposed: E[c][i] = X[i][c]
-#pragma unroll
-      for (int p = 0; p < P; ++p)
-#pragma unroll
-        for (int q = 0; q < kNB; ++q)
-          if (32 * p + lane < R && c0 + q < ce) E[(c0 + q) * LD + 32 * p + lane] = x[p][q];
-    }
-    __syncthreads();
-    for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[P][kNB];
-      get_cols<R>(E, LD, c0, ce, x);
-      trsv_upper<R, false>(L, 1, LD, rd, x);
-      put_cols<R>(dK, LD, c0, ce, x);
-    }
-  }
+  tile_gemm<R, square_nb<R>()>(
+      R, R, [&](int i, int k) { return dK[i * LD + k]; }, [&](int k, int j) { return Li[k * LD + j]; },
+      [&](int i, int j, float acc) { E[i * LD + j] = acc; });
+  __syncthreads();
+  tile_gemm<R, square_nb<R>()>(
+      R, R, [&](int i, int k) { return Li[k * LD + i]; }, [&](int k, int j) { return E[k * LD + j]; },
+      [&](int i, int j, float acc) { dK[j * LD + i] = acc; });
   __syncthreads();
   // dK now holds Q^T; B1a[n = i][k = j] = -Q[j][i] / n = -dK[i][j] / n
   uint8_t* b1a = reinterpret_cast<uint8_t*>(a.b1a + bh * R * R);
@@ -818,7 +799,7 @@ size_t fwd_smem(int d) {
 }
 template <int R>
 size_t bwd_smem(int d) {
-  return sizeof(float) * (4 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
+  return sizeof(float) * (6 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
 }
 
 template <int R>
