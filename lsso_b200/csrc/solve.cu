@@ -592,10 +592,10 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   extern __shared__ __align__(16) float fsm[];
   const int d = a.d;
   const int XLD = d + 1;
-  float* L = fsm;               // [R][LD]
-  float* Mm = L + R * LD;       // [R][LD] packed LU; after pass A dTheta, then E, then Psi L^{-1}
+  float* L = fsm;               // [R][LD] L, then L^{-1}
+  float* Mm = L + R * LD;       // [R][LD] packed LU, then L^{-1}; after pass A dTheta, then E, then Psi L^{-1}
   float* Th = Mm + R * LD;      // [R][LD]
-  float* dK = Th + R * LD;      // [R][LD] dK, then dTheta, then Psi, then Q^T
+  float* dK = Th + R * LD;      // [R][LD] M^{-1}, then dK, then dTheta, then Psi, then Q^T
   float* E = Mm;
   float* X1 = dK + R * LD;      // [R][XLD] A'^T dY, then D
   float* X2 = X1 + R * XLD;     // [R][XLD] lambda, then dZ
@@ -605,8 +605,8 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   float* dinv = fdiag + R;      // [R] 1 / L_ii
   float* uinv = dinv + R;       // [R] 1 / U_ii
   float* Ws = uinv + R;         // [d][R + 1] W_drive of this head
-  float* Li = Ws + d * LD;      // [R][LD] L^{-1}
-  float* Mi = Li + R * LD;      // [R][LD] M^{-1}
+  float* Li = L;                // L^{-1} replaces L (computed in Mm, then copied)
+  float* Mi = dK;               // M^{-1} until pass A is done
   __shared__ float red[kWWarps];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t bh = blockIdx.x;
@@ -648,9 +648,11 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   }
   __syncthreads();
 
-  // The explicit inverses L^{-1} and M^{-1} = U^{-1} L_u^{-1} (identity columns over the
-  // warps): three triangular-solve chains, after which every solve of this kernel (D,
-  // lambda, R_d, R_z and both sides of Q) is a register-blocked product instead of a chain.
+  // The explicit inverses M^{-1} = U^{-1} L_u^{-1} (into dK) and L^{-1} (into Mm, then
+  // over L), identity columns over the warps: three triangular-solve chains, after which
+  // every solve of this kernel (D, lambda, R_d, R_z and both sides of Q) is a
+  // register-blocked product instead of a chain.  No extra shared memory: at r = 64 the
+  // block must stay small enough for two CTAs per SM.
   {
     float rd[P], ru[P], one[P];
     lane_rows<R>(dinv, rd);
@@ -660,17 +662,30 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
     int cb, ce;
     warp_cols(R, cb, ce);
     for (int c0 = cb; c0 < ce; c0 += kNB) {
-      float x[P][kNB], y[P][kNB];
+      float y[P][kNB];
 #pragma unroll
       for (int p = 0; p < P; ++p)
 #pragma unroll
-        for (int q = 0; q < kNB; ++q) x[p][q] = y[p][q] = (32 * p + lane == c0 + q) ? 1.0f : 0.0f;
-      trsv_lower<R, false>(L, LD, 1, rd, x);
-      put_cols<R>(Li, LD, c0, ce, x);
+        for (int q = 0; q < kNB; ++q) y[p][q] = (32 * p + lane == c0 + q) ? 1.0f : 0.0f;
       trsv_lower<R, true>(Mm, LD, 1, one, y);  // unit lower factor of M
       trsv_upper<R, false>(Mm, LD, 1, ru, y);  // U
       put_cols<R>(Mi, LD, c0, ce, y);
     }
+    __syncthreads();
+    for (int c0 = cb; c0 < ce; c0 += kNB) {
+      float x[P][kNB];
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) x[p][q] = (32 * p + lane == c0 + q) ? 1.0f : 0.0f;
+      trsv_lower<R, false>(L, LD, 1, rd, x);
+      put_cols<R>(Mm, LD, c0, ce, x);
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < R * R; idx += kWThreads) {
+    const int i = idx / R, k = idx % R;
+    Li[i * LD + k] = Mm[i * LD + k];
   }
   __syncthreads();
   // Pass A: D = L^{-1} (A'^T dY) / sqrt(n) into X2, then lam = M^{-T} (2 D) into X1; the two
@@ -799,7 +814,7 @@ size_t fwd_smem(int d) {
 }
 template <int R>
 size_t bwd_smem(int d) {
-  return sizeof(float) * (6 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
+  return sizeof(float) * (4 * R * (R + 1) + 4 * R * (d + 1) + 3 * R + d * (R + 1));
 }
 
 template <int R>
