@@ -167,6 +167,7 @@ template <int OUT>
 __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                              const __grid_constant__ CUtensorMap tmap_out,
                                                              const LinearArgs a) {
+  pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem[];
   // Resident weight: [weight tile | stages | epilogue staging]; streamed: [stages | staging].
   uint8_t* sB = smem;
@@ -405,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
 // Zero outside [Nout, K].
 __global__ void prep_weight_kernel(const float* __restrict__ w, int Nout, int K, int transposed, int BN, int K_pad,
                                    int NT, uint8_t* __restrict__ out) {
+  pdl_wait();
   // 32-bit index arithmetic: a weight tile set is far below 2^31 elements.
   const int total = NT * BN * K_pad;
   const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -450,6 +452,7 @@ struct WgradArgs {
 __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                             const __grid_constant__ CUtensorMap tmap_b,
                                                             const WgradArgs a) {
+  pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem[];
   const int BNW = a.BNW;
   const int S = a.stages;
@@ -621,6 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
 constexpr int kSplitLanes = 8;
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int mtiles, int ntilesw, int BNW,
                                     int Mdim, int Ndim, int swapped, float* __restrict__ dw) {
+  pdl_wait();
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t q = t / kSplitLanes;
   const int g = static_cast<int>(t % kSplitLanes);
@@ -771,7 +775,7 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
     const int64_t total = static_cast<int64_t>(p.NT) * p.BN * p.K_pad;
     LaunchScope scope("prep_weight", stream);
     if (total >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
-    prep_weight_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+    launch_pdl(prep_weight_kernel, static_cast<unsigned>((total + 255) / 256), 256, 0, stream, 
         c.weight, static_cast<int>(p.Nout), static_cast<int>(p.K), c.weight_transposed, p.BN,
         static_cast<int>(p.K_pad), p.NT, c.prep);
     cudaError_t e = cudaGetLastError();
@@ -817,15 +821,15 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   switch (c.out_dtype) {
     case 0:
       e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<0>), p.smem);
-      if (e == cudaSuccess) linear_kernel<0><<<p.grid, kThreads, p.smem, stream>>>(tmap, tmap_out, a);
+      if (e == cudaSuccess) launch_pdl(linear_kernel<0>, p.grid, kThreads, p.smem, stream, tmap, tmap_out, a);
       break;
     case 1:
       e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<1>), p.smem);
-      if (e == cudaSuccess) linear_kernel<1><<<p.grid, kThreads, p.smem, stream>>>(tmap, tmap_out, a);
+      if (e == cudaSuccess) launch_pdl(linear_kernel<1>, p.grid, kThreads, p.smem, stream, tmap, tmap_out, a);
       break;
     default:
       e = allow_smem(reinterpret_cast<const void*>(&linear_kernel<2>), p.smem);
-      if (e == cudaSuccess) linear_kernel<2><<<p.grid, kThreads, p.smem, stream>>>(tmap, tmap_out, a);
+      if (e == cudaSuccess) launch_pdl(linear_kernel<2>, p.grid, kThreads, p.smem, stream, tmap, tmap_out, a);
       break;
   }
   if (e != cudaSuccess) return e;
@@ -859,13 +863,13 @@ cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t st
   if (e != cudaSuccess) return e;
   {
     LaunchScope scope("wgrad", stream);
-    wgrad_kernel<<<p.grid, kThreads, p.smem, stream>>>(ma, mb, a);
+    launch_pdl(wgrad_kernel, p.grid, kThreads, p.smem, stream, ma, mb, a);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int64_t lanes = p.Mdim * p.Ndim / 4 * kSplitLanes;
   LaunchScope scope("wgrad_reduce", stream);
-  wgrad_reduce_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
+  launch_pdl(wgrad_reduce_kernel, static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream, 
       c.partial, p.splits, p.mtiles, p.ntilesw, p.BNW, static_cast<int>(p.Mdim), static_cast<int>(p.Ndim), p.swapped,
       c.dw);
   return cudaGetLastError();

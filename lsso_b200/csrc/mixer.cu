@@ -39,6 +39,7 @@ struct InvFreq {
 __global__ void phase_kernel(const float* __restrict__ pos, int64_t rows, int N, int half,
                              const __grid_constant__ InvFreq f,
                              float2* __restrict__ out, __half2* __restrict__ out16) {
+  pdl_wait();
   const int i = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;  // t * half + k within the row
   if (i >= N * half) return;
   const int t = i / half, k = i - t * half;
@@ -69,6 +70,7 @@ __global__ void phase_kernel(const float* __restrict__ pos, int64_t rows, int N,
 // ============================================================================
 template <int R, bool BWD>
 __global__ void __launch_bounds__(128) moments_kernel(const MomentArgs a) {
+  pdl_wait();
   constexpr int M_PAD = (2 * R <= 64) ? 64 : 128;
   constexpr int RQ = R / 8;
   constexpr int X_BYTES = M_PAD * kMomentTile * 2;
@@ -367,6 +369,7 @@ size_t solve_forward_smem() {
 
 template <int R>
 __global__ void __launch_bounds__(kSolveThreads) solve_forward_kernel(const SolveFwdArgs a) {
+  pdl_wait();
   constexpr int LD = R + 1, CLD = kColChunk + 1;
   extern __shared__ __align__(16) float fsm[];
   float* L = fsm;
@@ -517,6 +520,7 @@ size_t readout_smem(int nb) {
 
 template <int R>
 __global__ void __launch_bounds__(128) readout_kernel(const ReadoutArgs a) {
+  pdl_wait();
   constexpr int RQ = R / 8;
   constexpr uint32_t SBO = R * 16;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -632,6 +636,7 @@ size_t solve_backward_smem() {
 
 template <int R>
 __global__ void __launch_bounds__(kSolveThreads) solve_backward_kernel(const SolveBwdArgs a) {
+  pdl_wait();
   constexpr int LD = R + 1, CLD = kColChunk + 1;
   extern __shared__ __align__(16) float fsm[];
   float* L = fsm;
@@ -874,6 +879,7 @@ size_t grad_smem(int nb) {
 
 template <int R>
 __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
+  pdl_wait();
   constexpr int RQ = R / 8;
   constexpr uint32_t SBO_R = R * 16;
   constexpr uint32_t SBO_C = 2 * kGradChunk * 16;  // dY|C chunk rows
@@ -1092,6 +1098,7 @@ constexpr int kReduceThreads = 256;
 // thread over samples; the last H blocks each reduce one head's complement
 // statistic over (sample, tile) with a fixed-order tree.  Deterministic.
 __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const ParamReduceArgs a) {
+  pdl_wait();
   const int64_t R = a.R, d = a.d, H = a.H;
   const int64_t nbase = H * R * R, nmain = nbase + H * d * R;
   const int64_t main_blocks = (nmain + kReduceThreads - 1) / kReduceThreads;
@@ -1153,6 +1160,7 @@ __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const Para
 // gradients (concatenated index space).
 __global__ void param_scale_kernel(float* __restrict__ g0, int64_t n0, float* __restrict__ g1, int64_t n1,
                                    float* __restrict__ g2, int64_t n2, float w) {
+  pdl_wait();
   int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n0) {
     g0[i] *= w;
@@ -1221,7 +1229,7 @@ static cudaError_t launch_phase(const Plan& p, const float* pos, float2* table, 
   const dim3 grid(static_cast<unsigned>(ceil_div(p.N * half, threads)),
                   static_cast<unsigned>(p.pos_rows < 65535 ? p.pos_rows : 65535));
   LaunchScope scope("phase", stream);
-  phase_kernel<<<grid, threads, 0, stream>>>(pos, p.pos_rows, static_cast<int>(p.N), half,
+  launch_pdl(phase_kernel, grid, threads, 0, stream, pos, p.pos_rows, static_cast<int>(p.N), half,
                                              inverse_frequencies(static_cast<int>(p.R)), table, table16);
   return cudaGetLastError();
 }
@@ -1235,7 +1243,7 @@ static cudaError_t launch_moments(const Plan& p, MomentArgs args, cudaStream_t s
   if (e != cudaSuccess) return e;
   const int64_t grid = p.BH * p.nchunks * p.ndt;
   LaunchScope scope(BWD ? "moments_bwd" : "moments_fwd", stream);
-  moments_kernel<R, BWD><<<static_cast<unsigned>(grid), 128, smem, stream>>>(args);
+  launch_pdl(moments_kernel<R, BWD>, static_cast<unsigned>(grid), 128, smem, stream, args);
   return cudaGetLastError();
 }
 
@@ -1299,7 +1307,7 @@ static cudaError_t forward_finish_r(const Plan& p, const ForwardBuffers& fb, con
     e = set_smem(reinterpret_cast<const void*>(&solve_forward_kernel<R>), ssm);
     if (e != cudaSuccess) return e;
     LaunchScope scope("solve_fwd", stream);
-    solve_forward_kernel<R><<<static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream>>>(s);
+    launch_pdl(solve_forward_kernel<R>, static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream, s);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return e;
@@ -1330,7 +1338,7 @@ static cudaError_t forward_finish_r(const Plan& p, const ForwardBuffers& fb, con
   e = set_smem(reinterpret_cast<const void*>(&readout_kernel<R>), rsm);
   if (e != cudaSuccess) return e;
   LaunchScope scope("readout", stream);
-  readout_kernel<R><<<static_cast<unsigned>(p.B * p.ntiles * p.H * p.njd), 128, rsm, stream>>>(r);
+  launch_pdl(readout_kernel<R>, static_cast<unsigned>(p.B * p.ntiles * p.H * p.njd), 128, rsm, stream, r);
   return cudaGetLastError();
 }
 
@@ -1408,7 +1416,7 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
     e = set_smem(reinterpret_cast<const void*>(&solve_backward_kernel<R>), ssm);
     if (e != cudaSuccess) return e;
     LaunchScope scope("solve_bwd", stream);
-    solve_backward_kernel<R><<<static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream>>>(s);
+    launch_pdl(solve_backward_kernel<R>, static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream, s);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return e;
@@ -1444,7 +1452,7 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
     e = set_smem(reinterpret_cast<const void*>(&grad_kernel<R>), gsm);
     if (e != cudaSuccess) return e;
     LaunchScope scope("grad", stream);
-    grad_kernel<R><<<static_cast<unsigned>(p.B * p.ntiles * p.H * p.njd), 128, gsm, stream>>>(g);
+    launch_pdl(grad_kernel<R>, static_cast<unsigned>(p.B * p.ntiles * p.H * p.njd), 128, gsm, stream, g);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return e;
@@ -1467,14 +1475,14 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
     // Sequence-parallel ranks: weight the solve-computed terms before they are reduced.
     const int64_t n = p.BH * (p.R * p.R + p.d * p.R + 1);
     LaunchScope scope("param_scale", stream);
-    param_scale_kernel<<<static_cast<unsigned>(ceil_div(n, kReduceThreads)), kReduceThreads, 0, stream>>>(
+    launch_pdl(param_scale_kernel, static_cast<unsigned>(ceil_div(n, kReduceThreads)), kReduceThreads, 0, stream, 
         bb.gbase, p.BH * p.R * p.R, bb.gdrive, p.BH * p.d * p.R, bb.etadot, p.BH, redundant);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   const int64_t main_blocks = ceil_div(p.H * p.R * p.R + p.H * p.d * p.R, kReduceThreads);
   LaunchScope scope("param_reduce", stream);
-  param_reduce_kernel<<<static_cast<unsigned>(main_blocks + p.H), kReduceThreads, 0, stream>>>(pr);
+  launch_pdl(param_reduce_kernel, static_cast<unsigned>(main_blocks + p.H), kReduceThreads, 0, stream, pr);
   return cudaGetLastError();
 }
 
@@ -1489,6 +1497,7 @@ static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStre
 // (ascending chunks), float4 per thread.
 __global__ void chunk_sum_kernel(const float4* __restrict__ partial, int64_t BH, int nchunks, int64_t per4,
                                  float4* __restrict__ out) {
+  pdl_wait();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= BH * per4) return;
   const int64_t bh = i / per4, e = i - bh * per4;
@@ -1508,7 +1517,7 @@ static cudaError_t sum_chunks(const Plan& p, bool bwd, const float* partial, flo
   const int64_t per = moment_elements(p, bwd) / p.BH;  // a multiple of 4 (R and dt are multiples of 16)
   const int64_t total4 = p.BH * per / 4;
   LaunchScope scope("chunk_sum", stream);
-  chunk_sum_kernel<<<static_cast<unsigned>(ceil_div(total4, 256)), 256, 0, stream>>>(
+  launch_pdl(chunk_sum_kernel, static_cast<unsigned>(ceil_div(total4, 256)), 256, 0, stream, 
       reinterpret_cast<const float4*>(partial), p.BH, static_cast<int>(p.nchunks), per / 4,
       reinterpret_cast<float4*>(moments));
   return cudaGetLastError();

@@ -423,6 +423,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // ============================================================================
 template <int R>
 __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const SolveFwdArgs a) {
+  pdl_wait();
   constexpr int LD = R + 1;
   constexpr int P = rows_per_lane<R>();
   extern __shared__ __align__(16) float fsm[];
@@ -587,6 +588,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
 // ============================================================================
 template <int R>
 __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const SolveBwdArgs a) {
+  pdl_wait();
   constexpr int LD = R + 1;
   constexpr int P = rows_per_lane<R>();
   extern __shared__ __align__(16) float fsm[];
@@ -823,7 +825,7 @@ cudaError_t launch_fwd(const SolveFwdArgs& s, int64_t systems, cudaStream_t stre
   cudaError_t e = allow_smem(reinterpret_cast<const void*>(&solve_forward_warp_kernel<R>), smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("solve_fwd", stream);
-  solve_forward_warp_kernel<R><<<static_cast<unsigned>(systems), kWThreads, smem, stream>>>(s);
+  launch_pdl(solve_forward_warp_kernel<R>, static_cast<unsigned>(systems), kWThreads, smem, stream, s);
   return cudaGetLastError();
 }
 
@@ -833,7 +835,7 @@ cudaError_t launch_bwd(const SolveBwdArgs& s, int64_t systems, cudaStream_t stre
   cudaError_t e = allow_smem(reinterpret_cast<const void*>(&solve_backward_warp_kernel<R>), smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("solve_bwd", stream);
-  solve_backward_warp_kernel<R><<<static_cast<unsigned>(systems), kWThreads, smem, stream>>>(s);
+  launch_pdl(solve_backward_warp_kernel<R>, static_cast<unsigned>(systems), kWThreads, smem, stream, s);
   return cudaGetLastError();
 }
 

@@ -10,6 +10,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace lsso {
 
 // Error codes written to the device status word.
@@ -27,6 +29,35 @@ constexpr uint32_t kSuspendHintNs = 20000u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the library is launched with programmatic stream
+// serialisation (launch_pdl): the launch of its grid proceeds as the blocks of
+// the previous kernel on the stream exit, instead of after that kernel's
+// completion has been processed.  Each kernel therefore starts with
+// pdl_wait(), which returns once the previous grid has completed and its
+// memory operations are visible (immediately when there is no such
+// dependency), and touches no global memory before it; since every kernel
+// waits, the outputs of all earlier kernels on the stream are complete too.
+// (Triggering the next launch explicitly at the start of each kernel was
+// measured slower: the dependent grid's blocks then crowd the tail.)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- cp.async

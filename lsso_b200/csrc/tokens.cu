@@ -314,6 +314,7 @@ template <int R, bool BWD>
 __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid_constant__ CUtensorMap tm_rel,
                                                                      const __grid_constant__ CUtensorMap tm_val,
                                                                      const TileArgs a) {
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   __shared__ TileShared sh;
   volatile int* abort_v = &sh.abort_flag;
@@ -629,6 +630,7 @@ template <int R>
 __global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                                      const __grid_constant__ CUtensorMap tm_proj,
                                                                      const FusedArgs a) {
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   __shared__ FusedShared sh;
   volatile int* abort_v = &sh.abort_flag;
@@ -990,6 +992,7 @@ __global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid
 // at chunk c ^ (n%8).  One thread per 16-byte chunk (coalesced FP32 reads).
 __global__ void fused_weight_kernel(const float* __restrict__ w, int D, int H, int R, int d, int hg, int groups,
                                     uint8_t* __restrict__ out) {
+  pdl_wait();
   const int per_row = D / 8;
   const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= groups * 128 * per_row) return;
@@ -1016,6 +1019,7 @@ template <int R>
 __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid_constant__ CUtensorMap tm_proj,
                                                                      const __grid_constant__ CUtensorMap tm_out,
                                                                      const TileArgs a) {
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   __shared__ TileShared sh;
   volatile int* abort_v = &sh.abort_flag;
@@ -1189,6 +1193,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
                                                                   const __grid_constant__ CUtensorMap tm_dy,
                                                                   const __grid_constant__ CUtensorMap tm_gproj,
                                                                   const TileArgs a) {
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   __shared__ TileShared sh;
   volatile int* abort_v = &sh.abort_flag;
@@ -1545,17 +1550,17 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   if (e != cudaSuccess) return e;
   LaunchScope scope(bwd ? "moments_bwd" : "moments_fwd", stream);
   if (p.R == 16) {
-    if (bwd) moments_tile_kernel<16, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
-    else moments_tile_kernel<16, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    if (bwd) launch_pdl(moments_tile_kernel<16, true>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
+    else launch_pdl(moments_tile_kernel<16, false>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
   } else if (p.R == 32) {
-    if (bwd) moments_tile_kernel<32, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
-    else moments_tile_kernel<32, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    if (bwd) launch_pdl(moments_tile_kernel<32, true>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
+    else launch_pdl(moments_tile_kernel<32, false>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
   } else if (p.R == 48) {
-    if (bwd) moments_tile_kernel<48, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
-    else moments_tile_kernel<48, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    if (bwd) launch_pdl(moments_tile_kernel<48, true>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
+    else launch_pdl(moments_tile_kernel<48, false>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
   } else {
-    if (bwd) moments_tile_kernel<64, true><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
-    else moments_tile_kernel<64, false><<<grid, kMThreads, smem, stream>>>(tm_rel, tm_val, a);
+    if (bwd) launch_pdl(moments_tile_kernel<64, true>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
+    else launch_pdl(moments_tile_kernel<64, false>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
   }
   return cudaGetLastError();
 }
@@ -1618,7 +1623,7 @@ cudaError_t launch_proj_moments(const Plan& p, const FusedInput& in, float* part
   {
     const int chunks = a.groups * 128 * static_cast<int>(p.D / 8);
     LaunchScope scope("fused_weight", stream);
-    fused_weight_kernel<<<static_cast<unsigned>((chunks + 255) / 256), 256, 0, stream>>>(
+    launch_pdl(fused_weight_kernel, static_cast<unsigned>((chunks + 255) / 256), 256, 0, stream, 
         in.weight, static_cast<int>(p.D), a.H, static_cast<int>(p.R), a.d, a.hg, a.groups, in.wprep);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -1629,9 +1634,9 @@ cudaError_t launch_proj_moments(const Plan& p, const FusedInput& in, float* part
   if (e != cudaSuccess) return e;
   LaunchScope scope("proj_moments", stream);
   if (p.R == 32) {
-    proj_moments_kernel<32><<<grid, kFThreads, smem, stream>>>(tm_x, tm_proj, a);
+    launch_pdl(proj_moments_kernel<32>, grid, kFThreads, smem, stream, tm_x, tm_proj, a);
   } else {
-    proj_moments_kernel<64><<<grid, kFThreads, smem, stream>>>(tm_x, tm_proj, a);
+    launch_pdl(proj_moments_kernel<64>, grid, kFThreads, smem, stream, tm_x, tm_proj, a);
   }
   return cudaGetLastError();
 }
@@ -1663,13 +1668,13 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2*
   if (e != cudaSuccess) return e;
   LaunchScope scope("readout", stream);
   if (p.R == 16) {
-    readout_tile_kernel<16><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
+    launch_pdl(readout_tile_kernel<16>, grid, kThreadsS, smem, stream, tm_proj, tm_out, a);
   } else if (p.R == 32) {
-    readout_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
+    launch_pdl(readout_tile_kernel<32>, grid, kThreadsS, smem, stream, tm_proj, tm_out, a);
   } else if (p.R == 48) {
-    readout_tile_kernel<48><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
+    launch_pdl(readout_tile_kernel<48>, grid, kThreadsS, smem, stream, tm_proj, tm_out, a);
   } else {
-    readout_tile_kernel<64><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_out, a);
+    launch_pdl(readout_tile_kernel<64>, grid, kThreadsS, smem, stream, tm_proj, tm_out, a);
   }
   return cudaGetLastError();
 }
@@ -1709,13 +1714,13 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   if (e != cudaSuccess) return e;
   LaunchScope scope("grad", stream);
   if (p.R == 16) {
-    grad_tile_kernel<16><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+    launch_pdl(grad_tile_kernel<16>, grid, kThreadsS, smem, stream, tm_proj, tm_dy, tm_gproj, a);
   } else if (p.R == 32) {
-    grad_tile_kernel<32><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+    launch_pdl(grad_tile_kernel<32>, grid, kThreadsS, smem, stream, tm_proj, tm_dy, tm_gproj, a);
   } else if (p.R == 48) {
-    grad_tile_kernel<48><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+    launch_pdl(grad_tile_kernel<48>, grid, kThreadsS, smem, stream, tm_proj, tm_dy, tm_gproj, a);
   } else {
-    grad_tile_kernel<64><<<grid, kThreadsS, smem, stream>>>(tm_proj, tm_dy, tm_gproj, a);
+    launch_pdl(grad_tile_kernel<64>, grid, kThreadsS, smem, stream, tm_proj, tm_dy, tm_gproj, a);
   }
   return cudaGetLastError();
 }
