@@ -1317,6 +1317,8 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
       const int s = sp.s;
       const int tb = bp.s, tu = bp.u;
       const int tok = x.t * kTT + r;
+      // eta of this warp's first head, computed while the accumulator is still being produced
+      const float eta_first = half < a.hg ? bounded_complement(a.eta_raw[x.g * a.hg + half]) : 0.0f;
       ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
@@ -1353,7 +1355,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
             }
           }
           // content gradient eta dY + dC, and the statistic sum(dY * C)
-          const float eta = bounded_complement(a.eta_raw[x.g * a.hg + hl]);
+          const float eta = hl == half ? eta_first : bounded_complement(a.eta_raw[x.g * a.hg + hl]);
           float stat = 0.0f;
           for (int c0 = 0; c0 < d; c0 += 32) {
             float v[32];
