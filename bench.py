@@ -34,7 +34,9 @@ if str(ROOT) not in sys.path:
 
 METRIC = "LSSO mixer tokens/s fwd & fwd+bwd (L=4096,r=32) 1–8 B200; % HBM roofline"
 DIM, HEADS, RANK = 256, 8, 32
-PUBLISHED_FWD_BWD = 64 * 4096 / 29.160e-3  # RTX 5070 Ti, native contract 6, fwd+bwd at N=4096
+# The reference's published fwd+bwd time at this shape (B=64, N=4096, its native CUDA path, contract 6)
+# on one RTX 5070 Ti: 29.160 ms per step, i.e. 8.99 M tokens/s.
+PUBLISHED_FWD_BWD = 64 * 4096 / 29.160e-3
 
 
 def parse_args():
@@ -435,7 +437,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": train_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": value / PUBLISHED_FWD_BWD if headline(args) else None,
-            "vs_baseline_note": "BASELINE.md fwd+bwd at N=4096 (8.99 M tokens/s, RTX 5070 Ti, one GPU)",
+            "vs_baseline_note": "the reference's published fwd+bwd at N=4096 (8.99 M tokens/s, RTX 5070 Ti, one GPU)",
             "dtype": "bf16", "data": "synthetic", "config": workload(args, world),
             "fwd": {"value": tokens * args.steps / (fwd_ms / 1e3), "unit": "tokens/s",
                     "ms_per_step": fwd_ms / args.steps, "eager_ms_per_step": fwd_eager_ms / args.steps},

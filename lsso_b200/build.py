@@ -51,11 +51,22 @@ def is_stale() -> bool:
     return any(p.stat().st_mtime > built for p in _inputs())
 
 
+LAST_BUILD = {"compiled": False, "seconds": 0.0}
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the library unless it is up to date; return its path."""
+    """Compile the library unless it is up to date; return its path.
+
+    ``LAST_BUILD["compiled"]`` says whether this call ran nvcc (False: the
+    existing library was newer than every source and was reused).
+    """
+    import time
+
     target = library_path()
+    LAST_BUILD.update(compiled=False, seconds=0.0)
     if not force and not is_stale():
         return target
+    start = time.perf_counter()
     LIBDIR.mkdir(parents=True, exist_ok=True)
     tmp = target.with_suffix(".so.tmp")
     command = [
@@ -70,6 +81,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if result.returncode != 0:
         raise RuntimeError(f"nvcc failed ({result.returncode}):\n{result.stdout}\n{result.stderr}")
     os.replace(tmp, target)
+    LAST_BUILD.update(compiled=True, seconds=time.perf_counter() - start)
     return target
 
 

@@ -20,6 +20,17 @@ Two numeric modes exist:
   rounds the packed projection to BF16, rounds Rank-Rotary phases to FP16 and
   rounds the mixer output to BF16 (``lsso/ball/model.py:441-446,574-575``,
   ``lsso/ball/reference.py:711-715``).  This is the timed CPU baseline.
+
+and ``contract=True`` (with ``float64``): the mixer core in FP64, with every
+rounding the reference's FP32 path on CUDA tensors applies at its tensor
+boundaries -- FP16 Rank-Rotary phases from FP32 angles, BF16 projection
+operands with wide accumulation, BF16 packed projection and mixer output, and
+in the backward the BF16 upstream gradient of each projection, the BF16
+gradient of the BF16 mixer output and of the BF16 packed projection
+(``lsso/ball/reference.py:170-247``, ``lsso/ball/model.py:441-446,574-575``,
+``csrc/ball/backward.cu:295-296``).  A CUDA result compared with this mode
+shows the error of its own arithmetic, not of the roundings the contract
+prescribes.
 """
 
 from __future__ import annotations
@@ -251,8 +262,13 @@ def mixer_forward(
     *,
     dtype=np.float64,
     return_state: bool = False,
+    contract: bool = False,
 ):
     """Mixed coordinates ``[B, N, D]`` of the native ABI (test_fast_path.py:33-86).
+
+    ``contract=True`` takes the phases of the CUDA contract (FP32 angles,
+    cos/sin rounded to FP16; reference.py:711-715) into the ``dtype``
+    arithmetic.
 
     ``projected`` is the packed ``[B, N, H*r + D]`` tensor (BF16 values in any
     float dtype), ``centered_positions`` is ``[N]`` or ``[B, N]`` (default
@@ -278,7 +294,10 @@ def mixer_forward(
         if positions.ndim == 1:
             positions = np.broadcast_to(positions[None], (batch, length))
     relation, content = split_projected(projected, heads, rank)
-    cos, sin = rank_phases(positions, rank, dtype)
+    if contract:
+        cos, sin = (v.astype(dtype) for v in rank_phases(positions.astype(np.float32), rank, np.float32))
+    else:
+        cos, sin = rank_phases(positions, rank, dtype)
     root = np.sqrt(counts)[:, None, None, None]
     A = rank_rotary(relation, cos, sin) / root
     frame = qr_soft_frame(A)
@@ -383,14 +402,22 @@ def linear(value: np.ndarray, weight: np.ndarray, bias: np.ndarray | None, *, bf
 
 
 def module_forward(params: dict, x: np.ndarray, valid_mask=None, position_ids=None, *,
-                   heads: int, rank: int, dtype=np.float64, return_state: bool = False):
+                   heads: int, rank: int, dtype=np.float64, return_state: bool = False, contract: bool = False,
+                   activation: str | None = None):
     """Complete LSSO forward (model.py:542-585) for DYNAMIC + Rank-Rotary.
 
     ``dtype=float64`` is the FP64 oracle; ``dtype=float32`` mirrors the
-    reference's CPU FP32 path (BF16 packed coordinates and BF16 mixer output).
-    ``params`` holds ``w_bc``, ``b_bc`` (or None), ``w_o``, ``b_o``,
-    ``core_base_raw``, ``core_drive_weight``, ``eta_raw``.
+    reference's CPU FP32 path (BF16 packed coordinates and BF16 mixer output);
+    ``contract=True`` (FP64) adds the roundings of the reference's path on
+    CUDA tensors (module docstring); there ``activation`` ("float16" or
+    "bfloat16", x's dtype) also rounds y and the gradient of x to it, as the
+    projections store them (reference.py:202,224).  ``params`` holds
+    ``w_bc``, ``b_bc`` (or None), ``w_o``, ``b_o``, ``core_base_raw``,
+    ``core_drive_weight``, ``eta_raw``.
     """
+    if contract:
+        return _module_forward_contract(params, x, valid_mask, position_ids, heads=heads, rank=rank,
+                                        return_state=return_state, activation=activation)
     x = np.asarray(x, dtype=dtype)
     batch, length, dim = x.shape
     mask = None if valid_mask is None else np.asarray(valid_mask, dtype=bool)
@@ -423,8 +450,73 @@ def module_forward(params: dict, x: np.ndarray, valid_mask=None, position_ids=No
                      has_bias=b_bc is not None)
 
 
+def _bf16(value: np.ndarray) -> np.ndarray:
+    return round_bf16(value).astype(np.float64)
+
+
+def _round_activation(value: np.ndarray, activation: str | None) -> np.ndarray:
+    if activation is None:
+        return value
+    if activation == "bfloat16":
+        return _bf16(value)
+    if activation == "float16":
+        return round_fp16(value).astype(np.float64)
+    raise ValueError(f"activation must be 'float16', 'bfloat16' or None, got {activation!r}")
+
+
+def _module_forward_contract(params, x, valid_mask, position_ids, *, heads, rank, return_state, activation):
+    """FP64 module forward with the CUDA contract's roundings.
+
+    Projections follow ``_TensorCoreLinear.forward`` (reference.py:172-202):
+    BF16 value and weight, wide accumulation, FP32 bias added before the one
+    store (BF16 for the packed projection, model.py:376-378).  Positions are
+    centered in FP32 (model.py:163-243 with the FP32 calculation dtype of the
+    CUDA path) and the mixer output is rounded to BF16 (model.py:441-446).
+    """
+    x = np.asarray(x, dtype=np.float64)
+    batch, length, dim = x.shape
+    mask = None if valid_mask is None else np.asarray(valid_mask, dtype=bool)
+    safe_x = x if mask is None else np.where(mask[:, :, None], x, 0.0)
+    x_bf16 = _bf16(safe_x)
+    w_bc = _bf16(np.asarray(params["w_bc"], np.float32))
+    w_o = _bf16(np.asarray(params["w_o"], np.float32))
+    b_bc = None if params.get("b_bc") is None else np.asarray(params["b_bc"], np.float32).astype(np.float64)
+    b_o = None if params.get("b_o") is None else np.asarray(params["b_o"], np.float32).astype(np.float64)
+    projected = (x_bf16.reshape(-1, dim) @ w_bc.T).reshape(batch, length, -1)
+    if b_bc is not None:
+        projected = projected + b_bc
+    projected = _bf16(projected)
+    if mask is not None:
+        projected = np.where(mask[:, :, None], projected, 0.0)
+    positions = center_positions(position_ids, mask, batch, length, dtype=np.float32)
+    counts = None if mask is None else np.maximum(mask.sum(axis=-1).astype(np.float32), 1.0)
+    mixed, state = mixer_forward(projected, params["core_base_raw"], params["core_drive_weight"],
+                                 params["eta_raw"], positions, counts, dtype=np.float64, return_state=True,
+                                 contract=True)
+    mixed = _bf16(mixed)
+    out = (mixed.reshape(-1, dim) @ w_o.T).reshape(batch, length, dim)
+    if b_o is not None:
+        out = out + b_o
+    out = _round_activation(out, activation)
+    if mask is not None:
+        out = np.where(mask[:, :, None], out, 0.0)
+    if not return_state:
+        return out
+    return out, dict(mixer=state, x=x_bf16, mixed=mixed, mask=mask, w_bc=w_bc, w_o=w_o,
+                     has_bias=b_bc is not None, contract=True, activation=activation)
+
+
 def module_backward(grad_out: np.ndarray, mstate: dict):
-    """Gradients of :func:`module_forward` for x and every parameter."""
+    """Gradients of :func:`module_forward` for x and every parameter.
+
+    For a ``contract`` forward the VJPs follow ``_TensorCoreLinear.backward``
+    (reference.py:204-247): the upstream gradient of each projection is
+    rounded to BF16 before both GEMMs, the bias gradient sums it unrounded,
+    and the gradients of the BF16 tensors (mixer output, packed projection)
+    are BF16.
+    """
+    if mstate.get("contract"):
+        return _module_backward_contract(grad_out, mstate)
     mask = mstate["mask"]
     dtype = mstate["x"].dtype
     grad_out = np.asarray(grad_out, dtype=dtype)
@@ -449,6 +541,31 @@ def module_backward(grad_out: np.ndarray, mstate: dict):
     grads = dict(x=grad_x, w_bc=grad_w_bc, b_bc=grad_b_bc, w_o=grad_w_o, b_o=grad_b_o,
                  core_base_raw=gbase, core_drive_weight=gdrive, eta_raw=geta)
     return grads
+
+
+def _module_backward_contract(grad_out, mstate):
+    mask = mstate["mask"]
+    grad_out = np.asarray(grad_out, dtype=np.float64)
+    if mask is not None:
+        grad_out = np.where(mask[:, :, None], grad_out, 0.0)
+    batch, length, dim = grad_out.shape
+    go_raw = grad_out.reshape(-1, dim)
+    go = _bf16(go_raw)
+    grad_w_o = go.T @ mstate["mixed"].reshape(-1, dim)
+    grad_b_o = go_raw.sum(axis=0) if mstate["has_bias"] else None
+    grad_mixed = _bf16(go @ mstate["w_o"]).reshape(batch, length, dim)
+    gproj, gbase, gdrive, geta = mixer_backward(grad_mixed, mstate["mixer"])
+    gproj = _bf16(gproj)
+    if mask is not None:
+        gproj = np.where(mask[:, :, None], gproj, 0.0)
+    gp = gproj.reshape(batch * length, -1)
+    grad_w_bc = gp.T @ mstate["x"].reshape(-1, dim)
+    grad_b_bc = gp.sum(axis=0) if mstate["has_bias"] else None
+    grad_x = _round_activation((gp @ mstate["w_bc"]).reshape(batch, length, dim), mstate["activation"])
+    if mask is not None:
+        grad_x = np.where(mask[:, :, None], grad_x, 0.0)
+    return dict(x=grad_x, w_bc=grad_w_bc, b_bc=grad_b_bc, w_o=grad_w_o, b_o=grad_b_o,
+                core_base_raw=gbase, core_drive_weight=gdrive, eta_raw=geta)
 
 
 def init_params(dim: int, heads: int, rank: int, *, bias: bool = False, seed: int = 0,

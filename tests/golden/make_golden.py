@@ -130,8 +130,37 @@ def config1(LSSO, LSSOConfig):
     np.savez_compressed(HERE / "config1_forward.npz", **record)
 
 
-def main(root: str) -> None:
+def checkpoint_case(LSSO, LSSOConfig, name, *, dim, heads, rank, bias, batch, length, seed, core=0.0):
+    """A ``state_dict()`` written by the reference's own module (weights and the
+    ``_extra_state`` configuration contract) plus an input and the reference's
+    FP32 CPU output for it, saved with ``torch.save`` (plain tensors and a dict
+    of str/int/bool, loadable with ``weights_only=True``)."""
+    torch.manual_seed(seed)
+    layer = LSSO(LSSOConfig(dim=dim, num_heads=heads, rank=rank, bias=bias))
+    if core:
+        with torch.no_grad():
+            layer.core_base_raw.normal_(0.0, core)
+            layer.core_drive_weight.normal_(0.0, core)
+    x = torch.randn(batch, length, dim)
+    with torch.no_grad():
+        y = layer(x)
+    record = {"config": dict(dim=dim, num_heads=heads, rank=rank, bias=bias),
+              "state_dict": layer.state_dict(), "x": x, "y": y}
+    torch.save(record, HERE / f"checkpoint_{name}.pt")
+
+
+def checkpoints(LSSO, LSSOConfig) -> None:
+    checkpoint_case(LSSO, LSSOConfig, "d32_h2_r16_bias", dim=32, heads=2, rank=16, bias=True, batch=2, length=33,
+                    seed=2024, core=0.05)
+    checkpoint_case(LSSO, LSSOConfig, "d64_h2_r32", dim=64, heads=2, rank=32, bias=False, batch=1, length=40,
+                    seed=2025)
+
+
+def main(root: str, only: str | None = None) -> None:
     ref_mix, LSSO, LSSOConfig = _load_reference(root)
+    if only == "checkpoints":
+        checkpoints(LSSO, LSSOConfig)
+        return
     cases = [
         dict(name="r16_d8_n33", batch=2, length=33, heads=2, rank=16, head_dim=8, seed=1),
         dict(name="r32_d17_n65", batch=1, length=65, heads=3, rank=32, head_dim=17, seed=2),
@@ -159,9 +188,11 @@ def main(root: str) -> None:
     module_case(LSSO, LSSOConfig, "fp32path_nobias", dim=64, heads=2, rank=32, bias=False, batch=2,
                 length=40, seed=7, fp32_path=True)
     config1(LSSO, LSSOConfig)
+    checkpoints(LSSO, LSSOConfig)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: python tests/golden/make_golden.py /path/to/LSSO  (the reference checkout)")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        raise SystemExit("usage: python tests/golden/make_golden.py /path/to/LSSO [checkpoints]  "
+                         "(the reference checkout; 'checkpoints' writes only the checkpoint fixtures)")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) == 3 else None)

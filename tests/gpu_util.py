@@ -38,6 +38,13 @@ def max_abs(actual, expected) -> float:
     return float(np.abs(np.asarray(actual, np.float64) - np.asarray(expected, np.float64)).max())
 
 
+def scaled_max_abs(actual, expected) -> float:
+    """max|actual - expected| / max|expected| (the max-abs bound of the parity tests)."""
+    expected = np.asarray(expected.detach().double().cpu().numpy() if isinstance(expected, torch.Tensor)
+                          else expected, np.float64)
+    return max_abs(actual, expected) / max(float(np.abs(expected).max()), 1e-30)
+
+
 def seeded_mixer_inputs(seed: int, batch: int, length: int, heads: int, rank: int, head_dim: int, *,
                         core: float = 0.05, eta: float = 0.05, relscale: float = 1.0, mask=None):
     g = torch.Generator().manual_seed(seed)
@@ -73,11 +80,20 @@ def run_cuda(projected, base, drive, eta_raw, positions=None, counts=None, upstr
     return out, grads
 
 
-def run_oracle(projected, base, drive, eta_raw, positions=None, counts=None, upstream=None):
+def run_oracle(projected, base, drive, eta_raw, positions=None, counts=None, upstream=None, *, contract=True):
+    """The oracle on the same inputs.
+
+    ``contract=True`` (default): FP64 mixer with the CUDA contract's FP16
+    phases, fed the BF16 upstream gradient the native backward receives
+    (its grad_output is BF16).  ``contract=False``: the exact FP64 operator
+    with the FP32 upstream, the reference tests' FP64 oracle."""
     n = lambda t: None if t is None else np.asarray(t.detach().cpu().numpy() if isinstance(t, torch.Tensor) else t,
                                                      np.float64)  # noqa: E731
     out, state = O.mixer_forward(n(projected), n(base), n(drive), n(eta_raw), n(positions), n(counts),
-                                 return_state=True)
+                                 return_state=True, contract=contract)
     if upstream is None:
         return out, None
-    return out, O.mixer_backward(n(upstream), state)
+    up = n(upstream)
+    if contract:
+        up = O.round_bf16(up).astype(np.float64)
+    return out, O.mixer_backward(up, state)

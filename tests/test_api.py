@@ -75,6 +75,60 @@ def test_checkpoint_contract_holds_inside_a_parent_module() -> None:
         torch.nn.Sequential(LSSO(LSSOConfig(32, 2, 16))).load_state_dict(state)
 
 
+CHECKPOINTS = sorted(p.name for p in (Path(__file__).resolve().parent / "golden").glob("checkpoint_*.pt"))
+
+
+def _reference_checkpoint(name: str) -> dict:
+    return torch.load(Path(__file__).resolve().parent / "golden" / name, weights_only=True)
+
+
+def test_reference_checkpoint_fixtures_exist() -> None:
+    assert len(CHECKPOINTS) == 2
+
+
+@pytest.mark.parametrize("name", CHECKPOINTS)
+def test_reference_written_checkpoint_loads_strictly_and_reproduces_its_output(name: str) -> None:
+    """A state_dict written by the reference's own module (tests/golden/make_golden.py,
+    reference model.py:79-140) loads strictly here and gives the reference's y."""
+    record = _reference_checkpoint(name)
+    layer = LSSO(LSSOConfig(**record["config"]))
+    result = layer.load_state_dict(record["state_dict"], strict=True)
+    assert not result.missing_keys and not result.unexpected_keys
+    for key, value in layer.state_dict().items():
+        if key != "_extra_state":
+            assert torch.equal(value, record["state_dict"][key]), key
+    with torch.no_grad():
+        y = layer(record["x"])
+    assert y.dtype == record["y"].dtype and y.shape == record["y"].shape
+    assert torch.equal(y, record["y"])
+
+
+@pytest.mark.parametrize("name", CHECKPOINTS)
+def test_state_dict_matches_the_reference_key_by_key(name: str) -> None:
+    """This module's state_dict has the reference's keys in the reference's order,
+    with the same shapes and dtypes and an equal configuration contract, so
+    checkpoints written here load into the reference and vice versa."""
+    record = _reference_checkpoint(name)
+    ours = LSSO(LSSOConfig(**record["config"])).state_dict()
+    theirs = record["state_dict"]
+    assert list(ours) == list(theirs)
+    for key in theirs:
+        if key == "_extra_state":
+            assert ours[key] == theirs[key]
+            assert [type(v) for v in ours[key].values()] == [type(v) for v in theirs[key].values()]
+        else:
+            assert (ours[key].shape, ours[key].dtype) == (theirs[key].shape, theirs[key].dtype), key
+
+
+@pytest.mark.parametrize("name", CHECKPOINTS)
+def test_reference_checkpoint_is_rejected_by_a_different_configuration(name: str) -> None:
+    record = _reference_checkpoint(name)
+    config = dict(record["config"])
+    config["rank"] = 48 if config["rank"] != 48 else 16
+    with pytest.raises(RuntimeError, match="incompatible LSSO checkpoint contract"):
+        LSSO(LSSOConfig(**config)).load_state_dict(record["state_dict"], strict=False)
+
+
 # ------------------------------------------------------------------ reference path vs golden fixtures
 @pytest.mark.parametrize("name", [n for n in module_case_names() if n.startswith("fp64")])
 def test_reference_path_matches_golden_fp64(name: str) -> None:

@@ -1,9 +1,19 @@
 """Parity of the sm_100a mixer with the oracle and the reference's golden fixtures.
 
-Budgets are the reference's (tests/cuda/test_fast_path.py, docs/CUDA_CONTRACT.md:
-relative L2 <= 5e-3 for outputs, <= 3e-2 for gradients, 1e-2 for the
-complement gradient of the narrow-head and tail fixtures); the measured
-values are far inside them and are printed for the record.
+Each case is checked twice:
+
+* against the oracle with the contract's roundings (FP16 Rank-Rotary phases,
+  the BF16 upstream gradient the native backward receives): relative L2
+  <= 5e-3 for the output and for every gradient and max|actual - expected|
+  <= MAXABS x max|expected| per tensor -- the error of the kernels' own
+  arithmetic;
+* against the exact FP64 operator with the FP32 upstream (the reference
+  tests' oracle, tests/cuda/test_fast_path.py:33-86): relative L2 <= 1e-2
+  for every tensor -- the contract's roundings included.  The reference's own
+  CUDA suite allows 3e-2 for gradients there (test_fast_path.py:737-742).
+
+The complement gradient of the narrow-head and tail fixtures keeps the
+reference's 1e-2 (test_fast_path.py:745-856).  Measured values are printed.
 """
 
 from __future__ import annotations
@@ -14,12 +24,17 @@ import torch
 
 from oracle import lsso_oracle as O
 from tests.golden_io import load_mixer_case, mixer_case_names
-from tests.gpu_util import (max_abs, relative_l2, require_native, run_cuda, run_oracle, seeded_mixer_inputs)
+from tests.gpu_util import (max_abs, relative_l2, require_native, run_cuda, run_oracle, scaled_max_abs,
+                            seeded_mixer_inputs)
 
 pytestmark = pytest.mark.gpu
 
 FWD = 5e-3
-GRAD = 3e-2
+GRAD = 5e-3
+EXACT = 1e-2  # against the exact FP64 operator
+# max|actual - expected| <= MAXABS * max|expected|, per tensor: BF16 outputs
+# and operands put single elements a few BF16 ulps (2^-8 relative) off.
+MAXABS = 1e-2
 GRAD_NAMES = ("projected", "core_base_raw", "core_drive_weight", "eta_raw")
 
 
@@ -28,18 +43,30 @@ def native() -> None:
     require_native()
 
 
-def _check(out, grads, ref_out, ref_grads, *, fwd=FWD, grad=GRAD, label=""):
+def _check(out, grads, ref_out, ref_grads, *, fwd=FWD, grad=GRAD, maxabs=MAXABS, label="", exact=None):
+    """Compare with the contract oracle (``ref_*``) and, given ``exact = (out, grads)``
+    of the exact FP64 operator, with that at EXACT.  Prints relL2/scaled-maxabs."""
     assert torch.isfinite(out.float()).all()
-    e = relative_l2(out, ref_out)
-    line = [f"{label} fwd={e:.2e} maxabs={max_abs(out, ref_out):.2e}"]
-    assert e <= fwd, line
+    e, m = relative_l2(out, ref_out), scaled_max_abs(out, ref_out)
+    line = [f"{label} fwd={e:.2e}/{m:.2e}"]
+    assert e <= fwd and m <= maxabs, line
     if grads is not None:
         for name, g, r in zip(GRAD_NAMES, grads, ref_grads):
             assert torch.isfinite(g.float()).all(), name
-            ge = relative_l2(g, r)
-            line.append(f"{name}={ge:.2e}")
-            assert ge <= grad, (name, line)
+            ge, gm = relative_l2(g, r), scaled_max_abs(g, r)
+            line.append(f"{name}={ge:.2e}/{gm:.2e}")
+            assert ge <= grad and gm <= maxabs, (name, line)
+    if exact is not None:
+        xe = [relative_l2(out, exact[0])] + ([] if grads is None else
+                                             [relative_l2(g, r) for g, r in zip(grads, exact[1])])
+        line.append("exact=" + ",".join(f"{v:.2e}" for v in xe))
+        assert max(xe) <= EXACT, line
     print(" ".join(line))
+
+
+def _both(p, b, d, e, pos, counts, up):
+    """(contract oracle) and (exact FP64 operator) on the same inputs."""
+    return run_oracle(p, b, d, e, pos, counts, up), run_oracle(p, b, d, e, pos, counts, up, contract=False)
 
 
 @pytest.mark.parametrize("name", mixer_case_names())
@@ -61,7 +88,13 @@ def test_golden_fixtures(name: str) -> None:
         assert max_abs(out, case["out"]) < 1e-2
         print(f"{name} eta_raw={relative_l2(grads[3], ref[3]):.2e}")
         return
-    _check(out, grads, case["out"], ref, fwd=fwd, label=name)
+    # the reference's own FP64 output and gradients (FP32 upstream), at the reference's budgets
+    assert relative_l2(out, case["out"]) <= fwd
+    assert all(relative_l2(g, r) <= 3e-2 for g, r in zip(grads, ref))
+    # the contract oracle (pinned to these fixtures by tests/test_oracle.py) at this library's budgets
+    contract = run_oracle(t("projected"), t("core_base_raw"), t("core_drive_weight"), t("eta_raw"),
+                          case["centered_positions"], case["valid_counts"], t("upstream"))
+    _check(out, grads, *contract, label=name, exact=(case["out"], ref))
     if case["valid_mask"] is not None:
         mask = torch.from_numpy(case["valid_mask"]).cuda()
         assert torch.count_nonzero(out[~mask]) == 0
@@ -73,7 +106,8 @@ def test_lengths_match_oracle(length: int) -> None:
     pos = np.arange(length, dtype=np.float32)
     pos = pos - pos.mean()
     out, grads = run_cuda(p, b, d, e, pos, None, up)
-    _check(out, grads, *run_oracle(p, b, d, e, pos, None, up), label=f"N={length}")
+    contract, exact = _both(p, b, d, e, pos, None, up)
+    _check(out, grads, *contract, label=f"N={length}", exact=exact)
 
 
 EXPANDED = [
@@ -97,7 +131,8 @@ def test_expanded_shapes_match_oracle(batch, rank, heads, head_dim, length) -> N
     pos = np.arange(length, dtype=np.float32)
     pos = pos - pos.mean()
     out, grads = run_cuda(p, b, d, e, pos, None, up)
-    _check(out, grads, *run_oracle(p, b, d, e, pos, None, up), label=f"{(batch, rank, heads, head_dim, length)}")
+    contract, exact = _both(p, b, d, e, pos, None, up)
+    _check(out, grads, *contract, label=f"{(batch, rank, heads, head_dim, length)}", exact=exact)
 
 
 @pytest.mark.parametrize(("rank", "head_dim", "length"),
@@ -116,7 +151,8 @@ def test_masked_batch_specific_positions_match_oracle(rank, head_dim, length) ->
     out, grads = run_cuda(p, b, d, e, positions, counts, up)
     assert torch.count_nonzero(out[~mask.cuda()]) == 0
     assert torch.count_nonzero(grads[0][~mask.cuda()]) == 0
-    _check(out, grads, *run_oracle(p, b, d, e, positions, counts, up), label=f"masked {(rank, head_dim, length)}")
+    contract, exact = _both(p, b, d, e, positions, counts, up)
+    _check(out, grads, *contract, label=f"masked {(rank, head_dim, length)}", exact=exact)
 
 
 @pytest.mark.parametrize(("rank", "head_dim", "length"),
@@ -173,8 +209,8 @@ def test_bf16_content_beyond_fp16_range() -> None:
     upstream = torch.ones(1, 33, 16)
     out, grads = run_cuda(projected, base, drive, eta, None, None, upstream)
     assert out.float().abs().max() > torch.finfo(torch.float16).max
-    ro, rg = run_oracle(projected, base, drive, eta, None, None, upstream)
-    _check(out, grads, ro, rg, grad=1e-2, label="bf16-range")
+    contract, exact = _both(projected, base, drive, eta, None, None, upstream)
+    _check(out, grads, *contract, label="bf16-range", exact=exact)
 
 
 def test_results_are_deterministic() -> None:
@@ -190,7 +226,8 @@ def test_bench_shape_batch_slice_matches_oracle() -> None:
     """Bench shape (N=4096, H=8, r=32, d=32) on 4 samples against the FP64 oracle."""
     p, b, d, e, up = seeded_mixer_inputs(2026, 4, 4096, 8, 32, 32)
     out, grads = run_cuda(p, b, d, e, None, None, up)
-    _check(out, grads, *run_oracle(p, b, d, e, None, None, up), label="bench-slice")
+    contract, exact = _both(p, b, d, e, None, None, up)
+    _check(out, grads, *contract, label="bench-slice", exact=exact)
 
 
 def test_full_bench_batch_is_sample_independent() -> None:

@@ -1,6 +1,15 @@
 """Complete-module parity on the GPU: ``layer(x, implementation="cuda")``
 (projections + native mixer) against the FP64 oracle, and the BASELINE
-configurations at full size through size-independent properties."""
+configurations at full size through size-independent properties.
+
+Budgets, outputs and gradients alike, against the oracle with the roundings
+of the reference's FP32 path on CUDA tensors (BF16 projection operands and
+packed projection, FP16 phases, BF16 mixer output and the BF16 gradients at
+the same boundaries; oracle/lsso_oracle.py, ``contract=True``): relative L2
+<= 5e-3 for FP16 x and <= 1e-2 for BF16 x, and max|actual - expected| <=
+MAXABS[dtype] x max|expected| per tensor.  Against the exact FP64 operator
+(no rounding anywhere) every tensor stays within EXACT.
+"""
 
 from __future__ import annotations
 
@@ -12,12 +21,18 @@ import torch
 
 from oracle import lsso_oracle as O
 from lsso import LSSO, LSSOConfig
-from tests.gpu_util import max_abs, relative_l2, require_native
+from tests.gpu_util import relative_l2, require_native, scaled_max_abs
+from tests.golden_io import GOLDEN
 
 pytestmark = pytest.mark.gpu
 
 _PARAM_KEYS = {"w_bc.weight": "w_bc", "w_bc.bias": "b_bc", "w_o.weight": "w_o", "w_o.bias": "b_o",
                "core_base_raw": "core_base_raw", "core_drive_weight": "core_drive_weight", "eta_raw": "eta_raw"}
+
+
+BUDGET = {torch.float16: 5e-3, torch.bfloat16: 1e-2}
+MAXABS = {torch.float16: 1e-2, torch.bfloat16: 2e-2}
+EXACT = 1.5e-2  # against the exact FP64 operator (the contract's BF16 roundings included)
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -34,33 +49,71 @@ def _layer(config: LSSOConfig, seed: int, core: float = 0.05) -> LSSO:
     return layer.cuda()
 
 
-def _oracle(layer: LSSO, x: torch.Tensor, mask, position_ids, upstream):
+def _oracle(layer: LSSO, x: torch.Tensor, mask, position_ids, upstream, *, contract: bool, activation=None):
     params = {"b_bc": None, "b_o": None}
     for name, p in layer.named_parameters():
         params[_PARAM_KEYS[name]] = p.detach().double().cpu().numpy()
     n = lambda t: None if t is None else t.detach().cpu().numpy()  # noqa: E731
     y, state = O.module_forward(params, n(x).astype(np.float64), n(mask), n(position_ids),
-                                heads=layer.config.num_heads, rank=layer.config.rank, return_state=True)
+                                heads=layer.config.num_heads, rank=layer.config.rank, return_state=True,
+                                contract=contract, activation=activation)
     grads = O.module_backward(n(upstream).astype(np.float64), state)
     return y, grads
 
 
-def _compare(layer, x, mask=None, position_ids=None, *, fwd=5e-3, grad=3e-2, label=""):
+def _compare(layer, x, mask=None, position_ids=None, *, fwd=None, grad=None, maxabs=None, loss="random",
+             loss_scale=1.0, label=""):
+    """Forward + backward through the CUDA path against the oracle.
+
+    ``loss="random"`` back-propagates a seeded random upstream gradient,
+    ``loss="square_mean"`` the benchmark's ``y.float().square().mean()`` times
+    ``loss_scale``.  The oracle receives the gradient autograd actually hands
+    the layer's output (captured by a hook, in x's dtype).
+
+    y and every gradient are compared with the contract oracle at the dtype's
+    budget (relative L2 and scaled max-abs), and with the exact FP64 operator
+    at EXACT -- except the complement gradient, H scalars that are each a
+    difference of two O(N) sums (<dY, C> - <D, Z>), whose cancellation
+    magnifies the contract's BF16 roundings (the reference's own suite bounds
+    it only on dedicated fixtures).  Prints ``name=relL2/scaled-maxabs`` and
+    the exact errors.
+    """
+    fwd = BUDGET[x.dtype] if fwd is None else fwd
+    grad = BUDGET[x.dtype] if grad is None else grad
+    maxabs = MAXABS[x.dtype] if maxabs is None else maxabs
     xg = x.detach().clone().requires_grad_()
-    upstream = torch.randn(x.shape, generator=torch.Generator().manual_seed(1)).to(x.device, x.dtype)
     y = layer(xg, valid_mask=mask, position_ids=position_ids, implementation="cuda")
     assert y.dtype == x.dtype
+    seen = {}
+    y.register_hook(lambda g: seen.__setitem__("dy", g.detach().clone()))
+    if loss == "square_mean":
+        objective = y.float().square().mean() * loss_scale
+    else:
+        upstream = torch.randn(x.shape, generator=torch.Generator().manual_seed(1)).to(x.device, x.dtype)
+        objective = (y.float() * upstream.float()).sum()
     names = [n for n, _ in layer.named_parameters()]
-    grads = torch.autograd.grad((y.float() * upstream.float()).sum(), [xg, *layer.parameters()])
-    ry, rg = _oracle(layer, torch.nan_to_num(x.float()), mask, position_ids, upstream.float())
-    line = [f"{label} y={relative_l2(y, ry):.2e} maxabs={max_abs(y, ry):.2e}"]
-    assert relative_l2(y, ry) <= fwd, line
-    checks = [("x", grads[0], rg["x"])] + [(n, g, rg[_PARAM_KEYS[n]]) for n, g in zip(names, grads[1:])]
-    for name, g, r in checks:
+    grads = torch.autograd.grad(objective, [xg, *layer.parameters()])
+    dy = seen["dy"].float()
+    clean_x = torch.nan_to_num(x.float())
+    activation = {torch.float16: "float16", torch.bfloat16: "bfloat16"}[x.dtype]
+    ry, rg = _oracle(layer, clean_x, mask, position_ids, dy, contract=True, activation=activation)
+    ey, eg = _oracle(layer, clean_x, mask, position_ids, dy, contract=False)
+    e, m = relative_l2(y, ry), scaled_max_abs(y, ry)
+    line = [f"{label} y={e:.2e}/{m:.2e}"]
+    exact = [relative_l2(y, ey)]
+    assert e <= fwd and m <= maxabs, line
+    checks = [("x", grads[0], rg["x"], eg["x"])]
+    checks += [(n, g, rg[_PARAM_KEYS[n]], eg[_PARAM_KEYS[n]]) for n, g in zip(names, grads[1:])]
+    for name, g, r, xr in checks:
         assert torch.isfinite(g).all(), name
-        e = relative_l2(torch.nan_to_num(g), r)
-        line.append(f"{name}={e:.2e}")
-        assert e <= grad, (name, line)
+        g = torch.nan_to_num(g)
+        e, m = relative_l2(g, r), scaled_max_abs(g, r)
+        line.append(f"{name}={e:.2e}/{m:.2e}")
+        if name != "eta_raw":
+            exact.append(relative_l2(g, xr))
+        assert e <= grad and m <= maxabs, (name, line)
+    line.append("exact=" + ",".join(f"{v:.2e}" for v in exact))
+    assert max(exact) <= EXACT, line
     print(" ".join(line))
     return y, grads
 
@@ -111,9 +164,9 @@ def test_autocast_matches_production_reference(dtype) -> None:
     g = torch.autograd.grad((y * up).sum(), (x, *native.parameters()))
     rg = torch.autograd.grad((ry * up).sum(), (rx, *reference.parameters()))
     assert y.dtype == dtype
-    assert relative_l2(y, ry) <= 5e-3
-    for a, b in zip(g, rg):
-        assert relative_l2(a, b) <= 3e-2
+    errors = [relative_l2(y, ry)] + [relative_l2(a, b) for a, b in zip(g, rg)]
+    print(f"autocast {dtype}: " + " ".join(f"{e:.2e}" for e in errors))
+    assert max(errors) <= BUDGET[dtype], errors
 
 
 def test_config3_masked_rank64_bf16_full_size() -> None:
@@ -132,7 +185,7 @@ def test_config3_masked_rank64_bf16_full_size() -> None:
     assert torch.isfinite(xg.grad).all() and torch.count_nonzero(xg.grad[~mask]) == 0
     # Two samples of the same batch against the oracle (rows are independent).
     for b in (0, B - 1):
-        _compare(layer, x[b:b + 1], mask[b:b + 1], ids[b:b + 1], fwd=1e-2, label=f"config3 sample {b}")
+        _compare(layer, x[b:b + 1], mask[b:b + 1], ids[b:b + 1], label=f"config3 sample {b}")
 
 
 def test_config4_shell_four_layers_bf16() -> None:
@@ -165,3 +218,78 @@ def test_config5_long_sequence_rank64_slice() -> None:
     layer = _layer(LSSOConfig(512, 8, 64), 5)
     x = torch.randn(2, 16384, 512, generator=torch.Generator().manual_seed(5)).to("cuda", torch.float16)
     _compare(layer, x, label="config5 slice")
+
+
+# FP16 training scales the loss (torch.amp.GradScaler starts at 2^16): unscaled,
+# d mean(y^2)/dy = 2y/numel is ~1e-6 here (~1e-8 at B=64) and autograd hands the
+# layer that gradient in FP16, i.e. as subnormals of a few bits or zeros.
+FP16_LOSS_SCALE = 2.0 ** 16
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_headline_shape_module_matches_fp64_oracle(dtype) -> None:
+    """The timed workload (BASELINE config 2 at L=4096: D=256, H=8, r=32, seeded
+    default init, x ~ N(0,1), shared positions, loss y.float().square().mean(),
+    scaled for FP16) on a 2-sample slice of the B=64 batch: y and the gradients
+    of x, W_bc, W_o, core_base_raw, core_drive_weight and eta_raw."""
+    torch.manual_seed(0)
+    layer = LSSO(LSSOConfig(dim=256, num_heads=8, rank=32)).cuda()
+    x = torch.randn(64, 4096, 256, generator=torch.Generator().manual_seed(0))[:2].to("cuda", dtype)
+    scale = FP16_LOSS_SCALE if dtype == torch.float16 else 1.0
+    _compare(layer, x, loss="square_mean", loss_scale=scale, label=f"headline {dtype}")
+
+
+def test_headline_shape_trained_core_matches_fp64_oracle() -> None:
+    """Headline shape with non-zero compact parameters (as after training): the
+    default init has core_base_raw = core_drive_weight = 0, which leaves the
+    dynamic generator's drive path unexercised in the forward."""
+    layer = _layer(LSSOConfig(dim=256, num_heads=8, rank=32), 0, core=0.05)
+    x = torch.randn(2, 4096, 256, generator=torch.Generator().manual_seed(11)).to("cuda", torch.float16)
+    _compare(layer, x, loss="square_mean", loss_scale=FP16_LOSS_SCALE, label="headline trained-core")
+
+
+def test_headline_shape_unscaled_fp16_loss_matches_the_contract() -> None:
+    """The benchmark's unscaled FP16 loss: the layer receives FP16-subnormal
+    upstream gradients and stores x's gradient in FP16 subnormals too.  The
+    contract oracle, fed the same gradient and rounding x's gradient to FP16
+    as the projection stores it (reference.py:224), still agrees; x's gradient
+    (|dx| < 1e-6, FP16 steps of 6e-8) is held to 2.5e-2: a rounding flip of
+    one subnormal step is a few percent of such a value."""
+    torch.manual_seed(0)
+    layer = LSSO(LSSOConfig(dim=256, num_heads=8, rank=32)).cuda()
+    x = torch.randn(2, 4096, 256, generator=torch.Generator().manual_seed(0)).to("cuda", torch.float16)
+    xg = x.clone().requires_grad_()
+    y = layer(xg, implementation="cuda")
+    seen = {}
+    y.register_hook(lambda g: seen.__setitem__("dy", g.detach().clone()))
+    y.float().square().mean().backward()
+    dy = seen["dy"].float()
+    assert dy.abs().max() < 6.2e-5  # every upstream value is an FP16 subnormal
+    ry, rg = _oracle(layer, x.float(), None, None, dy, contract=True, activation="float16")
+    e_y, e_x = relative_l2(y, ry), relative_l2(xg.grad, rg["x"])
+    e_w = relative_l2(layer.w_o.weight.grad, rg["w_o"])
+    print(f"headline unscaled FP16: y={e_y:.2e} x={e_x:.2e} w_o={e_w:.2e} |dx|max={xg.grad.abs().max():.2e}")
+    assert e_y <= 5e-3 and e_w <= 5e-3 and e_x <= 2.5e-2
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_config1_through_cuda_matches_reference_fixture(dtype) -> None:
+    """BASELINE config 1 (LSSOConfig(192, 3, 16), default init from seed 0,
+    x = randn(8, 65, 192), positions 0..64) through implementation="cuda"
+    against the reference's own output (tests/golden/config1_forward.npz,
+    written by the reference's FP32 CPU path).  The CUDA contract takes
+    FP16/BF16 activations, so x is rounded to ``dtype`` first; the budget
+    is that dtype's."""
+    data = np.load(GOLDEN / "config1_forward.npz")
+    layer = LSSO(LSSOConfig(dim=192, num_heads=3, rank=16))
+    with torch.no_grad():
+        for name, p in layer.named_parameters():
+            p.copy_(torch.from_numpy(data["param_" + name.replace(".", "_")]))
+    layer = layer.cuda()
+    x = torch.from_numpy(data["x"]).to("cuda", dtype)
+    with torch.no_grad():
+        y = layer(x, implementation="cuda")
+    e, m = relative_l2(y, data["y"]), scaled_max_abs(y, data["y"])
+    print(f"config1 {dtype}: y={e:.2e}/{m:.2e}")
+    assert y.shape == (8, 65, 192) and y.dtype == dtype
+    assert e <= BUDGET[dtype] and m <= MAXABS[dtype]

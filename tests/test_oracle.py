@@ -104,3 +104,30 @@ def test_backward_matches_finite_differences() -> None:
             minus[index].reshape(-1)[position] -= step
             numeric = (loss(*plus) - loss(*minus)) / (2 * step)
             assert abs(numeric - grads[index].reshape(-1)[position]) < 1e-6 * max(1.0, abs(numeric))
+
+
+def test_contract_mode_rounds_only_at_the_contract_boundaries() -> None:
+    """``contract=True`` is the FP64 operator with the CUDA contract's roundings.
+    With FP16-exact phases (every position 0) its forward stays within BF16
+    rounding of the exact operator, its BF16 boundaries hold BF16 values, and
+    its mixer backward is the exact VJP of the BF16-rounded gradient."""
+    rng = np.random.default_rng(12)
+    params = O.init_params(32, 2, 16, bias=True, seed=4, core_scale=0.05)
+    x = rng.standard_normal((2, 17, 32))
+    zeros = np.zeros((2, 17), np.int64)
+    y_c, st_c = O.module_forward(params, x, None, zeros, heads=2, rank=16, return_state=True, contract=True)
+    y_e, st_e = O.module_forward(params, x, None, zeros, heads=2, rank=16, return_state=True)
+    assert 1e-5 < O.relative_l2(y_c, y_e) < 1e-2
+    # the BF16 boundaries: packed projection and mixer output are BF16 values
+    for value in (st_c["mixed"], st_c["x"]):
+        assert np.array_equal(O.round_bf16(value), value.astype(np.float32))
+    upstream = rng.standard_normal(y_c.shape)
+    g_c = O.module_backward(upstream, st_c)
+    g_e = O.module_backward(upstream, st_e)
+    for key in ("x", "w_bc", "w_o", "core_base_raw", "core_drive_weight"):
+        assert O.relative_l2(g_c[key], g_e[key]) < 2e-2, key
+    # the mixer part of the contract backward is the exact VJP of the rounded gradient
+    go = O.round_bf16(upstream.reshape(-1, 32)).astype(np.float64)
+    grad_mixed = O.round_bf16(go @ st_c["w_o"]).astype(np.float64).reshape(2, 17, 32)
+    _, base, _, _ = O.mixer_backward(grad_mixed, st_c["mixer"])
+    assert np.array_equal(base, g_c["core_base_raw"])

@@ -101,7 +101,7 @@ def test_emulated_ranks_match_unsplit(batch, rank, heads, head_dim, length, part
     o_out, o_grads = run_oracle(p, b, d, e, pos, counts, up.to(torch.bfloat16).float())
     assert relative_l2(out, o_out) <= 5e-3
     for g, r in zip(grads, o_grads):
-        assert relative_l2(g, r) <= 3e-2
+        assert relative_l2(g, r) <= 5e-3
 
 
 def test_one_rank_group_reproduces_the_layer_bit_for_bit(tmp_path) -> None:

@@ -54,15 +54,16 @@ def test_shell_cuda_matches_the_reference_path_in_bf16() -> None:
         return y.detach().float(), [p.grad.detach().clone() for p in shell.parameters()]
 
     # BF16 CUDA blocks against the FP32 reference path of the same shell.  Four
-    # BF16 layers compound their roundings, so the bound is the larger of the
-    # per-layer BF16 budget (1e-2) and 1.25x the error of the reference path's
-    # own BF16 (autocast) run.
+    # BF16 layers compound their roundings, so each bound (output and every
+    # gradient) is the larger of the per-layer BF16 budget (1e-2) and 1.25x the
+    # error of the reference path's own BF16 (autocast) run of the same tensor.
     y_cuda, g_cuda = run("cuda", True)
     y_ref, g_ref = run("reference", False)
-    y_bf16, _ = run("reference", True)
+    y_bf16, g_bf16 = run("reference", True)
     e, e_ref = relative_l2(y_cuda, y_ref), relative_l2(y_bf16, y_ref)
     print(f"shell output rel L2: cuda {e:.2e}, reference path in BF16 {e_ref:.2e}")
     assert e <= max(1e-2, 1.25 * e_ref)
-    for (name, _), a, b in zip(shell.named_parameters(), g_cuda, g_ref):
-        ge = relative_l2(a, b)
-        assert ge <= 3e-2, (name, ge)
+    for (name, _), a, b, c in zip(shell.named_parameters(), g_cuda, g_ref, g_bf16):
+        ge, ge_ref = relative_l2(a, b), relative_l2(c, b)
+        print(f"shell grad {name}: cuda {ge:.2e}, reference path in BF16 {ge_ref:.2e}")
+        assert ge <= max(1e-2, 1.25 * ge_ref), (name, ge, ge_ref)

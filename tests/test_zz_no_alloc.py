@@ -6,9 +6,14 @@ allocation inside plugin calls, or a serving loop whose memory is fixed up
 front.  Instead of a caller-allocated workspace it uses one fixed scratch
 array inside the library.  This test calls it through the C ABI twice in a
 row (two shapes, so the shared scratch is reused with a different layout) and
-checks each result against the regular ``lsso_forward`` entry point, with the
-forward tolerance of the other parity tests; it also checks that a shape too
-large for the fixed area is rejected with a clear message.
+checks each result against the regular ``lsso_forward`` entry point: both run
+the same plan and the same kernels, so the outputs must be bit-identical.  A
+second test first leaves NaN-derived values throughout the scratch (a call on
+NaN inputs at a shape whose scratch is just under the limit), then runs a
+valid shape of that size and a small one, each again bit-identical to
+``lsso_forward``: every call overwrites all the scratch it reads.  It also
+checks that a shape too large for the fixed area is rejected with a clear
+message.
 
 The file name makes pytest collect it last, so a run that stops at the first
 failure has already run every other test; it also passes on its own in a
@@ -24,8 +29,8 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-FORWARD_BUDGET = 5e-3  # relative L2, as the other forward parity tests
 LSSO_ERR_WORKSPACE = 4
+LIMIT = 32 << 20  # LSSO_NOALLOC_SCRATCH_BYTES
 
 
 def _bind():
@@ -61,27 +66,56 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+def _run_pair(lib, seed, shape, batched, *, poison=False):
+    """lsso_forward (own workspace) and lsso_forward_inference_noalloc on the same inputs."""
+    B, N, H, R, d = shape
+    stream = torch.cuda.current_stream().cuda_stream
+    projected, base, drive, eta, positions, counts = _inputs(seed, B, N, H, R, d, batched)
+    if poison:
+        projected.fill_(float("nan"))
+    D = H * d
+    args = (_ptr(projected), _ptr(base), _ptr(drive), _ptr(eta), _ptr(positions), int(batched), _ptr(counts),
+            B, N, H, D, R)
+    expected = torch.empty(B, N, D, device="cuda", dtype=torch.bfloat16)
+    size = lib.lsso_forward_workspace_size(B, N, H, D, R, int(batched), 0)
+    workspace = torch.empty(size, device="cuda", dtype=torch.uint8)
+    assert lib.lsso_forward(*args, expected.data_ptr(), None, None, workspace.data_ptr(), size, stream) == 0, \
+        lib.lsso_last_error()
+    actual = torch.full((B, N, D), float("nan"), device="cuda", dtype=torch.bfloat16)
+    assert lib.lsso_forward_inference_noalloc(*args, actual.data_ptr(), stream) == 0, lib.lsso_last_error()
+    torch.cuda.synchronize()
+    return actual, expected, size
+
+
 def test_noalloc_forward_matches_forward_on_two_calls_in_a_row() -> None:
     lib = _bind()
-    stream = torch.cuda.current_stream().cuda_stream
     cases = [(1, (2, 1500, 4, 32, 32), False), (2, (3, 333, 2, 48, 17), True)]
-    for seed, (B, N, H, R, d), batched in cases:
-        projected, base, drive, eta, positions, counts = _inputs(seed, B, N, H, R, d, batched)
-        D = H * d
-        args = (_ptr(projected), _ptr(base), _ptr(drive), _ptr(eta), _ptr(positions), int(batched), _ptr(counts),
-                B, N, H, D, R)
-        expected = torch.empty(B, N, D, device="cuda", dtype=torch.bfloat16)
-        size = lib.lsso_forward_workspace_size(B, N, H, D, R, int(batched), 0)
-        workspace = torch.empty(size, device="cuda", dtype=torch.uint8)
-        assert lib.lsso_forward(*args, expected.data_ptr(), None, None, workspace.data_ptr(), size, stream) == 0, \
-            lib.lsso_last_error()
-        actual = torch.full((B, N, D), float("nan"), device="cuda", dtype=torch.bfloat16)
-        assert lib.lsso_forward_inference_noalloc(*args, actual.data_ptr(), stream) == 0, lib.lsso_last_error()
-        torch.cuda.synchronize()
+    for seed, shape, batched in cases:
+        actual, expected, size = _run_pair(lib, seed, shape, batched)
+        print(f"noalloc call {seed}: shape {shape}, {size} bytes of scratch")
         assert torch.isfinite(actual.float()).all()
-        error = float((actual.double() - expected.double()).norm() / expected.double().norm())
-        print(f"noalloc call {seed}: shape {(B, N, H, R, d)} rel-L2 vs lsso_forward {error:.2e}")
-        assert error <= FORWARD_BUDGET
+        assert torch.equal(actual, expected)
+
+
+def test_noalloc_reads_nothing_a_previous_call_left_behind() -> None:
+    lib = _bind()
+    # The longest sequence (B=1, H=8, r=32, d=32) whose scratch still fits the area.
+    best = None
+    for N in range(1024, 1 << 20, 1024):
+        size = lib.lsso_forward_workspace_size(1, N, 8, 256, 32, 0, 0)
+        if size <= LIMIT:
+            best = (N, size) if best is None or size > best[1] else best
+        elif size > 2 * LIMIT:
+            break
+    assert best is not None and best[1] > LIMIT // 2, best
+    near = (1, best[0], 8, 32, 32)
+    poisoned, _, _ = _run_pair(lib, 5, near, False, poison=True)
+    assert not torch.isfinite(poisoned.float()).all()  # NaN-derived values now fill the used scratch
+    for seed, shape in ((6, near), (7, (2, 257, 2, 16, 16))):
+        actual, expected, size = _run_pair(lib, seed, shape, False)
+        print(f"after a NaN call: shape {shape}, {size} of {LIMIT} bytes")
+        assert torch.isfinite(actual.float()).all()
+        assert torch.equal(actual, expected)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch() -> None:
