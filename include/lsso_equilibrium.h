@@ -201,7 +201,10 @@ LSSO_API int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_
  * LSSO_ERR_WORKSPACE and a message naming the size (use lsso_forward then).
  * The first call on a device resolves the array's device address with
  * cudaGetSymbolAddress while that device is current; make that first call
- * before any stream capture.  All calls share the array and every call
+ * before any stream capture.  The address is kept per device number for the
+ * device's primary context (the one the CUDA runtime and PyTorch use): a
+ * caller that runs the library in a context of its own, or that resets the
+ * device (cudaDeviceReset) between calls, must load the library anew.  All calls share the array and every call
  * overwrites the parts it reads, so nothing needs clearing; calls whose
  * kernels overlap on the same GPU (e.g. on two streams) race on it. */
 LSSO_API int lsso_forward_inference_noalloc(const void* projected, const float* core_base_raw,
