@@ -165,6 +165,29 @@ LSSO_API int lsso_linear(const void* a, int a_dtype, int64_t M, int64_t K, const
                          void* out, int out_dtype, int64_t ldo, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* The same GEMM with the weight conversion split off, so that one launch
+ * prepares every weight image a layer step needs (the input and output
+ * projections' weights, each in the forward and the transposed orientation)
+ * instead of one conversion kernel per product.  Replaces the BF16 weight
+ * copy the reference's _TensorCoreLinear makes in its forward and keeps for
+ * its backward (lsso/ball/reference.py:181-183,204-205).
+ *
+ * lsso_linear_image_size: bytes of one image for a [.., K] x [Nout, K]^T
+ *   product (depends on K and Nout only); 0 if unsupported.
+ * lsso_linear_prepare: converts count (1..4) FP32 weights, weights[i] being
+ *   [Nout[i], K[i]] (or [K[i], Nout[i]] if weight_transposed[i]), into
+ *   images[i] (lsso_linear_image_size(K[i], Nout[i]) bytes, 16-byte aligned),
+ *   in one kernel launch on `stream`.
+ * lsso_linear_prepared: lsso_linear reading the weight from an image made by
+ *   lsso_linear_prepare for the same K, Nout and orientation; no conversion
+ *   kernel, no workspace.  Bit-identical to lsso_linear. */
+LSSO_API size_t lsso_linear_image_size(int64_t K, int64_t Nout);
+LSSO_API int lsso_linear_prepare(int count, const float* const* weights, const int* weight_transposed,
+                                 const int64_t* K, const int64_t* Nout, void* const* images, void* stream);
+LSSO_API int lsso_linear_prepared(const void* a, int a_dtype, int64_t M, int64_t K, const void* image,
+                                  int64_t Nout, const float* bias, const uint8_t* row_mask, void* out,
+                                  int out_dtype, int64_t ldo, void* stream);
+
 /* Workspace bytes of lsso_linear_wgrad for T tokens, Nout outputs, K inputs
  * (per-split FP32 partial tiles, enough for either operand orientation the
  * kernel picks from the dtypes); 0 if unsupported (Nout and K must be

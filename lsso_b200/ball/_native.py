@@ -23,7 +23,8 @@ EXPORTED_SYMBOLS = (
     "lsso_contract_version", "lsso_compiled_sm", "lsso_check_device", "lsso_last_error", "lsso_device_status",
     "lsso_tape_stride", "lsso_forward_workspace_size", "lsso_forward", "lsso_backward_workspace_size",
     "lsso_backward", "lsso_profile_start", "lsso_profile_stop", "lsso_forward_inference_noalloc",
-    "lsso_linear_workspace_size", "lsso_linear", "lsso_linear_wgrad_workspace_size", "lsso_linear_wgrad",
+    "lsso_linear_workspace_size", "lsso_linear", "lsso_linear_image_size", "lsso_linear_prepare",
+    "lsso_linear_prepared", "lsso_linear_wgrad_workspace_size", "lsso_linear_wgrad",
     "lsso_moment_elements", "lsso_forward_moments", "lsso_forward_finish", "lsso_backward_moments",
     "lsso_backward_finish", "lsso_fused_forward_supported", "lsso_fused_forward_workspace_size",
     "lsso_fused_forward",
@@ -54,6 +55,10 @@ class NativeLibrary:
                                    vp, sz, vp]),
             "lsso_linear_workspace_size": (sz, [i64, i64, i64]),
             "lsso_linear": (ci, [vp, ci, i64, i64, vp, ci, i64, vp, vp, vp, ci, i64, vp, sz, vp]),
+            "lsso_linear_image_size": (sz, [i64, i64]),
+            "lsso_linear_prepare": (ci, [ci, c.POINTER(vp), c.POINTER(ci), c.POINTER(i64), c.POINTER(i64),
+                                         c.POINTER(vp), vp]),
+            "lsso_linear_prepared": (ci, [vp, ci, i64, i64, vp, i64, vp, vp, vp, ci, i64, vp]),
             "lsso_linear_wgrad_workspace_size": (sz, [i64, i64, i64]),
             "lsso_linear_wgrad": (ci, [vp, ci, vp, ci, vp, i64, i64, i64, vp, vp, sz, vp]),
             "lsso_forward_inference_noalloc": (ci, [vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp]),

@@ -233,16 +233,21 @@ class LSSO(nn.Module):
         if not all_valid:
             valid_counts = mask.sum(dim=-1).to(dtype=torch.float32).clamp_min(1.0).contiguous()
 
+        # One launch converts every weight image this step's GEMMs use (forward, and
+        # the input-gradient products of the backward when one will run).
+        wants_backward = torch.is_grad_enabled() and (
+            x.requires_grad or any(p.requires_grad for p in (self.w_bc.weight, self.w_o.weight)))
+        images = projection.layer_images(self.w_bc.weight, self.w_o.weight, wants_backward)
         if projection.fused_input_covers(x, c.num_heads, c.rank):
             # the projection fused with the mixer's moment pass (same projected coordinates)
             cuda_backend.require_available()
             mixed = projection.fused_input_mix(x, self.w_bc.weight, self.w_bc.bias, mask, self.core_base_raw,
                                                self.core_drive_weight, self.eta_raw, centered_positions, valid_counts)
         else:
-            projected = projection.input_projection(x, self.w_bc.weight, self.w_bc.bias, mask)
+            projected = projection.input_projection(x, self.w_bc.weight, self.w_bc.bias, mask, images)
             mixed = cuda_backend.fast_mix(projected, self.core_base_raw, self.core_drive_weight, self.eta_raw,
                                           centered_positions, valid_counts)
-        return projection.output_projection(mixed, self.w_o.weight, self.w_o.bias, x.dtype, mask)
+        return projection.output_projection(mixed, self.w_o.weight, self.w_o.bias, x.dtype, mask, images)
 
     # ------------------------------------------------------------------ reference path
     def _compact_coordinates(self, compact_state, valid_count):

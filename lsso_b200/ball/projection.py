@@ -13,6 +13,8 @@ gradient ``bf16(g)^T bf16(x)`` in FP32 and the bias gradient an FP32 sum.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.nn.functional as F
 from torch.autograd.function import once_differentiable
@@ -27,15 +29,73 @@ def _pad_features(value: torch.Tensor, multiple: int = 8) -> torch.Tensor:
     return value if extra == 0 else F.pad(value, (0, extra))
 
 
+def prepare_images(specs: list[tuple[torch.Tensor, bool]]) -> list[torch.Tensor]:
+    """BF16 tensor-core images of FP32 weights, all converted in one kernel launch.
+
+    ``specs`` holds up to four ``(weight, transposed)`` pairs: ``weight`` FP32
+    ``[Nout, K]`` for ``a W^T`` (``transposed=False``) or ``[K, Nout]`` read as
+    ``a W`` (``transposed=True``), K and Nout multiples of 8.  Returns one
+    uint8 image per pair for :func:`linear`'s ``image`` argument.
+    """
+    lib = _native.library()
+    device = specs[0][0].device
+    weights, sizes, shapes = [], [], []
+    with torch.cuda.device(device):
+        for weight, transposed in specs:
+            w = weight.detach().float().contiguous()
+            k, nout = (w.shape[0], w.shape[1]) if transposed else (w.shape[1], w.shape[0])
+            size = lib.lib.lsso_linear_image_size(k, nout)
+            if size == 0:
+                lib.check(1)
+            weights.append(w)
+            sizes.append((size + 255) // 256 * 256)
+            shapes.append((k, nout, int(transposed)))
+        buffer = torch.empty((sum(sizes),), dtype=torch.uint8, device=device)
+        images = list(buffer.split(sizes))
+        n = len(specs)
+        vp, ci, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+        lib.check(lib.lib.lsso_linear_prepare(
+            n, (vp * n)(*[w.data_ptr() for w in weights]), (ci * n)(*[t for _, _, t in shapes]),
+            (i64 * n)(*[k for k, _, _ in shapes]), (i64 * n)(*[o for _, o, _ in shapes]),
+            (vp * n)(*[im.data_ptr() for im in images]), torch.cuda.current_stream(device).cuda_stream))
+    return images
+
+
+def layer_images(w_bc: torch.Tensor, w_o: torch.Tensor, backward: bool) -> dict | None:
+    """The four weight images of one layer step (one launch), or None when a
+    feature width is not a multiple of 8 (the per-call conversion then runs)."""
+    if any(n % 8 for n in (*w_bc.shape, *w_o.shape)):
+        return None
+    specs = [(w_bc, False), (w_o, False)] + ([(w_o, True), (w_bc, True)] if backward else [])
+    images = prepare_images(specs)
+    names = ("bc", "o", "o_t", "bc_t")
+    return dict(zip(names, images))
+
+
 def linear(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, row_mask: torch.Tensor | None,
-           out_dtype: torch.dtype, *, weight_transposed: bool = False) -> torch.Tensor:
+           out_dtype: torch.dtype, *, weight_transposed: bool = False, image: torch.Tensor | None = None
+           ) -> torch.Tensor:
     """One native GEMM: ``a [.., K] (BF16/FP16) x W -> [.., Nout]`` in ``out_dtype``.
 
     ``weight`` is FP32 ``[Nout, K]`` (or ``[K, Nout]`` with ``weight_transposed``).
+    ``image``: the same weight already converted by :func:`prepare_images` in
+    this orientation (then no conversion kernel runs; the result is identical).
     """
     lib = _native.library()
     lead = a.shape[:-1]
     k = a.shape[-1]
+    if image is not None and k % 8 == 0:
+        flat = a.reshape(-1, k).contiguous()
+        nout = weight.shape[1] if weight_transposed else weight.shape[0]
+        out = torch.empty((flat.shape[0], nout), dtype=out_dtype, device=a.device)
+        mask = None if row_mask is None else row_mask.reshape(-1).contiguous().view(torch.uint8)
+        with torch.cuda.device(a.device):
+            lib.check(lib.lib.lsso_linear_prepared(
+                flat.data_ptr(), 1 if flat.dtype == torch.float16 else 0, flat.shape[0], k, image.data_ptr(), nout,
+                None if bias is None else bias.detach().float().contiguous().data_ptr(),
+                None if mask is None else mask.data_ptr(), out.data_ptr(), _OUT_CODES[out_dtype], nout,
+                torch.cuda.current_stream(a.device).cuda_stream))
+        return out.reshape(*lead, nout)
     flat = a.reshape(-1, k)
     w = weight.detach().float()
     if k % 8:
@@ -90,12 +150,16 @@ def weight_gradient(g: torch.Tensor, x: torch.Tensor, row_mask: torch.Tensor | N
 
 
 class _ProjectionFunction(torch.autograd.Function):
+    """``value W^T + bias``; ``image`` / ``image_t`` are the weight's prepared
+    images for the forward and for the input-gradient product (both made at
+    forward time, as the reference keeps its BF16 weight copy for the backward)."""
+
     @staticmethod
-    def forward(ctx, value, weight, bias, row_mask, out_dtype):
+    def forward(ctx, value, weight, bias, row_mask, out_dtype, image, image_t):
         if value.dtype not in (torch.float16, torch.bfloat16):
             value = value.to(torch.bfloat16)
-        out = linear(value, weight, bias, row_mask, out_dtype)
-        ctx.save_for_backward(value, weight, row_mask)
+        out = linear(value, weight, bias, row_mask, out_dtype, image=image)
+        ctx.save_for_backward(value, weight, row_mask, image_t)
         ctx.has_bias = bias is not None
         ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
         return out
@@ -103,13 +167,13 @@ class _ProjectionFunction(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_output):
-        value, weight, row_mask = ctx.saved_tensors
+        value, weight, row_mask, image_t = ctx.saved_tensors
         grads = _linear_vjp(grad_output, value, weight, row_mask, ctx.needs_input_grad[:3],
-                            ctx.bias_meta if ctx.has_bias else None)
-        return (*grads, None, None)
+                            ctx.bias_meta if ctx.has_bias else None, image_t)
+        return (*grads, None, None, None, None)
 
 
-def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta):
+def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=None):
     """(grad_value, grad_weight, grad_bias) of ``value W^T + bias`` (reference.py:170-247)."""
     g = grad_output
     if g.dtype not in (torch.float16, torch.bfloat16):
@@ -119,7 +183,7 @@ def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta):
     # Masked rows: the input-gradient GEMM writes them as zero and the
     # weight-gradient kernel skips them, so only the bias sum masks here.
     if needs[0]:
-        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True)
+        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True, image=image_t)
     if needs[1]:
         grad_weight = weight_gradient(g, value, row_mask)
     if bias_meta is not None and needs[2]:
@@ -198,16 +262,20 @@ def fused_input_mix(x, weight, bias, row_mask, core_base_raw, core_drive_weight,
 
 
 def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
-                     mask: torch.Tensor | None) -> torch.Tensor:
-    projected = _ProjectionFunction.apply(x, weight, bias, mask, torch.bfloat16)
+                     mask: torch.Tensor | None, images: dict | None = None) -> torch.Tensor:
+    images = images or {}
+    projected = _ProjectionFunction.apply(x, weight, bias, mask, torch.bfloat16, images.get("bc"),
+                                          images.get("bc_t"))
     if not projected.is_contiguous():
         raise RuntimeError("implementation='cuda' requires w_bc to produce contiguous projected coordinates")
     return projected
 
 
 def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
-                      dtype: torch.dtype, mask: torch.Tensor | None) -> torch.Tensor:
-    return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype)
+                      dtype: torch.dtype, mask: torch.Tensor | None, images: dict | None = None) -> torch.Tensor:
+    images = images or {}
+    return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype, images.get("o"), images.get("o_t"))
 
 
-__all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "linear", "output_projection", "weight_gradient"]
+__all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "layer_images", "linear", "output_projection",
+           "prepare_images", "weight_gradient"]

@@ -286,6 +286,95 @@ int lsso_linear(const void* a, int a_dtype, int64_t M, int64_t K, const float* w
   return LSSO_OK;
 }
 
+size_t lsso_linear_image_size(int64_t K, int64_t Nout) {
+  g_last_error.clear();
+  if (Nout <= 0 || !lsso::linear_shape_supported(K)) {
+    fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_image_size: K must be a positive multiple of 8 (at most 1024), "
+                                    "Nout positive");
+    return 0;
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  if (device_info(&device, &sms, &status) != LSSO_OK) return 0;
+  return lsso::image_bytes(K, Nout, sms);
+}
+
+int lsso_linear_prepare(int count, const float* const* weights, const int* weight_transposed, const int64_t* K,
+                        const int64_t* Nout, void* const* images, void* stream) {
+  g_last_error.clear();
+  if (count < 1 || count > lsso::kMaxImages) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepare: count must be 1..%d", lsso::kMaxImages);
+  }
+  if (weights == nullptr || weight_transposed == nullptr || K == nullptr || Nout == nullptr || images == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepare: a required pointer is NULL");
+  }
+  lsso::WeightImage list[lsso::kMaxImages];
+  for (int i = 0; i < count; ++i) {
+    if (weights[i] == nullptr || images[i] == nullptr) {
+      return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepare: weight or image %d is NULL", i);
+    }
+    if (Nout[i] <= 0 || Nout[i] > (int64_t(1) << 20) || !lsso::linear_shape_supported(K[i])) {
+      return fail(LSSO_ERR_INVALID_ARGUMENT,
+                  "lsso_linear_prepare: image %d: K must be a positive multiple of 8 (at most 1024), Nout positive", i);
+    }
+    if (!aligned16(images[i])) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepare: image %d is not 16-byte "
+                                                                      "aligned", i);
+    list[i] = lsso::WeightImage{weights[i], K[i], Nout[i], weight_transposed[i] != 0 ? 1 : 0,
+                                static_cast<uint8_t*>(images[i])};
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  const int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  const cudaError_t e = lsso::launch_prepare_images(list, count, sms, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_linear_prepare");
+  return LSSO_OK;
+}
+
+int lsso_linear_prepared(const void* a, int a_dtype, int64_t M, int64_t K, const void* image, int64_t Nout,
+                         const float* bias, const uint8_t* row_mask, void* out, int out_dtype, int64_t ldo,
+                         void* stream) {
+  g_last_error.clear();
+  if (a == nullptr || image == nullptr || out == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepared: a required pointer is NULL");
+  }
+  if (M <= 0 || Nout <= 0 || !lsso::linear_shape_supported(K)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT,
+                "lsso_linear_prepared: K must be a positive multiple of 8 (at most 1024), M and Nout positive");
+  }
+  if (M > (int64_t(1) << 31) - 1 || Nout > (int64_t(1) << 20)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepared: shape exceeds the supported launch range");
+  }
+  if (a_dtype != 0 && a_dtype != 1) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepared: a_dtype must be 0 or 1");
+  if (out_dtype < 0 || out_dtype > 2) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepared: out_dtype must be 0..2");
+  }
+  if (ldo < Nout) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepared: ldo must be at least Nout");
+  if (!aligned16(a) || !aligned16(image)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_prepared: a and image must be 16-byte aligned");
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  const lsso::LinearPlan plan = lsso::make_linear_plan(M, K, Nout, sms);
+  lsso::LinearCall c{};
+  c.a = a;
+  c.a_fp16 = a_dtype;
+  c.weight = nullptr;
+  c.bias = bias;
+  c.row_mask = row_mask;
+  c.out = out;
+  c.ldo = ldo;
+  c.out_dtype = out_dtype;
+  c.prep = static_cast<uint8_t*>(const_cast<void*>(image));
+  c.prepared = 1;
+  c.status = status;
+  const cudaError_t e = lsso::launch_linear(plan, c, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_linear_prepared");
+  return LSSO_OK;
+}
+
 size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_t K) {
   g_last_error.clear();
   if (T <= 0 || Nout <= 0 || K <= 0 || Nout % 8 != 0 || K % 8 != 0) {

@@ -403,14 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
 // Weight (FP32, [Nout, K] or transposed [K, Nout]) -> BF16 K-major SW128
 // canonical tiles of BN rows: 64-wide K regions of BN rows x 128 bytes; row n
 // at (n/8)*1024 + (n%8)*128, its 16-byte chunk c stored at chunk c ^ (n%8).
-// Zero outside [Nout, K].
-__global__ void prep_weight_kernel(const float* __restrict__ w, int Nout, int K, int transposed, int BN, int K_pad,
-                                   int NT, uint8_t* __restrict__ out) {
-  pdl_wait();
-  // 32-bit index arithmetic: a weight tile set is far below 2^31 elements.
-  const int total = NT * BN * K_pad;
-  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= total) return;
+// Zero outside [Nout, K].  Element idx of the image (32-bit index arithmetic:
+// a weight tile set is far below 2^31 elements).
+__device__ __forceinline__ void prep_weight_element(const float* __restrict__ w, int Nout, int K, int transposed,
+                                                    int BN, int K_pad, uint8_t* __restrict__ out, int idx) {
   const int tile = BN * K_pad;
   const int j = idx / tile;
   const int rem = idx - j * tile;
@@ -423,6 +419,34 @@ __global__ void prep_weight_kernel(const float* __restrict__ w, int Nout, int K,
                      static_cast<size_t>(nl / 8) * 1024 + (nl % 8) * 128 + ((((kk * 2) / 16) ^ (nl % 8)) * 16) +
                      (kk * 2) % 16;
   *reinterpret_cast<__nv_bfloat16*>(out + off) = __float2bfloat16_rn(v);
+}
+
+__global__ void prep_weight_kernel(const float* __restrict__ w, int Nout, int K, int transposed, int BN, int K_pad,
+                                   int NT, uint8_t* __restrict__ out) {
+  pdl_wait();
+  const int total = NT * BN * K_pad;
+  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  prep_weight_element(w, Nout, K, transposed, BN, K_pad, out, idx);
+}
+
+// Several images in one launch: the grid covers their elements back to back
+// (image e owns [end[e-1], end[e])).
+struct PrepBatch {
+  const float* w[kMaxImages];
+  uint8_t* out[kMaxImages];
+  int Nout[kMaxImages], K[kMaxImages], transposed[kMaxImages], BN[kMaxImages], K_pad[kMaxImages];
+  int end[kMaxImages];
+  int count;
+};
+
+__global__ void prep_weights_kernel(const __grid_constant__ PrepBatch b) {
+  pdl_wait();
+  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  int e = 0, begin = 0;
+  while (e < b.count && idx >= b.end[e]) begin = b.end[e++];
+  if (e >= b.count) return;
+  prep_weight_element(b.w[e], b.Nout[e], b.K[e], b.transposed[e], b.BN[e], b.K_pad[e], b.out[e], idx - begin);
 }
 
 // ============================================================================
@@ -768,10 +792,36 @@ WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int 
   return p;
 }
 
+size_t image_bytes(int64_t K, int64_t Nout, int sm_count) { return make_linear_plan(1, K, Nout, sm_count).prep_bytes; }
+
+cudaError_t launch_prepare_images(const WeightImage* images, int count, int sm_count, cudaStream_t stream) {
+  if (count < 1 || count > kMaxImages) return cudaErrorInvalidValue;
+  PrepBatch b{};
+  int64_t total = 0;
+  for (int e = 0; e < count; ++e) {
+    const WeightImage& im = images[e];
+    const LinearPlan p = make_linear_plan(1, im.K, im.Nout, sm_count);
+    b.w[e] = im.weight;
+    b.out[e] = im.image;
+    b.Nout[e] = static_cast<int>(p.Nout);
+    b.K[e] = static_cast<int>(p.K);
+    b.transposed[e] = im.transposed;
+    b.BN[e] = p.BN;
+    b.K_pad[e] = static_cast<int>(p.K_pad);
+    total += static_cast<int64_t>(p.NT) * p.BN * p.K_pad;
+    if (total >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
+    b.end[e] = static_cast<int>(total);
+  }
+  b.count = count;
+  LaunchScope scope("prep_weight", stream);
+  launch_pdl(prep_weights_kernel, static_cast<unsigned>((total + 255) / 256), 256, 0, stream, b);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return cudaErrorNotSupported;
-  {
+  if (!c.prepared) {
     const int64_t total = static_cast<int64_t>(p.NT) * p.BN * p.K_pad;
     LaunchScope scope("prep_weight", stream);
     if (total >= (int64_t{1} << 31)) return cudaErrorInvalidValue;

@@ -29,8 +29,20 @@ struct LinearCall {
   int64_t ldo;
   int out_dtype;            // 0 BF16, 1 FP16, 2 FP32
   uint8_t* prep;            // workspace for the prepared weight (plan.prep_bytes, 16-byte aligned)
+  int prepared;             // 1: `prep` already holds this weight's image (launch_prepare_images); no prep kernel
   int* status;
 };
+
+// One weight to convert into the GEMM's BF16 image (the layout launch_linear's
+// prep kernel writes into its workspace; it depends on K, Nout and the
+// orientation only, not on M).
+struct WeightImage {
+  const float* weight;  // FP32 [Nout, K], or [K, Nout] when transposed
+  int64_t K, Nout;
+  int transposed;
+  uint8_t* image;       // image_bytes(K, Nout) bytes, 16-byte aligned
+};
+constexpr int kMaxImages = 4;
 
 struct WgradPlan {
   int64_t T, Nout, K;
@@ -60,5 +72,10 @@ cudaError_t launch_wgrad(const WgradPlan& plan, const WgradCall& call, cudaStrea
 LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count);
 bool linear_shape_supported(int64_t K);
 cudaError_t launch_linear(const LinearPlan& plan, const LinearCall& call, cudaStream_t stream);
+
+// Bytes of one prepared weight image.
+size_t image_bytes(int64_t K, int64_t Nout, int sm_count);
+// Converts up to kMaxImages weights in one launch.
+cudaError_t launch_prepare_images(const WeightImage* images, int count, int sm_count, cudaStream_t stream);
 
 }  // namespace lsso
