@@ -66,6 +66,16 @@ LSSO_API const char* lsso_last_error(void);
  * reset != 0 clears it afterwards. */
 LSSO_API int lsso_device_status(int reset);
 
+/* Test hook (no counterpart in the reference): time limit, in nanoseconds,
+ * of the pipeline waits of the current device's tensor-core kernels (default
+ * and limit_ns == 0: one second).  A test sets a tiny limit so that those
+ * waits run out: the kernels then take their abort path (each role stops,
+ * in-flight TMA loads, tensor-core operations and bulk stores are awaited,
+ * TMEM is freed), the status word reads 1 and the outputs are undefined; it
+ * restores the default afterwards.  Synchronous; not for use while kernels of
+ * the library run. */
+LSSO_API int lsso_set_wait_limit_ns(unsigned long long limit_ns);
+
 /* Floats per (sample, head) row of the training tape:
  * N*R + 3*R*R + 2*R*(D/H) + 1 (pinned by the reference's tape-size test,
  * tests/cuda/test_fast_path.py:1508-1509). */

@@ -21,6 +21,7 @@ import torch
 CONTRACT_VERSION = 8
 EXPORTED_SYMBOLS = (
     "lsso_contract_version", "lsso_compiled_sm", "lsso_check_device", "lsso_last_error", "lsso_device_status",
+    "lsso_set_wait_limit_ns",
     "lsso_tape_stride", "lsso_forward_workspace_size", "lsso_forward", "lsso_backward_workspace_size",
     "lsso_backward", "lsso_profile_start", "lsso_profile_stop", "lsso_forward_inference_noalloc",
     "lsso_linear_workspace_size", "lsso_linear", "lsso_linear_image_size", "lsso_linear_prepare",
@@ -47,6 +48,7 @@ class NativeLibrary:
             "lsso_check_device": (ci, [ci]),
             "lsso_last_error": (c.c_char_p, []),
             "lsso_device_status": (ci, [ci]),
+            "lsso_set_wait_limit_ns": (ci, [c.c_ulonglong]),
             "lsso_tape_stride": (i64, [i64, i64, i64, i64]),
             "lsso_forward_workspace_size": (sz, [i64, i64, i64, i64, i64, ci, ci]),
             "lsso_forward": (ci, [vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, sz, vp]),
@@ -559,5 +561,13 @@ def device_status(reset: bool = True) -> int:
     return library().lib.lsso_device_status(int(reset))
 
 
+def set_wait_limit_ns(limit_ns: int) -> None:
+    """Test hook: time limit of the tensor-core kernels' pipeline waits on the
+    current device (0 restores the default of one second)."""
+    lib = library()
+    lib.check(lib.lib.lsso_set_wait_limit_ns(int(limit_ns)))
+
+
 __all__ = ["CONTRACT_VERSION", "EXPORTED_SYMBOLS", "NativeLibrary", "backward", "device_status", "forward",
-           "library", "open_library", "profile_start", "profile_stop", "register", "validate_fast_inputs"]
+           "library", "open_library", "profile_start", "profile_stop", "register", "set_wait_limit_ns",
+           "validate_fast_inputs"]

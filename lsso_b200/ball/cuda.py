@@ -197,4 +197,19 @@ def device_status(reset: bool = True) -> int:
     return _native.device_status(reset)
 
 
-__all__ = ["device_status", "fast_mix", "is_available", "load", "require_available"]
+def check_device_status() -> None:
+    """Raise if a kernel of the library gave up waiting since the last check.
+
+    Synchronizes the device.  A kernel whose bounded wait ran out stops,
+    frees its resources and leaves its outputs undefined; this reports it
+    (once: the status word is reset) so that the caller can discard the
+    results of the calls made since the previous check.
+    """
+    status = _native.device_status(reset=True)
+    if status != 0:
+        raise RuntimeError(
+            f"an LSSO CUDA kernel gave up waiting (device status {status}); the outputs of the calls since the "
+            "last check are undefined")
+
+
+__all__ = ["check_device_status", "device_status", "fast_mix", "is_available", "load", "require_available"]

@@ -36,7 +36,9 @@ int cuda_fail(cudaError_t e, const char* where) {
   return fail(LSSO_ERR_CUDA, "CUDA error in %s: %s", where, cudaGetErrorString(e));
 }
 
-__device__ int g_status;
+// Per-device status word and pipeline-wait limit (lsso::DeviceControl); the
+// kernels receive the address of its first member as their `int* status`.
+__device__ lsso::DeviceControl g_control = {0, 0, lsso::kWaitLimitNs};
 
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices];
@@ -76,7 +78,7 @@ int device_info(int* device, int* sm_count, int** status) {
     cudaError_t e = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, *device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
     void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_status);
+    e = cudaGetSymbolAddress(&ptr, g_control);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
     g_sm_count[*device] = count;
     g_status_ptr[*device] = static_cast<int*>(ptr);
@@ -557,6 +559,19 @@ int lsso_device_status(int reset) {
     if (cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return -1;
   }
   return value;
+}
+
+int lsso_set_wait_limit_ns(unsigned long long limit_ns) {
+  g_last_error.clear();
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  const int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  const unsigned long long value = limit_ns == 0 ? lsso::kWaitLimitNs : limit_ns;
+  auto* control = reinterpret_cast<lsso::DeviceControl*>(status);
+  const cudaError_t e = cudaMemcpy(&control->wait_limit_ns, &value, sizeof(value), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_set_wait_limit_ns");
+  return LSSO_OK;
 }
 
 int64_t lsso_tape_stride(int64_t N, int64_t H, int64_t D, int64_t R) {

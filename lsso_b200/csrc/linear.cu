@@ -62,6 +62,11 @@ struct LinearArgs {
 __device__ __forceinline__ bool lwait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
   return mbar_wait_bounded(bar, parity, abort_flag, status);
 }
+// The same wait by a whole warp that goes on to tcgen05.ld (warp-collective):
+// its lanes agree on the outcome, so after an abort none runs a load the others skip.
+__device__ __forceinline__ bool lwait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, status));
+}
 
 __device__ __forceinline__ uint32_t half2_to_bf162(uint32_t h) {
   __half2 v = *reinterpret_cast<__half2*>(&h);
@@ -175,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   const uint32_t SB = a.stage_bytes;
   const int S = a.stages;
   uint8_t* sOut = sA + S * SB;
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], conv[kStages], tfull[2], tempty[2], bbar;
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], conv[kStages], tfull[2], tempty[2], bbar, mdrain;
   __shared__ uint32_t tmem_s;
   __shared__ int abort_flag;
   __shared__ __align__(16) float sbias[256];  // this N tile's bias (zero past Nout)
@@ -202,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       mbar_init(smem_u32(&tempty[b]), kEpiWarps);
     }
     mbar_init(smem_u32(&bbar), 1);
+    mbar_init(smem_u32(&mdrain), 1);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -235,6 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     __syncwarp();
     RingPos rp;
     bool ok = true;
+    int last_use[kStages];  // lane 0: the use of each stage whose load was issued last
+    for (int s = 0; s < kStages; ++s) last_use[s] = -1;
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int m = mstart + i * mstep;
       for (int kb = 0; kb < KB && ok; ++kb, rp.next(S)) {
@@ -246,10 +254,19 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           tma_load_2d(smem_u32(stage), &tmap_a, kb * kBK, m * kBM, smem_u32(&full[s]));
           // Streamed weight: k-block kb of this N tile (L2-resident, reused by every M tile).
           if (a.b_stream) bulk_load(smem_u32(stage + kStageBytes), bsrc + kb * b_region, b_region, smem_u32(&full[s]));
+          last_use[s] = u;
         }
         __syncwarp();
       }
     }
+    if (lane == 0) {
+      // loads still in flight (only after an abort): wait for them, bounded
+      if (!a.b_stream) mbar_wait(smem_u32(&bbar), 0, a.status);
+      for (int s = 0; s < S; ++s) {
+        if (last_use[s] >= 0) mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>(last_use[s]) & 1u, a.status);
+      }
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer
     bool ok = a.b_stream ? true : lwait(smem_u32(&bbar), 0, abort_v, a.status);
@@ -282,6 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       if (ok && lane == 0) mma_commit(smem_u32(&tfull[b]));
       __syncwarp();
     }
+    if (lane == 0) mma_drain(smem_u32(&mdrain), a.status);
+    __syncwarp();
   } else if (warp < 2 + kConvWarps) {
     // ---------------- FP16 -> BF16 rounding in shared memory
     if (a.a_fp16) {
@@ -328,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int b = i & 1, v = i >> 1;
       const int m = mstart + i * mstep;
-      ok = lwait(smem_u32(&tfull[b]), v & 1, abort_v, a.status);
+      ok = lwait_warp(smem_u32(&tfull[b]), v & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
         const int64_t row0 = static_cast<int64_t>(m) * kBM + 32 * sub;
@@ -483,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
   const uint32_t a_bytes = 2 * kWBox;                                // 128 features
   const uint32_t b_bytes = static_cast<uint32_t>(BNW / 64) * kWBox;  // BNW features
   const uint32_t stage_bytes = a_bytes + b_bytes;
-  __shared__ __align__(8) uint64_t full[kWMaxStages], empty[kWMaxStages], conv[kWMaxStages], done;
+  __shared__ __align__(8) uint64_t full[kWMaxStages], empty[kWMaxStages], conv[kWMaxStages], done, mdrain;
   __shared__ uint32_t tmem_s;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
@@ -506,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
       mbar_init(smem_u32(&conv[s]), kConvWarps);
     }
     mbar_init(smem_u32(&done), 1);
+    mbar_init(smem_u32(&mdrain), 1);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -522,6 +542,8 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
     }
     bool ok = true;
     RingPos rp;
+    int last_use[kWMaxStages];  // lane 0: the use of each stage whose load was issued last
+    for (int s = 0; s < kWMaxStages; ++s) last_use[s] = -1;
     for (int i = 0; i < nst && ok; ++i, rp.next(S)) {
       const int s = rp.s, u = rp.u;
       ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
@@ -534,9 +556,17 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
         for (int g = 0; g < BNW / 64; ++g) {
           tma_load_2d(dst + a_bytes + g * kWBox, &tmap_b, ntw * BNW + g * 64, t0, smem_u32(&full[s]));
         }
+        last_use[s] = u;
       }
       __syncwarp();
     }
+    if (lane == 0) {
+      // loads still in flight (only after an abort): wait for them, bounded
+      for (int s = 0; s < S; ++s) {
+        if (last_use[s] >= 0) mbar_wait(smem_u32(&full[s]), static_cast<uint32_t>(last_use[s]) & 1u, a.status);
+      }
+    }
+    __syncwarp();
   } else if (warp == 1) {
     bool ok = true;
     RingPos rp;
@@ -565,6 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
       } else {
         mbar_arrive(smem_u32(&done));
       }
+      mma_drain(smem_u32(&mdrain), a.status);
     }
     __syncwarp();
   } else if (warp < 2 + kConvWarps) {
@@ -615,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1) wgrad_kernel(const __grid_constan
     const int sub = warp & 3;
     const int half = (warp - (2 + kConvWarps)) >> 2;
     const int row = 32 * sub + lane;  // feature m within the tile
-    bool ok = lwait(smem_u32(&done), 0, abort_v, a.status);
+    bool ok = lwait_warp(smem_u32(&done), 0, abort_v, a.status);
     tc_fence_after();
     float* out = a.partial + (static_cast<size_t>(split) * tiles + tile) * 128 * BNW + static_cast<size_t>(row) * BNW;
     for (int c0 = 32 * half; c0 < BNW; c0 += 64) {

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(128) moments_kernel(const MomentArgs a) {
   uint8_t* xbuf = smem;
   uint8_t* rawbuf = xbuf + 2 * X_BYTES;
   uint8_t* vbuf = rawbuf + 3 * RAW_BYTES;
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[3];  // [2]: teardown drain of the MMA thread
   __shared__ uint32_t tmem_s;
 
   int64_t blk = blockIdx.x;
@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(128) moments_kernel(const MomentArgs a) {
   if (tid == 0) {
     mbar_init(smem_u32(&bars[0]), 1);
     mbar_init(smem_u32(&bars[1]), 1);
+    mbar_init(smem_u32(&bars[2]), 1);
     fence_mbar_init();
   }
   if (tid < 32) tmem_alloc(smem_u32(&tmem_s), tcols);
@@ -238,6 +239,7 @@ __global__ void __launch_bounds__(128) moments_kernel(const MomentArgs a) {
       }
     }
   }
+  if (tid == 0) mma_drain(smem_u32(&bars[2]), a.status);  // tid 0 issued the MMAs
   tc_fence_before();
   __syncthreads();
   if (tid < 32) {
@@ -526,7 +528,7 @@ __global__ void __launch_bounds__(128) readout_kernel(const ReadoutArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sA = smem;
   uint8_t* sB = smem + kTokenTile * R * 2;
-  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t bar, drain;
   __shared__ uint32_t tmem_s;
 
   int64_t blk = blockIdx.x;
@@ -545,6 +547,7 @@ __global__ void __launch_bounds__(128) readout_kernel(const ReadoutArgs a) {
 
   if (tid == 0) {
     mbar_init(smem_u32(&bar), 1);
+    mbar_init(smem_u32(&drain), 1);
     fence_mbar_init();
   }
   if (tid < 32) tmem_alloc(smem_u32(&tmem_s), tcols);
@@ -611,6 +614,7 @@ __global__ void __launch_bounds__(128) readout_kernel(const ReadoutArgs a) {
       }
     }
   }
+  if (tid == 0) mma_drain(smem_u32(&drain), a.status);  // tid 0 issued the MMAs
   tc_fence_before();
   __syncthreads();
   if (tid < 32) {
@@ -891,7 +895,7 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
   uint8_t* sAp = sBc + R * kGradChunk * 2;
   uint8_t* sBa = sAp + kTokenTile * R * 2;
   uint8_t* sB2 = sBa + R * R * 2;
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[3];  // [2]: teardown drain of the MMA thread
   __shared__ uint32_t tmem_s;
   __shared__ float red[4];
 
@@ -916,6 +920,7 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
   if (tid == 0) {
     mbar_init(smem_u32(&bars[0]), 1);
     mbar_init(smem_u32(&bars[1]), 1);
+    mbar_init(smem_u32(&bars[2]), 1);
     fence_mbar_init();
   }
   if (tid < 32) tmem_alloc(smem_u32(&tmem_s), tcols);
@@ -1081,6 +1086,7 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
     const float s = block_sum_128(stat, red);
     if (tid == 0) a.etastat[bh * a.ntiles + tile] = s;
   }
+  if (tid == 0) mma_drain(smem_u32(&bars[2]), a.status);  // tid 0 issued the MMAs
   tc_fence_before();
   __syncthreads();
   if (tid < 32) {

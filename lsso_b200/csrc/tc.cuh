@@ -23,6 +23,18 @@ enum DeviceStatus : int {
 // Time bound of a sleeping mbarrier wait: any legitimate wait inside one of
 // these kernels takes microseconds, so one second means a broken schedule.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+// The status word the kernels receive (`int* status`) is the first member of
+// this per-device block.  `wait_limit_ns` bounds the pipeline waits (the
+// waits that also watch an in-CTA abort flag); it is kWaitLimitNs unless a
+// test shortens it (lsso_set_wait_limit_ns) to make those waits run out and
+// exercise the abort path.  Drain waits of the abort path always keep
+// kWaitLimitNs.
+struct DeviceControl {
+  int status;
+  int reserved;
+  unsigned long long wait_limit_ns;
+};
 // Suspend-time hint of one sleeping try_wait: the thread wakes when the phase
 // completes or after this long, whichever comes first.
 constexpr uint32_t kSuspendHintNs = 20000u;
@@ -110,16 +122,25 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 // Bounded, sleeping wait on one phase of an mbarrier.  Gives up (returns
-// false) when *abort_flag is set by another role, or after kWaitLimitNs, in
+// false) when *abort_flag is set by another role, or after the time limit, in
 // which case it sets *abort_flag and records a timeout in the status word.
+// The limit is the control block's wait_limit_ns for a pipeline wait (one
+// with an abort flag) and kWaitLimitNs otherwise; a limit below the sleep
+// hint polls without sleeping, so it runs out as soon as the phase is late.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                                   int* status) {
   if (mbar_try_wait(bar, parity)) return true;
+  uint64_t limit = kWaitLimitNs;
+  if (abort_flag != nullptr && status != nullptr) {
+    limit = *reinterpret_cast<const volatile unsigned long long*>(&reinterpret_cast<DeviceControl*>(status)
+                                                                       ->wait_limit_ns);
+  }
+  const bool sleep = limit >= kSuspendHintNs;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
-    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (sleep ? mbar_try_wait_sleep(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if (globaltimer_ns() - t0 > limit) break;
   }
   if (abort_flag != nullptr) *abort_flag = 1;
   if (status != nullptr) atomicExch(status, kStatusMmaWaitTimeout);
@@ -267,6 +288,16 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
                : "memory");
+}
+
+// Teardown by the MMA-issuing thread: one more commit, to `bar` (an mbarrier
+// of count 1 used for nothing else), tracks every tensor-core operation this
+// thread issued; waiting on it (bounded by kWaitLimitNs) means none still
+// writes TMEM or reads shared memory when the CTA frees its TMEM and exits --
+// after an abort as much as after a normal run (then it returns at once).
+__device__ __forceinline__ void mma_drain(uint32_t bar, int* status) {
+  mma_commit(bar);
+  mbar_wait_bounded(bar, 0, nullptr, status);
 }
 
 // Warp-collective TMEM load: 32 lanes x 8 consecutive 32-bit columns.

@@ -95,6 +95,7 @@ struct TileShared {
   uint64_t tfull[4];          // MMA -> epilogue (accumulator ready)
   uint64_t tempty[4];         // epilogue -> MMA (accumulator drained)
   uint64_t lofree[2];         // moment pass: lo box free (MMA done with it)
+  uint64_t mdrain;            // teardown: the MMA thread's last commit (mma_drain)
   uint32_t tmem;
   int abort_flag;
   float red[kMaxSlots][4][4];  // per slot, head, sub-partition: complement statistic
@@ -102,6 +103,12 @@ struct TileShared {
 
 __device__ __forceinline__ bool twait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
   return mbar_wait_bounded(bar, parity, abort_flag, status);
+}
+// The same wait by a whole warp that goes on to warp-collective instructions
+// (tcgen05.ld, shuffles): its lanes agree on the outcome, so after an abort
+// none of them runs a collective the others skip.
+__device__ __forceinline__ bool twait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, status));
 }
 
 // 16-byte chunk c (features 8c .. 8c+7) of token row r in a 128B-swizzled box
@@ -125,6 +132,7 @@ __device__ __forceinline__ uint8_t* tile_setup(TileShared& sh, uint8_t* raw, int
       mbar_init(smem_u32(&sh.tempty[b]), ewarps);
     }
     for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&sh.lofree[b]), 1);
+    mbar_init(smem_u32(&sh.mdrain), 1);
     sh.abort_flag = 0;
     fence_mbar_init();
   }
@@ -136,8 +144,13 @@ __device__ __forceinline__ uint8_t* tile_setup(TileShared& sh, uint8_t* raw, int
   return raw + (((base + 1023u) & ~1023u) - base);
 }
 
-// Common epilogue: producer drains its last loads (bounded), TMEM freed.
+// Common epilogue: the MMA thread (warp 1, lane 0 in every tile kernel) waits
+// for its tensor-core operations and the producer (thread 0) for its last
+// loads, both bounded; then TMEM is freed.  Each storing role has already
+// waited for its bulk stores.  After an abort this is what keeps the CTA from
+// freeing TMEM or exiting under operations still in flight.
 __device__ __forceinline__ void tile_teardown(TileShared& sh, int slots, const int* last_use, int* status) {
+  if (threadIdx.x == 32) mma_drain(smem_u32(&sh.mdrain), status);
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -465,7 +478,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb), bp.next(a.nbuf)) {
       const int tb = bp.s, tu = bp.u;
-      ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
+      ok = twait_warp(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
         drain_moments<R, BWD>(lane_base + static_cast<uint32_t>(tb * a.cols), sub, lane, a.partial, w.b, w.g, w.m,
@@ -553,6 +566,7 @@ struct FusedShared {
   uint64_t stored[2];            // storer -> epilogue (store read the boxes)
   uint64_t xdone[2];             // epilogue -> MMA (operands ready)
   uint64_t mfull[2], mempty[2];  // moment accumulators: MMA -> drain, drain -> MMA
+  uint64_t mdrain;               // teardown: the MMA thread's last commit (mma_drain)
   uint32_t tmem;
   int abort_flag;
   __align__(16) float bias[128];  // the group's bias (relation box, value box)
@@ -660,6 +674,7 @@ __global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid
       mbar_init(smem_u32(&sh.mfull[i]), 1);
       mbar_init(smem_u32(&sh.mempty[i]), kFEWarps);
     }
+    mbar_init(smem_u32(&sh.mdrain), 1);
     sh.abort_flag = 0;
     fence_mbar_init();
   }
@@ -871,9 +886,9 @@ __global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid
         uint8_t* lo_box = slots + s * kFSlotBytes;
         uint8_t* hi_box = lo_box + kBox;
         uint8_t* val_box = lo_box + 2 * kBox;
-        ok = twait(smem_u32(&sh.pfull[s]), par, abort_v, a.status);
+        ok = twait_warp(smem_u32(&sh.pfull[s]), par, abort_v, a.status);
         tc_fence_after();
-        if (ok) ok = twait(smem_u32(&sh.sfree[s]), par ^ 1, abort_v, a.status);
+        if (ok) ok = twait_warp(smem_u32(&sh.sfree[s]), par ^ 1, abort_v, a.status);
         uint4 rel[2];
         if (ok) {
           // the relation and value features: + bias, masked rows zero, BF16; the
@@ -932,7 +947,7 @@ __global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.nchunks, a.dm, a.db)) {
       const int mb = i & 1;
-      ok = twait(smem_u32(&sh.mfull[mb]), (i >> 1) & 1, abort_v, a.status);
+      ok = twait_warp(smem_u32(&sh.mfull[mb]), (i >> 1) & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
         drain_moments<R, false>(lane_base + static_cast<uint32_t>(256 + mb * 128), sub, lane, a.partial, w.b, g, w.m,
@@ -970,6 +985,7 @@ __global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid
     __syncwarp();
   }
 
+  if (threadIdx.x == 32) mma_drain(smem_u32(&sh.mdrain), a.status);  // warp 1, lane 0 issues the MMAs
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1119,7 +1135,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
       const TileItem x = w.item();
       const int s = sp.s;
       const int tb = bp.s, tu = bp.u;
-      ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
+      ok = twait_warp(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       uint8_t* con = smem + static_cast<size_t>(s) * a.slot_bytes + a.off_val;
       if (ok) {
@@ -1319,7 +1335,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
       const int tok = x.t * kTT + r;
       // eta of this warp's first head, computed while the accumulator is still being produced
       const float eta_first = half < a.hg ? bounded_complement(a.eta_raw[x.g * a.hg + half]) : 0.0f;
-      ok = twait(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
+      ok = twait_warp(smem_u32(&sh.tfull[tb]), tu & 1, abort_v, a.status);
       tc_fence_after();
       uint8_t* slot = smem + static_cast<size_t>(s) * a.slot_bytes;
       uint8_t* con = slot + a.off_val;
