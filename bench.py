@@ -251,19 +251,19 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     fused = projection.fused_input_covers(x, args.heads, args.rank)
     ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank, fused)  # noqa: E731
-    from lsso_b200.ball.distributed import allreduce_gradients
+    from lsso_b200.ball.distributed import GradientExchange, layer_buckets
 
-    flat = torch.empty(sum(p.numel() for p in params), device=device, dtype=torch.float32)
-
-    def reduce_gradients() -> None:
-        if world > 1:
-            allreduce_gradients(params, buffer=flat)
+    # Several ranks: the gradient average runs under the backward (buckets launched on a side
+    # stream as the backward completes them) and is part of every step, captured with it.
+    exchange = GradientExchange(layer_buckets(layer)) if world > 1 else None
 
     def fwd_bwd(xx):
         # cache_enabled=False: autocast's weight-cast cache must not outlive a graph capture.
         with torch.autocast("cuda", dtype=act, cache_enabled=False):
             loss = layer(xx, mask, ids, implementation="cuda").float().square().mean()
         loss.backward()
+        if exchange is not None:
+            exchange.finish()
         return loss.detach()
 
     def clear_grads(xx) -> None:
@@ -273,9 +273,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     def train_step(xx):
         clear_grads(xx)
-        loss = fwd_bwd(xx)
-        reduce_gradients()
-        return loss
+        return fwd_bwd(xx)
 
     def fwd_step(xx):
         with torch.inference_mode(), torch.autocast("cuda", dtype=act, cache_enabled=False):
@@ -341,13 +339,12 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     eager_ms = timed(lambda: train_step(x), args.steps)
     kernels = _native.profile_stop()
 
-    # ---- device-resident fwd+bwd (the headline `value`): graph replay + eager gradient all-reduce
+    # ---- device-resident fwd+bwd (the headline `value`): graph replay (gradient exchange included)
     train_graph, _, train_grads = capture(fwd_bwd, x)
     use_grads(train_grads)
 
     def graph_train_step():
         train_graph.replay()
-        reduce_gradients()
 
     for _ in range(args.warmup):
         graph_train_step()
@@ -375,12 +372,17 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     compute = torch.cuda.current_stream(device)
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
+    # each copy bracketed by timing events on the copy stream: this rank's host->device rate
+    copy_marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
 
     def issue_copy(i: int) -> None:
         k = i % 2
         copy_stream.wait_stream(compute) if i == 0 else copy_stream.wait_event(free[k])
         with torch.cuda.stream(copy_stream), torch.no_grad():
+            copy_marks[i][0].record(copy_stream)
             bufs[k].copy_(x_host, non_blocking=True)
+            copy_marks[i][1].record(copy_stream)
             ready[k].record(copy_stream)
 
     def e2e_run() -> None:
@@ -391,14 +393,17 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             k = i % 2
             compute.wait_event(ready[k])
             graphs[k][0].replay()
-            if world > 1:
-                use_grads(graphs[k][2])
-                reduce_gradients()
             free[k].record(compute)
             loss_host[i].copy_(graphs[k][1].detach(), non_blocking=True)
 
     timed(e2e_run, 1)
     e2e_ms = timed(e2e_run, 1)
+    copy_ms = statistics.median(a.elapsed_time(b) for a, b in copy_marks)
+    h2d = torch.tensor([x_host.numel() * x_host.element_size() / (copy_ms / 1e3) / 1e9], device=device)
+    h2d_slowest, h2d_fastest = h2d.clone(), h2d.clone()
+    if world > 1:
+        dist.all_reduce(h2d_slowest, op=dist.ReduceOp.MIN)
+        dist.all_reduce(h2d_fastest, op=dist.ReduceOp.MAX)
     clocks = sampler.stop()
     status = cuda.device_status(reset=False)
     del train_graph, fwd_graph, graphs
@@ -447,6 +452,9 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             "e2e": {"value": tokens * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(), "d2h_bytes_per_step": 4,
                     "ms_per_step": e2e_ms / args.steps,
+                    "h2d_gbs_per_rank": {"slowest": float(h2d_slowest.item()), "fastest": float(h2d_fastest.item()),
+                                         "note": "median duration of each rank's x copies (copy-stream events) "
+                                                 "during the e2e run; all ranks copy at once"},
                     "note": "pinned host x -> device on a copy stream (double-buffered, overlapping the previous "
                             "step), graph-replayed fwd+bwd, loss -> pinned host, every step"},
             "roofline": roofline, "kernels": step_kernels, "cpu_baseline": cpu, "clocks": clocks,

@@ -2,9 +2,21 @@
 
 Samples are independent, so the batch shards over ranks and the forward needs
 no collective.  After the backward, every rank holds the parameter gradients
-of its shard; ``allreduce_gradients`` packs them into one flat FP32 buffer,
-runs a single ``all_reduce`` (NCCL over NVLink on B200 ranks, gloo on CPU) and
-writes the average back, matching DDP's mean over ranks.
+of its shard, and their average over ranks (DDP's mean) is what every rank
+applies.  Two ways to get it:
+
+* ``allreduce_gradients``: after the backward, pack every gradient into one
+  flat FP32 buffer, one ``all_reduce`` (NCCL over NVLink on B200 ranks, gloo
+  on CPU), write the average back.  Simple; the exchange follows the backward.
+* ``GradientExchange``: every gradient has a slot in a persistent flat
+  buffer, grouped into buckets in the order the backward produces them
+  (``layer_buckets``: the output projection and the mixer's compact
+  parameters, then the input projection).  The projection weight gradients
+  are written by the library straight into their slots, and a bucket's
+  ``all_reduce`` is launched on a side stream the moment it is complete --
+  from inside the input projection's backward, before its input-gradient
+  GEMM -- so the exchange runs under the rest of the backward.  ``finish()``
+  joins the side stream and points each ``p.grad`` at its averaged slot.
 """
 
 from __future__ import annotations
@@ -13,6 +25,8 @@ from typing import Iterable
 
 import torch
 import torch.distributed as dist
+
+from . import projection
 
 
 def allreduce_gradients(parameters: Iterable[torch.nn.Parameter], *, group=None,
@@ -51,4 +65,131 @@ def allreduce_gradients(parameters: Iterable[torch.nn.Parameter], *, group=None,
     return buffer
 
 
-__all__ = ["allreduce_gradients"]
+def layer_buckets(layer) -> list[list[torch.nn.Parameter]]:
+    """Buckets of an ``LSSO`` layer's parameters in the order its backward
+    finishes them: output projection + compact parameters, then the input
+    projection."""
+    first = [layer.w_o.weight, layer.w_o.bias, layer.core_base_raw, layer.core_drive_weight, layer.eta_raw]
+    last = [layer.w_bc.weight, layer.w_bc.bias]
+    return [[p for p in first if p is not None], [p for p in last if p is not None]]
+
+
+class GradientExchange:
+    """Gradient average over the process group, overlapped with the backward.
+
+    ``buckets``: lists of parameters, each list complete at one point of the
+    backward (``layer_buckets(layer)``, or the concatenation of several
+    layers' buckets).  Usage per step: clear the gradients (``p.grad = None``,
+    as ``optimizer.zero_grad()`` does), run the backward, call ``finish()``.
+    Works under CUDA-graph capture (the collectives are recorded with the
+    step).  With one rank it only points ``p.grad`` at the flat buffer.
+    """
+
+    def __init__(self, buckets: list[list[torch.nn.Parameter]], *, group=None, average: bool = True) -> None:
+        self.buckets = [list(b) for b in buckets if b]
+        params = [p for b in self.buckets for p in b]
+        if not params:
+            raise ValueError("GradientExchange needs at least one parameter")
+        self.group = group
+        self.average = average
+        device = params[0].device
+        self.flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=device)
+        views = self.flat.split([p.numel() for p in params])
+        self.slot = {}
+        self.bucket_of = {}
+        index = 0
+        for k, bucket in enumerate(self.buckets):
+            for p in bucket:
+                if p.dtype != torch.float32:
+                    raise TypeError("GradientExchange keeps FP32 gradients; got a parameter of " + str(p.dtype))
+                self.slot[p] = views[index].view_as(p)
+                self.bucket_of[p] = k
+                index += 1
+        self.bucket_flat = []
+        start = 0
+        for bucket in self.buckets:
+            size = sum(p.numel() for p in bucket)
+            self.bucket_flat.append(self.flat.narrow(0, start, size))
+            start += size
+        self.stream = torch.cuda.Stream(device) if device.type == "cuda" else None
+        self._ready = [set() for _ in self.buckets]
+        self._launched = [False] * len(self.buckets)
+        self._side_used = False
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_accumulated) for p in params]
+        for p in params:  # the projections write their weight and bias gradients straight into these
+            projection.register_gradient_slot(p, self.slot[p], self._on_written)
+
+    # ------------------------------------------------------------------ internals
+    def _world(self) -> int:
+        if not dist.is_available() or not dist.is_initialized():
+            return 1
+        return dist.get_world_size(self.group)
+
+    def _mark(self, p: torch.nn.Parameter) -> None:
+        k = self.bucket_of[p]
+        self._ready[k].add(p)
+        if not self._launched[k] and len(self._ready[k]) == len(self.buckets[k]):
+            self._launch(k)
+
+    def _on_written(self, p: torch.nn.Parameter) -> None:
+        """The library wrote p's gradient of this backward into its slot."""
+        self._mark(p)
+
+    def _on_accumulated(self, p: torch.nn.Parameter) -> None:
+        if p in self._ready[self.bucket_of[p]]:
+            return
+        slot = self.slot[p]
+        if p.grad is not None and p.grad.data_ptr() != slot.data_ptr():
+            slot.copy_(p.grad)
+        self._mark(p)
+
+    def _launch(self, k: int) -> None:
+        self._launched[k] = True
+        world = self._world()
+        if world == 1:
+            return
+        buf = self.bucket_flat[k]
+        if self.stream is None:
+            dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
+            if self.average:
+                buf.div_(world)
+            return
+        current = torch.cuda.current_stream(buf.device)
+        self.stream.wait_stream(current)
+        self._side_used = True
+        with torch.cuda.stream(self.stream):
+            op = dist.ReduceOp.AVG if self.average else dist.ReduceOp.SUM
+            dist.all_reduce(buf, op=op, group=self.group)
+
+    # ------------------------------------------------------------------ API
+    def finish(self) -> None:
+        """Complete the exchange of this backward: launch what is left (a
+        parameter that got no gradient contributes zeros), make the current
+        stream wait for the collectives, and set every ``p.grad`` to its
+        averaged slot."""
+        for k, bucket in enumerate(self.buckets):
+            if self._launched[k]:
+                continue
+            for p in bucket:
+                if p not in self._ready[k]:
+                    self.slot[p].zero_()
+            self._launch(k)
+        if self._side_used:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self.stream)
+        for bucket in self.buckets:
+            for p in bucket:
+                p.grad = self.slot[p]
+        self._ready = [set() for _ in self.buckets]
+        self._launched = [False] * len(self.buckets)
+        self._side_used = False
+
+    def close(self) -> None:
+        """Remove the hooks and the library's gradient slots of these parameters."""
+        for h in self._hooks:
+            h.remove()
+        for p in self.slot:
+            projection.register_gradient_slot(p, None, None)
+        self._hooks = []
+
+
+__all__ = ["GradientExchange", "allreduce_gradients", "layer_buckets"]

@@ -18,10 +18,34 @@ import ctypes
 import torch
 import torch.nn.functional as F
 from torch.autograd.function import once_differentiable
+from torch.utils.weak import WeakIdKeyDictionary
 
 from . import _native
 
 _OUT_CODES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+# Parameters whose gradient has a preassigned slot (a gradient exchange's flat
+# buffer): parameter -> (slot tensor, callback(parameter) run once written).
+# (Keyed by identity: tensors compare elementwise.)
+_GRADIENT_SLOTS = WeakIdKeyDictionary()
+
+
+def register_gradient_slot(parameter: torch.Tensor, slot: torch.Tensor | None, on_written=None) -> None:
+    """Have the projection backward write ``parameter``'s gradient into ``slot``
+    (same shape, FP32) whenever ``parameter.grad`` is None at that point, and
+    call ``on_written(parameter)`` right after -- before the input-gradient
+    GEMM, so whoever owns the slot can start exchanging it under that GEMM.
+    ``slot=None`` removes the registration."""
+    if slot is None:
+        _GRADIENT_SLOTS.pop(parameter, None)
+    else:
+        _GRADIENT_SLOTS[parameter] = (slot, on_written)
+
+
+def _slot_for(parameter: torch.Tensor | None):
+    if parameter is None or parameter.grad is not None:
+        return None
+    return _GRADIENT_SLOTS.get(parameter)
 
 
 def _pad_features(value: torch.Tensor, multiple: int = 8) -> torch.Tensor:
@@ -122,8 +146,12 @@ def linear(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, row
     return out.reshape(*lead, nout)
 
 
-def weight_gradient(g: torch.Tensor, x: torch.Tensor, row_mask: torch.Tensor | None) -> torch.Tensor:
-    """``bf16(g)^T bf16(x)`` over valid rows, FP32 ``[Nout, K]`` (native, deterministic)."""
+def weight_gradient(g: torch.Tensor, x: torch.Tensor, row_mask: torch.Tensor | None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """``bf16(g)^T bf16(x)`` over valid rows, FP32 ``[Nout, K]`` (native, deterministic).
+
+    ``out``: a contiguous FP32 ``[Nout, K]`` tensor to hold the result (written
+    by the kernel itself unless a feature width needs padding)."""
     lib = _native.library()
     nout, k = g.shape[-1], x.shape[-1]
     gf = g.reshape(-1, nout)
@@ -136,7 +164,8 @@ def weight_gradient(g: torch.Tensor, x: torch.Tensor, row_mask: torch.Tensor | N
     xf = _pad_features(xf).contiguous()
     t, np_, kp = gf.shape[0], gf.shape[1], xf.shape[1]
     mask = None if row_mask is None else row_mask.reshape(-1).contiguous().view(torch.uint8)
-    dw = torch.empty((np_, kp), dtype=torch.float32, device=g.device)
+    direct = out is not None and (np_, kp) == (nout, k) and out.is_contiguous() and out.dtype == torch.float32
+    dw = out if direct else torch.empty((np_, kp), dtype=torch.float32, device=g.device)
     with torch.cuda.device(g.device):
         size = lib.lib.lsso_linear_wgrad_workspace_size(t, np_, kp)
         if size == 0:
@@ -146,7 +175,11 @@ def weight_gradient(g: torch.Tensor, x: torch.Tensor, row_mask: torch.Tensor | N
             gf.data_ptr(), 1 if gf.dtype == torch.float16 else 0, xf.data_ptr(),
             1 if xf.dtype == torch.float16 else 0, None if mask is None else mask.data_ptr(), t, np_, kp,
             dw.data_ptr(), workspace.data_ptr(), size, torch.cuda.current_stream(g.device).cuda_stream))
-    return dw[:nout, :k] if (np_ != nout or kp != k) else dw
+    result = dw[:nout, :k] if (np_ != nout or kp != k) else dw
+    if out is not None and not direct:
+        out.copy_(result)
+        return out
+    return result
 
 
 class _ProjectionFunction(torch.autograd.Function):
@@ -162,6 +195,7 @@ class _ProjectionFunction(torch.autograd.Function):
         ctx.save_for_backward(value, weight, row_mask, image_t)
         ctx.has_bias = bias is not None
         ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
+        ctx.bias_param = bias
         return out
 
     @staticmethod
@@ -169,29 +203,46 @@ class _ProjectionFunction(torch.autograd.Function):
     def backward(ctx, grad_output):
         value, weight, row_mask, image_t = ctx.saved_tensors
         grads = _linear_vjp(grad_output, value, weight, row_mask, ctx.needs_input_grad[:3],
-                            ctx.bias_meta if ctx.has_bias else None, image_t)
+                            ctx.bias_meta if ctx.has_bias else None, image_t, ctx.bias_param)
         return (*grads, None, None, None, None)
 
 
-def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=None):
-    """(grad_value, grad_weight, grad_bias) of ``value W^T + bias`` (reference.py:170-247)."""
+def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=None, bias=None):
+    """(grad_value, grad_weight, grad_bias) of ``value W^T + bias`` (reference.py:170-247).
+
+    The weight and bias gradients come first, into their registered slots when
+    they have one (``register_gradient_slot``), whose owners are told before
+    the input-gradient GEMM runs.
+    """
     g = grad_output
     if g.dtype not in (torch.float16, torch.bfloat16):
         g = g.to(torch.bfloat16)
     g = g.contiguous()
     grad_value = grad_weight = grad_bias = None
+    written = []
     # Masked rows: the input-gradient GEMM writes them as zero and the
     # weight-gradient kernel skips them, so only the bias sum masks here.
-    if needs[0]:
-        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True, image=image_t)
     if needs[1]:
-        grad_weight = weight_gradient(g, value, row_mask)
+        wslot = _slot_for(weight)
+        grad_weight = weight_gradient(g, value, row_mask, out=None if wslot is None else wslot[0])
+        if wslot is not None:
+            written.append((weight, wslot[1]))
     if bias_meta is not None and needs[2]:
         dims = tuple(range(grad_output.ndim - 1))
         src = grad_output if row_mask is None else torch.where(row_mask[..., None], grad_output,
                                                                torch.zeros_like(grad_output))
-        total = src.sum(dim=dims, dtype=torch.float32) if dims else src.float()
-        grad_bias = total.to(device=bias_meta[1], dtype=bias_meta[0])
+        bslot = _slot_for(bias) if bias_meta[0] == torch.float32 else None
+        if bslot is not None and dims:
+            grad_bias = torch.sum(src, dim=dims, dtype=torch.float32, out=bslot[0])
+            written.append((bias, bslot[1]))
+        else:
+            total = src.sum(dim=dims, dtype=torch.float32) if dims else src.float()
+            grad_bias = total.to(device=bias_meta[1], dtype=bias_meta[0])
+    for parameter, on_written in written:
+        if on_written is not None:
+            on_written(parameter)
+    if needs[0]:
+        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True, image=image_t)
     return grad_value, grad_weight, grad_bias
 
 
@@ -212,6 +263,7 @@ class _FusedInputMix(torch.autograd.Function):
         ctx.save_for_backward(x, weight, row_mask, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
                               centered_positions, valid_counts)
         ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
+        ctx.bias_param = bias
         return mixed
 
     @staticmethod
@@ -223,7 +275,7 @@ class _FusedInputMix(torch.autograd.Function):
             grad_mixed.contiguous(), projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
             centered_positions, valid_counts)
         grad_x, grad_w, grad_b = _linear_vjp(grad_projected, x, weight, row_mask, ctx.needs_input_grad[:3],
-                                             ctx.bias_meta)
+                                             ctx.bias_meta, None, ctx.bias_param)
         return grad_x, grad_w, grad_b, None, grad_base, grad_drive, grad_eta, None, None
 
 
@@ -278,4 +330,4 @@ def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Ten
 
 
 __all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "layer_images", "linear", "output_projection",
-           "prepare_images", "weight_gradient"]
+           "prepare_images", "register_gradient_slot", "weight_gradient"]

@@ -64,6 +64,66 @@ def test_two_rank_gradient_average_matches_full_batch(tmp_path) -> None:
         assert err < 1e-6, (name, err)
 
 
+def _exchange_worker(rank: int, world: int, port: int, result_path: str) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    from lsso import LSSO, LSSOConfig
+    from lsso_b200.ball.distributed import GradientExchange, layer_buckets
+
+    torch.manual_seed(0)
+    layer = LSSO(LSSOConfig(32, 2, 16, bias=True))
+    exchange = GradientExchange(layer_buckets(layer))
+    x = torch.randn(4, 9, 32, generator=torch.Generator().manual_seed(1))
+    steps = []
+    for step in range(2):  # two steps: the slots are reused
+        for q in layer.parameters():
+            q.grad = None
+        shard = x[rank * 2:(rank + 1) * 2] * (1 + step)
+        layer(shard).square().mean().backward()
+        exchange.finish()
+        assert all(q.grad.data_ptr() == exchange.slot[q].data_ptr() for q in layer.parameters())
+        steps.append({n: q.grad.clone() for n, q in layer.named_parameters()})
+    if rank == 0:
+        torch.save(steps, result_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_gradient_exchange_matches_full_batch(tmp_path) -> None:
+    """GradientExchange (buckets exchanged as the backward completes them, each
+    p.grad a view of the averaged flat buffer) gives the full-batch gradient,
+    on two consecutive steps."""
+    path = str(tmp_path / "exchange.pt")
+    mp.spawn(_exchange_worker, args=(2, _free_port(), path), nprocs=2, join=True)
+    got = torch.load(path)
+    from lsso import LSSO, LSSOConfig
+
+    torch.manual_seed(0)
+    layer = LSSO(LSSOConfig(32, 2, 16, bias=True))
+    x = torch.randn(4, 9, 32, generator=torch.Generator().manual_seed(1))
+    for step in range(2):
+        for q in layer.parameters():
+            q.grad = None
+        xs = x * (1 + step)
+        loss = 0.5 * (layer(xs[:2]).square().mean() + layer(xs[2:]).square().mean())
+        loss.backward()
+        for name, q in layer.named_parameters():
+            err = float((got[step][name] - q.grad).norm() / q.grad.norm())
+            assert err < 1e-5, (step, name, err)
+
+
+def test_layer_buckets_cover_every_parameter_once() -> None:
+    from lsso import LSSO, LSSOConfig
+    from lsso_b200.ball.distributed import layer_buckets
+
+    for bias in (False, True):
+        layer = LSSO(LSSOConfig(32, 2, 16, bias=bias))
+        flat = [p for b in layer_buckets(layer) for p in b]
+        assert len(flat) == len(set(map(id, flat))) == len(list(layer.parameters()))
+        assert layer_buckets(layer)[-1][0] is layer.w_bc.weight  # the input projection finishes last
+
+
 def _failing_worker(rank: int, world: int, port: int, result_path: str) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -154,3 +214,23 @@ def test_sequence_parallel_positions_are_slices_of_the_whole_sequence(tmp_path) 
             assert (offset, total) == (a, length), case
             assert torch.equal(positions, full[..., a:b].contiguous()), case
             assert torch.equal(got_counts, counts), case
+
+
+def test_gradient_slot_registry_keys_by_identity() -> None:
+    """Slots are found by parameter identity (tensors compare elementwise, so an
+    equality-keyed mapping would fail on any multi-element parameter)."""
+    from lsso_b200.ball import projection
+
+    a = torch.nn.Parameter(torch.zeros(4, 4))
+    b = torch.nn.Parameter(torch.zeros(4, 4))  # equal values, another parameter
+    slot = torch.empty(4, 4)
+    projection.register_gradient_slot(a, slot, None)
+    try:
+        assert projection._slot_for(a)[0] is slot
+        assert projection._slot_for(b) is None
+        a.grad = torch.zeros(4, 4)
+        assert projection._slot_for(a) is None  # an existing gradient accumulates instead
+    finally:
+        projection.register_gradient_slot(a, None)
+    a.grad = None
+    assert projection._slot_for(a) is None
