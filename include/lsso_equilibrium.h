@@ -190,13 +190,17 @@ LSSO_API int lsso_linear(const void* a, int a_dtype, int64_t M, int64_t K, const
  *   in one kernel launch on `stream`.
  * lsso_linear_prepared: lsso_linear reading the weight from an image made by
  *   lsso_linear_prepare for the same K, Nout and orientation; no conversion
- *   kernel, no workspace.  Bit-identical to lsso_linear. */
+ *   kernel, no workspace.  Bit-identical to lsso_linear.  flags:
+ *   LSSO_LINEAR_REVERSE walks the 128-row tiles of `a` from the last to the
+ *   first (same result), so that a product can start with the rows the
+ *   kernel before it wrote or read last, which are still in L2. */
+#define LSSO_LINEAR_REVERSE 1
 LSSO_API size_t lsso_linear_image_size(int64_t K, int64_t Nout);
 LSSO_API int lsso_linear_prepare(int count, const float* const* weights, const int* weight_transposed,
                                  const int64_t* K, const int64_t* Nout, void* const* images, void* stream);
 LSSO_API int lsso_linear_prepared(const void* a, int a_dtype, int64_t M, int64_t K, const void* image,
                                   int64_t Nout, const float* bias, const uint8_t* row_mask, void* out,
-                                  int out_dtype, int64_t ldo, void* stream);
+                                  int out_dtype, int64_t ldo, int flags, void* stream);
 
 /* Workspace bytes of lsso_linear_wgrad for T tokens, Nout outputs, K inputs
  * (per-split FP32 partial tiles, enough for either operand orientation the

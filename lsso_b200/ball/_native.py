@@ -60,7 +60,7 @@ class NativeLibrary:
             "lsso_linear_image_size": (sz, [i64, i64]),
             "lsso_linear_prepare": (ci, [ci, c.POINTER(vp), c.POINTER(ci), c.POINTER(i64), c.POINTER(i64),
                                          c.POINTER(vp), vp]),
-            "lsso_linear_prepared": (ci, [vp, ci, i64, i64, vp, i64, vp, vp, vp, ci, i64, vp]),
+            "lsso_linear_prepared": (ci, [vp, ci, i64, i64, vp, i64, vp, vp, vp, ci, i64, ci, vp]),
             "lsso_linear_wgrad_workspace_size": (sz, [i64, i64, i64]),
             "lsso_linear_wgrad": (ci, [vp, ci, vp, ci, vp, i64, i64, i64, vp, vp, sz, vp]),
             "lsso_forward_inference_noalloc": (ci, [vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp]),

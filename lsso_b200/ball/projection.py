@@ -97,13 +97,16 @@ def layer_images(w_bc: torch.Tensor, w_o: torch.Tensor, backward: bool) -> dict 
 
 
 def linear(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, row_mask: torch.Tensor | None,
-           out_dtype: torch.dtype, *, weight_transposed: bool = False, image: torch.Tensor | None = None
-           ) -> torch.Tensor:
+           out_dtype: torch.dtype, *, weight_transposed: bool = False, image: torch.Tensor | None = None,
+           reverse: bool = False) -> torch.Tensor:
     """One native GEMM: ``a [.., K] (BF16/FP16) x W -> [.., Nout]`` in ``out_dtype``.
 
     ``weight`` is FP32 ``[Nout, K]`` (or ``[K, Nout]`` with ``weight_transposed``).
     ``image``: the same weight already converted by :func:`prepare_images` in
     this orientation (then no conversion kernel runs; the result is identical).
+    ``reverse`` (with ``image``): walk the rows of ``a`` from the last to the
+    first -- same result; used where the kernel before wrote ``a`` forwards,
+    so the rows it wrote last are still in L2 when this product starts.
     """
     lib = _native.library()
     lead = a.shape[:-1]
@@ -118,7 +121,7 @@ def linear(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, row
                 flat.data_ptr(), 1 if flat.dtype == torch.float16 else 0, flat.shape[0], k, image.data_ptr(), nout,
                 None if bias is None else bias.detach().float().contiguous().data_ptr(),
                 None if mask is None else mask.data_ptr(), out.data_ptr(), _OUT_CODES[out_dtype], nout,
-                torch.cuda.current_stream(a.device).cuda_stream))
+                1 if reverse else 0, torch.cuda.current_stream(a.device).cuda_stream))
         return out.reshape(*lead, nout)
     flat = a.reshape(-1, k)
     w = weight.detach().float()
@@ -188,11 +191,12 @@ class _ProjectionFunction(torch.autograd.Function):
     forward time, as the reference keeps its BF16 weight copy for the backward)."""
 
     @staticmethod
-    def forward(ctx, value, weight, bias, row_mask, out_dtype, image, image_t):
+    def forward(ctx, value, weight, bias, row_mask, out_dtype, image, image_t, reverse):
         if value.dtype not in (torch.float16, torch.bfloat16):
             value = value.to(torch.bfloat16)
-        out = linear(value, weight, bias, row_mask, out_dtype, image=image)
+        out = linear(value, weight, bias, row_mask, out_dtype, image=image, reverse=reverse)
         ctx.save_for_backward(value, weight, row_mask, image_t)
+        ctx.reverse = reverse
         ctx.has_bias = bias is not None
         ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
         ctx.bias_param = bias
@@ -203,11 +207,11 @@ class _ProjectionFunction(torch.autograd.Function):
     def backward(ctx, grad_output):
         value, weight, row_mask, image_t = ctx.saved_tensors
         grads = _linear_vjp(grad_output, value, weight, row_mask, ctx.needs_input_grad[:3],
-                            ctx.bias_meta if ctx.has_bias else None, image_t, ctx.bias_param)
-        return (*grads, None, None, None, None)
+                            ctx.bias_meta if ctx.has_bias else None, image_t, ctx.bias_param, ctx.reverse)
+        return (*grads, None, None, None, None, None)
 
 
-def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=None, bias=None):
+def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=None, bias=None, reverse=False):
     """(grad_value, grad_weight, grad_bias) of ``value W^T + bias`` (reference.py:170-247).
 
     The weight and bias gradients come first, into their registered slots when
@@ -242,7 +246,8 @@ def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=
         if on_written is not None:
             on_written(parameter)
     if needs[0]:
-        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True, image=image_t)
+        grad_value = linear(g, weight, None, row_mask, value.dtype, weight_transposed=True, image=image_t,
+                            reverse=reverse)
     return grad_value, grad_weight, grad_bias
 
 
@@ -317,7 +322,7 @@ def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor |
                      mask: torch.Tensor | None, images: dict | None = None) -> torch.Tensor:
     images = images or {}
     projected = _ProjectionFunction.apply(x, weight, bias, mask, torch.bfloat16, images.get("bc"),
-                                          images.get("bc_t"))
+                                          images.get("bc_t"), False)
     if not projected.is_contiguous():
         raise RuntimeError("implementation='cuda' requires w_bc to produce contiguous projected coordinates")
     return projected
@@ -326,7 +331,10 @@ def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor |
 def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                       dtype: torch.dtype, mask: torch.Tensor | None, images: dict | None = None) -> torch.Tensor:
     images = images or {}
-    return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype, images.get("o"), images.get("o_t"))
+    # Rows walked last to first, forward and input-gradient product alike: the
+    # readout writes `mixed` forwards, and the loss' gradient arrives written
+    # forwards too, so these products start with rows still in L2.
+    return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype, images.get("o"), images.get("o_t"), True)
 
 
 __all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "layer_images", "linear", "output_projection",

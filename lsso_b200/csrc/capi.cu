@@ -334,7 +334,7 @@ int lsso_linear_prepare(int count, const float* const* weights, const int* weigh
 }
 
 int lsso_linear_prepared(const void* a, int a_dtype, int64_t M, int64_t K, const void* image, int64_t Nout,
-                         const float* bias, const uint8_t* row_mask, void* out, int out_dtype, int64_t ldo,
+                         const float* bias, const uint8_t* row_mask, void* out, int out_dtype, int64_t ldo, int flags,
                          void* stream) {
   g_last_error.clear();
   if (a == nullptr || image == nullptr || out == nullptr) {
@@ -371,6 +371,7 @@ int lsso_linear_prepared(const void* a, int a_dtype, int64_t M, int64_t K, const
   c.out_dtype = out_dtype;
   c.prep = static_cast<uint8_t*>(const_cast<void*>(image));
   c.prepared = 1;
+  c.reverse = (flags & LSSO_LINEAR_REVERSE) != 0 ? 1 : 0;
   c.status = status;
   const cudaError_t e = lsso::launch_linear(plan, c, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lsso_linear_prepared");

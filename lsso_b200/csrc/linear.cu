@@ -55,6 +55,7 @@ struct LinearArgs {
   int b_stream;             // weight k-blocks ride in the stages instead of staying resident
   int stages;               // pipeline stages (<= kStages)
   uint32_t stage_bytes;     // A box (16 KB) [+ streamed weight k-block]
+  int rev;                  // M tiles in reverse order (start with the rows the producer wrote last)
   int* status;
 };
 
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     int last_use[kStages];  // lane 0: the use of each stage whose load was issued last
     for (int s = 0; s < kStages; ++s) last_use[s] = -1;
     for (int i = 0; i < ntile_local && ok; ++i) {
-      const int m = mstart + i * mstep;
+      const int m = a.rev ? mtiles - 1 - (mstart + i * mstep) : mstart + i * mstep;
       for (int kb = 0; kb < KB && ok; ++kb, rp.next(S)) {
         const int s = rp.s, u = rp.u;
         ok = lwait(smem_u32(&empty[s]), (u & 1) ^ 1, abort_v, a.status);
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     bool ok = true;
     for (int i = 0; i < ntile_local && ok; ++i) {
       const int b = i & 1, v = i >> 1;
-      const int m = mstart + i * mstep;
+      const int m = a.rev ? mtiles - 1 - (mstart + i * mstep) : mstart + i * mstep;
       ok = lwait_warp(smem_u32(&tfull[b]), v & 1, abort_v, a.status);
       tc_fence_after();
       if (ok) {
@@ -896,6 +897,7 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   a.BN = p.BN;
   a.NT = p.NT;
   a.a_fp16 = c.a_fp16;
+  a.rev = c.reverse;
   a.status = c.status;
   cudaError_t e = cudaSuccess;
   LaunchScope scope("linear", stream);

@@ -30,6 +30,7 @@ struct LinearCall {
   int out_dtype;            // 0 BF16, 1 FP16, 2 FP32
   uint8_t* prep;            // workspace for the prepared weight (plan.prep_bytes, 16-byte aligned)
   int prepared;             // 1: `prep` already holds this weight's image (launch_prepare_images); no prep kernel
+  int reverse;              // 1: M tiles from the last to the first
   int* status;
 };
 

@@ -75,6 +75,7 @@ struct TileArgs {
   int* status;
   int N, H, d, hg, groups, nrel, nval, ntiles, ct, nchunks, items, pos_batched, slots, nbuf, cols;
   int rel_tma;          // gradient pass: relation boxes wholly inside the group (stored by TMA)
+  int rev;              // walk the items in reverse order (ItemWalk)
   int wdg, wdm, wdb;    // the grid stride as (group, tile or chunk, sample) steps of the item walk
   int W;                // packed width
   uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
@@ -185,21 +186,36 @@ __device__ __forceinline__ TileItem decode_tile(int it, int ntiles, int groups) 
 // integer divisions run once per role, not once per tile.
 struct ItemWalk {
   int g, m, b;
-  __device__ __forceinline__ void start(int groups, int mids) {
-    const TileItem x = decode_tile(static_cast<int>(blockIdx.x), mids, groups);
+  bool rev;
+  // rev: the items in reverse (it -> items - 1 - it), so that a pass can start
+  // with the rows its producer wrote last, which are still in L2.
+  __device__ __forceinline__ void start(int groups, int mids, int reverse = 0, int items = 0) {
+    rev = reverse != 0;
+    const int it = rev ? items - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
+    const TileItem x = decode_tile(it, mids, groups);
     g = x.g;
     m = x.t;
     b = x.b;
   }
   // (dg, dm, db): gridDim.x decomposed the same way.
   __device__ __forceinline__ void next(int groups, int mids, int dg, int dm, int db) {
-    g += dg;
-    int c = g >= groups ? 1 : 0;
-    g -= c * groups;
-    m += dm + c;
-    c = m >= mids ? 1 : 0;
-    m -= c * mids;
-    b += db + c;
+    if (!rev) {
+      g += dg;
+      int c = g >= groups ? 1 : 0;
+      g -= c * groups;
+      m += dm + c;
+      c = m >= mids ? 1 : 0;
+      m -= c * mids;
+      b += db + c;
+    } else {
+      g -= dg;
+      int c = g < 0 ? 1 : 0;
+      g += c * groups;
+      m -= dm + c;
+      c = m < 0 ? 1 : 0;
+      m += c * mids;
+      b -= db + c;
+    }
   }
   __device__ __forceinline__ TileItem item() const { return TileItem{b, g, m}; }
 };
@@ -345,7 +361,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
       prefetch_tmap(&tm_val);
     }
     ItemWalk w;
-    w.start(a.groups, a.nchunks);
+    w.start(a.groups, a.nchunks, a.rev, a.items);
     RingPos sp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
@@ -376,7 +392,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_f = make_idesc(128, BWD ? 64 * a.nval : 64 + 64 * a.nval, true, true);
     ItemWalk w;
-    w.start(a.groups, a.nchunks);
+    w.start(a.groups, a.nchunks, a.rev, a.items);
     RingPos sp, bp, lp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb), bp.next(a.nbuf)) {
@@ -415,7 +431,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     const int xt = threadIdx.x - kXWarp0 * 32;
     const int total = a.nrel * kTT * 8;
     ItemWalk w;
-    w.start(a.groups, a.nchunks);
+    w.start(a.groups, a.nchunks, a.rev, a.items);
     RingPos sp, lp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
@@ -473,7 +489,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     const int sub = warp & 3;
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     ItemWalk w;
-    w.start(a.groups, a.nchunks);
+    w.start(a.groups, a.nchunks, a.rev, a.items);
     RingPos bp;
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb), bp.next(a.nbuf)) {
@@ -1054,7 +1070,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     }
     bool ok = true;
     ItemWalk w;
-    w.start(a.groups, a.ntiles);
+    w.start(a.groups, a.ntiles, a.rev, a.items);
     RingPos sp;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
       const TileItem x = w.item();
@@ -1109,7 +1125,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     const int xt = threadIdx.x - kXWarp0 * 32;
     bool ok = true;
     ItemWalk w;
-    w.start(a.groups, a.ntiles);
+    w.start(a.groups, a.ntiles, a.rev, a.items);
     RingPos sp;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
       const TileItem x = w.item();
@@ -1129,7 +1145,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
     ItemWalk w;
-    w.start(a.groups, a.ntiles);
+    w.start(a.groups, a.ntiles, a.rev, a.items);
     RingPos sp, bp;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots), bp.next(a.nbuf)) {
       const TileItem x = w.item();
@@ -1174,7 +1190,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) readout_tile_kernel(const __grid
     if (lane == 0) {
       bool ok = true;
       ItemWalk w;
-      w.start(a.groups, a.ntiles);
+      w.start(a.groups, a.ntiles, a.rev, a.items);
       RingPos sp;
       for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
         const TileItem x = w.item();
@@ -1235,7 +1251,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     }
     bool ok = true;
     ItemWalk w;
-    w.start(a.groups, a.ntiles);
+    w.start(a.groups, a.ntiles, a.rev, a.items);
     RingPos sp;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
       const TileItem x = w.item();
@@ -1306,7 +1322,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     const int xt = threadIdx.x - kXWarp0 * 32;
     bool ok = true;
     ItemWalk w;
-    w.start(a.groups, a.ntiles);
+    w.start(a.groups, a.ntiles, a.rev, a.items);
     RingPos sp;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
       const TileItem x = w.item();
@@ -1326,7 +1342,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
     bool ok = true;
     ItemWalk w;
-    w.start(a.groups, a.ntiles);
+    w.start(a.groups, a.ntiles, a.rev, a.items);
     RingPos sp, bp;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots), bp.next(a.nbuf)) {
       const TileItem x = w.item();
@@ -1415,7 +1431,7 @@ __global__ void __launch_bounds__(kThreadsS, 1) grad_tile_kernel(const __grid_co
     if (lane == 0) {
       bool ok = true;
       ItemWalk w;
-      w.start(a.groups, a.ntiles);
+      w.start(a.groups, a.ntiles, a.rev, a.items);
       RingPos sp;
       for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.ntiles, a.wdg, a.wdm, a.wdb), sp.next(a.slots)) {
         const TileItem x = w.item();
@@ -1531,6 +1547,13 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   }
   TileArgs a = base_args(p, phase16, nullptr, status);
   a.partial = partial;
+  // Traversal order (L2 reuse between consecutive passes): the forward moment
+  // pass walks the projection backwards, from the rows the input projection
+  // wrote last; the readout then walks forwards, from the rows the moment pass
+  // read last.  The backward moment pass walks forwards from the rows the
+  // output projection's input-gradient GEMM (reversed) wrote last, and the
+  // gradient pass backwards from the rows the backward moment pass read last.
+  a.rev = bwd ? 0 : 1;
   // One relation box per item: two heads at R = 32, one at R = 64, and the
   // value boxes holding those heads.  Slot: [relation box (hi in place) |
   // value boxes | the tile's FP16 phase rows]; the lo boxes, written by the
@@ -1666,6 +1689,7 @@ cudaError_t launch_readout_tiled(const Plan& p, const bf16* proj, const __half2*
   if (encode_boxes(encode, &tm_proj, proj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_out, out, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   TileArgs a = base_args(p, phase16, eta_raw, status);
+  a.rev = 0;  // forwards: the forward moment pass read the first rows last (see launch_moments_tiled)
   a.m0 = rmat;
   a.off_val = p.nrel * kBox;
   a.off_mat = (p.nrel + p.nval) * kBox;
@@ -1706,6 +1730,7 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
   if (encode_boxes(encode, &tm_dy, gout, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (encode_boxes(encode, &tm_gproj, gproj, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   TileArgs a = base_args(p, phase16, eta_raw, status);
+  a.rev = 1;  // backwards: the backward moment pass read the last rows last
   a.m0 = b1y;
   a.m1 = b1c;
   a.m2 = b1a;

@@ -136,10 +136,12 @@ def test_prepared_weight_image_is_bit_identical(m, k, nout, a_dtype, out_dtype, 
     images = prepare_images([(other, False), (w, transposed)])
     plain = linear(a, w, b, mask, out_dtype, weight_transposed=transposed)
     prepared = linear(a, w, b, mask, out_dtype, weight_transposed=transposed, image=images[1])
+    backwards = linear(a, w, b, mask, out_dtype, weight_transposed=transposed, image=images[1], reverse=True)
     other_out = linear(a, other.T.contiguous(), None, None, out_dtype, weight_transposed=True)
     other_prepared = linear(a, other, None, None, out_dtype, image=images[0]) if k == other.shape[1] else None
     torch.cuda.synchronize()
     assert torch.equal(plain, prepared)
+    assert torch.equal(plain, backwards)  # rows walked last to first: same result
     if other_prepared is not None:
         assert torch.equal(other_out, other_prepared)
 
