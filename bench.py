@@ -349,6 +349,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     for _ in range(args.warmup):
         graph_train_step()
     train_ms = timed(graph_train_step, args.steps)
+    # each graph's activations are released before the next capture (config 5 at B=256 on one GPU)
+    del train_graph
 
     fwd_eager_ms = timed(lambda: fwd_step(x), args.steps)
     with torch.inference_mode():
@@ -357,6 +359,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         for _ in range(args.warmup):
             fwd_graph.replay()
         fwd_ms = timed(fwd_graph.replay, args.steps)
+        del fwd_graph, x_inf
 
     # ---- end to end through the public API: every step copies its x from pinned
     # host memory and reads its loss back.  Two input buffers, each with its own
@@ -406,7 +409,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         dist.all_reduce(h2d_fastest, op=dist.ReduceOp.MAX)
     clocks = sampler.stop()
     status = cuda.device_status(reset=False)
-    del train_graph, fwd_graph, graphs
+    del graphs
 
     tokens = B * N * world
     value = tokens * args.steps / (train_ms / 1e3)
