@@ -56,12 +56,16 @@ def parse_args():
     ap.add_argument("--bf16", action="store_true", help="BF16 activations (default FP16)")
     ap.add_argument("--masked", action="store_true",
                     help="per-sample valid prefix ~U[L/4, L], position ids arange(valid) then zeros (config 3)")
+    ap.add_argument("--shell", type=int, default=0, metavar="DEPTH",
+                    help="time a SequenceShell of DEPTH pre-LayerNorm residual LSSO blocks on token ids from an "
+                         "embedding (vocabulary 8) instead of one layer (config 4: --shell 4 --dim 128 --heads 4 "
+                         "--rank 48 --bf16)")
     return ap.parse_args()
 
 
 def headline(args) -> bool:
-    return (args.dim, args.heads, args.rank, args.seq, args.bf16, args.masked) == (DIM, HEADS, RANK, 4096, False,
-                                                                                    False)
+    return (args.dim, args.heads, args.rank, args.seq, args.bf16, args.masked, args.shell) == (
+        DIM, HEADS, RANK, 4096, False, False, 0)
 
 
 def dist_env():
@@ -73,7 +77,19 @@ def dist_env():
 
 def workload(args, world: int) -> dict:
     name = "BASELINE config 2 (mixer bench shape)" if (args.dim, args.heads, args.rank) == (DIM, HEADS, RANK) \
-        and not (args.bf16 or args.masked) else "LSSO mixer"
+        and not (args.bf16 or args.masked or args.shell) else "LSSO mixer"
+    if args.shell:
+        return {
+            "workload": f"SequenceShell: embedding (vocabulary 8, N(0, 0.02)) + {args.shell} pre-LayerNorm residual "
+                        f"blocks x + LSSO(dim={args.dim}, heads={args.heads}, rank={args.rank})(LN(x)), token ids "
+                        f"~U[0, 8) [B={args.batch} per GPU, {args.seq}], {'BF16' if args.bf16 else 'FP16'} autocast, "
+                        "fwd+bwd with loss=y.float().square().mean()",
+            "global_batch": args.batch * world,
+            "seq_len": args.seq,
+            "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (per layer: packed projection "
+                  f"{2 * args.batch * args.seq * (args.heads * args.rank + args.dim) / 1e6:.0f} MB)",
+        }
     return {
         "workload": f"{name} at L={args.seq}: LSSO(dim={args.dim}, heads={args.heads}, "
                     f"rank={args.rank}) DYNAMIC + Rank-Rotary, x [B={args.batch} per GPU, {args.seq}, {args.dim}] "
@@ -235,12 +251,19 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     cuda.load(device=local)
     torch.manual_seed(0)
-    layer = LSSO(LSSOConfig(args.dim, args.heads, args.rank)).to(device)
-    params = list(layer.parameters())
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     B, N = args.batch, args.seq
     act = torch.bfloat16 if args.bf16 else torch.float16
-    x = torch.randn(B, N, args.dim, device=device, generator=gen).to(act).requires_grad_()
+    if args.shell:
+        from lsso_b200.ball.shell import SequenceShell
+
+        model = SequenceShell(LSSOConfig(args.dim, args.heads, args.rank), depth=args.shell, vocab=8).to(device)
+        layer = model.blocks[0].mixer
+        x = torch.randint(0, 8, (B, N), device=device, generator=gen)
+    else:
+        model = layer = LSSO(LSSOConfig(args.dim, args.heads, args.rank)).to(device)
+        x = torch.randn(B, N, args.dim, device=device, generator=gen).to(act).requires_grad_()
+    params = list(model.parameters())
     mask = ids = None
     if args.masked:
         lens = torch.randint(N // 4, N + 1, (B,), device=device, generator=gen)
@@ -255,12 +278,19 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     # Several ranks: the gradient average runs under the backward (buckets launched on a side
     # stream as the backward completes them) and is part of every step, captured with it.
-    exchange = GradientExchange(layer_buckets(layer)) if world > 1 else None
+    exchange = None
+    if world > 1:
+        exchange = GradientExchange([params] if args.shell else layer_buckets(layer))
+
+    def forward(xx):
+        if args.shell:
+            return model(xx, mask, implementation="cuda")
+        return layer(xx, mask, ids, implementation="cuda")
 
     def fwd_bwd(xx):
         # cache_enabled=False: autocast's weight-cast cache must not outlive a graph capture.
         with torch.autocast("cuda", dtype=act, cache_enabled=False):
-            loss = layer(xx, mask, ids, implementation="cuda").float().square().mean()
+            loss = forward(xx).float().square().mean()
         loss.backward()
         if exchange is not None:
             exchange.finish()
@@ -269,7 +299,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     def clear_grads(xx) -> None:
         for p in params:
             p.grad = None
-        xx.grad = None
+        if xx.is_floating_point():
+            xx.grad = None
 
     def train_step(xx):
         clear_grads(xx)
@@ -277,7 +308,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
 
     def fwd_step(xx):
         with torch.inference_mode(), torch.autocast("cuda", dtype=act, cache_enabled=False):
-            return layer(xx, mask, ids, implementation="cuda")
+            return forward(xx)
 
     def timed(fn, steps: int) -> float:
         if world > 1:
@@ -296,23 +327,23 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         return float(ms.item())
 
-    def capture(fn, xx):
+    def capture(fn, xx, train=True):
         """CUDA graph of fn(xx) (the same public-API calls, launches recorded once)."""
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(side):
             for _ in range(3):
-                if xx.requires_grad:
+                if train:
                     clear_grads(xx)
                 fn(xx)
         torch.cuda.current_stream(device).wait_stream(side)
-        if xx.requires_grad:
+        if train:
             clear_grads(xx)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             out = fn(xx)
-        # The gradients this graph writes (reduced across ranks after each replay).
-        grads = [p.grad for p in params] if xx.requires_grad else None
+        # The gradients this graph writes.
+        grads = [p.grad for p in params] if train else None
         return graph, out, grads
 
     def use_grads(grads) -> None:
@@ -340,6 +371,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     kernels = _native.profile_stop()
 
     # ---- device-resident fwd+bwd (the headline `value`): graph replay (gradient exchange included)
+    torch.cuda.empty_cache()  # the eager pass's cached blocks: a graph allocates from its own pool
     train_graph, _, train_grads = capture(fwd_bwd, x)
     use_grads(train_grads)
 
@@ -351,22 +383,24 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     train_ms = timed(graph_train_step, args.steps)
     # each graph's activations are released before the next capture (config 5 at B=256 on one GPU)
     del train_graph
+    torch.cuda.empty_cache()
 
     fwd_eager_ms = timed(lambda: fwd_step(x), args.steps)
     with torch.inference_mode():
         x_inf = x.detach().clone()
-        fwd_graph, _, _ = capture(fwd_step, x_inf)
+        fwd_graph, _, _ = capture(fwd_step, x_inf, train=False)
         for _ in range(args.warmup):
             fwd_graph.replay()
         fwd_ms = timed(fwd_graph.replay, args.steps)
         del fwd_graph, x_inf
+    torch.cuda.empty_cache()
 
     # ---- end to end through the public API: every step copies its x from pinned
     # host memory and reads its loss back.  Two input buffers, each with its own
     # graph; the copy of step i+1 runs on a copy stream while step i computes.
     x_host = x.detach().to("cpu").pin_memory()
     loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
-    bufs = [torch.empty_like(x.detach()).requires_grad_() for _ in range(2)]
+    bufs = [torch.empty_like(x.detach()).requires_grad_(x.is_floating_point()) for _ in range(2)]
     with torch.no_grad():
         for buf in bufs:
             buf.copy_(x)
@@ -438,9 +472,13 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         if world == 1:
             cpu_value, n, median = cpu_fwd_bwd_tokens_per_s(N, args.cpu_seconds, dim=args.dim, heads=args.heads,
                                                             rank=args.rank)
+            sample = (f"1 sample x {N} tokens fwd+bwd (bench shape), median of {n} steps, NumPy oracle "
+                      "(FP32 reference-path rounding) on all host threads")
+            if args.shell:
+                cpu_value /= args.shell
+                sample += f"; one layer timed, rate divided by the {args.shell} layers (LayerNorm, embedding not counted)"
             cpu = {"value": cpu_value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
-                   "sample": f"1 sample x {N} tokens fwd+bwd (bench shape), median of {n} steps, NumPy oracle "
-                             "(FP32 reference-path rounding) on all host threads"}
+                   "sample": sample}
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": train_ms / args.steps, "higher_is_better": True,
