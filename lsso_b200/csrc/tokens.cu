@@ -76,6 +76,7 @@ struct TileArgs {
   int N, H, d, hg, groups, nrel, nval, ntiles, ct, nchunks, items, pos_batched, slots, nbuf, cols;
   int rel_tma;          // gradient pass: relation boxes wholly inside the group (stored by TMA)
   int rev;              // walk the items in reverse order (ItemWalk)
+  int loring;           // moment pass: boxes in the lo ring (1 or 2)
   int wdg, wdm, wdb;    // the grid stride as (group, tile or chunk, sample) steps of the item walk
   int W;                // packed width
   uint32_t slot_bytes;  // bytes per slot (multiple of 1024)
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
       const int tb = bp.s, tu = bp.u;
       ok = twait(smem_u32(&sh.tempty[tb]), (tu & 1) ^ 1, abort_v, a.status);
       tc_fence_after();
-      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(2)) {
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(a.loring)) {
         const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.xdone[s]), u & 1, abort_v, a.status);
         tc_fence_after();
@@ -436,7 +437,7 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
     bool ok = true;
     for (int i = 0; i < nloc && ok; ++i, w.next(a.groups, a.nchunks, a.wdg, a.wdm, a.wdb)) {
       const int t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
-      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(2)) {
+      for (int tt = 0; tt < nt && ok; ++tt, sp.next(a.slots), lp.next(a.loring)) {
         const int s = sp.s, u = sp.u;
         ok = twait(smem_u32(&sh.full[s]), u & 1, abort_v, a.status);
         if (ok) ok = twait(smem_u32(&sh.lofree[lp.s]), (lp.u & 1) ^ 1, abort_v, a.status);
@@ -1563,7 +1564,16 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   a.groups = static_cast<int>(p.H / a.hg);
   a.nrel = 1;
   a.nval = static_cast<int>(ceil_div(a.hg * p.d, 64));
-  a.off_slots = 2 * kBox;
+  // lo ring: two boxes if the slots can stay as many with it, else one (one more slot in flight)
+  a.loring = 2;
+  {
+    const uint32_t slot_bytes =
+        ((1 + a.nval) * kBox + static_cast<uint32_t>(kTT * p.R * 2) + 1023u) & ~1023u;
+    const int64_t with2 = (kTileSmemBudget - 1024 - 2 * kBox) / slot_bytes;
+    const int64_t with1 = (kTileSmemBudget - 1024 - kBox) / slot_bytes;
+    if (with1 > with2 && with2 < kMaxSlots) a.loring = 1;
+  }
+  a.off_slots = a.loring * kBox;
   a.off_rel = 0;
   a.off_val = kBox;
   a.load_bytes = (1 + a.nval) * kBox;
@@ -1573,7 +1583,7 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   int grid = 0;
   a.off_ph = static_cast<uint32_t>((1 + a.nval) * kBox);
   const uint32_t slot = (a.off_ph + static_cast<uint32_t>(kTT * p.R * 2) + 1023u) & ~1023u;
-  if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid, 2 * kBox)) return cudaErrorInvalidValue;
+  if (!finish_args(a, slot, cols, items, sm_count, &smem, &grid, a.loring * kBox)) return cudaErrorInvalidValue;
   set_walk(a, grid, a.nchunks);
   const void* fn = nullptr;
   switch (p.R) {
