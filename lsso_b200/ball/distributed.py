@@ -85,13 +85,17 @@ class GradientExchange:
     step).  With one rank it only points ``p.grad`` at the flat buffer.
     """
 
-    def __init__(self, buckets: list[list[torch.nn.Parameter]], *, group=None, average: bool = True) -> None:
+    def __init__(self, buckets: list[list[torch.nn.Parameter]], *, group=None, average: bool = True,
+                 overlap: bool = True) -> None:
         self.buckets = [list(b) for b in buckets if b]
         params = [p for b in self.buckets for p in b]
         if not params:
             raise ValueError("GradientExchange needs at least one parameter")
         self.group = group
         self.average = average
+        # overlap=False: every bucket goes out in finish(), after the backward, in one collective
+        # on the current stream (no side stream competing with the backward's kernels for SMs)
+        self.overlap = overlap
         device = params[0].device
         self.flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=device)
         views = self.flat.split([p.numel() for p in params])
@@ -128,7 +132,7 @@ class GradientExchange:
     def _mark(self, p: torch.nn.Parameter) -> None:
         k = self.bucket_of[p]
         self._ready[k].add(p)
-        if not self._launched[k] and len(self._ready[k]) == len(self.buckets[k]):
+        if self.overlap and not self._launched[k] and len(self._ready[k]) == len(self.buckets[k]):
             self._launch(k)
 
     def _on_written(self, p: torch.nn.Parameter) -> None:
@@ -173,7 +177,16 @@ class GradientExchange:
             for p in bucket:
                 if p not in self._ready[k]:
                     self.slot[p].zero_()
-            self._launch(k)
+            if self.overlap:
+                self._launch(k)
+        if not self.overlap and self._world() > 1:
+            if self.stream is None:
+                dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
+                if self.average:
+                    self.flat.div_(self._world())
+            else:
+                op = dist.ReduceOp.AVG if self.average else dist.ReduceOp.SUM
+                dist.all_reduce(self.flat, op=op, group=self.group)
         if self._side_used:
             torch.cuda.current_stream(self.flat.device).wait_stream(self.stream)
         for bucket in self.buckets:

@@ -1564,15 +1564,9 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   a.groups = static_cast<int>(p.H / a.hg);
   a.nrel = 1;
   a.nval = static_cast<int>(ceil_div(a.hg * p.d, 64));
-  // lo ring: two boxes if the slots can stay as many with it, else one (one more slot in flight)
+  // lo ring of two boxes (measured: a ring of one, which leaves room for a fifth slot at r = d = 32,
+  // serialises the rotation behind the MMA: moment passes 69 / 64 -> 85 / 80 us)
   a.loring = 2;
-  {
-    const uint32_t slot_bytes =
-        ((1 + a.nval) * kBox + static_cast<uint32_t>(kTT * p.R * 2) + 1023u) & ~1023u;
-    const int64_t with2 = (kTileSmemBudget - 1024 - 2 * kBox) / slot_bytes;
-    const int64_t with1 = (kTileSmemBudget - 1024 - kBox) / slot_bytes;
-    if (with1 > with2 && with2 < kMaxSlots) a.loring = 1;
-  }
   a.off_slots = a.loring * kBox;
   a.off_rel = 0;
   a.off_val = kBox;
