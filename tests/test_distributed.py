@@ -64,7 +64,7 @@ def test_two_rank_gradient_average_matches_full_batch(tmp_path) -> None:
         assert err < 1e-6, (name, err)
 
 
-def _exchange_worker(rank: int, world: int, port: int, result_path: str) -> None:
+def _exchange_worker(rank: int, world: int, port: int, result_path: str, overlap: bool = True) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
@@ -73,7 +73,7 @@ def _exchange_worker(rank: int, world: int, port: int, result_path: str) -> None
 
     torch.manual_seed(0)
     layer = LSSO(LSSOConfig(32, 2, 16, bias=True))
-    exchange = GradientExchange(layer_buckets(layer))
+    exchange = GradientExchange(layer_buckets(layer), overlap=overlap)
     x = torch.randn(4, 9, 32, generator=torch.Generator().manual_seed(1))
     steps = []
     for step in range(2):  # two steps: the slots are reused
@@ -90,12 +90,13 @@ def _exchange_worker(rank: int, world: int, port: int, result_path: str) -> None
     dist.destroy_process_group()
 
 
-def test_two_rank_gradient_exchange_matches_full_batch(tmp_path) -> None:
-    """GradientExchange (buckets exchanged as the backward completes them, each
-    p.grad a view of the averaged flat buffer) gives the full-batch gradient,
-    on two consecutive steps."""
+@pytest.mark.parametrize("overlap", (True, False))
+def test_two_rank_gradient_exchange_matches_full_batch(tmp_path, overlap) -> None:
+    """GradientExchange (buckets exchanged as the backward completes them, or the
+    whole flat buffer after it; each p.grad a view of the averaged buffer) gives
+    the full-batch gradient, on two consecutive steps."""
     path = str(tmp_path / "exchange.pt")
-    mp.spawn(_exchange_worker, args=(2, _free_port(), path), nprocs=2, join=True)
+    mp.spawn(_exchange_worker, args=(2, _free_port(), path, overlap), nprocs=2, join=True)
     got = torch.load(path)
     from lsso import LSSO, LSSOConfig
 
