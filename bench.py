@@ -276,11 +276,18 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank, fused)  # noqa: E731
     from lsso_b200.ball.distributed import GradientExchange, layer_buckets
 
-    # Several ranks: the gradient average runs under the backward (buckets launched on a side
-    # stream as the backward completes them) and is part of every step, captured with it.
+    # Several ranks: the gradient average is part of every step, captured with it.  On one host
+    # it is the library's one-shot all-reduce kernel over NVLink peer memory after the backward;
+    # otherwise NCCL all-reduces per bucket on a side stream under the backward.
     exchange = None
+    exchange_note = None
     if world > 1:
         exchange = GradientExchange([params] if args.shell else layer_buckets(layer))
+        exchange_note = {
+            "peer": "library one-shot all-reduce kernel over NVLink peer memory (CUDA IPC regions) after the "
+                    "backward, in the step's CUDA graph",
+            "nccl": "NCCL all_reduce(AVG) per bucket on a side stream under the backward, in the step's CUDA graph",
+        }[exchange.transport]
 
     def forward(xx):
         if args.shell:
@@ -443,6 +450,10 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         dist.all_reduce(h2d_fastest, op=dist.ReduceOp.MAX)
     clocks = sampler.stop()
     status = cuda.device_status(reset=False)
+    if world > 1:
+        worst = torch.tensor([status], device=device)
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+        status = int(worst.item())
     del graphs
 
     tokens = B * N * world
@@ -484,7 +495,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             "warmup": args.warmup, "ms_per_step": train_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": value / PUBLISHED_FWD_BWD if headline(args) else None,
             "vs_baseline_note": "the reference's published fwd+bwd at N=4096 (8.99 M tokens/s, RTX 5070 Ti, one GPU)",
-            "dtype": "bf16", "data": "synthetic", "config": workload(args, world),
+            "dtype": "bf16", "data": "synthetic",
+            "config": dict(workload(args, world), **({"gradient_exchange": exchange_note} if exchange_note else {})),
             "fwd": {"value": tokens * args.steps / (fwd_ms / 1e3), "unit": "tokens/s",
                     "ms_per_step": fwd_ms / args.steps, "eager_ms_per_step": fwd_eager_ms / args.steps},
             "eager": {"value": tokens * args.steps / (eager_ms / 1e3), "unit": "tokens/s",
@@ -502,6 +514,10 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             "gpu_launches": sum(v[1] for v in kernels.values()), "device_status": status,
         }
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank's exchange kernel still reads a peer's region
+        if exchange is not None:
+            exchange.close()
         dist.barrier()
         dist.destroy_process_group()
     if line is not None:

@@ -12,8 +12,9 @@
  * Conventions
  *  - All pointers are device pointers on the current CUDA device, except
  *    where noted.  BF16 tensors are passed as void*.
- *  - The caller allocates every output and the workspace; the library never
- *    allocates device memory.  Sizes come from the *_workspace_size queries.
+ *  - The caller allocates every output and the workspace; the library
+ *    allocates no device memory except the IPC-shareable exchange region of
+ *    lsso_peer_region_create.  Sizes come from the *_workspace_size queries.
  *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
  *    legacy default stream).  Entry points do not synchronize.
  *  - Return value 0 means success.  Non-zero codes are LSSO_ERR_*; the text
@@ -62,7 +63,8 @@ LSSO_API int lsso_check_device(int device);
 LSSO_API const char* lsso_last_error(void);
 
 /* Read the kernel status word of the current device (0 = no kernel reported a
- * failure, 1 = a bounded tensor-core wait ran out).  Synchronizes the device.
+ * failure, 1 = a bounded tensor-core wait ran out, 2 = a peer rank did not reach
+ * a gradient exchange in time).  Synchronizes the device.
  * reset != 0 clears it afterwards. */
 LSSO_API int lsso_device_status(int reset);
 
@@ -301,6 +303,49 @@ LSSO_API int lsso_backward_finish(const void* grad_output, const void* projected
                                   const float* moments, float redundant, void* grad_projected,
                                   float* grad_core_base_raw, float* grad_core_drive_weight, float* grad_eta_raw,
                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Peer-memory gradient exchange (replaces the NCCL all-reduce that DDP
+ * or the reference's training loop runs over the parameter gradients after
+ * the backward; no counterpart in the reference's own code).
+ *
+ * One process per GPU, all ranks on one node with peer access (NVLink /
+ * NVSwitch).  Each rank creates one exchange region: a 512-byte header of
+ * flags (LSSO_PEER_DATA_OFFSET) followed by `count` FP32 values, the flat
+ * gradient buffer its backward writes.  The regions are shared with CUDA IPC:
+ * every rank sends its 64-byte handle to the others (any host channel, e.g.
+ * torch.distributed.all_gather_object) and opens theirs.  Then each
+ * lsso_peer_allreduce call, made by every rank in the same order, writes
+ * out[i] = scale * (sum over ranks r = 0..world-1, in that order, of region
+ * r's value i) on every rank: bit-identical results on all ranks.  The call
+ * returns at once; its kernel waits for the other ranks' kernels of the same
+ * exchange (flags in the regions, each wait bounded by wait_limit_ns, 0 = 30
+ * s).  When a peer does not come in time the status word
+ * (lsso_device_status) reads 2 and `out` is undefined.  A region's values
+ * may be rewritten once that rank's call has completed on its stream.  The
+ * call can be captured in a CUDA graph (exchanges are numbered on the
+ * device).  Regions persist across calls; counts must match on all ranks. */
+#define LSSO_PEER_HANDLE_BYTES 64
+#define LSSO_PEER_DATA_OFFSET 512
+#define LSSO_PEER_MAX_RANKS 8
+#define LSSO_PEER_DEFAULT_WAIT_NS 30000000000ull
+
+/* Bytes of one exchange region holding `count` FP32 values (header included). */
+LSSO_API size_t lsso_peer_region_bytes(int64_t count);
+/* Allocate and zero this rank's region on the current device (cudaMalloc,
+ * synchronous); `handle` receives LSSO_PEER_HANDLE_BYTES bytes to send to the
+ * peers.  The values start at (char*)*region + LSSO_PEER_DATA_OFFSET. */
+LSSO_API int lsso_peer_region_create(int64_t count, void** region, void* handle);
+/* Map another process's region from its handle (not one of this process). */
+LSSO_API int lsso_peer_region_open(const void* handle, void** region);
+/* Unmap a region opened with lsso_peer_region_open. */
+LSSO_API int lsso_peer_region_close(void* region);
+/* Free this rank's region (after every peer has closed it or stopped using it). */
+LSSO_API int lsso_peer_region_destroy(void* region);
+/* One exchange: `regions` (host array of `world` pointers) holds every
+ * rank's region as mapped in this process, this rank's own at [rank];
+ * `out` is a local 16-byte aligned [count] FP32 buffer. */
+LSSO_API int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t count, float scale, float* out,
+                                 unsigned long long wait_limit_ns, void* stream);
 
 /* Per-kernel timing (no counterpart in the reference; instrumentation only).
  * lsso_profile_start() makes every subsequent kernel launch of the library

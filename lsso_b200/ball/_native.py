@@ -28,7 +28,8 @@ EXPORTED_SYMBOLS = (
     "lsso_linear_prepared", "lsso_linear_wgrad_workspace_size", "lsso_linear_wgrad",
     "lsso_moment_elements", "lsso_forward_moments", "lsso_forward_finish", "lsso_backward_moments",
     "lsso_backward_finish", "lsso_fused_forward_supported", "lsso_fused_forward_workspace_size",
-    "lsso_fused_forward",
+    "lsso_fused_forward", "lsso_peer_region_bytes", "lsso_peer_region_create", "lsso_peer_region_open",
+    "lsso_peer_region_close", "lsso_peer_region_destroy", "lsso_peer_allreduce",
 )
 
 _LIBRARY: "NativeLibrary | None" = None
@@ -75,6 +76,12 @@ class NativeLibrary:
             "lsso_fused_forward_workspace_size": (sz, [i64, i64, i64, i64, i64, ci, ci]),
             "lsso_fused_forward": (ci, [vp, ci, vp, vp, vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp,
                                         vp, vp, vp, sz, vp]),
+            "lsso_peer_region_bytes": (sz, [i64]),
+            "lsso_peer_region_create": (ci, [i64, c.POINTER(vp), c.c_char_p]),
+            "lsso_peer_region_open": (ci, [c.c_char_p, c.POINTER(vp)]),
+            "lsso_peer_region_close": (ci, [vp]),
+            "lsso_peer_region_destroy": (ci, [vp]),
+            "lsso_peer_allreduce": (ci, [c.POINTER(vp), ci, ci, i64, c.c_float, vp, c.c_ulonglong, vp]),
             "lsso_profile_start": (ci, []),
             "lsso_profile_stop": (ci, [ci, c.c_char_p, c.POINTER(c.c_float), c.POINTER(c.c_int)]),
         }

@@ -206,6 +206,10 @@ def check_device_status() -> None:
     results of the calls made since the previous check.
     """
     status = _native.device_status(reset=True)
+    if status == 2:
+        raise RuntimeError(
+            "a peer rank did not reach the LSSO gradient exchange within its wait limit (device status 2); the "
+            "exchanged gradients since the last check are undefined")
     if status != 0:
         raise RuntimeError(
             f"an LSSO CUDA kernel gave up waiting (device status {status}); the outputs of the calls since the "

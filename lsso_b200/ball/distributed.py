@@ -17,6 +17,12 @@ applies.  Two ways to get it:
   from inside the input projection's backward, before its input-gradient
   GEMM -- so the exchange runs under the rest of the backward.  ``finish()``
   joins the side stream and points each ``p.grad`` at its averaged slot.
+
+  With ``transport="peer"`` (the default for CUDA ranks on one host, through
+  ``"auto"``) the flat buffer is the library's IPC-shared exchange region and
+  ``finish()`` launches the library's one-shot all-reduce kernel, which reads
+  every rank's buffer over NVLink and writes the average on every rank, in
+  place of NCCL.
 """
 
 from __future__ import annotations
@@ -26,7 +32,7 @@ from typing import Iterable
 import torch
 import torch.distributed as dist
 
-from . import projection
+from . import peer, projection
 
 
 def allreduce_gradients(parameters: Iterable[torch.nn.Parameter], *, group=None,
@@ -86,20 +92,46 @@ class GradientExchange:
     """
 
     def __init__(self, buckets: list[list[torch.nn.Parameter]], *, group=None, average: bool = True,
-                 overlap: bool = True) -> None:
+                 overlap: bool = True, transport: str = "auto") -> None:
         self.buckets = [list(b) for b in buckets if b]
         params = [p for b in self.buckets for p in b]
         if not params:
             raise ValueError("GradientExchange needs at least one parameter")
+        if transport not in ("auto", "peer", "nccl"):
+            raise ValueError(f"transport must be 'auto', 'peer' or 'nccl', got {transport!r}")
         self.group = group
         self.average = average
         # overlap=False: every bucket goes out in finish(), after the backward, in one collective
         # on the current stream (no side stream competing with the backward's kernels for SMs)
         self.overlap = overlap
         device = params[0].device
-        self.flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=device)
+        total = sum(p.numel() for p in params)
+        # transport: "peer" sums the ranks' buffers with the library's exchange kernel over peer
+        # memory (finish() launches it after the backward); "nccl" uses the process group's
+        # all_reduce; "auto" takes "peer" when every rank can map the others' memory.
+        self.peers = None
+        if transport != "nccl" and self._world() > 1:
+            if device.type != "cuda":
+                if transport == "peer":
+                    raise ValueError("transport='peer' needs CUDA parameters")
+            else:
+                try:
+                    self.peers = peer.PeerGroup(total, device, group=group)
+                except peer.PeerUnavailable:
+                    if transport == "peer":
+                        raise
+        self.transport = "peer" if self.peers is not None else ("nccl" if self._world() > 1 else "none")
+        if self.peers is not None:
+            self.flat = self.peers.values
+            self.flat.zero_()
+            self.averaged = torch.empty_like(self.flat)
+        else:
+            self.flat = torch.zeros(total, dtype=torch.float32, device=device)
+            self.averaged = self.flat
         views = self.flat.split([p.numel() for p in params])
+        averaged_views = self.averaged.split([p.numel() for p in params])
         self.slot = {}
+        self.result = {}
         self.bucket_of = {}
         index = 0
         for k, bucket in enumerate(self.buckets):
@@ -107,6 +139,7 @@ class GradientExchange:
                 if p.dtype != torch.float32:
                     raise TypeError("GradientExchange keeps FP32 gradients; got a parameter of " + str(p.dtype))
                 self.slot[p] = views[index].view_as(p)
+                self.result[p] = averaged_views[index].view_as(p)
                 self.bucket_of[p] = k
                 index += 1
         self.bucket_flat = []
@@ -132,7 +165,8 @@ class GradientExchange:
     def _mark(self, p: torch.nn.Parameter) -> None:
         k = self.bucket_of[p]
         self._ready[k].add(p)
-        if self.overlap and not self._launched[k] and len(self._ready[k]) == len(self.buckets[k]):
+        if (self.overlap and self.peers is None and not self._launched[k]
+                and len(self._ready[k]) == len(self.buckets[k])):
             self._launch(k)
 
     def _on_written(self, p: torch.nn.Parameter) -> None:
@@ -177,9 +211,11 @@ class GradientExchange:
             for p in bucket:
                 if p not in self._ready[k]:
                     self.slot[p].zero_()
-            if self.overlap:
+            if self.overlap and self.peers is None:
                 self._launch(k)
-        if not self.overlap and self._world() > 1:
+        if self.peers is not None:
+            self.peers.reduce(self.averaged, 1.0 / self.peers.world if self.average else 1.0)
+        elif not self.overlap and self._world() > 1:
             if self.stream is None:
                 dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
                 if self.average:
@@ -191,7 +227,7 @@ class GradientExchange:
             torch.cuda.current_stream(self.flat.device).wait_stream(self.stream)
         for bucket in self.buckets:
             for p in bucket:
-                p.grad = self.slot[p]
+                p.grad = self.result[p]
         self._ready = [set() for _ in self.buckets]
         self._launched = [False] * len(self.buckets)
         self._side_used = False
@@ -203,6 +239,8 @@ class GradientExchange:
         for p in self.slot:
             projection.register_gradient_slot(p, None, None)
         self._hooks = []
+        if self.peers is not None:
+            self.peers.close()
 
 
 __all__ = ["GradientExchange", "allreduce_gradients", "layer_buckets"]

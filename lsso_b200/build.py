@@ -19,8 +19,8 @@ ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBDIR = PACKAGE / "lib"
 LIBRARY_NAME = "lsso_equilibrium_sm100.so"
-SOURCES = ("mixer.cu", "linear.cu", "tokens.cu", "solve.cu", "capi.cu")
-HEADERS = ("mixer.h", "mixer_common.cuh", "tc.cuh", "linear.h")
+SOURCES = ("mixer.cu", "linear.cu", "tokens.cu", "solve.cu", "peer.cu", "capi.cu")
+HEADERS = ("mixer.h", "mixer_common.cuh", "tc.cuh", "linear.h", "peer.h")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

@@ -11,6 +11,7 @@
 #include "linear.h"
 #include "mixer.h"
 #include "mixer_common.cuh"
+#include "peer.h"
 
 // Fixed device scratch of lsso_forward_inference_noalloc (see below).  Host
 // code must never pass `g_noalloc_scratch` itself to a kernel: on the host it
@@ -492,6 +493,110 @@ int lsso_forward_inference_noalloc(const void* projected, const float* core_base
   fb.vec = p.vec && aligned16(projected) && aligned16(mixed);
   const cudaError_t e = lsso::launch_forward(p, fb, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lsso_forward_inference_noalloc");
+  return LSSO_OK;
+}
+
+// ---------------------------------------------------------------- peer-memory gradient exchange
+static_assert(sizeof(cudaIpcMemHandle_t) == LSSO_PEER_HANDLE_BYTES, "IPC handle size");
+static_assert(lsso::kPeerDataOffset == LSSO_PEER_DATA_OFFSET, "exchange region layout");
+static_assert(lsso::kPeerMaxRanks == LSSO_PEER_MAX_RANKS, "exchange rank limit");
+
+size_t lsso_peer_region_bytes(int64_t count) {
+  if (count < 0) return 0;
+  return lsso::kPeerDataOffset + align256(sizeof(float) * static_cast<size_t>(count));
+}
+
+int lsso_peer_region_create(int64_t count, void** region, void* handle) {
+  g_last_error.clear();
+  if (count < 0 || region == nullptr || handle == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_peer_region_create needs count >= 0 and region / handle outputs");
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  const size_t bytes = lsso_peer_region_bytes(count);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (exchange region)");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "lsso_peer_region_create");
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *region = p;
+  return LSSO_OK;
+}
+
+int lsso_peer_region_open(const void* handle, void** region) {
+  g_last_error.clear();
+  if (handle == nullptr || region == nullptr) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_peer_region_open needs a handle and a region output");
+  }
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle (peer exchange region)");
+  *region = p;
+  return LSSO_OK;
+}
+
+int lsso_peer_region_close(void* region) {
+  g_last_error.clear();
+  if (region == nullptr) return LSSO_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(region);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return LSSO_OK;
+}
+
+int lsso_peer_region_destroy(void* region) {
+  g_last_error.clear();
+  if (region == nullptr) return LSSO_OK;
+  const cudaError_t e = cudaFree(region);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree (exchange region)");
+  return LSSO_OK;
+}
+
+int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t count, float scale, float* out,
+                        unsigned long long wait_limit_ns, void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > LSSO_PEER_MAX_RANKS) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "the peer exchange supports 1 to %d ranks, got %d", LSSO_PEER_MAX_RANKS,
+                world);
+  }
+  if (rank < 0 || rank >= world) return fail(LSSO_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, world);
+  if (count < 0) return fail(LSSO_ERR_INVALID_ARGUMENT, "count must be non-negative");
+  if (regions == nullptr) return fail(LSSO_ERR_INVALID_ARGUMENT, "regions must not be NULL");
+  if (count > 0 && (out == nullptr || (reinterpret_cast<uintptr_t>(out) & 15) != 0)) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "out must be a 16-byte aligned device buffer");
+  }
+  lsso::PeerArgs a{};
+  for (int r = 0; r < world; ++r) {
+    if (regions[r] == nullptr || (reinterpret_cast<uintptr_t>(regions[r]) & 255) != 0) {
+      return fail(LSSO_ERR_INVALID_ARGUMENT, "region %d is NULL or not an exchange region", r);
+    }
+    a.region[r] = static_cast<char*>(regions[r]);
+  }
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  int rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  a.world = world;
+  a.rank = rank;
+  a.count = count;
+  a.scale = scale;
+  a.out = out;
+  a.status = status;
+  a.limit_ns = wait_limit_ns == 0 ? LSSO_PEER_DEFAULT_WAIT_NS : wait_limit_ns;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  lsso::LaunchScope scope("peer_allreduce", s);
+  const cudaError_t e = lsso::launch_peer_allreduce(a, sms, s);
+  if (e != cudaSuccess) return cuda_fail(e, "peer_allreduce_kernel");
   return LSSO_OK;
 }
 

@@ -18,6 +18,7 @@ namespace lsso {
 enum DeviceStatus : int {
   kStatusOk = 0,
   kStatusMmaWaitTimeout = 1,
+  kStatusPeerWaitTimeout = 2,  // a peer rank did not reach the gradient exchange in time
 };
 
 // Time bound of a sleeping mbarrier wait: any legitimate wait inside one of

@@ -1,6 +1,8 @@
-"""Two NCCL ranks (launched by tests/test_exchange_gpu.py): the overlapped
-GradientExchange against allreduce_gradients' single collective, eagerly and
-as CUDA-graph replays holding the collectives."""
+"""Two NCCL ranks (launched by tests/test_exchange_gpu.py): GradientExchange
+against allreduce_gradients' single collective, eagerly and as CUDA-graph
+replays holding the exchange, for both transports: NCCL collectives
+overlapped with the backward, and the library's peer-memory kernel (whose
+averages must also be bit-identical on the two ranks)."""
 
 from __future__ import annotations
 
@@ -38,35 +40,47 @@ def main() -> int:
     allreduce_gradients(params)
     reference = [q.grad.clone() for q in params]
 
-    exchange = GradientExchange(layer_buckets(layer))
     ok = True
     rel = lambda u, v: float((u - v).norm() / v.norm().clamp_min(1e-30))  # noqa: E731
-    for _ in range(2):
-        step()
-        exchange.finish()
+    for transport in ("nccl", "peer"):
+        exchange = GradientExchange(layer_buckets(layer), transport=transport)
+        ok &= exchange.transport == transport
+        for _ in range(2):
+            step()
+            exchange.finish()
+            errors = [rel(q.grad, g) for q, g in zip(params, reference)]
+            ok &= max(errors) < 1e-6
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            step()
+            exchange.finish()
+        torch.cuda.current_stream(device).wait_stream(side)
+        for q in params:
+            q.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+            exchange.finish()
+        for _ in range(3):
+            exchange.flat.zero_()
+            graph.replay()
+        torch.cuda.synchronize()
         errors = [rel(q.grad, g) for q, g in zip(params, reference)]
+        if rank == 0:
+            print(f"{transport}: graph replay errors vs one-collective average:",
+                  " ".join(f"{e:.1e}" for e in errors))
         ok &= max(errors) < 1e-6
-    side = torch.cuda.Stream(device)
-    side.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(side):
-        step()
-        exchange.finish()
-    torch.cuda.current_stream(device).wait_stream(side)
-    for q in params:
-        q.grad = None
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-        exchange.finish()
-    for _ in range(3):
-        exchange.flat.zero_()
-        graph.replay()
-    torch.cuda.synchronize()
-    errors = [rel(q.grad, g) for q, g in zip(params, reference)]
-    if rank == 0:
-        print("graph replay errors vs one-collective average:", " ".join(f"{e:.1e}" for e in errors))
-    ok &= max(errors) < 1e-6
-    del graph
+        if transport == "peer":
+            # every rank sums in rank order: the averages agree bit for bit
+            mine = torch.cat([q.grad.reshape(-1) for q in params])
+            both = [torch.empty_like(mine) for _ in range(dist.get_world_size())]
+            dist.all_gather(both, mine)
+            ok &= all(torch.equal(both[0], b) for b in both)
+            from lsso_b200.ball import _native
+            ok &= _native.device_status(reset=True) == 0
+        del graph
+        exchange.close()
     flag = torch.tensor([1 if ok else 0], device=device)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()
