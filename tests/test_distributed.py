@@ -74,6 +74,14 @@ def _exchange_worker(rank: int, world: int, port: int, result_path: str, overlap
     torch.manual_seed(0)
     layer = LSSO(LSSOConfig(32, 2, 16, bias=True))
     exchange = GradientExchange(layer_buckets(layer), overlap=overlap)
+    # CPU ranks: "auto" takes the process group's all_reduce; the peer kernel needs CUDA
+    assert exchange.transport == "nccl"
+    try:
+        GradientExchange(layer_buckets(layer), transport="peer")
+    except ValueError as exc:
+        assert "needs CUDA" in str(exc)
+    else:
+        raise AssertionError("transport='peer' accepted CPU parameters")
     x = torch.randn(4, 9, 32, generator=torch.Generator().manual_seed(1))
     steps = []
     for step in range(2):  # two steps: the slots are reused
@@ -235,3 +243,19 @@ def test_gradient_slot_registry_keys_by_identity() -> None:
         projection.register_gradient_slot(a, None)
     a.grad = None
     assert projection._slot_for(a) is None
+
+
+def test_exchange_transport_choice_without_a_process_group() -> None:
+    """One process: no exchange at all ("none"), whatever transport is asked;
+    an unknown transport name is rejected before any hook is installed."""
+    from lsso import LSSO, LSSOConfig
+    from lsso_b200.ball.distributed import GradientExchange, layer_buckets
+
+    layer = LSSO(LSSOConfig(32, 2, 16, bias=True))
+    with pytest.raises(ValueError, match="transport must be"):
+        GradientExchange(layer_buckets(layer), transport="mpi")
+    for transport in ("auto", "peer", "nccl"):
+        exchange = GradientExchange(layer_buckets(layer), transport=transport)
+        assert exchange.transport == "none"
+        assert exchange.averaged is exchange.flat
+        exchange.close()
