@@ -156,6 +156,36 @@ LSSO_API int lsso_backward(const void* grad_output, const void* projected, const
                   void* grad_projected, float* grad_core_base_raw, float* grad_core_drive_weight,
                   float* grad_eta_raw, void* workspace, size_t workspace_bytes, void* stream);
 
+/* lsso_backward plus one projection weight gradient, the output
+ * projection's dW_o = bf16(dY)^T bf16(mixed) in the LSSO layer (the
+ * reference computes it in _TensorCoreLinear.backward,
+ * lsso/ball/reference.py:229-234, before the mixer's backward of
+ * csrc/ball/binding.cpp:91-96 runs; the two are independent).  The first 21
+ * arguments are lsso_backward's, the wg_* ones lsso_linear_wgrad's (wg_dw,
+ * wg_workspace of lsso_linear_wgrad_workspace_size(wg_T, wg_Nout, wg_K)).
+ * With `concurrent` nonzero, the backward's per-(sample, head) solves, which
+ * are latency-bound and fill less than one wave, run as a persistent grid on
+ * a stream of the library's own (forked from and joined back into `stream`
+ * with events, so the call still behaves as stream-ordered on `stream` and
+ * can be captured in a CUDA graph), while the weight gradient runs on
+ * `stream`, one of its CTAs beside two solve CTAs on every SM.  The library
+ * creates that stream and its two events on the first such call on a device
+ * (make the first call before any stream capture).  Calls from several
+ * host threads share it.  When the kernels cannot share an SM (ranks above
+ * 32, a per-head kernel path) or `concurrent` is 0, the same kernels run
+ * one after the other on `stream`.  All outputs are bit-identical to
+ * lsso_backward followed by lsso_linear_wgrad. */
+LSSO_API int lsso_backward_with_wgrad(const void* grad_output, const void* projected, const float* core_base_raw,
+                                      const float* core_drive_weight, const float* eta_raw, const float* tape,
+                                      const int32_t* pivots, const float* centered_positions,
+                                      int positions_batched, const float* valid_counts, int64_t B, int64_t N,
+                                      int64_t H, int64_t D, int64_t R, void* grad_projected,
+                                      float* grad_core_base_raw, float* grad_core_drive_weight, float* grad_eta_raw,
+                                      void* workspace, size_t workspace_bytes, const void* wg_g, int wg_g_dtype,
+                                      const void* wg_x, int wg_x_dtype, const uint8_t* wg_row_mask, int64_t wg_T,
+                                      int64_t wg_Nout, int64_t wg_K, float* wg_dw, void* wg_workspace,
+                                      size_t wg_workspace_bytes, int concurrent, void* stream);
+
 /* Workspace bytes of lsso_linear (the BF16 copy of the weight in tensor-core
  * layout) for an [M, K] x [Nout, K]^T product; 0 if the shape is unsupported
  * (K must be a positive multiple of 8, at most 1024). */

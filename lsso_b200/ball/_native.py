@@ -29,7 +29,7 @@ EXPORTED_SYMBOLS = (
     "lsso_moment_elements", "lsso_forward_moments", "lsso_forward_finish", "lsso_backward_moments",
     "lsso_backward_finish", "lsso_fused_forward_supported", "lsso_fused_forward_workspace_size",
     "lsso_fused_forward", "lsso_peer_region_bytes", "lsso_peer_region_create", "lsso_peer_region_open",
-    "lsso_peer_region_close", "lsso_peer_region_destroy", "lsso_peer_allreduce",
+    "lsso_peer_region_close", "lsso_peer_region_destroy", "lsso_peer_allreduce", "lsso_backward_with_wgrad",
 )
 
 _LIBRARY: "NativeLibrary | None" = None
@@ -56,6 +56,9 @@ class NativeLibrary:
             "lsso_backward_workspace_size": (sz, [i64, i64, i64, i64, i64, ci]),
             "lsso_backward": (ci, [vp, vp, vp, vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp, vp, vp,
                                    vp, sz, vp]),
+            "lsso_backward_with_wgrad": (ci, [vp, vp, vp, vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp,
+                                              vp, vp, vp, vp, sz, vp, ci, vp, ci, vp, i64, i64, i64, vp, vp, sz,
+                                              ci, vp]),
             "lsso_linear_workspace_size": (sz, [i64, i64, i64]),
             "lsso_linear": (ci, [vp, ci, i64, i64, vp, ci, i64, vp, vp, vp, ci, i64, vp, sz, vp]),
             "lsso_linear_image_size": (sz, [i64, i64]),
@@ -271,8 +274,15 @@ def fused_forward(x, weight, bias, row_mask, core_base_raw, core_drive_weight, e
 
 
 def backward(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots, centered_positions,
-             valid_counts):
-    """Run the native backward; returns the four gradients."""
+             valid_counts, wgrad=None):
+    """Run the native backward; returns the four gradients.
+
+    ``wgrad``: optionally ``(g, x, row_mask, dw, concurrent)``, one projection
+    weight gradient ``dw = bf16(g)^T bf16(x)`` (g ``[T, Nout]``, x ``[T, K]``,
+    FP16 / BF16, contiguous; dw a contiguous FP32 ``[Nout, K]`` it writes)
+    computed in the same call (``lsso_backward_with_wgrad``): with
+    ``concurrent`` its kernels share the SMs with the backward's solves.
+    """
     lib = library()
     batch, length, heads, dim, rank = validate_fast_inputs(
         projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts)
@@ -309,11 +319,37 @@ def backward(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, 
         if size == 0:
             lib.check(1)
         workspace = torch.empty((size,), dtype=torch.uint8, device=device)
-        lib.check(lib.lib.lsso_backward(
-            _ptr(grad_output), _ptr(projected), _ptr(core_base_raw), _ptr(core_drive_weight), _ptr(eta_raw),
-            _ptr(tape), _ptr(pivots), _ptr(centered_positions), int(batched), _ptr(valid_counts), batch, length,
-            heads, dim, rank, _ptr(grad_projected), _ptr(grad_base), _ptr(grad_drive), _ptr(grad_eta),
-            _ptr(workspace), size, _stream(device)))
+        if wgrad is None:
+            lib.check(lib.lib.lsso_backward(
+                _ptr(grad_output), _ptr(projected), _ptr(core_base_raw), _ptr(core_drive_weight), _ptr(eta_raw),
+                _ptr(tape), _ptr(pivots), _ptr(centered_positions), int(batched), _ptr(valid_counts), batch,
+                length, heads, dim, rank, _ptr(grad_projected), _ptr(grad_base), _ptr(grad_drive), _ptr(grad_eta),
+                _ptr(workspace), size, _stream(device)))
+        else:
+            g, x, row_mask, dw, concurrent = wgrad
+            for name, value in (("wgrad g", g), ("wgrad x", x), ("wgrad dw", dw)):
+                _same_device(value, projected, name)
+                if not value.is_contiguous():
+                    raise RuntimeError(f"{name} must be contiguous")
+            if g.dtype not in (torch.float16, torch.bfloat16) or x.dtype not in (torch.float16, torch.bfloat16):
+                raise RuntimeError("wgrad g and x must use float16 or bfloat16")
+            if dw.dtype != torch.float32:
+                raise RuntimeError("wgrad dw must use float32")
+            tokens, nout, k = g.shape[0], g.shape[-1], x.shape[-1]
+            if g.dim() != 2 or x.dim() != 2 or x.shape[0] != tokens or tuple(dw.shape) != (nout, k):
+                raise RuntimeError("wgrad expects g [T, Nout], x [T, K] and dw [Nout, K]")
+            mask = None if row_mask is None else row_mask.reshape(-1).contiguous().view(torch.uint8)
+            wsize = lib.lib.lsso_linear_wgrad_workspace_size(tokens, nout, k)
+            if wsize == 0:
+                lib.check(1)
+            wspace = torch.empty((wsize,), dtype=torch.uint8, device=device)
+            lib.check(lib.lib.lsso_backward_with_wgrad(
+                _ptr(grad_output), _ptr(projected), _ptr(core_base_raw), _ptr(core_drive_weight), _ptr(eta_raw),
+                _ptr(tape), _ptr(pivots), _ptr(centered_positions), int(batched), _ptr(valid_counts), batch,
+                length, heads, dim, rank, _ptr(grad_projected), _ptr(grad_base), _ptr(grad_drive), _ptr(grad_eta),
+                _ptr(workspace), size, _ptr(g), 1 if g.dtype == torch.float16 else 0, _ptr(x),
+                1 if x.dtype == torch.float16 else 0, _ptr(mask), tokens, nout, k, _ptr(dw), _ptr(wspace), wsize,
+                int(bool(concurrent)), _stream(device)))
     return grad_projected, grad_base, grad_drive, grad_eta
 
 

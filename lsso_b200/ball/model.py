@@ -245,8 +245,11 @@ class LSSO(nn.Module):
                                                self.core_drive_weight, self.eta_raw, centered_positions, valid_counts)
         else:
             projected = projection.input_projection(x, self.w_bc.weight, self.w_bc.bias, mask, images)
-            mixed = cuda_backend.fast_mix(projected, self.core_base_raw, self.core_drive_weight, self.eta_raw,
-                                          centered_positions, valid_counts)
+            # the mixer and the output projection as one autograd node: its backward computes the
+            # output projection's weight gradient beside the mixer backward's solves
+            return projection.mix_output(projected, self.core_base_raw, self.core_drive_weight, self.eta_raw,
+                                         centered_positions, valid_counts, self.w_o.weight, self.w_o.bias, x.dtype,
+                                         mask, images)
         return projection.output_projection(mixed, self.w_o.weight, self.w_o.bias, x.dtype, mask, images)
 
     # ------------------------------------------------------------------ reference path

@@ -251,6 +251,110 @@ def _linear_vjp(grad_output, value, weight, row_mask, needs, bias_meta, image_t=
     return grad_value, grad_weight, grad_bias
 
 
+class _MixOutput(torch.autograd.Function):
+    """The mixer followed by the output projection, as one autograd node.
+
+    Forward: the mixer's training forward, then ``mixed W_o^T + b_o`` (the
+    same calls as ``fast_mix`` followed by :func:`output_projection`).
+    Backward: the output projection's input-gradient GEMM (d mixed), then the
+    mixer's backward and the output projection's weight gradient in ONE native
+    call (``lsso_backward_with_wgrad``).  The weight gradient does not depend
+    on the mixer's backward, so the library runs it beside the backward's
+    latency-bound per-(sample, head) solves, sharing every SM with them
+    (reference order: lsso/ball/reference.py:229-234 computes it in the output
+    projection's backward, then csrc/ball/binding.cpp:91-96 runs the mixer's).
+    Every result is bit-identical to the separate calls.
+    """
+
+    @staticmethod
+    def forward(ctx, projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts, weight,
+                bias, row_mask, out_dtype, image, image_t):
+        mixed, tape, pivots = _native.forward(projected, core_base_raw, core_drive_weight, eta_raw,
+                                              centered_positions, valid_counts, train=True)
+        out = linear(mixed, weight, bias, row_mask, out_dtype, image=image, reverse=True)
+        ctx.save_for_backward(projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots, centered_positions,
+                              valid_counts, mixed, weight, row_mask, image_t)
+        ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
+        ctx.bias_param = bias
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        (projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots, centered_positions, valid_counts, mixed,
+         weight, row_mask, image_t) = ctx.saved_tensors
+        needs = ctx.needs_input_grad
+        g = grad_output
+        if g.dtype not in (torch.float16, torch.bfloat16):
+            g = g.to(torch.bfloat16)
+        g = g.contiguous()
+        written = []
+        grad_bias = None
+        if ctx.bias_meta is not None and needs[7]:
+            dims = tuple(range(grad_output.ndim - 1))
+            src = grad_output if row_mask is None else torch.where(row_mask[..., None], grad_output,
+                                                                   torch.zeros_like(grad_output))
+            bslot = _slot_for(ctx.bias_param) if ctx.bias_meta[0] == torch.float32 else None
+            if bslot is not None and dims:
+                grad_bias = torch.sum(src, dim=dims, dtype=torch.float32, out=bslot[0])
+                written.append((ctx.bias_param, bslot[1]))
+            else:
+                total = src.sum(dim=dims, dtype=torch.float32) if dims else src.float()
+                grad_bias = total.to(device=ctx.bias_meta[1], dtype=ctx.bias_meta[0])
+        grad_weight = None
+        wgrad = None
+        if needs[6]:
+            wslot = _slot_for(weight)
+            grad_weight = wslot[0] if wslot is not None else torch.empty(weight.shape, dtype=torch.float32,
+                                                                          device=weight.device)
+            if wslot is not None:
+                written.append((weight, wslot[1]))
+            d = mixed.shape[-1]
+            wgrad = (g.reshape(-1, g.shape[-1]), mixed.reshape(-1, d), row_mask, grad_weight, CONCURRENT_WGRAD)
+        mixer_grads = (None, None, None, None)
+        if any(needs[:4]):
+            grad_mixed = linear(g, weight, None, row_mask, mixed.dtype, weight_transposed=True, image=image_t,
+                                reverse=True)
+            mixer_grads = _native.backward(grad_mixed, projected, core_base_raw, core_drive_weight, eta_raw, tape,
+                                           pivots, centered_positions, valid_counts, wgrad=wgrad)
+        elif wgrad is not None:
+            weight_gradient(g, mixed, row_mask, out=grad_weight)
+        for parameter, on_written in written:
+            if on_written is not None:
+                on_written(parameter)
+        grad_projected, grad_base, grad_drive, grad_eta = mixer_grads
+        return (grad_projected if needs[0] else None, grad_base if needs[1] else None,
+                grad_drive if needs[2] else None, grad_eta if needs[3] else None, None, None, grad_weight, grad_bias,
+                None, None, None, None)
+
+
+# The output projection's weight gradient runs beside the backward solves
+# (lsso_backward_with_wgrad with concurrent=1).  False: the same kernels one
+# after the other (identical results).
+CONCURRENT_WGRAD = True
+
+
+def mix_output(projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts, weight,
+               bias, dtype: torch.dtype, mask: torch.Tensor | None, images: dict | None = None) -> torch.Tensor:
+    """``output_projection(fast_mix(projected, ...), ...)`` as one autograd node (see :class:`_MixOutput`)."""
+    from . import cuda as cuda_backend
+
+    images = images or {}
+    if centered_positions is not None and centered_positions.requires_grad:
+        raise ValueError("the LSSO CUDA fast path does not support gradients for centered_positions")
+    if valid_counts is not None and valid_counts.requires_grad:
+        raise ValueError("the LSSO CUDA fast path does not support gradients for valid_counts")
+    cuda_backend.require_available()
+    trains = torch.is_grad_enabled() and any(
+        v is not None and v.requires_grad for v in (projected, core_base_raw, core_drive_weight, eta_raw, weight, bias))
+    if not trains:
+        mixed = cuda_backend.fast_mix(projected, core_base_raw, core_drive_weight, eta_raw, centered_positions,
+                                      valid_counts)
+        return output_projection(mixed, weight, bias, dtype, mask, images)
+    return _MixOutput.apply(projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts,
+                            weight, bias, mask, dtype, images.get("o"), images.get("o_t"))
+
+
 class _FusedInputMix(torch.autograd.Function):
     """Input projection + mixer with the projection fused into the moment pass (lsso_fused_forward).
 
@@ -337,5 +441,5 @@ def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Ten
     return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype, images.get("o"), images.get("o_t"), True)
 
 
-__all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "layer_images", "linear", "output_projection",
-           "prepare_images", "register_gradient_slot", "weight_gradient"]
+__all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "layer_images", "linear", "mix_output",
+           "output_projection", "prepare_images", "register_gradient_slot", "weight_gradient"]

@@ -394,32 +394,34 @@ size_t lsso_linear_wgrad_workspace_size(int64_t T, int64_t Nout, int64_t K) {
   return plain > swapped ? plain : swapped;
 }
 
-int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask, int64_t T,
-                      int64_t Nout, int64_t K, float* dw, void* workspace, size_t workspace_bytes, void* stream) {
-  g_last_error.clear();
+// Validation and plan of one weight gradient (lsso_linear_wgrad and
+// lsso_backward_with_wgrad; `who` names the entry point in the messages).
+static int prepare_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask, int64_t T,
+                         int64_t Nout, int64_t K, float* dw, void* workspace, size_t workspace_bytes, const char* who,
+                         lsso::WgradPlan* plan, lsso::WgradCall* call) {
   if (g == nullptr || x == nullptr || dw == nullptr || workspace == nullptr) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: a required pointer is NULL");
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "%s: a required pointer is NULL", who);
   }
   if (T <= 0 || Nout <= 0 || K <= 0 || Nout % 8 != 0 || K % 8 != 0) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: T positive, Nout and K positive multiples of 8");
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "%s: T positive, Nout and K positive multiples of 8", who);
   }
   if (T > (int64_t(1) << 31) - 1 || Nout > (int64_t(1) << 16) || K > (int64_t(1) << 16)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: shape exceeds the supported launch range");
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "%s: shape exceeds the supported launch range", who);
   }
   if ((g_dtype != 0 && g_dtype != 1) || (x_dtype != 0 && x_dtype != 1)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: dtypes must be 0 (BF16) or 1 (FP16)");
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "%s: dtypes must be 0 (BF16) or 1 (FP16)", who);
   }
   if (!aligned16(g) || !aligned16(x) || !aligned16(dw) || !aligned16(workspace)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_linear_wgrad: g, x, dw and workspace must be 16-byte aligned");
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "%s: g, x, dw and workspace must be 16-byte aligned", who);
   }
   int device = 0, sms = 0;
   int* status = nullptr;
   int rc = device_info(&device, &sms, &status);
   if (rc != LSSO_OK) return rc;
-  const lsso::WgradPlan plan = lsso::make_wgrad_plan(T, Nout, K, sms, g_dtype, x_dtype);
-  if (workspace_bytes < plan.partial_bytes) {
-    return fail(LSSO_ERR_WORKSPACE, "lsso_linear_wgrad: workspace of %zu bytes is smaller than the required %zu",
-                workspace_bytes, plan.partial_bytes);
+  *plan = lsso::make_wgrad_plan(T, Nout, K, sms, g_dtype, x_dtype);
+  if (workspace_bytes < plan->partial_bytes) {
+    return fail(LSSO_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the required %zu", who,
+                workspace_bytes, plan->partial_bytes);
   }
   lsso::WgradCall c{};
   c.g = g;
@@ -430,6 +432,18 @@ int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, co
   c.dw = dw;
   c.partial = static_cast<float*>(workspace);
   c.status = status;
+  *call = c;
+  return LSSO_OK;
+}
+
+int lsso_linear_wgrad(const void* g, int g_dtype, const void* x, int x_dtype, const uint8_t* row_mask, int64_t T,
+                      int64_t Nout, int64_t K, float* dw, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  lsso::WgradPlan plan{};
+  lsso::WgradCall c{};
+  const int rc = prepare_wgrad(g, g_dtype, x, x_dtype, row_mask, T, Nout, K, dw, workspace, workspace_bytes,
+                               "lsso_linear_wgrad", &plan, &c);
+  if (rc != LSSO_OK) return rc;
   const cudaError_t e = lsso::launch_wgrad(plan, c, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lsso_linear_wgrad");
   return LSSO_OK;
@@ -835,13 +849,15 @@ int lsso_fused_forward(const void* x, int x_dtype, const float* w_bc, const floa
   return LSSO_OK;
 }
 
-int lsso_backward(const void* grad_output, const void* projected, const float* core_base_raw,
-                  const float* core_drive_weight, const float* eta_raw, const float* tape, const int32_t* pivots,
-                  const float* centered_positions, int positions_batched, const float* valid_counts, int64_t B,
-                  int64_t N, int64_t H, int64_t D, int64_t R, void* grad_projected, float* grad_core_base_raw,
-                  float* grad_core_drive_weight, float* grad_eta_raw, void* workspace, size_t workspace_bytes,
-                  void* stream) {
-  g_last_error.clear();
+// Validation, plan and buffers of the mixer backward (lsso_backward and
+// lsso_backward_with_wgrad).
+static int prepare_backward(const void* grad_output, const void* projected, const float* core_base_raw,
+                            const float* core_drive_weight, const float* eta_raw, const float* tape,
+                            const int32_t* pivots, const float* centered_positions, int positions_batched,
+                            const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                            void* grad_projected, float* grad_core_base_raw, float* grad_core_drive_weight,
+                            float* grad_eta_raw, void* workspace, size_t workspace_bytes, lsso::Plan* plan,
+                            lsso::BackwardBuffers* buffers) {
   (void)core_base_raw;  // Theta (and with it the base) is read from the tape
   (void)pivots;         // the LU factors carry no row exchanges (one-based identity)
   (void)valid_counts;   // the tape records each sample's count
@@ -890,8 +906,90 @@ int lsso_backward(const void* grad_output, const void* projected, const float* c
   bb.etadot = reinterpret_cast<float*>(ws + l.etadot);
   bb.status = status;
   bb.vec = p.vec && aligned16(projected) && aligned16(grad_output) && aligned16(grad_projected);
+  *plan = p;
+  *buffers = bb;
+  return LSSO_OK;
+}
+
+int lsso_backward(const void* grad_output, const void* projected, const float* core_base_raw,
+                  const float* core_drive_weight, const float* eta_raw, const float* tape, const int32_t* pivots,
+                  const float* centered_positions, int positions_batched, const float* valid_counts, int64_t B,
+                  int64_t N, int64_t H, int64_t D, int64_t R, void* grad_projected, float* grad_core_base_raw,
+                  float* grad_core_drive_weight, float* grad_eta_raw, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  g_last_error.clear();
+  lsso::Plan p{};
+  lsso::BackwardBuffers bb{};
+  const int rc = prepare_backward(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
+                                  centered_positions, positions_batched, valid_counts, B, N, H, D, R,
+                                  grad_projected, grad_core_base_raw, grad_core_drive_weight, grad_eta_raw,
+                                  workspace, workspace_bytes, &p, &bb);
+  if (rc != LSSO_OK) return rc;
   const cudaError_t e = lsso::launch_backward(p, bb, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lsso_backward");
+  return LSSO_OK;
+}
+
+// The library's own side stream per device (with its fork / join events),
+// created on the first lsso_backward_with_wgrad call on that device.
+static lsso::SideStream g_side[kMaxDevices];
+
+static int side_stream(int device, lsso::SideStream* out) {
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  lsso::SideStream& s = g_side[device];
+  if (s.stream == nullptr) {
+    lsso::SideStream n{};
+    cudaError_t e = cudaStreamCreateWithFlags(&n.stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "creating the library's side stream");
+    s = n;
+  }
+  *out = s;
+  return LSSO_OK;
+}
+
+int lsso_backward_with_wgrad(const void* grad_output, const void* projected, const float* core_base_raw,
+                             const float* core_drive_weight, const float* eta_raw, const float* tape,
+                             const int32_t* pivots, const float* centered_positions, int positions_batched,
+                             const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
+                             void* grad_projected, float* grad_core_base_raw, float* grad_core_drive_weight,
+                             float* grad_eta_raw, void* workspace, size_t workspace_bytes, const void* wg_g,
+                             int wg_g_dtype, const void* wg_x, int wg_x_dtype, const uint8_t* wg_row_mask,
+                             int64_t wg_T, int64_t wg_Nout, int64_t wg_K, float* wg_dw, void* wg_workspace,
+                             size_t wg_workspace_bytes, int concurrent, void* stream) {
+  g_last_error.clear();
+  lsso::Plan p{};
+  lsso::BackwardBuffers bb{};
+  int rc = prepare_backward(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
+                            centered_positions, positions_batched, valid_counts, B, N, H, D, R, grad_projected,
+                            grad_core_base_raw, grad_core_drive_weight, grad_eta_raw, workspace, workspace_bytes,
+                            &p, &bb);
+  if (rc != LSSO_OK) return rc;
+  lsso::WgradPlan wp{};
+  lsso::WgradCall wc{};
+  rc = prepare_wgrad(wg_g, wg_g_dtype, wg_x, wg_x_dtype, wg_row_mask, wg_T, wg_Nout, wg_K, wg_dw, wg_workspace,
+                     wg_workspace_bytes, "lsso_backward_with_wgrad", &wp, &wc);
+  if (rc != LSSO_OK) return rc;
+  int device = 0, sms = 0;
+  int* status = nullptr;
+  rc = device_info(&device, &sms, &status);
+  if (rc != LSSO_OK) return rc;
+  int solve_ctas = 0;
+  lsso::SideStream side{};
+  if (concurrent) {
+    // three pipeline stages leave the shared memory for solve CTAs beside each weight-gradient CTA
+    const lsso::WgradPlan shared = lsso::make_wgrad_plan(wg_T, wg_Nout, wg_K, sms, wg_g_dtype, wg_x_dtype, 3);
+    solve_ctas = lsso::solve_ctas_beside(p, shared, device);
+    if (solve_ctas > 0) {
+      wp = shared;
+      rc = side_stream(device, &side);
+      if (rc != LSSO_OK) return rc;
+    }
+  }
+  const cudaError_t e =
+      lsso::launch_backward_with_wgrad(p, bb, wp, wc, solve_ctas, side, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lsso_backward_with_wgrad");
   return LSSO_OK;
 }
 

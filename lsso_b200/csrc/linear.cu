@@ -788,7 +788,8 @@ LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count) {
 
 bool linear_shape_supported(int64_t K) { return K % 8 == 0 && K > 0 && K <= 1024; }
 
-WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int g_fp16, int x_fp16) {
+WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int g_fp16, int x_fp16,
+                          int max_stages) {
   WgradPlan p{};
   p.T = T;
   p.Nout = Nout;
@@ -808,6 +809,7 @@ WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int 
   const size_t stage = static_cast<size_t>(2 + p.BNW / 64) * kWBox;
   p.stages = static_cast<int>((200 * 1024) / stage);
   if (p.stages > kWMaxStages) p.stages = kWMaxStages;
+  if (max_stages >= 2 && p.stages > max_stages) p.stages = max_stages;
   const int tiles = p.mtiles * p.ntilesw;
   const int sms = sm_count > 0 ? sm_count : 148;
   int splits = sms / tiles;
@@ -919,6 +921,16 @@ cudaError_t launch_linear(const LinearPlan& p, const LinearCall& c, cudaStream_t
   return cudaGetLastError();
 }
 
+CtaFootprint wgrad_footprint(const WgradPlan& p) {
+  cudaFuncAttributes fa{};
+  CtaFootprint f{};
+  if (cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(&wgrad_kernel)) != cudaSuccess) return f;
+  f.threads = kThreads;
+  f.regs = fa.numRegs;
+  f.smem = p.smem + fa.sharedSizeBytes;
+  return f;
+}
+
 cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t stream) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return cudaErrorNotSupported;
@@ -944,6 +956,12 @@ cudaError_t launch_wgrad(const WgradPlan& p, const WgradCall& c, cudaStream_t st
   a.status = c.status;
   cudaError_t e = allow_smem(reinterpret_cast<const void*>(&wgrad_kernel), p.smem);
   if (e != cudaSuccess) return e;
+  if (p.stages < kWMaxStages) {
+    // sharing its SMs with another kernel: the carveout that leaves room for both
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&wgrad_kernel),
+                             cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+  }
   {
     LaunchScope scope("wgrad", stream);
     launch_pdl(wgrad_kernel, p.grid, kThreads, p.smem, stream, ma, mb, a);

@@ -64,11 +64,23 @@ struct WgradCall {
   int* status;
 };
 
+// What one CTA of a kernel holds on its SM (for kernels meant to share SMs).
+struct CtaFootprint {
+  int threads = 0;
+  int regs = 0;     // per thread, as compiled
+  size_t smem = 0;  // dynamic + static bytes (the per-CTA reservation not included)
+};
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (null if unavailable).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
-WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int g_fp16, int x_fp16);
+// max_stages (<= 4): fewer pipeline stages leave shared memory for a kernel
+// that runs beside this one (the split over tokens, hence the partials and
+// the result, do not depend on it).
+WgradPlan make_wgrad_plan(int64_t T, int64_t Nout, int64_t K, int sm_count, int g_fp16, int x_fp16,
+                          int max_stages = 4);
 cudaError_t launch_wgrad(const WgradPlan& plan, const WgradCall& call, cudaStream_t stream);
+CtaFootprint wgrad_footprint(const WgradPlan& plan);
 
 LinearPlan make_linear_plan(int64_t M, int64_t K, int64_t Nout, int sm_count);
 bool linear_shape_supported(int64_t K);

@@ -1389,10 +1389,8 @@ static cudaError_t backward_moments_r(const Plan& p, const BackwardBuffers& bb, 
 // Backward solves (over `nchunks` partials per (b, h)), the gradient pass and
 // the parameter reduction; the phase tables are already in bb.
 template <int R>
-static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, const float* partial, int64_t nchunks,
-                                     float redundant, cudaStream_t stream) {
-  cudaError_t e = cudaSuccess;
-  const int pos_batched = p.pos_rows > 1 ? 1 : 0;
+static SolveBwdArgs solve_backward_args(const Plan& p, const BackwardBuffers& bb, const float* partial,
+                                        int64_t nchunks) {
   SolveBwdArgs s{};
   s.partial = partial;
   s.tape = bb.tape;
@@ -1415,6 +1413,16 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
   s.dt = static_cast<int>(p.dt);
   s.ndt = static_cast<int>(p.ndt);
   s.nchunks = static_cast<int>(nchunks);
+  return s;
+}
+
+// The backward solves: per (b, h) adjoint solves, parameter-gradient partials
+// and the gradient pass's operand matrices.
+template <int R>
+static cudaError_t backward_solve_r(const Plan& p, const BackwardBuffers& bb, const float* partial, int64_t nchunks,
+                                    cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
+  const SolveBwdArgs s = solve_backward_args<R>(p, bb, partial, nchunks);
   if (warp_solves_usable(p)) {
     e = launch_solve_backward_warp(p, s, stream);
   } else {
@@ -1425,8 +1433,14 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
     launch_pdl(solve_backward_kernel<R>, static_cast<unsigned>(p.BH), kSolveThreads, ssm, stream, s);
     e = cudaGetLastError();
   }
-  if (e != cudaSuccess) return e;
+  return e;
+}
 
+// The gradient pass and the parameter reduction (after the backward solves).
+template <int R>
+static cudaError_t backward_grads_r(const Plan& p, const BackwardBuffers& bb, float redundant, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
+  const int pos_batched = p.pos_rows > 1 ? 1 : 0;
   GradArgs g{};
   g.gout = bb.grad_output;
   g.proj = bb.projected;
@@ -1492,11 +1506,47 @@ static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, c
   return cudaGetLastError();
 }
 
+// Backward solves (over `nchunks` partials per (b, h)), the gradient pass and
+// the parameter reduction; the phase tables are already in bb.
+template <int R>
+static cudaError_t backward_finish_r(const Plan& p, const BackwardBuffers& bb, const float* partial, int64_t nchunks,
+                                     float redundant, cudaStream_t stream) {
+  const cudaError_t e = backward_solve_r<R>(p, bb, partial, nchunks, stream);
+  if (e != cudaSuccess) return e;
+  return backward_grads_r<R>(p, bb, redundant, stream);
+}
+
 template <int R>
 static cudaError_t backward_r(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream) {
   const cudaError_t e = backward_moments_r<R>(p, bb, stream);
   if (e != cudaSuccess) return e;
   return backward_finish_r<R>(p, bb, bb.partial, p.nchunks, 1.0f, stream);
+}
+
+template <int R>
+static cudaError_t backward_with_wgrad_r(const Plan& p, const BackwardBuffers& bb, const WgradPlan& wp,
+                                         const WgradCall& wc, int solve_ctas, const SideStream& side,
+                                         cudaStream_t stream) {
+  cudaError_t e = backward_moments_r<R>(p, bb, stream);
+  if (e != cudaSuccess) return e;
+  if (solve_ctas <= 0) {
+    e = backward_solve_r<R>(p, bb, bb.partial, p.nchunks, stream);
+    if (e == cudaSuccess) e = launch_wgrad(wp, wc, stream);
+    if (e != cudaSuccess) return e;
+    return backward_grads_r<R>(p, bb, 1.0f, stream);
+  }
+  // fork: the solves on the side stream, the weight gradient on this one; join before the gradient pass
+  e = cudaEventRecord(side.fork, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(side.stream, side.fork, 0);
+  if (e != cudaSuccess) return e;
+  const SolveBwdArgs s = solve_backward_args<R>(p, bb, bb.partial, p.nchunks);
+  e = launch_solve_backward_persistent(p, s, solve_ctas * p.sms, side.stream);
+  if (e == cudaSuccess) e = cudaEventRecord(side.join, side.stream);
+  if (e != cudaSuccess) return e;
+  e = launch_wgrad(wp, wc, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, side.join, 0);
+  if (e != cudaSuccess) return e;
+  return backward_grads_r<R>(p, bb, 1.0f, stream);
 }
 
 // Sum of the chunk partials of every (b, h): out[bh][e] = sum_ch partial[bh][ch][e]
@@ -1600,6 +1650,41 @@ cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t
     case 32: return forward_r<32>(p, fb, stream);
     case 48: return forward_r<48>(p, fb, stream);
     case 64: return forward_r<64>(p, fb, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int solve_ctas_beside(const Plan& p, const WgradPlan& wp, int device) {
+  if (!warp_solves_usable(p) || !p.tiled) return 0;
+  const CtaFootprint fs = solve_backward_footprint(p);
+  const CtaFootprint fw = wgrad_footprint(wp);
+  if (fs.threads == 0 || fw.threads == 0) return 0;
+  int regs = 0, smem = 0, reserved = 0, threads = 0;
+  if (cudaDeviceGetAttribute(&regs, cudaDevAttrMaxRegistersPerMultiprocessor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&threads, cudaDevAttrMaxThreadsPerMultiProcessor, device) != cudaSuccess) {
+    return 0;
+  }
+  // registers are allocated per warp in units of 256
+  auto cta_regs = [](const CtaFootprint& f) { return (f.regs * 32 + 255) / 256 * 256 * (f.threads / 32); };
+  for (int k = 2; k >= 1; --k) {
+    const bool fit = cta_regs(fw) + k * cta_regs(fs) <= regs &&
+                     fw.smem + reserved + k * (fs.smem + reserved) <= static_cast<size_t>(smem) &&
+                     fw.threads + k * fs.threads <= threads;
+    if (fit) return k;
+  }
+  return 0;
+}
+
+cudaError_t launch_backward_with_wgrad(const Plan& p, const BackwardBuffers& bb, const WgradPlan& wp,
+                                       const WgradCall& wc, int solve_ctas, const SideStream& side,
+                                       cudaStream_t stream) {
+  switch (p.R) {
+    case 16: return backward_with_wgrad_r<16>(p, bb, wp, wc, solve_ctas, side, stream);
+    case 32: return backward_with_wgrad_r<32>(p, bb, wp, wc, solve_ctas, side, stream);
+    case 48: return backward_with_wgrad_r<48>(p, bb, wp, wc, solve_ctas, side, stream);
+    case 64: return backward_with_wgrad_r<64>(p, bb, wp, wc, solve_ctas, side, stream);
     default: return cudaErrorInvalidValue;
   }
 }

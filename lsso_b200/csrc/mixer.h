@@ -8,6 +8,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "linear.h"
+
 namespace lsso {
 
 struct Plan;
@@ -202,9 +204,32 @@ cudaError_t launch_forward_fused(const Plan& p, const ForwardBuffers& fb, const 
 bool warp_solves_usable(const Plan& p);
 cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cudaStream_t stream);
 cudaError_t launch_solve_backward_warp(const Plan& p, const SolveBwdArgs& s, cudaStream_t stream);
+// The backward warp solve as a persistent grid of `grid` CTAs (each takes
+// systems blockIdx.x, + grid, ...), and what one of its CTAs holds on an SM.
+cudaError_t launch_solve_backward_persistent(const Plan& p, const SolveBwdArgs& s, int grid, cudaStream_t stream);
+CtaFootprint solve_backward_footprint(const Plan& p);
 
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream);
 cudaError_t launch_backward(const Plan& p, const BackwardBuffers& bb, cudaStream_t stream);
+
+// The backward with one projection weight gradient beside it.  The weight
+// gradient does not depend on the mixer's backward, and the backward solves
+// (latency-bound, less than one wave) leave most of each SM idle: after the
+// moment pass, the solves run as a persistent grid on `side` (forked from and
+// joined back into `stream` with the two events) while the weight gradient
+// runs on `stream`, its CTA and `solve_ctas` solve CTAs on every SM at once;
+// then the gradient pass and the parameter reduction.  solve_ctas = 0 runs
+// the same kernels one after the other on `stream`.  Results are identical
+// either way.
+struct SideStream {
+  cudaStream_t stream;
+  cudaEvent_t fork, join;
+};
+cudaError_t launch_backward_with_wgrad(const Plan& p, const BackwardBuffers& bb, const WgradPlan& wp,
+                                       const WgradCall& wc, int solve_ctas, const SideStream& side,
+                                       cudaStream_t stream);
+// Solve CTAs per SM that fit beside one CTA of the weight gradient (0: none).
+int solve_ctas_beside(const Plan& p, const WgradPlan& wp, int device);
 
 // Sequence-parallel halves.  The moment halves run the phase table and the
 // token moment pass over this rank's tokens and sum the chunk partials into

@@ -586,14 +586,23 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
 //   dZ = lam - (1+eta) D + dTheta W^T/sqrt(n), E = M' D^T + dZ Z^T,
 //   R_d = L^{-T} M'/sqrt(n), R_z = L^{-T} dZ/sqrt(n), Q = L^{-T} Psi L^{-1}/n.
 // ============================================================================
+// One CTA per system, or (systems > gridDim.x) a persistent grid whose CTAs
+// take systems blockIdx.x, blockIdx.x + gridDim.x, ...: the form that runs
+// beside a weight-gradient GEMM, two CTAs per SM next to its CTA (at R <= 32
+// the register cap of five CTAs per SM, 48 per thread, is what lets the three
+// share an SM's register file).
 template <int R>
-__global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const SolveBwdArgs a) {
+__global__ void __launch_bounds__(kWThreads, R <= 32 ? 5 : 4)
+    solve_backward_warp_kernel(const SolveBwdArgs a, int64_t systems) {
   pdl_wait();
   constexpr int LD = R + 1;
   constexpr int P = rows_per_lane<R>();
   extern __shared__ __align__(16) float fsm[];
   const int d = a.d;
   const int XLD = d + 1;
+  __shared__ float red[kWWarps];
+  const int tid = threadIdx.x, lane = tid & 31;
+  for (int64_t bh = blockIdx.x; bh < systems; bh += gridDim.x) {
   float* L = fsm;               // [R][LD] L, then L^{-1}
   float* Mm = L + R * LD;       // [R][LD] packed LU, then L^{-1}; after pass A dTheta, then E, then Psi L^{-1}
   float* Th = Mm + R * LD;      // [R][LD]
@@ -609,9 +618,6 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   float* Ws = uinv + R;         // [d][R + 1] W_drive of this head
   float* Li = L;                // L^{-1} replaces L (computed in Mm, then copied)
   float* Mi = dK;               // M^{-1} until pass A is done
-  __shared__ float red[kWWarps];
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int64_t bh = blockIdx.x;
   const int h = static_cast<int>(bh % a.H);
   const TapeLayout tl = tape_layout(a.N, R, d);
   const float* tape = a.tape + bh * a.tape_stride;
@@ -808,6 +814,8 @@ __global__ void __launch_bounds__(kWThreads) solve_backward_warp_kernel(const So
   }
   const float s = block_sum(dz_dot, red);
   if (tid == 0) a.etadot[bh] = s;
+  __syncthreads();  // the next system overwrites this one's shared memory (and red)
+  }
 }
 
 template <int R>
@@ -835,8 +843,35 @@ cudaError_t launch_bwd(const SolveBwdArgs& s, int64_t systems, cudaStream_t stre
   cudaError_t e = allow_smem(reinterpret_cast<const void*>(&solve_backward_warp_kernel<R>), smem);
   if (e != cudaSuccess) return e;
   LaunchScope scope("solve_bwd", stream);
-  launch_pdl(solve_backward_warp_kernel<R>, static_cast<unsigned>(systems), kWThreads, smem, stream, s);
+  launch_pdl(solve_backward_warp_kernel<R>, static_cast<unsigned>(systems), kWThreads, smem, stream, s, systems);
   return cudaGetLastError();
+}
+
+template <int R>
+cudaError_t launch_bwd_persistent(const SolveBwdArgs& s, int64_t systems, int grid, cudaStream_t stream) {
+  const size_t smem = bwd_smem<R>(s.d);
+  cudaError_t e = allow_smem(reinterpret_cast<const void*>(&solve_backward_warp_kernel<R>), smem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&solve_backward_warp_kernel<R>),
+                           cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  const int64_t g = systems < grid ? systems : grid;
+  LaunchScope scope("solve_bwd", stream);
+  launch_pdl(solve_backward_warp_kernel<R>, static_cast<unsigned>(g), kWThreads, smem, stream, s, systems);
+  return cudaGetLastError();
+}
+
+template <int R>
+CtaFootprint bwd_footprint(int d) {
+  cudaFuncAttributes fa{};
+  CtaFootprint f{};
+  if (cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(&solve_backward_warp_kernel<R>)) != cudaSuccess) {
+    return f;
+  }
+  f.threads = kWThreads;
+  f.regs = fa.numRegs;
+  f.smem = bwd_smem<R>(d) + fa.sharedSizeBytes;
+  return f;
 }
 
 template <int R>
@@ -865,6 +900,27 @@ cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cuda
     case 32: return launch_fwd<32>(s, p.BH, stream);
     case 48: return launch_fwd<48>(s, p.BH, stream);
     case 64: return launch_fwd<64>(s, p.BH, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+CtaFootprint solve_backward_footprint(const Plan& p) {
+  const int d = static_cast<int>(p.d);
+  switch (p.R) {
+    case 16: return bwd_footprint<16>(d);
+    case 32: return bwd_footprint<32>(d);
+    case 48: return bwd_footprint<48>(d);
+    case 64: return bwd_footprint<64>(d);
+    default: return CtaFootprint{};
+  }
+}
+
+cudaError_t launch_solve_backward_persistent(const Plan& p, const SolveBwdArgs& s, int grid, cudaStream_t stream) {
+  switch (p.R) {
+    case 16: return launch_bwd_persistent<16>(s, p.BH, grid, stream);
+    case 32: return launch_bwd_persistent<32>(s, p.BH, grid, stream);
+    case 48: return launch_bwd_persistent<48>(s, p.BH, grid, stream);
+    case 64: return launch_bwd_persistent<64>(s, p.BH, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
