@@ -276,16 +276,16 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank, fused)  # noqa: E731
     from lsso_b200.ball.distributed import GradientExchange, layer_buckets
 
-    # Several ranks: the gradient average is part of every step, captured with it.  On one host
-    # it is the library's one-shot all-reduce kernel over NVLink peer memory after the backward;
-    # otherwise NCCL all-reduces per bucket on a side stream under the backward.
+    # Several ranks: the gradient average is part of every step, captured with it: per bucket, on a
+    # side stream under the rest of the backward -- on one host the library's one-shot all-reduce
+    # kernel over NVLink peer memory, otherwise NCCL all-reduces.
     exchange = None
     exchange_note = None
     if world > 1:
         exchange = GradientExchange([params] if args.shell else layer_buckets(layer))
         exchange_note = {
-            "peer": "library one-shot all-reduce kernel over NVLink peer memory (CUDA IPC regions) after the "
-                    "backward, in the step's CUDA graph",
+            "peer": "library one-shot all-reduce kernel over NVLink peer memory (CUDA IPC regions), one launch "
+                    "per bucket on a side stream under the backward, in the step's CUDA graph",
             "nccl": "NCCL all_reduce(AVG) per bucket on a side stream under the backward, in the step's CUDA graph",
         }[exchange.transport]
 

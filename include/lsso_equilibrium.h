@@ -15,6 +15,8 @@
  *  - The caller allocates every output and the workspace; the library
  *    allocates no device memory except the IPC-shareable exchange region of
  *    lsso_peer_region_create.  Sizes come from the *_workspace_size queries.
+ *    (lsso_backward_with_wgrad creates one stream and two events of its own
+ *    per device, on its first call there.)
  *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
  *    legacy default stream).  Entry points do not synchronize.
  *  - Return value 0 means success.  Non-zero codes are LSSO_ERR_*; the text
@@ -372,10 +374,13 @@ LSSO_API int lsso_peer_region_close(void* region);
 /* Free this rank's region (after every peer has closed it or stopped using it). */
 LSSO_API int lsso_peer_region_destroy(void* region);
 /* One exchange: `regions` (host array of `world` pointers) holds every
- * rank's region as mapped in this process, this rank's own at [rank];
- * `out` is a local 16-byte aligned [count] FP32 buffer. */
-LSSO_API int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t count, float scale, float* out,
-                                 unsigned long long wait_limit_ns, void* stream);
+ * rank's region as mapped in this process, this rank's own at [rank]; the
+ * values [first, first + count) of every region are summed (first a multiple
+ * of 4, so that several exchanges can each take one part of the buffer, in
+ * the same order on every rank) into `out`, a local 16-byte aligned [count]
+ * FP32 buffer. */
+LSSO_API int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t first, int64_t count,
+                                 float scale, float* out, unsigned long long wait_limit_ns, void* stream);
 
 /* Per-kernel timing (no counterpart in the reference; instrumentation only).
  * lsso_profile_start() makes every subsequent kernel launch of the library

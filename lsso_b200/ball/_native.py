@@ -84,7 +84,7 @@ class NativeLibrary:
             "lsso_peer_region_open": (ci, [c.c_char_p, c.POINTER(vp)]),
             "lsso_peer_region_close": (ci, [vp]),
             "lsso_peer_region_destroy": (ci, [vp]),
-            "lsso_peer_allreduce": (ci, [c.POINTER(vp), ci, ci, i64, c.c_float, vp, c.c_ulonglong, vp]),
+            "lsso_peer_allreduce": (ci, [c.POINTER(vp), ci, ci, i64, i64, c.c_float, vp, c.c_ulonglong, vp]),
             "lsso_profile_start": (ci, []),
             "lsso_profile_stop": (ci, [ci, c.c_char_p, c.POINTER(c.c_float), c.POINTER(c.c_int)]),
         }

@@ -20,9 +20,11 @@ applies.  Two ways to get it:
 
   With ``transport="peer"`` (the default for CUDA ranks on one host, through
   ``"auto"``) the flat buffer is the library's IPC-shared exchange region and
-  ``finish()`` launches the library's one-shot all-reduce kernel, which reads
-  every rank's buffer over NVLink and writes the average on every rank, in
-  place of NCCL.
+  each complete bucket is averaged by the library's one-shot all-reduce
+  kernel (on the side stream, under the rest of the backward), which reads
+  every rank's part of the buffer over NVLink and writes the average on
+  every rank, in place of NCCL.  Buckets go out in bucket order on every
+  rank whatever order they complete in, so the ranks' exchanges pair up.
 """
 
 from __future__ import annotations
@@ -105,10 +107,17 @@ class GradientExchange:
         # on the current stream (no side stream competing with the backward's kernels for SMs)
         self.overlap = overlap
         device = params[0].device
-        total = sum(p.numel() for p in params)
+        # each bucket starts at a multiple of four values (16 bytes: the peer
+        # exchange reads and writes whole float4 columns of a bucket)
+        sizes = [sum(p.numel() for p in b) for b in self.buckets]
+        self.bucket_start = []
+        total = 0
+        for size in sizes:
+            self.bucket_start.append(total)
+            total += (size + 3) // 4 * 4
         # transport: "peer" sums the ranks' buffers with the library's exchange kernel over peer
-        # memory (finish() launches it after the backward); "nccl" uses the process group's
-        # all_reduce; "auto" takes "peer" when every rank can map the others' memory.
+        # memory, one launch per bucket; "nccl" uses the process group's all_reduce; "auto"
+        # takes "peer" when every rank can map the others' memory.
         self.peers = None
         if transport != "nccl" and self._world() > 1:
             if device.type != "cuda":
@@ -128,29 +137,25 @@ class GradientExchange:
         else:
             self.flat = torch.zeros(total, dtype=torch.float32, device=device)
             self.averaged = self.flat
-        views = self.flat.split([p.numel() for p in params])
-        averaged_views = self.averaged.split([p.numel() for p in params])
         self.slot = {}
         self.result = {}
         self.bucket_of = {}
-        index = 0
         for k, bucket in enumerate(self.buckets):
+            offset = self.bucket_start[k]
             for p in bucket:
                 if p.dtype != torch.float32:
                     raise TypeError("GradientExchange keeps FP32 gradients; got a parameter of " + str(p.dtype))
-                self.slot[p] = views[index].view_as(p)
-                self.result[p] = averaged_views[index].view_as(p)
+                self.slot[p] = self.flat.narrow(0, offset, p.numel()).view_as(p)
+                self.result[p] = self.averaged.narrow(0, offset, p.numel()).view_as(p)
                 self.bucket_of[p] = k
-                index += 1
-        self.bucket_flat = []
-        start = 0
-        for bucket in self.buckets:
-            size = sum(p.numel() for p in bucket)
-            self.bucket_flat.append(self.flat.narrow(0, start, size))
-            start += size
+                offset += p.numel()
+        self.bucket_size = sizes
+        self.bucket_flat = [self.flat.narrow(0, s, n) for s, n in zip(self.bucket_start, sizes)]
+        self.bucket_out = [self.averaged.narrow(0, s, n) for s, n in zip(self.bucket_start, sizes)]
         self.stream = torch.cuda.Stream(device) if device.type == "cuda" else None
         self._ready = [set() for _ in self.buckets]
         self._launched = [False] * len(self.buckets)
+        self._next = 0  # buckets [0, _next) are launched; launches go in bucket order
         self._side_used = False
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_accumulated) for p in params]
         for p in params:  # the projections write their weight and bias gradients straight into these
@@ -165,9 +170,11 @@ class GradientExchange:
     def _mark(self, p: torch.nn.Parameter) -> None:
         k = self.bucket_of[p]
         self._ready[k].add(p)
-        if (self.overlap and self.peers is None and not self._launched[k]
-                and len(self._ready[k]) == len(self.buckets[k])):
-            self._launch(k)
+        if not self.overlap:
+            return
+        # every complete bucket from the next unlaunched one on, in order (the same on all ranks)
+        while self._next < len(self.buckets) and len(self._ready[self._next]) == len(self.buckets[self._next]):
+            self._launch(self._next)
 
     def _on_written(self, p: torch.nn.Parameter) -> None:
         """The library wrote p's gradient of this backward into its slot."""
@@ -183,10 +190,20 @@ class GradientExchange:
 
     def _launch(self, k: int) -> None:
         self._launched[k] = True
+        self._next = k + 1
         world = self._world()
         if world == 1:
             return
         buf = self.bucket_flat[k]
+        if self.peers is not None:
+            # the library's exchange kernel for this bucket's part of every rank's region
+            current = torch.cuda.current_stream(buf.device)
+            self.stream.wait_stream(current)
+            self._side_used = True
+            with torch.cuda.stream(self.stream):
+                self.peers.reduce(self.bucket_out[k], 1.0 / self.peers.world if self.average else 1.0,
+                                  first=self.bucket_start[k], count=self.bucket_size[k])
+            return
         if self.stream is None:
             dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
             if self.average:
@@ -211,9 +228,9 @@ class GradientExchange:
             for p in bucket:
                 if p not in self._ready[k]:
                     self.slot[p].zero_()
-            if self.overlap and self.peers is None:
+            if self.overlap:
                 self._launch(k)
-        if self.peers is not None:
+        if not self.overlap and self.peers is not None:
             self.peers.reduce(self.averaged, 1.0 / self.peers.world if self.average else 1.0)
         elif not self.overlap and self._world() > 1:
             if self.stream is None:
@@ -230,6 +247,7 @@ class GradientExchange:
                 p.grad = self.result[p]
         self._ready = [set() for _ in self.buckets]
         self._launched = [False] * len(self.buckets)
+        self._next = 0
         self._side_used = False
 
     def close(self) -> None:

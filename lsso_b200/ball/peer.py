@@ -91,8 +91,9 @@ class PeerRegion:
 
 
 def allreduce(regions: list[int], rank: int, count: int, out: torch.Tensor, *, scale: float = 1.0,
-              wait_limit_ns: int = 0, stream: torch.cuda.Stream | None = None) -> None:
-    """Launch one exchange: ``out = scale * sum over r of regions[r]``'s values.
+              first: int = 0, wait_limit_ns: int = 0, stream: torch.cuda.Stream | None = None) -> None:
+    """Launch one exchange: ``out = scale * sum over r of regions[r]``'s values
+    ``[first, first + count)`` (``first`` a multiple of 4).
 
     ``regions``: every rank's region address as mapped in this process (this
     rank's own at ``rank``).  Asynchronous on ``stream`` (default: current).
@@ -104,7 +105,7 @@ def allreduce(regions: list[int], rank: int, count: int, out: torch.Tensor, *, s
     array = (ctypes.c_void_p * world)(*regions)
     if stream is None:
         stream = torch.cuda.current_stream(out.device)
-    lib.check(lib.lib.lsso_peer_allreduce(array, world, int(rank), int(count), float(scale),
+    lib.check(lib.lib.lsso_peer_allreduce(array, world, int(rank), int(first), int(count), float(scale),
                                           ctypes.c_void_p(out.data_ptr()), int(wait_limit_ns),
                                           ctypes.c_void_p(stream.cuda_stream)))
 
@@ -173,8 +174,10 @@ class PeerGroup:
         """This rank's flat buffer (the values the exchange sums)."""
         return self.region.values
 
-    def reduce(self, out: torch.Tensor, scale: float = 1.0) -> None:
-        allreduce(self.addresses, self.rank, self.count, out, scale=scale, wait_limit_ns=self.wait_limit_ns)
+    def reduce(self, out: torch.Tensor, scale: float = 1.0, first: int = 0, count: int | None = None) -> None:
+        """Exchange values ``[first, first + count)`` (default: all) into ``out`` on the current stream."""
+        count = self.count - first if count is None else count
+        allreduce(self.addresses, self.rank, count, out, scale=scale, first=first, wait_limit_ns=self.wait_limit_ns)
 
     def close(self) -> None:
         """Unmap the peers' regions (this rank's own is freed with the last view of it)."""

@@ -576,8 +576,8 @@ int lsso_peer_region_destroy(void* region) {
   return LSSO_OK;
 }
 
-int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t count, float scale, float* out,
-                        unsigned long long wait_limit_ns, void* stream) {
+int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t first, int64_t count, float scale,
+                        float* out, unsigned long long wait_limit_ns, void* stream) {
   g_last_error.clear();
   if (world < 1 || world > LSSO_PEER_MAX_RANKS) {
     return fail(LSSO_ERR_INVALID_ARGUMENT, "the peer exchange supports 1 to %d ranks, got %d", LSSO_PEER_MAX_RANKS,
@@ -585,6 +585,10 @@ int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t count
   }
   if (rank < 0 || rank >= world) return fail(LSSO_ERR_INVALID_ARGUMENT, "rank %d outside [0, %d)", rank, world);
   if (count < 0) return fail(LSSO_ERR_INVALID_ARGUMENT, "count must be non-negative");
+  if (first < 0 || first % 4 != 0) {
+    return fail(LSSO_ERR_INVALID_ARGUMENT, "first must be a non-negative multiple of 4, got %lld",
+                static_cast<long long>(first));
+  }
   if (regions == nullptr) return fail(LSSO_ERR_INVALID_ARGUMENT, "regions must not be NULL");
   if (count > 0 && (out == nullptr || (reinterpret_cast<uintptr_t>(out) & 15) != 0)) {
     return fail(LSSO_ERR_INVALID_ARGUMENT, "out must be a 16-byte aligned device buffer");
@@ -602,6 +606,7 @@ int lsso_peer_allreduce(void* const* regions, int world, int rank, int64_t count
   if (rc != LSSO_OK) return rc;
   a.world = world;
   a.rank = rank;
+  a.first = first;
   a.count = count;
   a.scale = scale;
   a.out = out;

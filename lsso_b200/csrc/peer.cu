@@ -9,7 +9,8 @@
 //   arrive  CTA 0 tells every peer that this rank's buffer is complete (the
 //           kernels that wrote it finished before this launch started);
 //           every CTA waits until all peers have said the same;
-//   reduce  each thread sums one 16-byte column of all ranks' buffers in
+//   reduce  each thread sums one 16-byte column of all ranks' buffers (the
+//           values [first, first + count) of each region) in
 //           rank order 0..world-1 (so every rank gets bit-identical values)
 //           and writes sum * scale to its local output;
 //   depart  the last CTA to finish tells every peer that this rank is done
@@ -30,7 +31,7 @@
 namespace lsso {
 namespace {
 
-constexpr int kPeerThreads = 256;
+constexpr int kPeerThreads = 128;
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
@@ -67,30 +68,32 @@ __device__ __forceinline__ void signal_peers(const PeerArgs& a, size_t offset, u
 }
 
 template <int W>
-__global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const __grid_constant__ PeerArgs a) {
+__global__ void __launch_bounds__(kPeerThreads, 8) peer_allreduce_kernel(const __grid_constant__ PeerArgs a) {
   char* mine = a.region[0];
 #pragma unroll
   for (int j = 1; j < W; ++j) {
     if (j == a.rank) mine = a.region[j];
   }
   const unsigned epoch = *reinterpret_cast<volatile unsigned*>(mine + kPeerEpochOffset) + 1u;
-  __shared__ int s_ok;
 
-  // arrive
+  // arrive (thread 0's outcome reaches the CTA through the barrier itself: the
+  // kernel uses no shared memory, so a CTA fits on an SM beside a projection
+  // GEMM that leaves only the per-CTA reservation free)
+  int ok = 0;
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0) signal_peers<W>(a, kPeerArriveOffset, epoch);
-    const bool ok =
-        wait_peers(reinterpret_cast<const unsigned*>(mine + kPeerArriveOffset), W, a.rank, epoch, a.limit_ns);
+    ok = wait_peers(reinterpret_cast<const unsigned*>(mine + kPeerArriveOffset), W, a.rank, epoch, a.limit_ns);
     if (!ok) atomicExch(a.status, kStatusPeerWaitTimeout);
-    s_ok = ok;
   }
-  __syncthreads();
+  ok = __syncthreads_or(ok);
 
   // reduce
-  if (s_ok) {
+  if (ok) {
     const float4* src[W];
 #pragma unroll
-    for (int r = 0; r < W; ++r) src[r] = reinterpret_cast<const float4*>(a.region[r] + kPeerDataOffset);
+    for (int r = 0; r < W; ++r) {
+      src[r] = reinterpret_cast<const float4*>(a.region[r] + kPeerDataOffset) + (a.first >> 2);
+    }
     float4* out = reinterpret_cast<float4*>(a.out);
     const int64_t n4 = a.count >> 2;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kPeerThreads;
@@ -117,7 +120,9 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const __gr
       const int64_t i = tail + threadIdx.x;
       float v[W];
 #pragma unroll
-      for (int r = 0; r < W; ++r) v[r] = __ldcg(reinterpret_cast<const float*>(a.region[r] + kPeerDataOffset) + i);
+      for (int r = 0; r < W; ++r) {
+        v[r] = __ldcg(reinterpret_cast<const float*>(a.region[r] + kPeerDataOffset) + a.first + i);
+      }
       float s = v[0];
 #pragma unroll
       for (int r = 1; r < W; ++r) s += v[r];

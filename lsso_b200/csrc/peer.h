@@ -22,7 +22,8 @@ struct PeerArgs {
   char* region[kPeerMaxRanks];  // every rank's region as mapped in this process (own one at [rank])
   int world;
   int rank;
-  int64_t count;                // FP32 values per region
+  int64_t first;                // index of the first value exchanged (a multiple of 4)
+  int64_t count;                // FP32 values exchanged per region
   float scale;                  // applied to the sum (1/world for an average)
   float* out;                   // [count], 16-byte aligned, local
   int* status;                  // device status word

@@ -578,6 +578,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
     const int col = d + idx / R, i = idx % R;
     *reinterpret_cast<bf16*>(rm + kmajor_offset(col, i, RSBO)) = __float2bfloat16_rn(0.0f);
   }
+  // (end of the forward solve)
 }
 
 // ============================================================================

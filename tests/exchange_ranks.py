@@ -1,8 +1,9 @@
 """Two NCCL ranks (launched by tests/test_exchange_gpu.py): GradientExchange
 against allreduce_gradients' single collective, eagerly and as CUDA-graph
 replays holding the exchange, for both transports: NCCL collectives
-overlapped with the backward, and the library's peer-memory kernel (whose
-averages must also be bit-identical on the two ranks)."""
+overlapped with the backward, and the library's peer-memory kernel, per
+bucket under the backward and in one launch after it (whose averages must
+also be bit-identical on the two ranks)."""
 
 from __future__ import annotations
 
@@ -42,8 +43,8 @@ def main() -> int:
 
     ok = True
     rel = lambda u, v: float((u - v).norm() / v.norm().clamp_min(1e-30))  # noqa: E731
-    for transport in ("nccl", "peer"):
-        exchange = GradientExchange(layer_buckets(layer), transport=transport)
+    for transport, overlap in (("nccl", True), ("peer", True), ("peer", False)):
+        exchange = GradientExchange(layer_buckets(layer), transport=transport, overlap=overlap)
         ok &= exchange.transport == transport
         for _ in range(2):
             step()
@@ -68,7 +69,7 @@ def main() -> int:
         torch.cuda.synchronize()
         errors = [rel(q.grad, g) for q, g in zip(params, reference)]
         if rank == 0:
-            print(f"{transport}: graph replay errors vs one-collective average:",
+            print(f"{transport} (overlap={overlap}): graph replay errors vs one-collective average:",
                   " ".join(f"{e:.1e}" for e in errors))
         ok &= max(errors) < 1e-6
         if transport == "peer":

@@ -159,3 +159,30 @@ def test_invalid_arguments_are_rejected() -> None:
         peer.allreduce([mine.ptr], 0, 60, out[1:])
     with pytest.raises(RuntimeError, match="not an exchange region"):
         peer.allreduce([mine.ptr + 4], 0, 64, out)
+
+
+def test_bucketed_exchanges_take_their_part_of_the_buffer() -> None:
+    """Two exchanges per step over [0, 4096) and [4096, 10_001) (first a multiple of four), as the
+    overlapped gradient exchange launches its buckets: each sums only its part, in rank order."""
+    from lsso_b200.ball import _native, peer
+
+    regions = _regions(4, 10_001, seed=17)
+    rank = 1
+    mine = regions[rank]
+    out = torch.full((10_004,), float("nan"), device="cuda")
+    parts = [(0, 4096), (4096, 10_001 - 4096)]
+    epoch = 0
+    for _ in range(2):
+        for first, count in parts:
+            epoch += 1
+            _plant(mine, rank, 4, epoch)
+            peer.allreduce([r.ptr for r in regions], rank, count, out[first:], scale=0.25, first=first)
+            torch.cuda.synchronize()
+            assert int(mine.header[peer.EPOCH]) == epoch
+        assert torch.equal(out[:10_001], _expected(regions, 0.25))
+        for r in regions:
+            r.values.mul_(-0.5)
+    assert torch.isnan(out[10_001:]).all()
+    assert _native.device_status(reset=True) == 0
+    with pytest.raises(RuntimeError, match="multiple of 4"):
+        peer.allreduce([r.ptr for r in regions], rank, 16, out, first=6)
