@@ -133,8 +133,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t limit = kWaitLimitNs;
   if (abort_flag != nullptr && status != nullptr) {
-    limit = *reinterpret_cast<const volatile unsigned long long*>(&reinterpret_cast<DeviceControl*>(status)
-                                                                       ->wait_limit_ns);
+    // Through the read-only cache: the limit does not change while kernels of
+    // the library run (the host sets it between calls), and a wait that
+    // missed its first try re-checks the barrier only once this load returns,
+    // so an L2 round trip here would delay every such wait.
+    limit = __ldg(&reinterpret_cast<const DeviceControl*>(status)->wait_limit_ns);
   }
   const bool sleep = limit >= kSuspendHintNs;
   const uint64_t t0 = globaltimer_ns();
