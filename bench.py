@@ -201,27 +201,46 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------- GPU arm
 def algorithmic_bytes(kernel: str, B: int, N: int, dim: int = DIM, heads: int = HEADS,
-                      rank: int = RANK, fused: bool = False) -> float | None:
-    """Compulsory HBM bytes of one launch of our kernels at this workload (2-byte elements).
-
-    ``fused``: the input projection runs inside the fused projection + moment
-    pass (``proj_moments``), so the projection GEMMs are the other three.
-    """
+                      rank: int = RANK) -> float | None:
+    """Compulsory HBM bytes of one launch of our kernels at this workload (2-byte elements)."""
     D, W, HR = dim, heads * rank + dim, heads * rank
     T = B * N
     table = {
         "moments_fwd": 2 * W * T,            # read the packed projection once
-        "proj_moments": (2 * D + 2 * W) * T,  # read x, write the packed projection
         "readout": (2 * W + 2 * D) * T,      # read projection, write mixed coordinates
         "moments_bwd": (2 * HR + 2 * D) * T,  # read relation and the upstream gradient
         "grad": (2 * D + 4 * W) * T,         # read dY and projection, write the packed gradient
         # projection GEMMs, averaged over the launches of one step: x->projected, mixed->y,
-        # dy->dmixed, dprojected->dx (4 launches; 3 without x->projected) and the two weight
-        # gradients (read g and x)
-        "linear": (10 * D + 2 * W) * T / 3 if fused else (12 * D + 4 * W) * T / 4,
+        # dy->dmixed, dprojected->dx (4 launches) and the two weight gradients (read g and x)
+        "linear": (12 * D + 4 * W) * T / 4,
         "wgrad": (2 * W + 6 * D) * T / 2,
     }
     return table.get(kernel)
+
+
+def bind_near_gpu(uuid: str | None):
+    """Run this thread on the host cores NVML lists as closest to the GPU (its
+    NUMA node), so that the pinned host copy of x, allocated afterwards, sits
+    in that node's memory and the host-to-device copies do not cross the
+    sockets.  Returns the previous affinity (None if nothing changed)."""
+    if uuid is None or not hasattr(os, "sched_setaffinity"):
+        return None
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        words = ((os.cpu_count() or 64) + 63) // 64
+        mask = pynvml.nvmlDeviceGetCpuAffinity(handle, words)
+        near = {64 * w + bit for w, m in enumerate(mask) for bit in range(64) if (m >> bit) & 1}
+        previous = os.sched_getaffinity(0)
+        near &= previous
+        if not near or near == previous:
+            return None
+        os.sched_setaffinity(0, near)
+        return previous
+    except Exception:  # noqa: BLE001  (no NVML: leave the affinity as it is)
+        return None
 
 
 def measured_peaks() -> dict:
@@ -270,10 +289,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         pos = torch.arange(N, device=device)
         mask = pos[None, :] < lens[:, None]
         ids = torch.where(mask, pos[None, :].expand(B, N), torch.zeros_like(pos)[None, :])
-    from lsso_b200.ball import projection
-
-    fused = projection.fused_input_covers(x, args.heads, args.rank)
-    ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank, fused)  # noqa: E731
+    ab = lambda k: algorithmic_bytes(k, B, N, args.dim, args.heads, args.rank)  # noqa: E731
     from lsso_b200.ball.distributed import GradientExchange, layer_buckets
 
     # Several ranks: the gradient average is part of every step, captured with it: per bucket, on a
@@ -405,6 +421,7 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
     # ---- end to end through the public API: every step copies its x from pinned
     # host memory and reads its loss back.  Two input buffers, each with its own
     # graph; the copy of step i+1 runs on a copy stream while step i computes.
+    previous_affinity = bind_near_gpu(gpu_uuid)
     x_host = x.detach().to("cpu").pin_memory()
     loss_host = torch.empty(args.steps, dtype=torch.float32).pin_memory()
     bufs = [torch.empty_like(x.detach()).requires_grad_(x.is_floating_point()) for _ in range(2)]
@@ -449,6 +466,8 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
         dist.all_reduce(h2d_slowest, op=dist.ReduceOp.MIN)
         dist.all_reduce(h2d_fastest, op=dist.ReduceOp.MAX)
     clocks = sampler.stop()
+    if previous_affinity is not None:
+        os.sched_setaffinity(0, previous_affinity)  # the CPU baseline below uses every host core
     status = cuda.device_status(reset=False)
     if world > 1:
         worst = torch.tensor([status], device=device)
@@ -470,8 +489,6 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
             alg = ab(dominant)
             achieved = alg / per_launch_s / 1e9
             traffic = traffic_record().get(dominant) if headline(args) and B == 64 else None
-            if traffic is not None and dominant == "linear" and bool(traffic.get("input_fused")) != fused:
-                traffic = None  # measured over the other launch mix of the projection GEMMs
             roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                         "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
@@ -509,7 +526,9 @@ def gpu_arm(args, rank: int, world: int, local: int) -> int:
                                          "note": "median duration of each rank's x copies (copy-stream events) "
                                                  "during the e2e run; all ranks copy at once"},
                     "note": "pinned host x -> device on a copy stream (double-buffered, overlapping the previous "
-                            "step), graph-replayed fwd+bwd, loss -> pinned host, every step"},
+                            "step), graph-replayed fwd+bwd, loss -> pinned host, every step; the host thread runs "
+                            "on the GPU's NUMA-local cores (NVML) while x is pinned and copied",
+                    "numa_bound": previous_affinity is not None},
             "roofline": roofline, "kernels": step_kernels, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": sum(v[1] for v in kernels.values()), "device_status": status,
         }

@@ -109,34 +109,6 @@ LSSO_API int lsso_forward(const void* projected, const float* core_base_raw, con
                  void* mixed, float* tape, int32_t* pivots, void* workspace, size_t workspace_bytes,
                  void* stream);
 
-/* ---- Input projection fused with the mixer forward (no single counterpart
- * in the reference: it replaces the reference's projection
- * `projected = tensor_core_linear(x, w_bc.weight, w_bc.bias, BF16)` with masked
- * rows zeroed (lsso/ball/model.py:370-383) followed by
- * lsso_equilibrium::forward_train / forward_inference
- * (csrc/ball/binding.cpp:84-90), which the host side calls when the shape is
- * covered).  One pass reads x and writes the packed projection while the
- * moment sums are accumulated from it, then the solves and the readout run
- * as in lsso_forward.
- *   x          FP16 (x_dtype 1) or BF16 (0) [B, N, D], contiguous
- *   w_bc       FP32 [H*R + D, D]; b_bc FP32 [H*R + D] or NULL
- *   row_mask   [B*N] bytes, nonzero = valid token, or NULL (masked rows of
- *              `projected` are zero, as after the reference's projection)
- *   projected  BF16 [B, N, H*R + D] output (keep it for lsso_backward)
- *   other arguments as in lsso_forward.
- * Covered shapes (lsso_fused_forward_supported): R in {32, 64}, D/H in
- * {32, 64} with D/H <= R (the heads of a 64-feature relation box share one
- * 64-feature value box), D a multiple of 64 up to 256. */
-LSSO_API int lsso_fused_forward_supported(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R);
-LSSO_API size_t lsso_fused_forward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
-                                                  int positions_batched, int train);
-LSSO_API int lsso_fused_forward(const void* x, int x_dtype, const float* w_bc, const float* b_bc,
-                                const uint8_t* row_mask, const float* core_base_raw, const float* core_drive_weight,
-                                const float* eta_raw, const float* centered_positions, int positions_batched,
-                                const float* valid_counts, int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
-                                void* projected, void* mixed, float* tape, int32_t* pivots, void* workspace,
-                                size_t workspace_bytes, void* stream);
-
 /* Workspace bytes for lsso_backward. */
 LSSO_API size_t lsso_backward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R,
                                     int positions_batched);

@@ -27,8 +27,7 @@ EXPORTED_SYMBOLS = (
     "lsso_linear_workspace_size", "lsso_linear", "lsso_linear_image_size", "lsso_linear_prepare",
     "lsso_linear_prepared", "lsso_linear_wgrad_workspace_size", "lsso_linear_wgrad",
     "lsso_moment_elements", "lsso_forward_moments", "lsso_forward_finish", "lsso_backward_moments",
-    "lsso_backward_finish", "lsso_fused_forward_supported", "lsso_fused_forward_workspace_size",
-    "lsso_fused_forward", "lsso_peer_region_bytes", "lsso_peer_region_create", "lsso_peer_region_open",
+    "lsso_backward_finish", "lsso_peer_region_bytes", "lsso_peer_region_create", "lsso_peer_region_open",
     "lsso_peer_region_close", "lsso_peer_region_destroy", "lsso_peer_allreduce", "lsso_backward_with_wgrad",
 )
 
@@ -75,10 +74,6 @@ class NativeLibrary:
             "lsso_backward_moments": (ci, [vp, vp, vp, ci, i64, i64, i64, i64, i64, vp, vp, sz, vp]),
             "lsso_backward_finish": (ci, [vp, vp, vp, vp, vp, vp, ci, i64, i64, i64, i64, i64, vp, c.c_float, vp,
                                           vp, vp, vp, vp, sz, vp]),
-            "lsso_fused_forward_supported": (ci, [i64, i64, i64, i64, i64]),
-            "lsso_fused_forward_workspace_size": (sz, [i64, i64, i64, i64, i64, ci, ci]),
-            "lsso_fused_forward": (ci, [vp, ci, vp, vp, vp, vp, vp, vp, vp, ci, vp, i64, i64, i64, i64, i64, vp, vp,
-                                        vp, vp, vp, sz, vp]),
             "lsso_peer_region_bytes": (sz, [i64]),
             "lsso_peer_region_create": (ci, [i64, c.POINTER(vp), c.c_char_p]),
             "lsso_peer_region_open": (ci, [c.c_char_p, c.POINTER(vp)]),
@@ -212,65 +207,6 @@ def forward(projected, core_base_raw, core_drive_weight, eta_raw, centered_posit
             int(batched), _ptr(valid_counts), batch, length, heads, dim, rank, _ptr(mixed), _ptr(tape), _ptr(pivots),
             _ptr(workspace), size, _stream(device)))
     return mixed, tape, pivots
-
-
-def fused_supported(batch: int, length: int, heads: int, dim: int, rank: int) -> bool:
-    """Whether ``lsso_fused_forward`` covers this shape (rank 32 / 64, head width <= rank, D <= 256)."""
-    return bool(library().lib.lsso_fused_forward_supported(batch, length, heads, dim, rank))
-
-
-def fused_forward(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw, centered_positions,
-                  valid_counts, *, train: bool):
-    """Input projection fused with the forward moment pass, then the solves and the readout.
-
-    ``x`` FP16 / BF16 [B, N, D]; ``weight`` FP32 [H*R + D, D]; ``bias`` FP32
-    [H*R + D] or None; ``row_mask`` bool [B, N] or None.  Returns
-    ``(projected, mixed, tape, pivots)`` (tape / pivots None unless train);
-    ``projected`` is the BF16 packed projection the reference's
-    tensor_core_linear produces (masked rows zero).
-    """
-    lib = library()
-    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16) or x.dim() != 3:
-        raise ValueError("fused_forward takes FP16 or BF16 CUDA x [B, N, D]")
-    x = x.contiguous()
-    batch, length, dim = x.shape
-    device = x.device
-    width = weight.shape[0]
-    if weight.dtype != torch.float32 or not weight.is_contiguous() or weight.dim() != 2 or weight.shape[1] != dim:
-        raise ValueError("fused_forward: weight must be contiguous FP32 [H*R + D, D]")
-    if bias is not None and (bias.dtype != torch.float32 or bias.shape != (width,)):
-        raise ValueError("fused_forward: bias must be FP32 [H*R + D]")
-    mask = None
-    if row_mask is not None:
-        if row_mask.dtype != torch.bool or row_mask.shape != (batch, length):
-            raise ValueError("fused_forward: row_mask must be bool [B, N]")
-        if row_mask.device != device:
-            raise RuntimeError(f"row_mask must share x.device() (got {row_mask.device} vs {device})")
-        mask = row_mask.contiguous().view(torch.uint8)
-    projected = torch.empty((batch, length, width), dtype=torch.bfloat16, device=device)
-    _, _, heads, _, rank = validate_fast_inputs(
-        projected, core_base_raw, core_drive_weight, eta_raw, centered_positions, valid_counts)
-    for name, value in (("weight", weight), ("bias", bias)):
-        if value is not None:
-            _same_device(value, projected, name)
-    batched = centered_positions is not None and centered_positions.dim() == 2
-    with torch.cuda.device(device):
-        mixed = torch.empty((batch, length, dim), dtype=torch.bfloat16, device=device)
-        tape = pivots = None
-        if train:
-            stride = lib.lib.lsso_tape_stride(length, heads, dim, rank)
-            tape = torch.empty((batch * heads, stride), dtype=torch.float32, device=device)
-            pivots = torch.empty((batch * heads, rank), dtype=torch.int32, device=device)
-        size = lib.lib.lsso_fused_forward_workspace_size(batch, length, heads, dim, rank, int(batched), int(train))
-        if size == 0:
-            lib.check(1)
-        workspace = torch.empty((size,), dtype=torch.uint8, device=device)
-        lib.check(lib.lib.lsso_fused_forward(
-            _ptr(x), 1 if x.dtype == torch.float16 else 0, _ptr(weight), _ptr(bias), _ptr(mask),
-            _ptr(core_base_raw), _ptr(core_drive_weight), _ptr(eta_raw), _ptr(centered_positions), int(batched),
-            _ptr(valid_counts), batch, length, heads, dim, rank, _ptr(projected), _ptr(mixed), _ptr(tape),
-            _ptr(pivots), _ptr(workspace), size, _stream(device)))
-    return projected, mixed, tape, pivots
 
 
 def backward(grad_output, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots, centered_positions,

@@ -215,7 +215,6 @@ class LSSO(nn.Module):
             if not parameter.is_contiguous():
                 raise RuntimeError(f"implementation='cuda' requires contiguous {name}")
 
-        from . import cuda as cuda_backend
         from . import projection
 
         batch, length, _ = x.shape
@@ -238,19 +237,12 @@ class LSSO(nn.Module):
         wants_backward = torch.is_grad_enabled() and (
             x.requires_grad or any(p.requires_grad for p in (self.w_bc.weight, self.w_o.weight)))
         images = projection.layer_images(self.w_bc.weight, self.w_o.weight, wants_backward)
-        if projection.fused_input_covers(x, c.num_heads, c.rank):
-            # the projection fused with the mixer's moment pass (same projected coordinates)
-            cuda_backend.require_available()
-            mixed = projection.fused_input_mix(x, self.w_bc.weight, self.w_bc.bias, mask, self.core_base_raw,
-                                               self.core_drive_weight, self.eta_raw, centered_positions, valid_counts)
-        else:
-            projected = projection.input_projection(x, self.w_bc.weight, self.w_bc.bias, mask, images)
-            # the mixer and the output projection as one autograd node: its backward computes the
-            # output projection's weight gradient beside the mixer backward's solves
-            return projection.mix_output(projected, self.core_base_raw, self.core_drive_weight, self.eta_raw,
-                                         centered_positions, valid_counts, self.w_o.weight, self.w_o.bias, x.dtype,
-                                         mask, images)
-        return projection.output_projection(mixed, self.w_o.weight, self.w_o.bias, x.dtype, mask, images)
+        projected = projection.input_projection(x, self.w_bc.weight, self.w_bc.bias, mask, images)
+        # the mixer and the output projection as one autograd node: its backward computes the
+        # output projection's weight gradient beside the mixer backward's solves
+        return projection.mix_output(projected, self.core_base_raw, self.core_drive_weight, self.eta_raw,
+                                     centered_positions, valid_counts, self.w_o.weight, self.w_o.bias, x.dtype, mask,
+                                     images)
 
     # ------------------------------------------------------------------ reference path
     def _compact_coordinates(self, compact_state, valid_count):

@@ -312,12 +312,15 @@ class _MixOutput(torch.autograd.Function):
             d = mixed.shape[-1]
             wgrad = (g.reshape(-1, g.shape[-1]), mixed.reshape(-1, d), row_mask, grad_weight, CONCURRENT_WGRAD)
         mixer_grads = (None, None, None, None)
+        # the weight gradient rides on the mixer backward's call when that runs and the feature
+        # widths are multiples of 8; otherwise the separate (padding) weight-gradient call
+        fuse = (wgrad is not None and any(needs[:4]) and g.shape[-1] % 8 == 0 and mixed.shape[-1] % 8 == 0)
         if any(needs[:4]):
             grad_mixed = linear(g, weight, None, row_mask, mixed.dtype, weight_transposed=True, image=image_t,
                                 reverse=True)
             mixer_grads = _native.backward(grad_mixed, projected, core_base_raw, core_drive_weight, eta_raw, tape,
-                                           pivots, centered_positions, valid_counts, wgrad=wgrad)
-        elif wgrad is not None:
+                                           pivots, centered_positions, valid_counts, wgrad=wgrad if fuse else None)
+        if wgrad is not None and not fuse:
             weight_gradient(g, mixed, row_mask, out=grad_weight)
         for parameter, on_written in written:
             if on_written is not None:
@@ -355,73 +358,6 @@ def mix_output(projected, core_base_raw, core_drive_weight, eta_raw, centered_po
                             weight, bias, mask, dtype, images.get("o"), images.get("o_t"))
 
 
-class _FusedInputMix(torch.autograd.Function):
-    """Input projection + mixer with the projection fused into the moment pass (lsso_fused_forward).
-
-    Forward: ``projected = bf16(x) bf16(W_bc)^T + b`` (masked rows zero) and the
-    mixer on it, in one native call.  Backward: the mixer's VJP
-    (``lsso_backward`` on the saved projection) followed by the projection's.
-    """
-
-    @staticmethod
-    def forward(ctx, x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw, centered_positions,
-                valid_counts):
-        projected, mixed, tape, pivots = _native.fused_forward(
-            x, weight, None if bias is None else bias.detach(), row_mask, core_base_raw, core_drive_weight, eta_raw,
-            centered_positions, valid_counts, train=True)
-        ctx.save_for_backward(x, weight, row_mask, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
-                              centered_positions, valid_counts)
-        ctx.bias_meta = None if bias is None else (bias.dtype, bias.device)
-        ctx.bias_param = bias
-        return mixed
-
-    @staticmethod
-    @once_differentiable
-    def backward(ctx, grad_mixed):
-        (x, weight, row_mask, projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots, centered_positions,
-         valid_counts) = ctx.saved_tensors
-        grad_projected, grad_base, grad_drive, grad_eta = torch.ops.lsso_equilibrium.backward(
-            grad_mixed.contiguous(), projected, core_base_raw, core_drive_weight, eta_raw, tape, pivots,
-            centered_positions, valid_counts)
-        grad_x, grad_w, grad_b = _linear_vjp(grad_projected, x, weight, row_mask, ctx.needs_input_grad[:3],
-                                             ctx.bias_meta, None, ctx.bias_param)
-        return grad_x, grad_w, grad_b, None, grad_base, grad_drive, grad_eta, None, None
-
-
-# Opt-in: the fused input projection + moment pass is exact (bit-identical to
-# the separate calls) but, measured on B200 at the bench shape, slower than the
-# projection GEMM followed by the moment pass (one head group per CTA repeats
-# the x staging and conversion for every group).  Set True to use it.
-FUSED_INPUT = False
-_FUSED_SHAPES: dict[tuple[int, ...], bool] = {}
-
-
-def fused_input_covers(x: torch.Tensor, heads: int, rank: int) -> bool:
-    """Whether ``fused_input_mix`` runs for this input (library coverage, cached per shape)."""
-    if not FUSED_INPUT:
-        return False
-    key = (x.device.index or 0, *x.shape, heads, rank)
-    hit = _FUSED_SHAPES.get(key)
-    if hit is None:
-        batch, length, dim = x.shape
-        with torch.cuda.device(x.device):
-            hit = _native.fused_supported(batch, length, heads, dim, rank)
-        _FUSED_SHAPES[key] = hit
-    return hit
-
-
-def fused_input_mix(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw, centered_positions,
-                    valid_counts) -> torch.Tensor:
-    """``fast_mix(input_projection(x, ...), ...)`` through the fused native forward."""
-    if torch.is_grad_enabled() and any(
-            v is not None and v.requires_grad for v in (x, weight, bias, core_base_raw, core_drive_weight, eta_raw)):
-        return _FusedInputMix.apply(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw,
-                                    centered_positions, valid_counts)
-    _, mixed, _, _ = _native.fused_forward(x, weight, bias, row_mask, core_base_raw, core_drive_weight, eta_raw,
-                                           centered_positions, valid_counts, train=False)
-    return mixed
-
-
 def input_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                      mask: torch.Tensor | None, images: dict | None = None) -> torch.Tensor:
     images = images or {}
@@ -441,5 +377,5 @@ def output_projection(mixed: torch.Tensor, weight: torch.Tensor, bias: torch.Ten
     return _ProjectionFunction.apply(mixed, weight, bias, mask, dtype, images.get("o"), images.get("o_t"), True)
 
 
-__all__ = ["fused_input_covers", "fused_input_mix", "input_projection", "layer_images", "linear", "mix_output",
-           "output_projection", "prepare_images", "register_gradient_slot", "weight_gradient"]
+__all__ = ["input_projection", "layer_images", "linear", "mix_output", "output_projection", "prepare_images",
+           "register_gradient_slot", "weight_gradient"]

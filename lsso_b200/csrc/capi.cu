@@ -126,20 +126,6 @@ ForwardLayout forward_layout(const lsso::Plan& p, bool train) {
   return l;
 }
 
-// lsso_fused_forward: the forward layout, then the fused kernel's BF16 weight tiles.
-struct FusedLayout {
-  ForwardLayout f;
-  size_t wprep, total;
-};
-FusedLayout fused_layout(const lsso::Plan& p, bool train) {
-  FusedLayout l{};
-  l.f = forward_layout(p, train);
-  size_t off = l.f.total;
-  l.wprep = off;
-  off = align256(off + lsso::fused_weight_bytes(p));
-  l.total = off;
-  return l;
-}
 
 struct BackwardLayout {
   size_t phase, phase16, partial, dbuf, lbuf, b1y, b1c, b1a, b2, gbase, gdrive, etastat, etadot, total;
@@ -764,93 +750,6 @@ int lsso_forward(const void* projected, const float* core_base_raw, const float*
   fb.vec = p.vec && aligned16(projected) && aligned16(mixed);
   const cudaError_t e = lsso::launch_forward(p, fb, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lsso_forward");
-  return LSSO_OK;
-}
-
-int lsso_fused_forward_supported(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R) {
-  g_last_error.clear();
-  lsso::Plan p{};
-  if (plan_for(B, N, H, D, R, 0, &p) != LSSO_OK) return 0;
-  return lsso::fused_input_usable(p) ? 1 : 0;
-}
-
-size_t lsso_fused_forward_workspace_size(int64_t B, int64_t N, int64_t H, int64_t D, int64_t R, int positions_batched,
-                                         int train) {
-  g_last_error.clear();
-  lsso::Plan p{};
-  if (plan_for(B, N, H, D, R, positions_batched, &p) != LSSO_OK) return 0;
-  if (!lsso::fused_input_usable(p)) {
-    fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_fused_forward: shape not covered (lsso_fused_forward_supported)");
-    return 0;
-  }
-  return fused_layout(p, train != 0).total;
-}
-
-int lsso_fused_forward(const void* x, int x_dtype, const float* w_bc, const float* b_bc, const uint8_t* row_mask,
-                       const float* core_base_raw, const float* core_drive_weight, const float* eta_raw,
-                       const float* centered_positions, int positions_batched, const float* valid_counts, int64_t B,
-                       int64_t N, int64_t H, int64_t D, int64_t R, void* projected, void* mixed, float* tape,
-                       int32_t* pivots, void* workspace, size_t workspace_bytes, void* stream) {
-  g_last_error.clear();
-  if (x == nullptr || w_bc == nullptr || core_base_raw == nullptr || core_drive_weight == nullptr ||
-      eta_raw == nullptr || projected == nullptr || mixed == nullptr || workspace == nullptr) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_fused_forward: a required pointer is NULL");
-  }
-  if ((tape == nullptr) != (pivots == nullptr)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_fused_forward: tape and pivots must be given together");
-  }
-  if (x_dtype != 0 && x_dtype != 1) return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_fused_forward: x_dtype must be 0 or 1");
-  if (!aligned16(x) || !aligned16(w_bc) || !aligned16(projected) || !aligned16(mixed) || !aligned16(workspace)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT,
-                "lsso_fused_forward: x, w_bc, projected, mixed and workspace must be 16-byte aligned");
-  }
-  const bool batched = centered_positions != nullptr && positions_batched != 0;
-  lsso::Plan p{};
-  int rc = plan_for(B, N, H, D, R, batched ? 1 : 0, &p);
-  if (rc != LSSO_OK) return rc;
-  if (!lsso::fused_input_usable(p)) {
-    return fail(LSSO_ERR_INVALID_ARGUMENT, "lsso_fused_forward: shape not covered (lsso_fused_forward_supported)");
-  }
-  const bool train = tape != nullptr;
-  const FusedLayout l = fused_layout(p, train);
-  if (workspace_bytes < l.total) {
-    return fail(LSSO_ERR_WORKSPACE, "lsso_fused_forward: workspace of %zu bytes is smaller than the required %zu",
-                workspace_bytes, l.total);
-  }
-  int device = 0, sms = 0;
-  int* status = nullptr;
-  rc = device_info(&device, &sms, &status);
-  if (rc != LSSO_OK) return rc;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  lsso::ForwardBuffers fb{};
-  fb.projected = static_cast<const lsso::bf16*>(projected);
-  fb.base = core_base_raw;
-  fb.drive = core_drive_weight;
-  fb.eta_raw = eta_raw;
-  fb.positions = centered_positions;
-  fb.positions_batched = batched ? 1 : 0;
-  fb.counts = valid_counts;
-  fb.mixed = static_cast<lsso::bf16*>(mixed);
-  fb.tape = tape;
-  fb.pivots = pivots;
-  fb.phase = reinterpret_cast<float2*>(ws + l.f.phase);
-  fb.phase16 = reinterpret_cast<__half2*>(ws + l.f.phase16);
-  fb.partial = reinterpret_cast<float*>(ws + l.f.partial);
-  fb.zbuf = train ? nullptr : reinterpret_cast<float*>(ws + l.f.zbuf);
-  fb.rmat = reinterpret_cast<lsso::bf16*>(ws + l.f.rmat);
-  fb.status = status;
-  fb.vec = p.vec;
-  lsso::FusedInput in{};
-  in.x = x;
-  in.x_fp16 = x_dtype;
-  in.weight = w_bc;
-  in.bias = b_bc;
-  in.row_mask = row_mask;
-  in.projected = static_cast<lsso::bf16*>(projected);
-  in.wprep = ws + l.wprep;
-  in.phase16 = fb.phase16;
-  const cudaError_t e = lsso::launch_forward_fused(p, fb, in, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "lsso_fused_forward");
   return LSSO_OK;
 }
 

@@ -1100,44 +1100,61 @@ __global__ void __launch_bounds__(128) grad_kernel(const GradArgs a) {
 // ============================================================================
 constexpr int kReduceThreads = 256;
 
-// Blocks [0, main_blocks) sum the base/drive partials of one element each per
-// thread over samples; the last H blocks each reduce one head's complement
+// Blocks [0, main_blocks) sum the base/drive partials over samples, four
+// lanes per element; the last H blocks each reduce one head's complement
 // statistic over (sample, tile) with a fixed-order tree.  Deterministic.
+constexpr int kReduceLanes = 4;
 __global__ void __launch_bounds__(kReduceThreads) param_reduce_kernel(const ParamReduceArgs a) {
   pdl_wait();
   const int64_t R = a.R, d = a.d, H = a.H;
   const int64_t nbase = H * R * R, nmain = nbase + H * d * R;
-  const int64_t main_blocks = (nmain + kReduceThreads - 1) / kReduceThreads;
+  const int64_t main_blocks = (nmain * kReduceLanes + kReduceThreads - 1) / kReduceThreads;
   if (static_cast<int64_t>(blockIdx.x) < main_blocks) {
-    const int64_t idx = static_cast<int64_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
-    if (idx >= nmain) return;
+    // Sixteen partial sums per element (sample b goes to sum b % 16, ascending
+    // b), combined by the pairwise tree acc[j] += acc[j + w], w = 8, 4, 2, 1.
+    // Lane l of the element's four holds sums 4l .. 4l+3 (all their loads in
+    // flight at once); the tree's first two levels cross lanes by shuffles, so
+    // every addition happens in the same order as in one thread.
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
+    const int64_t idx = t / kReduceLanes;
+    const int l = static_cast<int>(t % kReduceLanes);
+    const bool live = idx < nmain;  // whole groups of four share this
     const bool is_base = idx < nbase;
-    const int64_t k = is_base ? idx : idx - nbase;
+    const int64_t k = live ? (is_base ? idx : idx - nbase) : 0;
     const int64_t per = is_base ? R * R : d * R;
     const int64_t h = k / per, e = k % per;
     const float* src = (is_base ? a.gbase : a.gdrive) + h * per + e;
     const int64_t stride = H * per;
-    // Sixteen partial sums (sample b goes to sum b % 16), so sixteen loads are
-    // in flight per thread; combined by a fixed pairwise tree.
-    float acc[16];
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (live) {
+#pragma unroll 4
+      for (int64_t b0 = 0; b0 < a.B; b0 += 16) {
+        float v[4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-    int64_t b = 0;
-    for (; b + 16 <= a.B; b += 16) {
-      float v[16];
+        for (int u = 0; u < 4; ++u) {
+          const int64_t b = b0 + 4 * l + u;
+          v[u] = b < a.B ? __ldg(src + b * stride) : 0.0f;
+        }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __ldg(src + (b + j) * stride);
+        for (int u = 0; u < 4; ++u)
+          if (b0 + 4 * l + u < a.B) acc[u] += v[u];
+      }
+    }
+    float o[4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) acc[j] += v[j];
+    for (int u = 0; u < 4; ++u) o[u] = __shfl_down_sync(0xffffffffu, acc[u], 2, kReduceLanes);
+    if (l < 2) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += o[u];  // w = 8: sums 4l+u and 4(l+2)+u
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (b + j < a.B) acc[j] += src[(b + j) * stride];
+    for (int u = 0; u < 4; ++u) o[u] = __shfl_down_sync(0xffffffffu, acc[u], 1, kReduceLanes);
+    if (l != 0 || !live) return;
 #pragma unroll
-    for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-      for (int j = 0; j < w; ++j) acc[j] += acc[j + w];
-    const float total = acc[0];
+    for (int u = 0; u < 4; ++u) acc[u] += o[u];  // w = 4: sums u and 4 + u
+    acc[0] += acc[2];                              // w = 2
+    acc[1] += acc[3];
+    const float total = acc[0] + acc[1];           // w = 1
     if (is_base) {
       a.grad_base[k] = total;
     } else {
@@ -1500,7 +1517,7 @@ static cudaError_t backward_grads_r(const Plan& p, const BackwardBuffers& bb, fl
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const int64_t main_blocks = ceil_div(p.H * p.R * p.R + p.H * p.d * p.R, kReduceThreads);
+  const int64_t main_blocks = ceil_div((p.H * p.R * p.R + p.H * p.d * p.R) * kReduceLanes, kReduceThreads);
   LaunchScope scope("param_reduce", stream);
   launch_pdl(param_reduce_kernel, static_cast<unsigned>(main_blocks + p.H), kReduceThreads, 0, stream, pr);
   return cudaGetLastError();
@@ -1632,16 +1649,6 @@ cudaError_t launch_backward_finish(const Plan& p, const BackwardBuffers& bb, con
     case 64: return backward_finish_r<64>(p, bb, moments, 1, redundant, stream);
     default: return cudaErrorInvalidValue;
   }
-}
-
-cudaError_t launch_forward_fused(const Plan& p, const ForwardBuffers& fb, const FusedInput& in, cudaStream_t stream) {
-  if (p.R != 32 && p.R != 64) return cudaErrorInvalidValue;
-  cudaError_t e = launch_phase(p, fb.positions, fb.phase, fb.phase16, stream);
-  if (e != cudaSuccess) return e;
-  e = launch_proj_moments(p, in, fb.partial, fb.status, p.sms, stream);
-  if (e != cudaSuccess) return e;
-  return p.R == 32 ? forward_finish_r<32>(p, fb, fb.partial, p.nchunks, stream)
-                   : forward_finish_r<64>(p, fb, fb.partial, p.nchunks, stream);
 }
 
 cudaError_t launch_forward(const Plan& p, const ForwardBuffers& fb, cudaStream_t stream) {

@@ -179,27 +179,6 @@ cudaError_t launch_grad_tiled(const Plan& p, const bf16* gout, const bf16* proj,
                               const bf16* b1c, const bf16* b1a, const float* eta_raw, bf16* gproj,
                               float* etastat, int* status, int sm_count, cudaStream_t stream);
 
-// Input projection fused with the forward moment pass (tokens.cu): the
-// projection of x written to `projected` and the moment partials, for R in
-// {32, 64} when the heads of a group fit one value box and D <= 256 is a
-// multiple of 64.
-struct FusedInput {
-  const void* x;            // [B, N, D] FP16 or BF16
-  int x_fp16;
-  const float* weight;      // FP32 [H*R + D, D]
-  const float* bias;        // nullable FP32 [H*R + D]
-  const uint8_t* row_mask;  // nullable [B*N], nonzero = valid
-  bf16* projected;          // [B, N, H*R + D] output
-  uint8_t* wprep;           // fused_weight_bytes(p)
-  __half2* phase16;         // FP16 phase table [pos_rows][N][R/2]
-};
-bool fused_input_usable(const Plan& p);
-size_t fused_weight_bytes(const Plan& p);
-cudaError_t launch_proj_moments(const Plan& p, const FusedInput& in, float* partial, int* status, int sm_count,
-                                cudaStream_t stream);
-// Phase tables, the fused projection + moment pass, the solves and the readout.
-cudaError_t launch_forward_fused(const Plan& p, const ForwardBuffers& fb, const FusedInput& in, cudaStream_t stream);
-
 // Register-resident warp solves for R <= 32 (solve.cu).
 bool warp_solves_usable(const Plan& p);
 cudaError_t launch_solve_forward_warp(const Plan& p, const SolveFwdArgs& s, cudaStream_t stream);

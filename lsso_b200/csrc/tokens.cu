@@ -510,539 +510,6 @@ __global__ void __launch_bounds__(kMThreads, 1) moments_tile_kernel(const __grid
 }
 
 // ============================================================================
-// Input projection fused with the forward moment pass.  The reference runs
-// them as two passes over HBM (lsso/ball/model.py:370-404 writes the packed
-// projection, the moment pass of lsso/ball/reference.py:411-447 reads it
-// back); here one pass reads x and writes the projection once.
-//
-// Item = (sample, head group, chunk of ct tiles), as in the moment pass, with
-// the head group fixed per CTA (the grid is a multiple of the group count).
-// The group's 128 projected features are its relation box (64 / R heads) and
-// the 64-feature value box holding those heads.  Per 128-token tile:
-//   GEMM     P = bf16(x) W_g^T into a TMEM buffer: M = 128 tokens, N = 128
-//            features, K = D; W_g (the group's weight rows) stays in shared
-//            memory, x arrives in 64-feature TMA boxes (FP16 rounded to BF16
-//            in place);
-//   epilogue + bias, masked and padding rows zero, BF16: the projected
-//            coordinates, staged as the group's relation and value boxes and
-//            stored to `projected` by TMA (the value box only by the group
-//            it starts with);
-//   moments  exactly as moments_tile_kernel<R, false> from those BF16
-//            coordinates: the rotated relation split into hi / lo,
-//            A = [lo | hi], B = [hi | values], accumulated in TMEM over the
-//            chunk and drained to the same partials.
-// `projected` and the partials equal those of the projection GEMM followed by
-// the moment pass.  The trade: HBM traffic drops by one read of the packed
-// projection, but each head group's CTA stages and rounds the x box and reads
-// it as a GEMM operand again, so at D = 256 the shared-memory traffic per
-// token tile exceeds that of the two separate kernels (two groups per CTA
-// would need 128 KB of weight plus 96 KB of operand slots per tile), and the
-// host side runs this kernel only on request.
-//
-// Warps: 0 producer (the weight once, then x boxes), 1 MMA issuer (the GEMMs
-// run two tiles ahead of the moment MMAs), 2-5 FP16 -> BF16 rounding of the x
-// boxes, 6-21 epilogue (four per TMEM sub-partition, 16 features of each box
-// per warp), 22-25 accumulator drain, 26 storer, 27 none (an 896-thread block
-// caps registers at 72, which seven warps per sub-partition can hold).  TMEM: P buffers at
-// columns 0 and 128, moment accumulators at 256 and 384.  Slot (two):
-// [lo box | hi box | value box]; the lo box first holds the unrotated
-// relation coordinates for the store, and receives lo once the store has
-// read them.
-// ============================================================================
-constexpr int kFConvWarp0 = 2, kFConvWarps = 4;
-constexpr int kFXWarp0 = 6, kFXWarps = 16;
-constexpr int kFEWarp0 = 22, kFEWarps = 4;
-constexpr int kFSWarp = 26;
-constexpr int kFThreads = 28 * 32;
-constexpr int kFMaxStages = 6;
-constexpr int kFPrefetch = 2;  // tiles of x prefetched into L2 ahead of the loads
-constexpr uint32_t kFSlotBytes = 3 * kBox;
-
-struct FusedArgs {
-  const uint8_t* wprep;     // [groups][KB][128 rows x 128 B] BF16, K-major 128-byte-swizzled canonical
-  const float* bias;        // nullable [W]
-  const uint8_t* row_mask;  // nullable [B*N], nonzero = valid
-  const __half2* phase16;   // [pos_rows][N][R/2] (cos, sin)
-  float* partial;           // [B*H][nchunks][2R][R + d]
-  int* status;
-  int N, H, d, hg, groups, ntiles, ct, nchunks;
-  int items_g;              // items of one group: B * nchunks
-  int cg, dm, db;           // CTAs per group, and that stride as (chunk, sample) steps
-  int pos_batched, x_fp16, KB, stages;
-  uint32_t off_x, off_slot;  // shared-memory offsets of the x stages and the slots (the weight is at 0)
-};
-
-struct FusedShared {
-  uint64_t xfull[kFMaxStages];   // producer -> converter / MMA (x box landed)
-  uint64_t xconv[kFMaxStages];   // converter -> MMA (FP16 x rounded to BF16)
-  uint64_t xempty[kFMaxStages];  // MMA -> producer
-  uint64_t wfull;                // weight landed
-  uint64_t pfull[2], pempty[2];  // GEMM buffers: MMA -> epilogue, epilogue -> MMA
-  uint64_t sfree[2];             // slot: moment MMA done reading
-  uint64_t staged[2];            // epilogue -> storer (store boxes written)
-  uint64_t stored[2];            // storer -> epilogue (store read the boxes)
-  uint64_t xdone[2];             // epilogue -> MMA (operands ready)
-  uint64_t mfull[2], mempty[2];  // moment accumulators: MMA -> drain, drain -> MMA
-  uint64_t mdrain;               // teardown: the MMA thread's last commit (mma_drain)
-  uint32_t tmem;
-  int abort_flag;
-  __align__(16) float bias[128];  // the group's bias (relation box, value box)
-};
-
-// The items of one CTA of a fixed head group, it = j + i * cg over
-// B * nchunks, as (chunk fastest, sample), advanced without division.
-struct GroupWalk {
-  int m, b;
-  __device__ __forceinline__ void start(int j, int nchunks) {
-    m = j % nchunks;
-    b = j / nchunks;
-  }
-  __device__ __forceinline__ void next(int nchunks, int dm, int db) {
-    m += dm;
-    const int c = m >= nchunks ? 1 : 0;
-    m -= c * nchunks;
-    b += db + c;
-  }
-};
-
-// A position in the tile sequence of GroupWalk's items (item i, tile tt of nt).
-struct TileCursor {
-  GroupWalk w;
-  int i, tt, nt;
-  __device__ __forceinline__ void start(int j, int nchunks, int ct, int ntiles, int nloc) {
-    w.start(j, nchunks);
-    i = 0;
-    tt = 0;
-    nt = nloc > 0 ? min(ct, ntiles - w.m * ct) : 0;
-  }
-  __device__ __forceinline__ void advance(int nchunks, int dm, int db, int ct, int ntiles, int nloc) {
-    if (i >= nloc) return;
-    if (++tt < nt) return;
-    ++i;
-    tt = 0;
-    w.next(nchunks, dm, db);
-    nt = i < nloc ? min(ct, ntiles - w.m * ct) : 0;
-  }
-  __device__ __forceinline__ int tile(int ct) const { return w.m * ct + tt; }
-};
-
-__device__ __forceinline__ uint4 half8_to_bf16x8(uint4 x) {
-  const uint32_t in[4] = {x.x, x.y, x.z, x.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&in[i]));
-    o[i] = pack_bf16(f.x, f.y);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// Four FP16 (cos, sin) pairs -> Phase4 (the FP16 table holds the same values as the FP32 one).
-__device__ __forceinline__ Phase4 phase4_from_half(uint4 h) {
-  const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
-  const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
-  const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&h.z));
-  const float2 p3 = __half22float2(*reinterpret_cast<const __half2*>(&h.w));
-  return Phase4{make_float4(p0.x, p0.y, p1.x, p1.y), make_float4(p2.x, p2.y, p3.x, p3.y)};
-}
-
-// 8 accumulator values + their bias (16-byte aligned in shared memory), zero
-// unless `live`, rounded to BF16 once.
-__device__ __forceinline__ uint4 bias_mask_bf16(const float (&v)[8], const float* bias8, bool live) {
-  const float4 b0 = *reinterpret_cast<const float4*>(bias8);
-  const float4 b1 = *reinterpret_cast<const float4*>(bias8 + 4);
-  float x[8] = {v[0] + b0.x, v[1] + b0.y, v[2] + b0.z, v[3] + b0.w, v[4] + b1.x, v[5] + b1.y, v[6] + b1.z, v[7] + b1.w};
-#pragma unroll
-  for (int e = 0; e < 8; ++e) x[e] = live ? x[e] : 0.0f;
-  return pack8_bf16(x);
-}
-
-template <int R>
-__global__ void __launch_bounds__(kFThreads, 1) proj_moments_kernel(const __grid_constant__ CUtensorMap tm_x,
-                                                                     const __grid_constant__ CUtensorMap tm_proj,
-                                                                     const FusedArgs a) {
-  pdl_wait();
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ FusedShared sh;
-  volatile int* abort_v = &sh.abort_flag;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = a.stages;
-  const int g = static_cast<int>(blockIdx.x) % a.groups;
-  const int j0 = static_cast<int>(blockIdx.x) / a.groups;
-  const int nloc = a.items_g > j0 ? (a.items_g - j0 + a.cg - 1) / a.cg : 0;
-  const int d = a.d;
-  const int rel0 = g * a.hg * R;                 // the group's relation box (64 features)
-  const int vbase = (g * a.hg * d) & ~63;        // its value box within the D content features
-  const bool vown = ((g * a.hg * d) & 63) == 0;  // the group the value box starts with stores it
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&sh.xfull[s]), 1);
-      mbar_init(smem_u32(&sh.xconv[s]), kFConvWarps);
-      mbar_init(smem_u32(&sh.xempty[s]), 1);
-    }
-    mbar_init(smem_u32(&sh.wfull), 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&sh.pfull[i]), 1);
-      mbar_init(smem_u32(&sh.pempty[i]), kFXWarps);
-      mbar_init(smem_u32(&sh.sfree[i]), 1);
-      mbar_init(smem_u32(&sh.staged[i]), kFXWarps);
-      mbar_init(smem_u32(&sh.stored[i]), 1);
-      mbar_init(smem_u32(&sh.xdone[i]), kFXWarps);
-      mbar_init(smem_u32(&sh.mfull[i]), 1);
-      mbar_init(smem_u32(&sh.mempty[i]), kFEWarps);
-    }
-    mbar_init(smem_u32(&sh.mdrain), 1);
-    sh.abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (threadIdx.x < 128) {
-    const int n = static_cast<int>(threadIdx.x);
-    const int col = n < 64 ? rel0 + n : a.H * R + vbase + (n - 64);
-    sh.bias[n] = a.bias != nullptr ? a.bias[col] : 0.0f;
-  }
-  if (warp == 1) tmem_alloc(smem_u32(&sh.tmem), 512);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t sbase = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + (((sbase + 1023u) & ~1023u) - sbase);
-  int last_use[kFMaxStages] = {-1, -1, -1, -1, -1, -1};
-  bool wloaded = false;
-  // tiles of this CTA, in walk order
-  int total = 0;
-  {
-    GroupWalk w;
-    w.start(j0, a.nchunks);
-    for (int i = 0; i < nloc; ++i, w.next(a.nchunks, a.dm, a.db)) total += min(a.ct, a.ntiles - w.m * a.ct);
-  }
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tm_x);
-      const uint32_t wbytes = static_cast<uint32_t>(a.KB) * kBox;  // 128 rows x 128 B per 64-wide K region
-      mbar_arrive_expect_tx(smem_u32(&sh.wfull), wbytes);
-      const uint8_t* src = a.wprep + static_cast<size_t>(g) * wbytes;
-      for (uint32_t off = 0; off < wbytes; off += kBox)
-        bulk_load(smem_u32(smem + off), src + off, kBox, smem_u32(&sh.wfull));
-      wloaded = true;
-    }
-    __syncwarp();
-    GroupWalk w;
-    w.start(j0, a.nchunks);
-    RingPos xs;
-    // x boxes kFPrefetch tiles ahead are prefetched into L2, so the loads
-    // the stages can hold (one or two tiles) do not wait for HBM.
-    TileCursor ahead;
-    ahead.start(j0, a.nchunks, a.ct, a.ntiles, nloc);
-    for (int k = 0; k < kFPrefetch; ++k) ahead.advance(a.nchunks, a.dm, a.db, a.ct, a.ntiles, nloc);
-    bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i, w.next(a.nchunks, a.dm, a.db)) {
-      const int t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
-      for (int tt = 0; tt < nt && ok; ++tt) {
-        if (lane == 0 && ahead.i < nloc) {
-          for (int kb = 0; kb < a.KB; ++kb) tma_prefetch_3d(&tm_x, kb * 64, ahead.tile(a.ct) * kTT, ahead.w.b);
-        }
-        ahead.advance(a.nchunks, a.dm, a.db, a.ct, a.ntiles, nloc);
-        for (int kb = 0; kb < a.KB && ok; ++kb, xs.next(S)) {
-          ok = twait(smem_u32(&sh.xempty[xs.s]), (xs.u & 1) ^ 1, abort_v, a.status);
-          if (ok && lane == 0) {
-            const uint32_t bar = smem_u32(&sh.xfull[xs.s]);
-            mbar_arrive_expect_tx(bar, kBox);
-            tma_load_3d(smem_u32(smem + a.off_x + xs.s * kBox), &tm_x, kb * 64, (t0 + tt) * kTT, w.b, bar);
-            last_use[xs.s] = xs.u;
-          }
-          __syncwarp();
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    bool ok = twait(smem_u32(&sh.wfull), 0, abort_v, a.status);
-    tc_fence_after();
-    const uint32_t idesc_g = make_idesc(128, 128, false, false);  // K-major x and weight
-    const uint32_t idesc_m = make_idesc(128, 128, true, true);    // MN-major boxes (K = tokens)
-    const uint32_t sw = smem_u32(smem), sx = smem_u32(smem + a.off_x), ss = smem_u32(smem + a.off_slot);
-    RingPos xs;
-    // GEMM of tile n into P buffer n & 1
-    auto gemm = [&](int n) -> bool {
-      const int pb = n & 1;
-      if (!twait(smem_u32(&sh.pempty[pb]), ((n >> 1) & 1) ^ 1, abort_v, a.status)) return false;
-      tc_fence_after();
-      const uint32_t dcol = sh.tmem + static_cast<uint32_t>(pb * 128);
-      for (int kb = 0; kb < a.KB; ++kb, xs.next(S)) {
-        if (!twait(smem_u32(a.x_fp16 ? &sh.xconv[xs.s] : &sh.xfull[xs.s]), xs.u & 1, abort_v, a.status)) return false;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t st = sx + xs.s * kBox, wk = sw + kb * kBox;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            mma_bf16(dcol, make_desc_sw128(st + ks * 32, 16, 1024), make_desc_sw128(wk + ks * 32, 16, 1024), idesc_g,
-                     (kb | ks) != 0 ? 1u : 0u);
-          }
-          mma_commit(smem_u32(&sh.xempty[xs.s]));
-        }
-        __syncwarp();
-      }
-      if (lane == 0) mma_commit(smem_u32(&sh.pfull[pb]));
-      __syncwarp();
-      return true;
-    };
-    // The GEMMs run two tiles ahead: tile n + 2's needs only the P buffer the
-    // epilogue of tile n has loaded, while tile n's moment MMA waits for its
-    // operands, which the epilogue completes during tile n + 1.
-    if (ok && total > 0) ok = gemm(0);
-    if (ok && total > 1) ok = gemm(1);
-    GroupWalk w;
-    w.start(j0, a.nchunks);
-    int n = 0;
-    for (int i = 0; i < nloc && ok; ++i, w.next(a.nchunks, a.dm, a.db)) {
-      const int nt = min(a.ct, a.ntiles - w.m * a.ct);
-      const int mb = i & 1;
-      for (int tt = 0; tt < nt && ok; ++tt, ++n) {
-        if (n + 2 < total) ok = gemm(n + 2);
-        if (!ok) break;
-        const int s = n & 1;
-        ok = twait(smem_u32(&sh.xdone[s]), (n >> 1) & 1, abort_v, a.status);
-        tc_fence_after();
-        if (ok && tt == 0) {
-          ok = twait(smem_u32(&sh.mempty[mb]), ((i >> 1) & 1) ^ 1, abort_v, a.status);
-          tc_fence_after();
-        }
-        if (ok && lane == 0) {
-          const uint32_t slot = ss + s * kFSlotBytes;
-          const uint32_t dcol = sh.tmem + static_cast<uint32_t>(256 + mb * 128);
-#pragma unroll
-          for (int ks = 0; ks < kTT / 16; ++ks) {
-            mma_bf16(dcol, make_desc_sw128(slot + ks * 2048, kBox, 1024),
-                     make_desc_sw128(slot + kBox + ks * 2048, kBox, 1024), idesc_m, (tt > 0 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(smem_u32(&sh.sfree[s]));
-          if (tt == nt - 1) mma_commit(smem_u32(&sh.mfull[mb]));
-        }
-        __syncwarp();
-      }
-    }
-  } else if (warp < kFConvWarp0 + kFConvWarps) {
-    // ------------------------------------------------------------ FP16 -> BF16 rounding of the x boxes
-    if (a.x_fp16) {
-      const int ct = static_cast<int>(threadIdx.x) - kFConvWarp0 * 32;
-      constexpr int kPer = static_cast<int>(kBox / 16) / (kFConvWarps * 32);
-      RingPos xs;
-      bool ok = true;
-      for (int n = 0; n < total && ok; ++n) {
-        for (int kb = 0; kb < a.KB && ok; ++kb, xs.next(S)) {
-          ok = twait(smem_u32(&sh.xfull[xs.s]), xs.u & 1, abort_v, a.status);
-          if (ok) {
-            uint4* p = reinterpret_cast<uint4*>(smem + a.off_x + xs.s * kBox);
-            uint4 v[kPer];
-#pragma unroll
-            for (int q = 0; q < kPer; ++q) v[q] = p[ct + q * kFConvWarps * 32];
-#pragma unroll
-            for (int q = 0; q < kPer; ++q) p[ct + q * kFConvWarps * 32] = half8_to_bf16x8(v[q]);
-            fence_proxy_async();
-          }
-          __syncwarp();
-          if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xconv[xs.s]));
-        }
-      }
-    }
-  } else if (warp < kFXWarp0 + kFXWarps) {
-    // ------------------------------------------------------------ epilogue: projected coordinates, rotation, hi/lo
-    const int sub = warp & 3;
-    const int q4 = (warp - kFXWarp0) >> 2;  // features 16 q4 .. 16 q4 + 15 of the relation and of the value box
-    const int c0 = 2 * q4;                  // their two 16-byte chunks of a 128-byte box row
-    const int r = 32 * sub + lane;          // tile row (token) of this thread
-    const uint32_t trow = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
-    const int pr0 = ((16 * q4) % R) / 2;    // the phase pair of its first relation feature
-    uint8_t* slots = smem + a.off_slot;
-    uint32_t ident;
-    {
-      const __half2 one = __floats2half2_rn(1.0f, 0.0f);
-      ident = *reinterpret_cast<const uint32_t*>(&one);
-    }
-    auto fetch = [&](int b, int tile, uint4 (&ph)[2]) {
-      const int tok = tile * kTT + r;
-      if (tok < a.N) {
-        const int64_t prow = a.pos_batched ? static_cast<int64_t>(b) * a.N : 0;
-        const uint4* src = reinterpret_cast<const uint4*>(a.phase16 + (prow + tok) * (R / 2) + pr0);
-        ph[0] = __ldg(src);
-        ph[1] = __ldg(src + 1);
-      } else {
-        ph[0] = ph[1] = make_uint4(ident, ident, ident, ident);
-      }
-    };
-    // Tile n's lo goes into the lo box once the store has read the unrotated
-    // coordinates there; that wait is taken after tile n + 1's accumulator
-    // has been staged, so the store's read overlaps the next tile's work.
-    GroupWalk w;
-    w.start(j0, a.nchunks);
-    uint4 ph[2], lo[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-    int n = 0, ps = 0, ppar = 0;
-    bool ok = true, pending = false;
-    auto finish_pending = [&]() {
-      ok = twait(smem_u32(&sh.stored[ps]), ppar, abort_v, a.status);
-      if (ok) {
-        uint8_t* plo = slots + ps * kFSlotBytes;
-        *reinterpret_cast<uint4*>(box_chunk(plo, r, c0)) = lo[0];
-        *reinterpret_cast<uint4*>(box_chunk(plo, r, c0 + 1)) = lo[1];
-        fence_proxy_async();
-      }
-      __syncwarp();
-      if (ok && lane == 0) mbar_arrive(smem_u32(&sh.xdone[ps]));
-      pending = false;
-    };
-    for (int i = 0; i < nloc && ok; ++i, w.next(a.nchunks, a.dm, a.db)) {
-      const int b = w.b, t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
-      for (int tt = 0; tt < nt && ok; ++tt, ++n) {
-        fetch(b, t0 + tt, ph);  // used by this tile's rotation, after the staging below
-        const int s = n & 1, par = (n >> 1) & 1;
-        const int tok = (t0 + tt) * kTT + r;
-        const bool live =
-            tok < a.N && (a.row_mask == nullptr || a.row_mask[static_cast<int64_t>(b) * a.N + tok] != 0);
-        uint8_t* lo_box = slots + s * kFSlotBytes;
-        uint8_t* hi_box = lo_box + kBox;
-        uint8_t* val_box = lo_box + 2 * kBox;
-        ok = twait_warp(smem_u32(&sh.pfull[s]), par, abort_v, a.status);
-        tc_fence_after();
-        if (ok) ok = twait_warp(smem_u32(&sh.sfree[s]), par ^ 1, abort_v, a.status);
-        uint4 rel[2];
-        if (ok) {
-          // the relation and value features: + bias, masked rows zero, BF16; the
-          // relation unrotated into the lo box for the store
-          const uint32_t pcol = trow + static_cast<uint32_t>(s * 128 + 16 * q4);
-          float vr[16], vv[16];
-          tmem_ld16(pcol, vr);
-          tmem_ld16(pcol + 64, vv);
-          tmem_ld_wait();
-          const float r0[8] = {vr[0], vr[1], vr[2], vr[3], vr[4], vr[5], vr[6], vr[7]};
-          const float r1[8] = {vr[8], vr[9], vr[10], vr[11], vr[12], vr[13], vr[14], vr[15]};
-          const float v0[8] = {vv[0], vv[1], vv[2], vv[3], vv[4], vv[5], vv[6], vv[7]};
-          const float v1[8] = {vv[8], vv[9], vv[10], vv[11], vv[12], vv[13], vv[14], vv[15]};
-          rel[0] = bias_mask_bf16(r0, &sh.bias[8 * c0], live);
-          rel[1] = bias_mask_bf16(r1, &sh.bias[8 * c0 + 8], live);
-          *reinterpret_cast<uint4*>(box_chunk(lo_box, r, c0)) = rel[0];
-          *reinterpret_cast<uint4*>(box_chunk(lo_box, r, c0 + 1)) = rel[1];
-          *reinterpret_cast<uint4*>(box_chunk(val_box, r, c0)) = bias_mask_bf16(v0, &sh.bias[64 + 8 * c0], live);
-          *reinterpret_cast<uint4*>(box_chunk(val_box, r, c0 + 1)) =
-              bias_mask_bf16(v1, &sh.bias[64 + 8 * c0 + 8], live);
-          fence_proxy_async();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (ok && lane == 0) {
-          mbar_arrive(smem_u32(&sh.pempty[s]));
-          mbar_arrive(smem_u32(&sh.staged[s]));
-        }
-        if (ok && pending) finish_pending();
-        if (ok) {
-          // rotation: hi into the hi box now, lo held until the store has read the lo box
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            float v[8];
-            rotate8(rel[q], phase4_from_half(ph[q]), v);
-            const uint4 hi = pack8_bf16(v);
-            const float2 h0 = unpack_bf16(hi.x), h1 = unpack_bf16(hi.y), h2 = unpack_bf16(hi.z), h3 = unpack_bf16(hi.w);
-            float l[8] = {v[0] - h0.x, v[1] - h0.y, v[2] - h1.x, v[3] - h1.y,
-                          v[4] - h2.x, v[5] - h2.y, v[6] - h3.x, v[7] - h3.y};
-            lo[q] = pack8_bf16(l);
-            *reinterpret_cast<uint4*>(box_chunk(hi_box, r, c0 + q)) = hi;
-          }
-          pending = true;
-          ps = s;
-          ppar = par;
-        }
-      }
-    }
-    if (ok && pending) finish_pending();
-  } else if (warp < kFEWarp0 + kFEWarps) {
-    // ------------------------------------------------------------ drain the moment accumulators
-    const int sub = warp & 3;
-    const uint32_t lane_base = sh.tmem + (static_cast<uint32_t>(32 * sub) << 16);
-    GroupWalk w;
-    w.start(j0, a.nchunks);
-    bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i, w.next(a.nchunks, a.dm, a.db)) {
-      const int mb = i & 1;
-      ok = twait_warp(smem_u32(&sh.mfull[mb]), (i >> 1) & 1, abort_v, a.status);
-      tc_fence_after();
-      if (ok) {
-        drain_moments<R, false>(lane_base + static_cast<uint32_t>(256 + mb * 128), sub, lane, a.partial, w.b, g, w.m,
-                                a.H, a.hg, d, a.nchunks);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.mempty[mb]));
-    }
-  } else if (warp == kFSWarp) {
-    // ------------------------------------------------------------ storer
-    if (lane == 0) prefetch_tmap(&tm_proj);
-    GroupWalk w;
-    w.start(j0, a.nchunks);
-    int n = 0;
-    bool ok = true;
-    for (int i = 0; i < nloc && ok; ++i, w.next(a.nchunks, a.dm, a.db)) {
-      const int t0 = w.m * a.ct, nt = min(a.ct, a.ntiles - t0);
-      for (int tt = 0; tt < nt && ok; ++tt, ++n) {
-        const int s = n & 1;
-        ok = twait(smem_u32(&sh.staged[s]), (n >> 1) & 1, abort_v, a.status);
-        if (ok && lane == 0) {
-          const uint8_t* slot = smem + a.off_slot + s * kFSlotBytes;
-          const int row = (t0 + tt) * kTT;
-          tma_store_3d(&tm_proj, smem_u32(slot), rel0, row, w.b);
-          if (vown) tma_store_3d(&tm_proj, smem_u32(slot + 2 * kBox), a.H * R + vbase, row, w.b);
-          bulk_commit();
-          bulk_wait_read<0>();
-          mbar_arrive(smem_u32(&sh.stored[s]));
-        }
-        __syncwarp();
-      }
-    }
-    if (lane == 0) bulk_wait<0>();
-    __syncwarp();
-  }
-
-  if (threadIdx.x == 32) mma_drain(smem_u32(&sh.mdrain), a.status);  // warp 1, lane 0 issues the MMAs
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    // the producer's loads still in flight (only after an abort)
-    if (wloaded) mbar_wait(smem_u32(&sh.wfull), 0, a.status);
-    for (int s = 0; s < S; ++s) {
-      if (last_use[s] >= 0) mbar_wait(smem_u32(&sh.xfull[s]), static_cast<uint32_t>(last_use[s]) & 1u, a.status);
-    }
-  }
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(sh.tmem, 512);
-  }
-}
-
-// The fused kernel's weight: each head group's 128 rows of the input
-// projection weight (its relation box, then its value box) as BF16 in the
-// K-major 128-byte-swizzled canonical layout, [groups][D/64][128 x 128 B]:
-// row n of a 64-wide K region at (n/8)*1024 + (n%8)*128, its 16-byte chunk c
-// at chunk c ^ (n%8).  One thread per 16-byte chunk (coalesced FP32 reads).
-__global__ void fused_weight_kernel(const float* __restrict__ w, int D, int H, int R, int d, int hg, int groups,
-                                    uint8_t* __restrict__ out) {
-  pdl_wait();
-  const int per_row = D / 8;
-  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= groups * 128 * per_row) return;
-  const int kc = idx % per_row;
-  const int gr = idx / per_row;
-  const int n = gr & 127, g = gr >> 7;
-  const int row = n < 64 ? g * hg * R + n : H * R + ((g * hg * d) & ~63) + (n - 64);
-  const float4* src = reinterpret_cast<const float4*>(w + static_cast<int64_t>(row) * D + kc * 8);
-  const float4 p = src[0], q = src[1];
-  const uint4 o = make_uint4(pack_bf16(p.x, p.y), pack_bf16(p.z, p.w), pack_bf16(q.x, q.y), pack_bf16(q.z, q.w));
-  const int kb = kc >> 3, c = kc & 7;
-  const size_t off = (static_cast<size_t>(g) * (D / 64) + kb) * kBox + (n >> 3) * 1024 + (n & 7) * 128 +
-                     ((c ^ (n & 7)) << 4);
-  *reinterpret_cast<uint4*>(out + off) = o;
-}
-
-// ============================================================================
 // Readout: Y = eta C + A' R_d per (sample, head group, tile).  MMA per head:
 // M = 128 tokens, K = R (rotated relation, K-major straight from its box),
 // N = d (R_d, K-major canonical from the solve).  The epilogue writes
@@ -1606,82 +1073,6 @@ cudaError_t launch_moments_tiled(const Plan& p, bool bwd, const bf16* proj, cons
   } else {
     if (bwd) launch_pdl(moments_tile_kernel<64, true>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
     else launch_pdl(moments_tile_kernel<64, false>, grid, kMThreads, smem, stream, tm_rel, tm_val, a);
-  }
-  return cudaGetLastError();
-}
-
-bool fused_input_usable(const Plan& p) {
-  if (!p.tiled || tensor_map_encoder() == nullptr) return false;
-  if (p.R != 32 && p.R != 64) return false;
-  if ((64 / p.R) * p.d > 64) return false;  // the group's heads fit one value box
-  if (p.D % 64 != 0 || p.D > 256) return false;
-  const int64_t wbytes = (p.D / 64) * kBox;
-  return (kTileSmemBudget - 1024 - wbytes - 2 * static_cast<int64_t>(kFSlotBytes)) / kBox >= 2;
-}
-
-size_t fused_weight_bytes(const Plan& p) {
-  const int64_t groups = p.H * p.R / 64;
-  return static_cast<size_t>(groups * (p.D / 64) * kBox);
-}
-
-cudaError_t launch_proj_moments(const Plan& p, const FusedInput& in, float* partial, int* status, int sm_count,
-                                cudaStream_t stream) {
-  if (!fused_input_usable(p) || !aligned16(in.x) || !aligned16(in.projected) || !aligned16(in.weight) ||
-      !aligned16(in.wprep) || !aligned16(in.phase16)) {
-    return cudaErrorInvalidValue;
-  }
-  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
-  CUtensorMap tm_x{}, tm_proj{};
-  // x boxes are copied bit for bit (FP16 or BF16: both 2-byte elements, zero fill past N)
-  if (encode_boxes(encode, &tm_x, in.x, p.D, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (encode_boxes(encode, &tm_proj, in.projected, p.W, p.N, p.B) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  FusedArgs a{};
-  a.wprep = in.wprep;
-  a.bias = in.bias;
-  a.row_mask = in.row_mask;
-  a.phase16 = in.phase16;
-  a.partial = partial;
-  a.status = status;
-  a.N = static_cast<int>(p.N);
-  a.H = static_cast<int>(p.H);
-  a.d = static_cast<int>(p.d);
-  a.hg = static_cast<int>(64 / p.R);
-  a.groups = static_cast<int>(p.H / a.hg);
-  a.ntiles = static_cast<int>(ceil_div(p.N, kTT));
-  a.ct = p.ct;
-  a.nchunks = static_cast<int>(p.nchunks);
-  a.items_g = static_cast<int>(p.B * p.nchunks);
-  const int sms = sm_count > 0 ? sm_count : 148;
-  a.cg = std::max(1, std::min(sms / a.groups, a.items_g));
-  a.dm = a.cg % a.nchunks;
-  a.db = a.cg / a.nchunks;
-  a.pos_batched = p.pos_rows > 1 ? 1 : 0;
-  a.x_fp16 = in.x_fp16;
-  a.KB = static_cast<int>(p.D / 64);
-  const uint32_t wbytes = static_cast<uint32_t>(a.KB) * kBox;
-  const int64_t avail = kTileSmemBudget - 1024 - wbytes - 2 * static_cast<int64_t>(kFSlotBytes);
-  a.stages = static_cast<int>(std::min<int64_t>(kFMaxStages, avail / kBox));
-  a.off_x = wbytes;
-  a.off_slot = wbytes + static_cast<uint32_t>(a.stages) * kBox;
-  const size_t smem = a.off_slot + 2 * static_cast<size_t>(kFSlotBytes) + 1024;
-  const int grid = a.cg * a.groups;
-  {
-    const int chunks = a.groups * 128 * static_cast<int>(p.D / 8);
-    LaunchScope scope("fused_weight", stream);
-    launch_pdl(fused_weight_kernel, static_cast<unsigned>((chunks + 255) / 256), 256, 0, stream, 
-        in.weight, static_cast<int>(p.D), a.H, static_cast<int>(p.R), a.d, a.hg, a.groups, in.wprep);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
-  const void* fn = p.R == 32 ? reinterpret_cast<const void*>(&proj_moments_kernel<32>)
-                             : reinterpret_cast<const void*>(&proj_moments_kernel<64>);
-  const cudaError_t e = allow_smem(fn, smem);
-  if (e != cudaSuccess) return e;
-  LaunchScope scope("proj_moments", stream);
-  if (p.R == 32) {
-    launch_pdl(proj_moments_kernel<32>, grid, kFThreads, smem, stream, tm_x, tm_proj, a);
-  } else {
-    launch_pdl(proj_moments_kernel<64>, grid, kFThreads, smem, stream, tm_x, tm_proj, a);
   }
   return cudaGetLastError();
 }
