@@ -389,7 +389,7 @@ __device__ __forceinline__ void add4(float4& a, const float4 b) {
 // e of the first R rows summed over the chunks, high and low rows separately,
 // in float4 steps (every load coalesced and independent of the others).
 // fn(row, col, hi4, lo4) receives the four columns starting at col.
-template <int R, typename Fn>
+template <int R, int BATCH, typename Fn>
 __device__ __forceinline__ void sum_chunks(const float* partial, int nchunks, int cols, Fn fn) {
   const int c4 = cols / 4;
   const int64_t lo = static_cast<int64_t>(R) * c4;
@@ -398,9 +398,25 @@ __device__ __forceinline__ void sum_chunks(const float* partial, int nchunks, in
   for (int e = threadIdx.x; e < R * c4; e += kWThreads) {
     float4 hi = __ldg(P4 + e);
     float4 lw = __ldg(P4 + lo + e);
-    for (int ch = 1; ch < nchunks; ++ch) {
-      add4(hi, __ldg(P4 + ch * stride + e));
-      add4(lw, __ldg(P4 + ch * stride + lo + e));
+    // The chunks BATCH at a time: their loads are all in flight before the
+    // additions, which still go in chunk order (the partials come from L2 or
+    // DRAM, so one round trip per chunk would dominate the sum).
+    for (int ch = 1; ch < nchunks; ch += BATCH) {
+      float4 h[BATCH], l[BATCH];
+#pragma unroll
+      for (int u = 0; u < BATCH; ++u) {
+        if (ch + u < nchunks) {
+          h[u] = __ldg(P4 + (ch + u) * stride + e);
+          l[u] = __ldg(P4 + (ch + u) * stride + lo + e);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < BATCH; ++u) {
+        if (ch + u < nchunks) {
+          add4(hi, h[u]);
+          add4(lw, l[u]);
+        }
+      }
     }
     const int row = e / c4;
     fn(row, (e - row * c4) * 4, hi, lw);
@@ -422,7 +438,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // M = I + F F^T + Omega = LU, U = M^{-1} Z, R_d = L^{-T}(2U - (1+eta) Z)/sqrt(n).
 // ============================================================================
 template <int R>
-__global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const SolveFwdArgs a) {
+__global__ void __launch_bounds__(kWThreads, 4) solve_forward_warp_kernel(const SolveFwdArgs a) {
   pdl_wait();
   constexpr int LD = R + 1;
   constexpr int P = rows_per_lane<R>();
@@ -455,7 +471,7 @@ __global__ void __launch_bounds__(kWThreads) solve_forward_warp_kernel(const Sol
   for (int idx = tid; idx < d * R; idx += kWThreads) Ws[(idx / R) * LD + idx % R] = Wd[idx];
   // 1. Sum the chunk partials (ndt == 1): L <- hh + lh, Th <- lh, S = (hC + lC)/sqrt(n);
   //    then G = (hh + lh + lh^T)/n + I on the lower triangle.
-  sum_chunks<R>(pbase, a.nchunks, NC, [&](int i, int c, float4 hi, float4 lo) {
+  sum_chunks<R, 3>(pbase, a.nchunks, NC, [&](int i, int c, float4 hi, float4 lo) {
     const float hv[4] = {hi.x, hi.y, hi.z, hi.w};
     const float lv[4] = {lo.x, lo.y, lo.z, lo.w};
 #pragma unroll
@@ -638,7 +654,7 @@ __global__ void __launch_bounds__(kWThreads, R <= 32 ? 5 : 4)
     Th[i * LD + jj] = tape[tl.Theta + idx];
   }
   // X1 = A'^T dY summed over the chunks (high + low halves)
-  sum_chunks<R>(pbase, a.nchunks, NC, [&](int i, int c, float4 hi, float4 lo) {
+  sum_chunks<R, 1>(pbase, a.nchunks, NC, [&](int i, int c, float4 hi, float4 lo) {
     const float v[4] = {hi.x + lo.x, hi.y + lo.y, hi.z + lo.z, hi.w + lo.w};
 #pragma unroll
     for (int u = 0; u < 4; ++u)
