@@ -259,3 +259,48 @@ def test_exchange_transport_choice_without_a_process_group() -> None:
         assert exchange.transport == "none"
         assert exchange.averaged is exchange.flat
         exchange.close()
+
+
+def test_buckets_go_out_in_bucket_order_whatever_order_they_complete() -> None:
+    """Every rank must launch its bucket exchanges in the same order (each launch of the peer
+    exchange pairs with the peers' launch of the same number): a bucket that completes before an
+    earlier one waits for it, and finish() launches what is left in order.  Each bucket also starts
+    at a multiple of four values (16-byte aligned parts of the exchange region)."""
+    from lsso import LSSO, LSSOConfig
+    from lsso_b200.ball.distributed import GradientExchange
+
+    layer = LSSO(LSSOConfig(36, 2, 16, bias=True))
+    params = list(layer.parameters())
+    buckets = [[params[0]], [params[1], params[2]], [params[3]], params[4:]]
+    exchange = GradientExchange(buckets)
+    order: list[int] = []
+    real_launch = exchange._launch
+
+    def record(k: int) -> None:
+        order.append(k)
+        real_launch(k)
+
+    exchange._launch = record
+    try:
+        assert all(start % 4 == 0 for start in exchange.bucket_start)
+        for k, bucket in enumerate(buckets):
+            for p in bucket:
+                assert exchange.slot[p].data_ptr() >= exchange.flat.data_ptr() + 4 * exchange.bucket_start[k]
+        # bucket 2 completes first, then 0 (which releases 0 only: 1 is still open), then 1 (releases 1, 2)
+        for p in buckets[2]:
+            exchange._mark(p)
+        assert order == []
+        for p in buckets[0]:
+            exchange._mark(p)
+        assert order == [0]
+        for p in buckets[1]:
+            exchange._mark(p)
+        assert order == [0, 1, 2]
+        exchange.finish()  # bucket 3 never completed: zero-filled and launched last
+        assert order == [0, 1, 2, 3]
+        assert all(torch.count_nonzero(p.grad) == 0 for p in buckets[3])
+        order.clear()
+        exchange.finish()  # a step with no backward at all: every bucket, in order
+        assert order == [0, 1, 2, 3]
+    finally:
+        exchange.close()
