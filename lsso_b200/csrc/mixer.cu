@@ -16,6 +16,7 @@
 //   solve_backward_kernel adjoint solves, parameter-gradient partials, pass-2 operands
 //   grad_kernel           d relation / d content per 128-token tile
 //   param_reduce_kernel   deterministic sum of parameter gradients over samples
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <vector>
@@ -1675,13 +1676,22 @@ int solve_ctas_beside(const Plan& p, const WgradPlan& wp, int device) {
   }
   // registers are allocated per warp in units of 256
   auto cta_regs = [](const CtaFootprint& f) { return (f.regs * 32 + 255) / 256 * 256 * (f.threads / 32); };
-  for (int k = 2; k >= 1; --k) {
-    const bool fit = cta_regs(fw) + k * cta_regs(fs) <= regs &&
-                     fw.smem + reserved + k * (fs.smem + reserved) <= static_cast<size_t>(smem) &&
-                     fw.threads + k * fs.threads <= threads;
-    if (fit) return k;
-  }
-  return 0;
+  // Two solve CTAs per SM beside the GEMM, and at most one round of systems more than the solve
+  // launched alone takes in waves: a solve CTA's time hardly shrinks with fewer CTAs per SM, so
+  // with one CTA per SM (rank 48) the concurrent form measured slower (2.015 -> 2.051 ms per step).
+  const int k = 2;
+  const bool fit = cta_regs(fw) + k * cta_regs(fs) <= regs &&
+                   fw.smem + reserved + k * (fs.smem + reserved) <= static_cast<size_t>(smem) &&
+                   fw.threads + k * fs.threads <= threads;
+  if (!fit) return 0;
+  int alone = 32;  // solve CTAs per SM without the GEMM
+  alone = std::min(alone, regs / std::max(1, cta_regs(fs)));
+  alone = std::min(alone, static_cast<int>(static_cast<size_t>(smem) / (fs.smem + reserved)));
+  alone = std::min(alone, threads / fs.threads);
+  if (alone < 1) return 0;
+  const int64_t waves = ceil_div(p.BH, static_cast<int64_t>(alone) * p.sms);
+  const int64_t rounds = ceil_div(p.BH, static_cast<int64_t>(k) * p.sms);
+  return rounds <= waves + 1 ? k : 0;
 }
 
 cudaError_t launch_backward_with_wgrad(const Plan& p, const BackwardBuffers& bb, const WgradPlan& wp,
